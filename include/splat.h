@@ -1,0 +1,350 @@
+/* splat.h — C ABI of the B200-native differentiable Gaussian-splatting rasterizer and
+ * optimiser step (libsplat_b200.so).
+ *
+ * The entry points mirror the Rust API of instantsplat-rs, so that its `Trainer`
+ * (instantsplat-rs/src/training.rs) can hold an sp_rasterizer / sp_adam instead of a
+ * `Rasterizer` / `Adam`:
+ *   Rasterizer  — instantsplat-rs/src/rasterizer.rs:134-565
+ *   Adam        — instantsplat-rs/src/optimizer.rs:118-276
+ *   camera      — instantsplat-rs/src/camera.rs:8-70
+ *   pose chain  — instantsplat-rs/src/camera_pose.rs:39-99, pose_refinement.rs:113-163
+ * Each declaration names the reference item it replaces.
+ *
+ * Conventions.
+ *  - Every call returns an sp_status; SP_OK is 0. Where the reference panics (an assert!
+ *    or expect), the matching call returns an error status instead and leaves its
+ *    outputs untouched; sp_last_error() gives the message.
+ *  - Device pointers passed in (parameters, ground truth) are borrowed: the caller owns
+ *    them and they must outlive the object that holds them (rasterizer.rs:176-184 takes
+ *    them as &wgpu::Buffer the same way). The library never frees them.
+ *  - All device work of a context is enqueued, in call order, on the context's CUDA
+ *    stream (its own, or one the caller lends). sp_read_* calls copy to host memory and
+ *    synchronise that stream, like the reference's blocking read_* wrappers.
+ *  - A context and everything made from it is used from one host thread at a time (the
+ *    reference runs one GPU job at a time, web/src/lib.rs:1-5). One context per GPU.
+ *  - Structures are #[repr(C)] compatible with the reference's Pod types: sizes are
+ *    checked by tests/test_abi.py (CameraUniform 80 B, CameraGradient 56 B,
+ *    IntersectionMeta 20 B, DensifyStats 16 B, Projected 80 B).
+ */
+#ifndef SPLAT_H
+#define SPLAT_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define SP_ABI_VERSION 1
+
+typedef enum sp_status {
+    SP_OK = 0,
+    /* A size or argument check failed: every assert! of rasterizer.rs:185-199, 399, 447,
+     * 454 and optimizer.rs:272-273, 302-303, 348-351. */
+    SP_ERR_INVALID = 1,
+    /* The tile grid is larger than the library holds (over 65535 tiles on a side). The
+     * reference stops at 4096 tiles in all (rasterizer.rs:188-192); this library moves to
+     * 64-bit keys there instead, keeping the same order. */
+    SP_ERR_TOO_MANY_TILES = 2,
+    /* The last forward pass had more (Gaussian, tile) pairs than the intersection list
+     * holds (the panic of read_intersections_async, rasterizer.rs:536-544). */
+    SP_ERR_OVERFLOW = 3,
+    /* A device-side wait gave up after its iteration limit (sort look-back). */
+    SP_ERR_TIMEOUT = 4,
+    SP_ERR_CUDA = 5,
+    SP_ERR_NCCL = 6,
+    /* A pose gradient was not finite (pose_refinement.rs:113-125). */
+    SP_ERR_NONFINITE = 7,
+    SP_ERR_NO_DEVICE = 8,
+    SP_ERR_OUT_OF_MEMORY = 9
+} sp_status;
+
+/* World-to-camera rows (r0, r1, r2, t), intrinsics and tile grid: CameraUniform,
+ * camera.rs:23-31 / common.wgsl:38-47. 80 bytes. */
+typedef struct sp_camera_uniform {
+    float world_to_camera_rows[3][4];
+    float focal[2];
+    float principal_point[2];
+    uint32_t width;
+    uint32_t height;
+    uint32_t tiles_x;
+    uint32_t tiles_y;
+} sp_camera_uniform;
+
+/* dL/d(world-to-camera rotation rows, translation, focal): CameraGradient,
+ * camera.rs:39-43. 56 bytes. */
+typedef struct sp_camera_gradient {
+    float world_to_camera_rotation_rows[3][3];
+    float world_to_camera_translation[3];
+    float focal[2];
+} sp_camera_gradient;
+
+/* IntersectionMeta, rasterizer.rs:29-37. 20 bytes. */
+typedef struct sp_intersection_meta {
+    uint32_t count;
+    uint32_t sort_blocks;
+    uint32_t histogram_length;
+    uint32_t overflow;
+    uint32_t capacity;
+} sp_intersection_meta;
+
+/* DensifyStats, rasterizer.rs:63-75. 16 bytes. */
+typedef struct sp_densify_stats {
+    float mean_gradient_sum;
+    float visible_count;
+    float max_radius;
+    float _pad;
+} sp_densify_stats;
+
+/* Projected, rasterizer.rs:46-61 / common.wgsl:49-61 (the diagnostics mirror). 80 bytes. */
+typedef struct sp_projected {
+    float mean[2];
+    float _pad0[2];
+    float conic[3];
+    float depth;
+    float color[3];
+    float opacity;
+    uint32_t radius;
+    uint32_t _pad1;
+    uint32_t tile_min[2];
+    uint32_t tile_max[2];
+    uint32_t _pad2[2];
+} sp_projected;
+
+/* LossWeights, loss.rs:20-36. */
+typedef struct sp_loss_weights {
+    float l1;
+    float dssim;
+    float alpha;
+} sp_loss_weights;
+
+/* LossTerms, loss.rs:38-64: means over the pixels (summed in double). */
+typedef struct sp_loss_terms {
+    float l1;
+    float alpha;
+    float dssim;
+    float total;
+} sp_loss_terms;
+
+/* LearningRates, optimizer.rs:17-26, plus the rate of the SH coefficients of degree 1-3
+ * (an extension; the reference has degree 0 only). */
+typedef struct sp_learning_rates {
+    float position;
+    float log_scale;
+    float rotation;
+    float opacity;
+    float sh_dc;
+    float camera_rotation;
+    float camera_translation;
+    float camera_focal;
+    float sh_rest;
+} sp_learning_rates;
+
+/* Sort key layouts. */
+enum {
+    /* (tile << 20) | (bits(depth) >> 12): the reference's order (emit_tile_keys.wgsl:24-29),
+     * held in 32 bits while tiles <= 4096 and in 64 bits above (the reference refuses
+     * those images; the order stays (tile, depth >> 12, Gaussian index)). */
+    SP_KEYS_REF20 = 0,
+    /* (tile << 32) | bits(depth): the full-precision depth order, 64-bit keys. */
+    SP_KEYS_FULL32 = 1
+};
+
+/* How the blend backward sums each Gaussian's gradient over the pixels of a tile. */
+enum {
+    /* One write per (Gaussian, tile) slot, summed per Gaussian afterwards in slot order,
+     * as rasterize_backward.wgsl:1-7 and project_backward.wgsl:38-55: bit-stable. */
+    SP_BWD_DETERMINISTIC = 0,
+    /* Warp-shuffle pre-reduction, then vector float atomics into per-Gaussian sums. */
+    SP_BWD_ATOMIC = 1
+};
+
+typedef struct sp_options {
+    uint32_t key_mode;                   /* SP_KEYS_* (default SP_KEYS_REF20) */
+    uint32_t backward_mode;              /* SP_BWD_* (default SP_BWD_ATOMIC) */
+    uint32_t sh_degree;                  /* 0 (stride 14, the reference) .. 3 (stride 59) */
+    uint32_t intersections_per_gaussian; /* capacity = this * N (default 24, rasterizer.rs:27) */
+    /* 0: each backward overwrites the parameter gradients (the reference). 1: it adds to
+     * them, for batches of views summed before one Adam step; clear with
+     * sp_zero_param_gradients. */
+    uint32_t accumulate_gradients;
+    sp_loss_weights loss_weights;        /* default LOSS_WEIGHTS (loss.rs:32-36) */
+} sp_options;
+
+typedef struct sp_context sp_context;
+typedef struct sp_rasterizer sp_rasterizer;
+typedef struct sp_adam sp_adam;
+
+/* ---------------------------------------------------------------- context / runtime */
+
+/* Library version string. */
+const char* sp_version(void);
+/* Human-readable name of a status. */
+const char* sp_status_string(sp_status status);
+/* Replaces Gpu::request / request_async (gpu.rs:29-66): device `device`, its own stream. */
+sp_status sp_context_create(int device, sp_context** out);
+/* As sp_context_create, but enqueues on `stream` (a cudaStream_t the caller keeps alive),
+ * so that the work orders with the caller's own (e.g. a torch stream). */
+sp_status sp_context_create_on_stream(int device, void* stream, sp_context** out);
+void sp_context_destroy(sp_context* ctx);
+/* Waits for every call enqueued on the context's stream (Gpu::submit + poll). */
+sp_status sp_context_sync(sp_context* ctx);
+/* The cudaStream_t the context enqueues on. */
+void* sp_context_stream(sp_context* ctx);
+/* Message of the last error status a call on this context returned. */
+const char* sp_last_error(const sp_context* ctx);
+
+/* --------------------------------------------------------------------------- camera */
+
+/* PinholeCamera::uniform (camera.rs:51-70): camera-to-world rotation (row-major 3x3) and
+ * centre in f64, focal and principal point in pixels; tiles of SP_TILE pixels. */
+sp_status sp_camera_uniform_from_pinhole(const double rotation_c2w[9], const double translation[3],
+                                         const double focal[2], const double principal_point[2],
+                                         uint32_t width, uint32_t height, sp_camera_uniform* out);
+
+/* ----------------------------------------------------------------------- rasterizer */
+
+/* Fills `out` with the defaults (reference behaviour, SH degree 0). */
+void sp_options_default(sp_options* out);
+
+/* Rasterizer::new (rasterizer.rs:176-391). `d_params` holds gaussian_count * stride floats
+ * (stride 14 at SH degree 0); `d_ground_truth` holds view_count images of
+ * width * height * 4 floats (loss::ground_truth_rgba, loss.rs:95-104). Both are device
+ * pointers the caller keeps alive. `options` may be NULL for the defaults. */
+sp_status sp_rasterizer_create(sp_context* ctx, const float* d_params, uint64_t gaussian_count,
+                               uint32_t width, uint32_t height, const float* d_ground_truth,
+                               uint32_t view_count, const sp_options* options, sp_rasterizer** out);
+void sp_rasterizer_destroy(sp_rasterizer* r);
+/* The parameter floats per Gaussian this rasterizer reads. */
+uint32_t sp_rasterizer_param_stride(const sp_rasterizer* r);
+/* Rasterizer::set_camera (rasterizer.rs:398-401). Takes effect at the next sp_forward /
+ * sp_backward. SP_ERR_INVALID when the image size differs. */
+sp_status sp_set_camera(sp_rasterizer* r, const sp_camera_uniform* camera);
+/* Rasterizer::encode_forward (rasterizer.rs:404-416): projection, binning, sort, blend. */
+sp_status sp_forward(sp_rasterizer* r);
+/* Rasterizer::encode_loss (rasterizer.rs:420-425): loss of the image against view `view`. */
+sp_status sp_loss(sp_rasterizer* r, uint32_t view);
+/* Rasterizer::encode_backward (rasterizer.rs:429-442). */
+sp_status sp_backward(sp_rasterizer* r);
+/* write_loss_gradient / write_image (rasterizer.rs:446-456): width*height*4 floats from
+ * host memory (src_is_device = 0) or device memory (1). */
+sp_status sp_write_loss_gradient(sp_rasterizer* r, const float* src, int src_is_device);
+sp_status sp_write_image(sp_rasterizer* r, const float* src, int src_is_device);
+/* Rasterizer::param_gradients (rasterizer.rs:467-469): device pointer to N * stride floats. */
+float* sp_param_gradients(sp_rasterizer* r);
+/* Zeroes the parameter gradients (for accumulate_gradients batches). */
+sp_status sp_zero_param_gradients(sp_rasterizer* r);
+/* Device pointer to the 14-float camera gradient of the last backward. */
+float* sp_camera_gradient_device(sp_rasterizer* r);
+/* The read_* calls of rasterizer.rs:458-549, into host memory. */
+sp_status sp_read_loss_gradient(sp_rasterizer* r, float* host);      /* P * 4 */
+sp_status sp_read_param_gradients(sp_rasterizer* r, float* host);    /* N * stride */
+sp_status sp_read_densify_stats(sp_rasterizer* r, sp_densify_stats* host); /* N */
+sp_status sp_read_camera_gradient(sp_rasterizer* r, sp_camera_gradient* host);
+sp_status sp_read_image(sp_rasterizer* r, float* host_rgbt);         /* P * 4 */
+sp_status sp_read_pixel_loss(sp_rasterizer* r, float* host);         /* P * 4 */
+sp_status sp_read_loss(sp_rasterizer* r, sp_loss_terms* out);        /* read_loss */
+/* read_intersections (rasterizer.rs:536-544): fills `out` and returns SP_ERR_OVERFLOW when
+ * the list overflowed (where the reference panics). */
+sp_status sp_read_intersections(sp_rasterizer* r, sp_intersection_meta* out);
+/* Rasterizer::render (rasterizer.rs:552-564): set_camera, forward, overflow check, image. */
+sp_status sp_render(sp_rasterizer* r, const sp_camera_uniform* camera, float* host_rgbt);
+/* Diagnostics, as the reference's `Projected` mirror "for tests and diagnostics"
+ * (rasterizer.rs:46-61): the per-Gaussian projection of the last forward pass. */
+sp_status sp_read_projected(sp_rasterizer* r, sp_projected* host);   /* N */
+/* The intersection list of the last forward pass in sorted order: `count` keys (as 64-bit
+ * values of the key layout) and the Gaussian index of each entry. */
+sp_status sp_read_sorted_intersections(sp_rasterizer* r, uint64_t* keys_host, uint32_t* gaussians_host);
+/* Per tile [start, end) of the sorted list, 2 * tiles entries (tile_ranges.wgsl:9-22). */
+sp_status sp_read_tile_ranges(sp_rasterizer* r, uint32_t* host);
+/* Per pixel, how many of the tile's entries contributed (rasterize_forward.wgsl:72). */
+sp_status sp_read_contributions(sp_rasterizer* r, uint32_t* host);
+/* Per Gaussian, the exclusive prefix sum of the tile counts (scan.wgsl:64-81). */
+sp_status sp_read_tile_offsets(sp_rasterizer* r, uint32_t* host);
+/* Per-Gaussian sums of the blend backward (mean xy, conic abc, colour rgb, opacity, 0)
+ * of the last sp_backward: SP_GRAD_STRIDE floats per Gaussian. */
+sp_status sp_read_gaussian_blend_gradients(sp_rasterizer* r, float* host);
+/* Resets the densification statistics to zero (a fresh rasterizer starts at zero). */
+sp_status sp_clear_densify_stats(sp_rasterizer* r);
+
+/* ---------------------------------------------------------------------------- Adam */
+
+/* Adam::new (optimizer.rs:137-159): moments zeroed, `position_scale` = camera extent
+ * (multiplies the position rate, sets the log-scale cap ln(0.02 * extent)). `d_params`
+ * is updated in place; `d_gradients` is read (typically sp_param_gradients). */
+sp_status sp_adam_create(sp_context* ctx, float* d_params, const float* d_gradients, uint64_t gaussian_count,
+                         uint32_t sh_degree, const sp_learning_rates* rates, float position_scale, sp_adam** out);
+/* Adam::resumed (optimizer.rs:164-188): the optimiser `from`'s rates, scale and step count
+ * over new buffers, starting from host moments of gaussian_count * stride floats each. */
+sp_status sp_adam_resume(const sp_adam* from, float* d_params, const float* d_gradients, uint64_t gaussian_count,
+                         const float* host_first_moment, const float* host_second_moment, sp_adam** out);
+void sp_adam_destroy(sp_adam* adam);
+/* Adam::encode_step (optimizer.rs:248-264): one update with the position rate times
+ * `position_rate_factor` in (0, 1], then the scale clamp (clamp_scales.wgsl), fused. */
+sp_status sp_adam_step(sp_adam* adam, float position_rate_factor);
+/* As sp_adam_step, restricted to Gaussians [first, first + count): the shard of a
+ * view-sharded multi-GPU step. Every shard of one step must pass the same
+ * position_rate_factor; call sp_adam_advance once per step before the shards. */
+sp_status sp_adam_advance(sp_adam* adam, float position_rate_factor);
+sp_status sp_adam_step_range(sp_adam* adam, uint64_t first, uint64_t count);
+/* Adam::steps_taken (optimizer.rs:266-268). */
+uint32_t sp_adam_steps_taken(const sp_adam* adam);
+/* Adam::read_moments_async (optimizer.rs:270-275), into host memory. */
+sp_status sp_adam_read_moments(sp_adam* adam, float* host_first, float* host_second);
+/* position_rate_factor (optimizer.rs:59-62): 0.01^(step / max(steps - 1, 1)). Returns a
+ * negative value where the reference asserts (steps == 0 or step >= steps). */
+float sp_position_rate_factor(uint64_t step, uint64_t steps);
+
+/* ------------------------------------------------------------- pose chain (host f64) */
+
+/* PinholeCamera (camera.rs:8-17): camera-to-world rotation (row-major), centre. */
+typedef struct sp_pinhole_camera {
+    double rotation[9];
+    double translation[3];
+    double focal[2];
+    double principal_point[2];
+    uint32_t width;
+    uint32_t height;
+} sp_pinhole_camera;
+
+/* PoseCorrection (camera_pose.rs:14-21). */
+typedef struct sp_pose_correction {
+    double rotation[3];
+    double translation[3];
+} sp_pose_correction;
+
+/* PoseGradient (camera_pose.rs:23-29). */
+typedef struct sp_pose_gradient {
+    double rotation[3];
+    double translation[3];
+    double focal_log_scale;
+} sp_pose_gradient;
+
+/* camera_pose::corrected_camera (camera_pose.rs:59-68). */
+sp_status sp_corrected_camera(const sp_pinhole_camera* initial, const sp_pose_correction* correction,
+                              double focal_log_scale, sp_pinhole_camera* out);
+/* camera_pose::pose_gradient (camera_pose.rs:81-99). */
+sp_status sp_pose_gradient_of(const sp_pinhole_camera* initial, const sp_pose_correction* correction,
+                              double focal_log_scale, const sp_camera_gradient* gradient, sp_pose_gradient* out);
+
+typedef struct sp_pose_refinement sp_pose_refinement;
+/* PoseRefinement::new (pose_refinement.rs:66-81). */
+sp_status sp_pose_refinement_create(const sp_pinhole_camera* initial, uint32_t view_count,
+                                    const sp_learning_rates* rates, float extent, sp_pose_refinement** out);
+void sp_pose_refinement_destroy(sp_pose_refinement* p);
+/* PoseRefinement::camera (pose_refinement.rs:83-85). */
+sp_status sp_pose_refinement_camera(const sp_pose_refinement* p, uint32_t view, sp_pinhole_camera* out);
+/* PoseRefinement::step (pose_refinement.rs:113-163); SP_ERR_NONFINITE where it asserts. */
+sp_status sp_pose_refinement_step(sp_pose_refinement* p, uint32_t view, const sp_camera_gradient* gradient,
+                                  float rate_factor);
+/* correction(view), focal_scale(), last_gradient() (pose_refinement.rs:91-105). */
+sp_status sp_pose_refinement_correction(const sp_pose_refinement* p, uint32_t view, sp_pose_correction* out);
+double sp_pose_refinement_focal_scale(const sp_pose_refinement* p);
+sp_status sp_pose_refinement_last_gradient(const sp_pose_refinement* p, sp_pose_gradient* out);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif

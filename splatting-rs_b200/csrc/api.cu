@@ -1,0 +1,787 @@
+// The C ABI of libsplat_b200 (include/splat.h): context, rasterizer and Adam objects that
+// own their device buffers and enqueue the kernels of this directory on one CUDA stream.
+// The host-side structure follows instantsplat-rs/src/rasterizer.rs (Rasterizer::new,
+// encode_forward / encode_loss / encode_backward, the read-backs) and optimizer.rs (Adam).
+#include <algorithm>
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <string>
+#include <vector>
+
+#include "kernels.h"
+
+using namespace splat;
+
+struct sp_context {
+    int device = 0;
+    cudaStream_t stream = nullptr;
+    bool own_stream = false;
+    std::string error;
+};
+
+struct sp_rasterizer {
+    sp_context* ctx = nullptr;
+    const float* params = nullptr;
+    uint64_t n = 0;
+    uint32_t width = 0, height = 0, tiles_x = 0, tiles_y = 0, tiles = 0;
+    const float* ground_truth = nullptr;
+    uint32_t views = 0;
+    sp_options options{};
+    uint32_t stride = 0;
+    uint64_t capacity = 0;
+    uint32_t blocks = 0;          // projection blocks of 256 Gaussians
+    uint32_t max_partitions = 0;  // sort partitions at full capacity
+    SortPlan plan{};
+    sp_camera_uniform camera{};
+    bool has_camera = false;
+    bool forward_done = false;
+    uint32_t sequence = 0;
+    int sorted_buffer = 0;
+    std::vector<void*> allocations;
+
+    float4* records = nullptr;
+    uint32_t* radii = nullptr;
+    uint32_t* offsets = nullptr;
+    uint32_t* block_totals = nullptr;
+    unsigned long long* block_offsets = nullptr;
+    DeviceMeta* meta = nullptr;
+    void* keys[2] = {nullptr, nullptr};
+    uint32_t* values[2] = {nullptr, nullptr};
+    uint32_t* sort_histograms = nullptr;
+    uint32_t* sort_tickets = nullptr;
+    unsigned long long* lookback = nullptr;
+    uint2* ranges = nullptr;
+    float4* image = nullptr;
+    uint32_t* contributions = nullptr;
+    float4* ssim_partials = nullptr;
+    float4* loss_gradient = nullptr;
+    float4* pixel_loss = nullptr;
+    double* loss_sums = nullptr;
+    float* slot_gradients = nullptr;
+    float4* gaussian_gradients = nullptr;
+    float* param_gradients = nullptr;
+    float* camera_partials = nullptr;
+    uint32_t* camera_done = nullptr;
+    float* camera_gradient = nullptr;
+    float4* densify_stats = nullptr;
+
+    uint64_t pixels() const { return (uint64_t)width * height; }
+};
+
+struct sp_adam {
+    sp_context* ctx = nullptr;
+    float* params = nullptr;
+    const float* gradients = nullptr;
+    uint64_t n = 0;
+    uint32_t sh_degree = 0, stride = 0;
+    sp_learning_rates rates{};
+    float position_scale = 1.0f;
+    uint32_t step = 0;
+    float* first_moment = nullptr;
+    float* second_moment = nullptr;
+    float max_log_scale = 0.0f, max_log_anisotropy = 0.0f;
+    // The rates of the step in progress (sp_adam_advance).
+    std::vector<float> lr_by_slot;
+    float bias1 = 0.0f, bias2 = 0.0f;
+};
+
+namespace {
+
+sp_status fail(sp_context* ctx, sp_status status, const std::string& message) {
+    if (ctx) ctx->error = message;
+    return status;
+}
+
+sp_status cuda_fail(sp_context* ctx, cudaError_t err, const char* what) {
+    return fail(ctx, err == cudaErrorMemoryAllocation ? SP_ERR_OUT_OF_MEMORY : SP_ERR_CUDA,
+                std::string(what) + ": " + cudaGetErrorString(err));
+}
+
+#define SP_CUDA(ctx, expr)                                      \
+    do {                                                        \
+        cudaError_t err_ = (expr);                              \
+        if (err_ != cudaSuccess) return cuda_fail(ctx, err_, #expr); \
+    } while (0)
+
+sp_status select_device(sp_context* ctx) {
+    SP_CUDA(ctx, cudaSetDevice(ctx->device));
+    return SP_OK;
+}
+
+template <typename T>
+sp_status alloc(sp_rasterizer* r, T** out, size_t count, bool zero = true) {
+    void* p = nullptr;
+    const size_t bytes = std::max<size_t>(count * sizeof(T), 16);
+    cudaError_t err = cudaMalloc(&p, bytes);
+    if (err != cudaSuccess) return cuda_fail(r->ctx, err, "cudaMalloc");
+    r->allocations.push_back(p);
+    if (zero) {
+        err = cudaMemset(p, 0, bytes);
+        if (err != cudaSuccess) return cuda_fail(r->ctx, err, "cudaMemset");
+    }
+    *out = static_cast<T*>(p);
+    return SP_OK;
+}
+
+uint32_t ceil_log2(uint64_t v) {
+    uint32_t bits = 0;
+    while ((1ull << bits) < v) ++bits;
+    return bits;
+}
+
+sp_status sync_stream(sp_context* ctx) {
+    SP_CUDA(ctx, cudaStreamSynchronize(ctx->stream));
+    return SP_OK;
+}
+
+sp_status read_device(sp_context* ctx, void* host, const void* device, size_t bytes) {
+    if (!host) return fail(ctx, SP_ERR_INVALID, "null host buffer");
+    if (bytes == 0) return SP_OK;
+    SP_CUDA(ctx, cudaMemcpyAsync(host, device, bytes, cudaMemcpyDeviceToHost, ctx->stream));
+    return sync_stream(ctx);
+}
+
+sp_status device_status(sp_rasterizer* r, DeviceMeta* meta_out) {
+    DeviceMeta meta;
+    sp_status s = read_device(r->ctx, &meta, r->meta, sizeof(meta));
+    if (s != SP_OK) return s;
+    if (meta_out) *meta_out = meta;
+    if (meta.status != 0) {
+        const sp_status status = (sp_status)meta.status;
+        // Clear it so that later passes report their own.
+        cudaMemsetAsync(&r->meta->status, 0, sizeof(uint32_t), r->ctx->stream);
+        return fail(r->ctx, status, "a device-side wait gave up (sort look-back timeout)");
+    }
+    return SP_OK;
+}
+
+#define SP_CHECK(expr)                   \
+    do {                                 \
+        const sp_status s_ = (expr);     \
+        if (s_ != SP_OK) return s_;      \
+    } while (0)
+
+#define SP_REQUIRE(ctx, cond, status, message) \
+    do {                                       \
+        if (!(cond)) return fail(ctx, status, message); \
+    } while (0)
+
+float position_rate_factor(uint64_t step, uint64_t steps) {
+    const uint64_t denominator = std::max<uint64_t>(steps - 1, 1);
+    return std::pow(SP_POSITION_RATE_FINAL_OVER_INITIAL, (float)step / (float)denominator);
+}
+
+void learning_rates_by_slot(const sp_learning_rates& rates, float position_scale, uint32_t stride, float* out) {
+    // LearningRates::by_slot (optimizer.rs:82-100); the SH degree 1-3 slots take sh_rest.
+    for (uint32_t slot = 0; slot < stride; ++slot) {
+        float rate;
+        if (slot < 3) rate = rates.position * position_scale;
+        else if (slot < 6) rate = rates.log_scale;
+        else if (slot < 10) rate = rates.rotation;
+        else if (slot == 10) rate = rates.opacity;
+        else if (slot < 14) rate = rates.sh_dc;
+        else rate = rates.sh_rest;
+        out[slot] = rate;
+    }
+}
+
+}  // namespace
+
+namespace splat {
+// loss.cu: deterministic sum of the per-pixel loss terms into workspace[0..4) (the
+// workspace holds 4 + 4 * 256 + 1 doubles).
+cudaError_t launch_loss_sums(const float4* pixel_loss, uint64_t pixels, double* workspace, cudaStream_t stream);
+}  // namespace splat
+
+extern "C" {
+
+const char* sp_version(void) { return "splat_b200 0.1 (sm_100a)"; }
+
+const char* sp_status_string(sp_status status) {
+    switch (status) {
+        case SP_OK: return "SP_OK";
+        case SP_ERR_INVALID: return "SP_ERR_INVALID";
+        case SP_ERR_TOO_MANY_TILES: return "SP_ERR_TOO_MANY_TILES";
+        case SP_ERR_OVERFLOW: return "SP_ERR_OVERFLOW";
+        case SP_ERR_TIMEOUT: return "SP_ERR_TIMEOUT";
+        case SP_ERR_CUDA: return "SP_ERR_CUDA";
+        case SP_ERR_NCCL: return "SP_ERR_NCCL";
+        case SP_ERR_NONFINITE: return "SP_ERR_NONFINITE";
+        case SP_ERR_NO_DEVICE: return "SP_ERR_NO_DEVICE";
+        case SP_ERR_OUT_OF_MEMORY: return "SP_ERR_OUT_OF_MEMORY";
+    }
+    return "unknown status";
+}
+
+static sp_status context_create(int device, void* stream, sp_context** out) {
+    if (!out) return SP_ERR_INVALID;
+    *out = nullptr;
+    int devices = 0;
+    if (cudaGetDeviceCount(&devices) != cudaSuccess || devices == 0) return SP_ERR_NO_DEVICE;
+    if (device < 0 || device >= devices) return SP_ERR_INVALID;
+    sp_context* ctx = new sp_context();
+    ctx->device = device;
+    if (cudaSetDevice(device) != cudaSuccess) {
+        delete ctx;
+        return SP_ERR_CUDA;
+    }
+    if (stream) {
+        ctx->stream = static_cast<cudaStream_t>(stream);
+    } else {
+        if (cudaStreamCreateWithFlags(&ctx->stream, cudaStreamNonBlocking) != cudaSuccess) {
+            delete ctx;
+            return SP_ERR_CUDA;
+        }
+        ctx->own_stream = true;
+    }
+    *out = ctx;
+    return SP_OK;
+}
+
+sp_status sp_context_create(int device, sp_context** out) { return context_create(device, nullptr, out); }
+
+sp_status sp_context_create_on_stream(int device, void* stream, sp_context** out) {
+    return context_create(device, stream, out);
+}
+
+void sp_context_destroy(sp_context* ctx) {
+    if (!ctx) return;
+    cudaSetDevice(ctx->device);
+    if (ctx->own_stream) {
+        cudaStreamSynchronize(ctx->stream);
+        cudaStreamDestroy(ctx->stream);
+    }
+    delete ctx;
+}
+
+sp_status sp_context_sync(sp_context* ctx) {
+    if (!ctx) return SP_ERR_INVALID;
+    SP_CHECK(select_device(ctx));
+    return sync_stream(ctx);
+}
+
+void* sp_context_stream(sp_context* ctx) { return ctx ? (void*)ctx->stream : nullptr; }
+
+const char* sp_last_error(const sp_context* ctx) { return ctx ? ctx->error.c_str() : "null context"; }
+
+sp_status sp_camera_uniform_from_pinhole(const double rotation_c2w[9], const double translation[3],
+                                         const double focal[2], const double principal_point[2], uint32_t width,
+                                         uint32_t height, sp_camera_uniform* out) {
+    if (!rotation_c2w || !translation || !focal || !principal_point || !out) return SP_ERR_INVALID;
+    // camera.rs:46-70: W = R^T, t = -W C, rows (W | t) to f32.
+    double w[3][3], t[3];
+    for (int r = 0; r < 3; ++r)
+        for (int c = 0; c < 3; ++c) w[r][c] = rotation_c2w[c * 3 + r];
+    for (int r = 0; r < 3; ++r) t[r] = -(w[r][0] * translation[0] + w[r][1] * translation[1] + w[r][2] * translation[2]);
+    for (int r = 0; r < 3; ++r) {
+        for (int c = 0; c < 3; ++c) out->world_to_camera_rows[r][c] = (float)w[r][c];
+        out->world_to_camera_rows[r][3] = (float)t[r];
+    }
+    out->focal[0] = (float)focal[0];
+    out->focal[1] = (float)focal[1];
+    out->principal_point[0] = (float)principal_point[0];
+    out->principal_point[1] = (float)principal_point[1];
+    out->width = width;
+    out->height = height;
+    out->tiles_x = (width + SP_TILE - 1) / SP_TILE;
+    out->tiles_y = (height + SP_TILE - 1) / SP_TILE;
+    return SP_OK;
+}
+
+void sp_options_default(sp_options* out) {
+    if (!out) return;
+    std::memset(out, 0, sizeof(*out));
+    out->key_mode = SP_KEYS_REF20;
+    out->backward_mode = SP_BWD_ATOMIC;
+    out->sh_degree = 0;
+    out->intersections_per_gaussian = SP_INTERSECTIONS_PER_GAUSSIAN;
+    out->accumulate_gradients = 0;
+    out->loss_weights.l1 = SP_LOSS_L1;
+    out->loss_weights.dssim = SP_LOSS_DSSIM;
+    out->loss_weights.alpha = SP_LOSS_ALPHA;
+}
+
+void sp_rasterizer_destroy(sp_rasterizer* r) {
+    if (!r) return;
+    cudaSetDevice(r->ctx->device);
+    cudaStreamSynchronize(r->ctx->stream);
+    for (void* p : r->allocations) cudaFree(p);
+    delete r;
+}
+
+sp_status sp_rasterizer_create(sp_context* ctx, const float* d_params, uint64_t gaussian_count, uint32_t width,
+                               uint32_t height, const float* d_ground_truth, uint32_t view_count,
+                               const sp_options* options, sp_rasterizer** out) {
+    if (!ctx || !out) return SP_ERR_INVALID;
+    *out = nullptr;
+    sp_options opt;
+    if (options) opt = *options;
+    else sp_options_default(&opt);
+    // rasterizer.rs:185-199.
+    SP_REQUIRE(ctx, gaussian_count > 0, SP_ERR_INVALID, "no Gaussians");
+    SP_REQUIRE(ctx, gaussian_count < (1ull << 31), SP_ERR_INVALID, "more than 2^31 Gaussians");
+    SP_REQUIRE(ctx, d_params != nullptr, SP_ERR_INVALID, "null params buffer");
+    SP_REQUIRE(ctx, width > 0 && height > 0, SP_ERR_INVALID, "empty image");
+    SP_REQUIRE(ctx, view_count == 0 || d_ground_truth != nullptr, SP_ERR_INVALID, "null ground truth buffer");
+    SP_REQUIRE(ctx, opt.sh_degree <= 3, SP_ERR_INVALID, "SH degree above 3");
+    SP_REQUIRE(ctx, opt.key_mode == SP_KEYS_REF20 || opt.key_mode == SP_KEYS_FULL32, SP_ERR_INVALID, "key mode");
+    SP_REQUIRE(ctx, opt.backward_mode == SP_BWD_DETERMINISTIC || opt.backward_mode == SP_BWD_ATOMIC, SP_ERR_INVALID,
+               "backward mode");
+    SP_REQUIRE(ctx, opt.intersections_per_gaussian > 0, SP_ERR_INVALID, "intersections per Gaussian");
+    const uint32_t tiles_x = (width + SP_TILE - 1) / SP_TILE, tiles_y = (height + SP_TILE - 1) / SP_TILE;
+    SP_REQUIRE(ctx, tiles_x <= 0xffffu && tiles_y <= 0xffffu, SP_ERR_TOO_MANY_TILES,
+               "over 65535 tiles on a side");
+    const uint64_t capacity = gaussian_count * opt.intersections_per_gaussian;
+    SP_REQUIRE(ctx, capacity < (1ull << 30), SP_ERR_INVALID, "intersection capacity must stay below 2^30");
+    SP_CHECK(select_device(ctx));
+
+    sp_rasterizer* r = new sp_rasterizer();
+    r->ctx = ctx;
+    r->params = d_params;
+    r->n = gaussian_count;
+    r->width = width;
+    r->height = height;
+    r->tiles_x = tiles_x;
+    r->tiles_y = tiles_y;
+    r->tiles = tiles_x * tiles_y;
+    r->ground_truth = d_ground_truth;
+    r->views = view_count;
+    r->options = opt;
+    r->stride = SP_PARAM_STRIDE(opt.sh_degree);
+    r->capacity = capacity;
+    r->blocks = (uint32_t)((gaussian_count + kBlock - 1) / kBlock);
+    r->max_partitions = (uint32_t)((capacity + kSortPartition - 1) / kSortPartition);
+    const uint32_t tile_bits = ceil_log2(r->tiles);
+    r->plan.key_bits = (int)tile_bits + (opt.key_mode == SP_KEYS_FULL32 ? 32 : SP_DEPTH_BITS);
+    r->plan.key64 = r->plan.key_bits > 32 || opt.key_mode == SP_KEYS_FULL32;
+    r->plan.passes = (r->plan.key_bits + 7) / 8;
+    r->plan.tile_shift = opt.key_mode == SP_KEYS_FULL32 ? 32 : SP_DEPTH_BITS;
+
+    const uint64_t n = gaussian_count, p = r->pixels();
+    const size_t key_bytes = r->plan.key64 ? 8 : 4;
+    sp_status s = SP_OK;
+#define SP_ALLOC(ptr, count)                                  \
+    if ((s = alloc(r, &(ptr), (count))) != SP_OK) {           \
+        sp_rasterizer_destroy(r);                             \
+        return s;                                             \
+    }
+    SP_ALLOC(r->records, n * kRecord);
+    SP_ALLOC(r->radii, n);
+    SP_ALLOC(r->offsets, n);
+    SP_ALLOC(r->block_totals, r->blocks);
+    SP_ALLOC(r->block_offsets, r->blocks);
+    SP_ALLOC(r->meta, 1);
+    {
+        unsigned char* k0 = nullptr;
+        unsigned char* k1 = nullptr;
+        SP_ALLOC(k0, capacity * key_bytes);
+        SP_ALLOC(k1, capacity * key_bytes);
+        r->keys[0] = k0;
+        r->keys[1] = k1;
+    }
+    SP_ALLOC(r->values[0], capacity);
+    SP_ALLOC(r->values[1], capacity);
+    SP_ALLOC(r->sort_histograms, (size_t)kSortMaxPasses * kSortRadix);
+    SP_ALLOC(r->sort_tickets, kSortMaxPasses);
+    SP_ALLOC(r->lookback, (size_t)std::max<uint32_t>(r->max_partitions, 1) * kSortRadix);
+    SP_ALLOC(r->ranges, r->tiles);
+    SP_ALLOC(r->image, p);
+    SP_ALLOC(r->contributions, p);
+    SP_ALLOC(r->ssim_partials, p * 3);
+    SP_ALLOC(r->loss_gradient, p);
+    SP_ALLOC(r->pixel_loss, p);
+    SP_ALLOC(r->loss_sums, 4 + 4 * 256 + 1);
+    if (opt.backward_mode == SP_BWD_DETERMINISTIC) {
+        SP_ALLOC(r->slot_gradients, capacity * SP_GRAD_STRIDE);
+    } else {
+        SP_ALLOC(r->gaussian_gradients, n * 3);
+    }
+    SP_ALLOC(r->param_gradients, n * r->stride);
+    SP_ALLOC(r->camera_partials, (size_t)r->blocks * SP_CAMERA_GRAD_STRIDE);
+    SP_ALLOC(r->camera_done, 1);
+    SP_ALLOC(r->camera_gradient, SP_CAMERA_GRAD_STRIDE);
+    SP_ALLOC(r->densify_stats, n);
+#undef SP_ALLOC
+    // The default camera of rasterizer.rs:202-213: identity pose, unit focal.
+    const double identity[9] = {1, 0, 0, 0, 1, 0, 0, 0, 1}, zero[3] = {0, 0, 0}, unit[2] = {1, 1}, origin[2] = {0, 0};
+    sp_camera_uniform_from_pinhole(identity, zero, unit, origin, width, height, &r->camera);
+    r->has_camera = true;
+    *out = r;
+    return SP_OK;
+}
+
+uint32_t sp_rasterizer_param_stride(const sp_rasterizer* r) { return r ? r->stride : 0; }
+
+sp_status sp_set_camera(sp_rasterizer* r, const sp_camera_uniform* camera) {
+    if (!r || !camera) return SP_ERR_INVALID;
+    // rasterizer.rs:399.
+    SP_REQUIRE(r->ctx, camera->width == r->width && camera->height == r->height, SP_ERR_INVALID, "camera image size");
+    SP_REQUIRE(r->ctx, camera->tiles_x == r->tiles_x && camera->tiles_y == r->tiles_y, SP_ERR_INVALID,
+               "camera tile grid");
+    r->camera = *camera;
+    return SP_OK;
+}
+
+sp_status sp_forward(sp_rasterizer* r) {
+    if (!r) return SP_ERR_INVALID;
+    sp_context* ctx = r->ctx;
+    SP_CHECK(select_device(ctx));
+    cudaStream_t st = ctx->stream;
+    SP_CUDA(ctx, launch_project(r->params, r->n, (int)r->options.sh_degree, r->camera, r->records, r->radii,
+                                r->offsets, r->block_totals, st));
+    SP_CUDA(ctx, launch_scan_blocks(r->block_totals, r->block_offsets, r->blocks, r->capacity, r->meta,
+                                    r->sort_histograms, r->sort_tickets, st));
+    SP_CUDA(ctx, launch_emit(r->records, r->offsets, r->block_offsets, r->n, r->camera, (int)r->options.key_mode,
+                             r->plan, r->meta, r->keys[0], r->values[0], r->sort_histograms, st));
+    for (int pass = 0; pass < r->plan.passes; ++pass) {
+        const int from = pass & 1, to = from ^ 1;
+        SP_CUDA(ctx, launch_sort_pass(r->plan, pass, ++r->sequence, r->keys[from], r->values[from], r->keys[to],
+                                      r->values[to], r->sort_histograms, r->sort_tickets, r->lookback,
+                                      r->max_partitions, r->meta, st));
+    }
+    r->sorted_buffer = r->plan.passes & 1;
+    SP_CUDA(ctx, launch_ranges(r->plan, r->keys[r->sorted_buffer], r->meta, r->capacity, r->ranges, r->tiles, st));
+    SP_CUDA(ctx, launch_blend_forward(r->records, r->values[r->sorted_buffer], r->ranges, r->camera, r->image,
+                                      r->contributions, st));
+    r->forward_done = true;
+    return SP_OK;
+}
+
+sp_status sp_loss(sp_rasterizer* r, uint32_t view) {
+    if (!r) return SP_ERR_INVALID;
+    SP_REQUIRE(r->ctx, view < r->views, SP_ERR_INVALID, "view index out of range");
+    SP_CHECK(select_device(r->ctx));
+    const float4* gt = reinterpret_cast<const float4*>(r->ground_truth) + (size_t)view * r->pixels();
+    SP_CUDA(r->ctx, launch_ssim(r->image, gt, r->width, r->height, r->ssim_partials, r->ctx->stream));
+    SP_CUDA(r->ctx, launch_loss(r->image, gt, r->ssim_partials, r->width, r->height, r->options.loss_weights,
+                                r->loss_gradient, r->pixel_loss, r->ctx->stream));
+    return SP_OK;
+}
+
+sp_status sp_backward(sp_rasterizer* r) {
+    if (!r) return SP_ERR_INVALID;
+    SP_REQUIRE(r->ctx, r->forward_done, SP_ERR_INVALID, "backward before any forward pass");
+    SP_CHECK(select_device(r->ctx));
+    cudaStream_t st = r->ctx->stream;
+    if (r->options.backward_mode == SP_BWD_ATOMIC)
+        SP_CUDA(r->ctx, cudaMemsetAsync(r->gaussian_gradients, 0, r->n * 3 * sizeof(float4), st));
+    SP_CUDA(r->ctx, launch_blend_backward((int)r->options.backward_mode, r->records, r->values[r->sorted_buffer],
+                                          r->ranges, r->offsets, r->camera, r->image, r->contributions,
+                                          r->loss_gradient, r->slot_gradients, r->gaussian_gradients, st));
+    SP_CUDA(r->ctx, launch_project_backward(r->params, r->n, (int)r->options.sh_degree, (int)r->options.backward_mode,
+                                            r->camera, r->records, r->radii, r->offsets, r->slot_gradients,
+                                            r->capacity, r->gaussian_gradients, r->param_gradients,
+                                            (int)r->options.accumulate_gradients, r->camera_partials, r->camera_done,
+                                            r->camera_gradient, r->densify_stats, st));
+    return SP_OK;
+}
+
+static sp_status write_pixels(sp_rasterizer* r, float4* dst, const float* src, int src_is_device) {
+    if (!r || !src) return SP_ERR_INVALID;
+    SP_CHECK(select_device(r->ctx));
+    SP_CUDA(r->ctx, cudaMemcpyAsync(dst, src, r->pixels() * sizeof(float4),
+                                    src_is_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice,
+                                    r->ctx->stream));
+    if (!src_is_device) return sync_stream(r->ctx);
+    return SP_OK;
+}
+
+sp_status sp_write_loss_gradient(sp_rasterizer* r, const float* src, int src_is_device) {
+    return write_pixels(r, r ? r->loss_gradient : nullptr, src, src_is_device);
+}
+
+sp_status sp_write_image(sp_rasterizer* r, const float* src, int src_is_device) {
+    return write_pixels(r, r ? r->image : nullptr, src, src_is_device);
+}
+
+float* sp_param_gradients(sp_rasterizer* r) { return r ? r->param_gradients : nullptr; }
+
+float* sp_camera_gradient_device(sp_rasterizer* r) { return r ? r->camera_gradient : nullptr; }
+
+sp_status sp_zero_param_gradients(sp_rasterizer* r) {
+    if (!r) return SP_ERR_INVALID;
+    SP_CHECK(select_device(r->ctx));
+    SP_CUDA(r->ctx, cudaMemsetAsync(r->param_gradients, 0, r->n * r->stride * sizeof(float), r->ctx->stream));
+    return SP_OK;
+}
+
+sp_status sp_clear_densify_stats(sp_rasterizer* r) {
+    if (!r) return SP_ERR_INVALID;
+    SP_CHECK(select_device(r->ctx));
+    SP_CUDA(r->ctx, cudaMemsetAsync(r->densify_stats, 0, r->n * sizeof(float4), r->ctx->stream));
+    return SP_OK;
+}
+
+sp_status sp_read_loss_gradient(sp_rasterizer* r, float* host) {
+    if (!r) return SP_ERR_INVALID;
+    return read_device(r->ctx, host, r->loss_gradient, r->pixels() * sizeof(float4));
+}
+
+sp_status sp_read_param_gradients(sp_rasterizer* r, float* host) {
+    if (!r) return SP_ERR_INVALID;
+    return read_device(r->ctx, host, r->param_gradients, r->n * r->stride * sizeof(float));
+}
+
+sp_status sp_read_densify_stats(sp_rasterizer* r, sp_densify_stats* host) {
+    if (!r) return SP_ERR_INVALID;
+    return read_device(r->ctx, host, r->densify_stats, r->n * sizeof(float4));
+}
+
+sp_status sp_read_camera_gradient(sp_rasterizer* r, sp_camera_gradient* host) {
+    if (!r) return SP_ERR_INVALID;
+    return read_device(r->ctx, host, r->camera_gradient, SP_CAMERA_GRAD_STRIDE * sizeof(float));
+}
+
+sp_status sp_read_image(sp_rasterizer* r, float* host_rgbt) {
+    if (!r) return SP_ERR_INVALID;
+    return read_device(r->ctx, host_rgbt, r->image, r->pixels() * sizeof(float4));
+}
+
+sp_status sp_read_pixel_loss(sp_rasterizer* r, float* host) {
+    if (!r) return SP_ERR_INVALID;
+    return read_device(r->ctx, host, r->pixel_loss, r->pixels() * sizeof(float4));
+}
+
+sp_status sp_read_loss(sp_rasterizer* r, sp_loss_terms* out) {
+    if (!r || !out) return SP_ERR_INVALID;
+    SP_CHECK(select_device(r->ctx));
+    // LossTerms::from_pixel_loss (loss.rs:49-63): means in f64, summed on the device.
+    SP_CUDA(r->ctx, launch_loss_sums(r->pixel_loss, r->pixels(), r->loss_sums, r->ctx->stream));
+    double sums[4];
+    SP_CHECK(read_device(r->ctx, sums, r->loss_sums, sizeof(sums)));
+    const double pixels = (double)r->pixels();
+    out->l1 = (float)(sums[0] / pixels);
+    out->alpha = (float)(sums[1] / pixels);
+    out->dssim = (float)(sums[2] / pixels);
+    out->total = (float)(sums[3] / pixels);
+    return SP_OK;
+}
+
+sp_status sp_read_intersections(sp_rasterizer* r, sp_intersection_meta* out) {
+    if (!r || !out) return SP_ERR_INVALID;
+    SP_CHECK(select_device(r->ctx));
+    DeviceMeta meta;
+    SP_CHECK(device_status(r, &meta));
+    out->count = meta.count;
+    out->sort_blocks = meta.sort_blocks;
+    out->histogram_length = meta.histogram_length;
+    out->overflow = meta.overflow;
+    out->capacity = meta.capacity;
+    // rasterizer.rs:536-544.
+    if (meta.overflow)
+        return fail(r->ctx, SP_ERR_OVERFLOW,
+                    "intersection list overflow: more than " + std::to_string(r->capacity) +
+                        " (Gaussian, tile) pairs; Gaussians are too large for the image");
+    return SP_OK;
+}
+
+sp_status sp_render(sp_rasterizer* r, const sp_camera_uniform* camera, float* host_rgbt) {
+    if (!r) return SP_ERR_INVALID;
+    SP_CHECK(sp_set_camera(r, camera));
+    SP_CHECK(sp_forward(r));
+    sp_intersection_meta meta;
+    SP_CHECK(sp_read_intersections(r, &meta));
+    return sp_read_image(r, host_rgbt);
+}
+
+sp_status sp_read_projected(sp_rasterizer* r, sp_projected* host) {
+    if (!r || !host) return SP_ERR_INVALID;
+    SP_CHECK(select_device(r->ctx));
+    sp_projected* tmp = nullptr;
+    SP_CUDA(r->ctx, cudaMallocAsync((void**)&tmp, r->n * sizeof(sp_projected), r->ctx->stream));
+    cudaError_t err = launch_to_projected(r->records, r->radii, r->n, tmp, r->ctx->stream);
+    sp_status s = err == cudaSuccess ? read_device(r->ctx, host, tmp, r->n * sizeof(sp_projected))
+                                     : cuda_fail(r->ctx, err, "launch_to_projected");
+    cudaFreeAsync(tmp, r->ctx->stream);
+    cudaStreamSynchronize(r->ctx->stream);
+    return s;
+}
+
+sp_status sp_read_sorted_intersections(sp_rasterizer* r, uint64_t* keys_host, uint32_t* gaussians_host) {
+    if (!r || !keys_host || !gaussians_host) return SP_ERR_INVALID;
+    SP_CHECK(select_device(r->ctx));
+    DeviceMeta meta;
+    SP_CHECK(device_status(r, &meta));
+    const uint64_t count = meta.count;
+    if (r->plan.key64) {
+        SP_CHECK(read_device(r->ctx, keys_host, r->keys[r->sorted_buffer], count * 8));
+    } else {
+        std::vector<uint32_t> keys(count);
+        SP_CHECK(read_device(r->ctx, keys.data(), r->keys[r->sorted_buffer], count * 4));
+        for (uint64_t i = 0; i < count; ++i) keys_host[i] = keys[i];
+    }
+    return read_device(r->ctx, gaussians_host, r->values[r->sorted_buffer], count * 4);
+}
+
+sp_status sp_read_tile_ranges(sp_rasterizer* r, uint32_t* host) {
+    if (!r) return SP_ERR_INVALID;
+    return read_device(r->ctx, host, r->ranges, (size_t)r->tiles * sizeof(uint2));
+}
+
+sp_status sp_read_contributions(sp_rasterizer* r, uint32_t* host) {
+    if (!r) return SP_ERR_INVALID;
+    return read_device(r->ctx, host, r->contributions, r->pixels() * sizeof(uint32_t));
+}
+
+sp_status sp_read_tile_offsets(sp_rasterizer* r, uint32_t* host) {
+    if (!r) return SP_ERR_INVALID;
+    return read_device(r->ctx, host, r->offsets, r->n * sizeof(uint32_t));
+}
+
+sp_status sp_read_gaussian_blend_gradients(sp_rasterizer* r, float* host) {
+    if (!r || !host) return SP_ERR_INVALID;
+    SP_CHECK(select_device(r->ctx));
+    const uint64_t n = r->n;
+    if (r->options.backward_mode == SP_BWD_ATOMIC) {
+        std::vector<float4> sums(n * 3);
+        SP_CHECK(read_device(r->ctx, sums.data(), r->gaussian_gradients, n * 3 * sizeof(float4)));
+        for (uint64_t g = 0; g < n; ++g) {
+            const float4 a = sums[g * 3], b = sums[g * 3 + 1], c = sums[g * 3 + 2];
+            const float v[SP_GRAD_STRIDE] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w, c.x, 0.0f};
+            std::memcpy(host + g * SP_GRAD_STRIDE, v, sizeof(v));
+        }
+        return SP_OK;
+    }
+    // Deterministic mode: each Gaussian's slots, in slot order (project_backward.wgsl:38-55).
+    std::vector<float4> records(n * kRecord);
+    std::vector<uint32_t> offsets(n), radii(n);
+    std::vector<float> slots(r->capacity * SP_GRAD_STRIDE);
+    SP_CHECK(read_device(r->ctx, records.data(), r->records, n * kRecord * sizeof(float4)));
+    SP_CHECK(read_device(r->ctx, offsets.data(), r->offsets, n * 4));
+    SP_CHECK(read_device(r->ctx, radii.data(), r->radii, n * 4));
+    SP_CHECK(read_device(r->ctx, slots.data(), r->slot_gradients, slots.size() * sizeof(float)));
+    for (uint64_t g = 0; g < n; ++g) {
+        float v[SP_GRAD_STRIDE] = {0};
+        if (radii[g] != 0) {
+            uint32_t lo, hi;
+            std::memcpy(&lo, &records[g * kRecord + 2].z, 4);
+            std::memcpy(&hi, &records[g * kRecord + 2].w, 4);
+            const uint32_t count = ((hi & 0xffffu) - (lo & 0xffffu)) * ((hi >> 16) - (lo >> 16));
+            for (uint32_t k = 0; k < count; ++k) {
+                const uint64_t slot = (uint64_t)offsets[g] + k;
+                if (slot >= r->capacity) break;
+                for (int c = 0; c < 9; ++c) v[c] += slots[slot * SP_GRAD_STRIDE + c];
+            }
+        }
+        std::memcpy(host + g * SP_GRAD_STRIDE, v, sizeof(v));
+    }
+    return SP_OK;
+}
+
+// ------------------------------------------------------------------------------- Adam
+
+static sp_status adam_make(sp_context* ctx, float* d_params, const float* d_gradients, uint64_t n, uint32_t sh_degree,
+                           const sp_learning_rates& rates, float position_scale, uint32_t step,
+                           const float* host_m, const float* host_v, sp_adam** out) {
+    // optimizer.rs:137-159, 200-243.
+    SP_REQUIRE(ctx, n > 0, SP_ERR_INVALID, "no Gaussians");
+    SP_REQUIRE(ctx, d_params && d_gradients, SP_ERR_INVALID, "null params or gradients buffer");
+    SP_REQUIRE(ctx, sh_degree <= 3, SP_ERR_INVALID, "SH degree above 3");
+    SP_REQUIRE(ctx, position_scale > 0.0f, SP_ERR_INVALID, "camera extent must be positive");  // prune.rs:34
+    SP_CHECK(select_device(ctx));
+    sp_adam* a = new sp_adam();
+    a->ctx = ctx;
+    a->params = d_params;
+    a->gradients = d_gradients;
+    a->n = n;
+    a->sh_degree = sh_degree;
+    a->stride = SP_PARAM_STRIDE(sh_degree);
+    a->rates = rates;
+    a->position_scale = position_scale;
+    a->step = step;
+    a->max_log_scale = std::log(SP_SCALE_MAX_EXTENT_FRACTION * position_scale);
+    a->max_log_anisotropy = std::log(SP_SCALE_MAX_ANISOTROPY);
+    const size_t bytes = n * a->stride * sizeof(float);
+    cudaError_t err = cudaMalloc(&a->first_moment, bytes);
+    if (err == cudaSuccess) err = cudaMalloc(&a->second_moment, bytes);
+    if (err == cudaSuccess) {
+        if (host_m) err = cudaMemcpy(a->first_moment, host_m, bytes, cudaMemcpyHostToDevice);
+        else err = cudaMemset(a->first_moment, 0, bytes);
+    }
+    if (err == cudaSuccess) {
+        if (host_v) err = cudaMemcpy(a->second_moment, host_v, bytes, cudaMemcpyHostToDevice);
+        else err = cudaMemset(a->second_moment, 0, bytes);
+    }
+    if (err != cudaSuccess) {
+        cudaFree(a->first_moment);
+        cudaFree(a->second_moment);
+        delete a;
+        return cuda_fail(ctx, err, "Adam moments");
+    }
+    *out = a;
+    return SP_OK;
+}
+
+sp_status sp_adam_create(sp_context* ctx, float* d_params, const float* d_gradients, uint64_t gaussian_count,
+                         uint32_t sh_degree, const sp_learning_rates* rates, float position_scale, sp_adam** out) {
+    if (!ctx || !rates || !out) return SP_ERR_INVALID;
+    *out = nullptr;
+    return adam_make(ctx, d_params, d_gradients, gaussian_count, sh_degree, *rates, position_scale, 0, nullptr,
+                     nullptr, out);
+}
+
+sp_status sp_adam_resume(const sp_adam* from, float* d_params, const float* d_gradients, uint64_t gaussian_count,
+                         const float* host_first_moment, const float* host_second_moment, sp_adam** out) {
+    if (!from || !out) return SP_ERR_INVALID;
+    *out = nullptr;
+    SP_REQUIRE(from->ctx, host_first_moment && host_second_moment, SP_ERR_INVALID, "moments");
+    return adam_make(from->ctx, d_params, d_gradients, gaussian_count, from->sh_degree, from->rates,
+                     from->position_scale, from->step, host_first_moment, host_second_moment, out);
+}
+
+void sp_adam_destroy(sp_adam* a) {
+    if (!a) return;
+    cudaSetDevice(a->ctx->device);
+    cudaStreamSynchronize(a->ctx->stream);
+    cudaFree(a->first_moment);
+    cudaFree(a->second_moment);
+    delete a;
+}
+
+sp_status sp_adam_advance(sp_adam* a, float position_rate_factor) {
+    if (!a) return SP_ERR_INVALID;
+    // optimizer.rs:248-256.
+    SP_REQUIRE(a->ctx, position_rate_factor > 0.0f && position_rate_factor <= 1.0f, SP_ERR_INVALID,
+               "position rate factor must be in (0, 1]");
+    a->step += 1;
+    a->lr_by_slot.assign(a->stride, 0.0f);
+    learning_rates_by_slot(a->rates, a->position_scale * position_rate_factor, a->stride, a->lr_by_slot.data());
+    a->bias1 = 1.0f - std::pow(SP_ADAM_BETA1, (float)a->step);
+    a->bias2 = 1.0f - std::pow(SP_ADAM_BETA2, (float)a->step);
+    return SP_OK;
+}
+
+sp_status sp_adam_step_range(sp_adam* a, uint64_t first, uint64_t count) {
+    if (!a) return SP_ERR_INVALID;
+    SP_REQUIRE(a->ctx, a->step > 0 && !a->lr_by_slot.empty(), SP_ERR_INVALID, "sp_adam_advance first");
+    SP_REQUIRE(a->ctx, first <= a->n && count <= a->n - first, SP_ERR_INVALID, "range outside the Gaussians");
+    SP_CHECK(select_device(a->ctx));
+    SP_CUDA(a->ctx, launch_adam(a->params, a->gradients, a->first_moment, a->second_moment, first, count, (int)a->stride,
+                                a->lr_by_slot.data(), a->bias1, a->bias2, a->max_log_scale, a->max_log_anisotropy,
+                                a->ctx->stream));
+    return SP_OK;
+}
+
+sp_status sp_adam_step(sp_adam* a, float position_rate_factor) {
+    SP_CHECK(sp_adam_advance(a, position_rate_factor));
+    return sp_adam_step_range(a, 0, a->n);
+}
+
+uint32_t sp_adam_steps_taken(const sp_adam* a) { return a ? a->step : 0; }
+
+sp_status sp_adam_read_moments(sp_adam* a, float* host_first, float* host_second) {
+    if (!a) return SP_ERR_INVALID;
+    SP_CHECK(select_device(a->ctx));
+    const size_t bytes = a->n * a->stride * sizeof(float);
+    SP_CHECK(read_device(a->ctx, host_first, a->first_moment, bytes));
+    return read_device(a->ctx, host_second, a->second_moment, bytes);
+}
+
+float sp_position_rate_factor(uint64_t step, uint64_t steps) {
+    // optimizer.rs:59-62 asserts steps > 0 && step < steps.
+    if (steps == 0 || step >= steps) return -1.0f;
+    return position_rate_factor(step, steps);
+}
+
+}  // extern "C"

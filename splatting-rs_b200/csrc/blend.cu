@@ -1,0 +1,262 @@
+// Alpha blending: forward (K6, rasterize_forward.wgsl:22-88) and backward (K8,
+// rasterize_backward.wgsl:30-133). One block of 16 x 16 threads per tile, one pixel per
+// thread; the tile's Gaussians are gathered (sorted list -> Gaussian -> 48-B record, an
+// L2-resident array) into shared memory a batch at a time and read back as broadcasts.
+//
+// The arithmetic per (pixel, Gaussian) is the reference's. exp is the hardware
+// approximation (__expf, MUFU.EX2), so images and gradients match the oracle within a
+// tolerance rather than bit for bit.
+#include "kernels.h"
+
+namespace splat {
+namespace {
+
+constexpr int kForwardBatch = 256;
+constexpr int kBackwardBatch = 32;
+
+__global__ void __launch_bounds__(kTilePixels) k_blend_forward(const float4* __restrict__ records,
+                                                               const uint32_t* __restrict__ sorted,
+                                                               const uint2* __restrict__ ranges,
+                                                               const sp_camera_uniform cam, float4* __restrict__ image,
+                                                               uint32_t* __restrict__ contributions) {
+    __shared__ float4 s_a[kForwardBatch];  // mean.x, mean.y, conic.a, conic.b
+    __shared__ float4 s_b[kForwardBatch];  // conic.c, opacity, colour.r, colour.g
+    __shared__ float s_c[kForwardBatch];   // colour.b
+    const uint32_t tile = blockIdx.x;
+    const uint32_t gx = tile % cam.tiles_x, gy = tile / cam.tiles_x;
+    const uint32_t t = threadIdx.x;
+    const uint32_t px = gx * SP_TILE + (t % SP_TILE), py = gy * SP_TILE + (t / SP_TILE);
+    const bool inside = px < cam.width && py < cam.height;
+    const float fpx = (float)px, fpy = (float)py;
+    const uint2 range = ranges[tile];
+    const uint32_t count = range.y - range.x;
+
+    float transmittance = 1.0f, cr = 0.0f, cg = 0.0f, cb = 0.0f;
+    uint32_t contributed = 0;
+    bool done = !inside;
+    for (uint32_t base = 0; base < count; base += kForwardBatch) {
+        // Also the barrier before the batch buffers are overwritten.
+        if (__syncthreads_count(!done) == 0) break;
+        const uint32_t j = base + t;
+        if (j < count) {
+            const float4* rec = records + (size_t)sorted[range.x + j] * kRecord;
+            s_a[t] = rec[0];
+            s_b[t] = rec[1];
+            s_c[t] = rec[2].x;
+        }
+        __syncthreads();
+        if (!done) {
+            const uint32_t n = min((uint32_t)kForwardBatch, count - base);
+            for (uint32_t k = 0; k < n; ++k) {
+                const float4 a = s_a[k];
+                const float4 b = s_b[k];
+                const float dx = a.x - fpx, dy = a.y - fpy;
+                const float power = -0.5f * (a.z * dx * dx + b.x * dy * dy) - a.w * dx * dy;
+                if (power > 0.0f) continue;
+                const float alpha = fminf(SP_MAX_ALPHA, b.y * __expf(power));
+                if (alpha < SP_MIN_ALPHA) continue;
+                const float next = transmittance * (1.0f - alpha);
+                if (next < SP_MIN_TRANSMITTANCE) {
+                    done = true;
+                    break;
+                }
+                const float w = alpha * transmittance;
+                cr += b.z * w;
+                cg += b.w * w;
+                cb += s_c[k] * w;
+                transmittance = next;
+                contributed = base + k + 1;
+            }
+        }
+    }
+    if (inside) {
+        const size_t index = (size_t)py * cam.width + px;
+        image[index] = make_float4(cr, cg, cb, transmittance);
+        contributions[index] = contributed;
+    }
+}
+
+// The slot of (Gaussian, tile) in the reference's per-intersection gradient list: the
+// Gaussian's tile offset plus the tile's row-major index in its rectangle
+// (emit_tile_keys.wgsl:21-33).
+__device__ __forceinline__ uint64_t slot_of(const float4* __restrict__ records, const uint32_t* __restrict__ offsets,
+                                            uint32_t g, uint32_t gx, uint32_t gy) {
+    const float4 r2 = records[(size_t)g * kRecord + 2];
+    const uint32_t lo = __float_as_uint(r2.z), hi = __float_as_uint(r2.w);
+    const uint32_t x0 = lo & 0xffffu, y0 = lo >> 16, x1 = hi & 0xffffu;
+    return (uint64_t)offsets[g] + (uint64_t)(gy - y0) * (x1 - x0) + (gx - x0);
+}
+
+template <int MODE>
+__global__ void __launch_bounds__(kTilePixels) k_blend_backward(
+    const float4* __restrict__ records, const uint32_t* __restrict__ sorted, const uint2* __restrict__ ranges,
+    const uint32_t* __restrict__ offsets, const sp_camera_uniform cam, const float4* __restrict__ image,
+    const uint32_t* __restrict__ contributions, const float4* __restrict__ loss_gradient,
+    float* __restrict__ slot_gradients, float4* __restrict__ gaussian_gradients) {
+    constexpr int B = kBackwardBatch;
+    constexpr int kWarps = kTilePixels / 32;
+    __shared__ float4 s_a[B];
+    __shared__ float4 s_b[B];
+    __shared__ float s_c[B];
+    __shared__ uint32_t s_g[B];
+    __shared__ float s_part[MODE == SP_BWD_DETERMINISTIC ? B : 1][kWarps][9];
+    __shared__ uint32_t s_limit;
+
+    const uint32_t tile = blockIdx.x;
+    const uint32_t gx = tile % cam.tiles_x, gy = tile / cam.tiles_x;
+    const uint32_t t = threadIdx.x, lane = lane_id(), warp = t / 32;
+    const uint32_t px = gx * SP_TILE + (t % SP_TILE), py = gy * SP_TILE + (t / SP_TILE);
+    const bool inside = px < cam.width && py < cam.height;
+    const float fpx = (float)px, fpy = (float)py;
+    const uint2 range = ranges[tile];
+    const uint32_t count = range.y - range.x;
+
+    float transmittance = 0.0f;
+    uint32_t contributed = 0;
+    float4 grad = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    if (inside) {
+        const size_t index = (size_t)py * cam.width + px;
+        transmittance = image[index].w;
+        contributed = contributions[index];
+        grad = loss_gradient[index];
+    }
+    // No pixel of the tile replays past the largest contributor count.
+    if (t == 0) s_limit = 0;
+    __syncthreads();
+    const uint32_t warp_max = __reduce_max_sync(0xffffffffu, contributed);
+    if (lane == 0) atomicMax(&s_limit, warp_max);
+    __syncthreads();
+    const uint32_t limit = min(s_limit, count);
+
+    float behind_r = 0.0f, behind_g = 0.0f, behind_b = 0.0f, behind_t = transmittance;
+    const uint32_t batches = (limit + B - 1) / B;
+    for (uint32_t bb = 0; bb < batches; ++bb) {
+        const uint32_t base = (batches - 1 - bb) * B;
+        __syncthreads();
+        if (t < (uint32_t)B && base + t < limit) {
+            const uint32_t g = sorted[range.x + base + t];
+            const float4* rec = records + (size_t)g * kRecord;
+            s_g[t] = g;
+            s_a[t] = rec[0];
+            s_b[t] = rec[1];
+            s_c[t] = rec[2].x;
+        }
+        __syncthreads();
+        const uint32_t n = min((uint32_t)B, limit - base);
+        for (int kk = (int)n - 1; kk >= 0; --kk) {
+            const uint32_t j = base + kk;
+            float v[9];
+#pragma unroll
+            for (int c = 0; c < 9; ++c) v[c] = 0.0f;
+            bool active = false;
+            if (j < contributed) {
+                const float4 a = s_a[kk];
+                const float4 b = s_b[kk];
+                const float dx = a.x - fpx, dy = a.y - fpy;
+                const float power = -0.5f * (a.z * dx * dx + b.x * dy * dy) - a.w * dx * dy;
+                if (power <= 0.0f) {
+                    const float gaussian = __expf(power);
+                    const float opacity = b.y;
+                    const float alpha_unclamped = opacity * gaussian;
+                    const float alpha = fminf(SP_MAX_ALPHA, alpha_unclamped);
+                    if (alpha >= SP_MIN_ALPHA) {
+                        active = true;
+                        const float one_minus = 1.0f - alpha;
+                        transmittance = transmittance / one_minus;
+                        const float cr = b.z, cgr = b.w, cbl = s_c[kk];
+                        const float d_alpha = grad.x * (cr * transmittance - behind_r / one_minus) +
+                                              grad.y * (cgr * transmittance - behind_g / one_minus) +
+                                              grad.z * (cbl * transmittance - behind_b / one_minus) +
+                                              grad.w * (0.0f * transmittance - behind_t / one_minus);
+                        const float w = alpha * transmittance;
+                        v[5] = grad.x * w;
+                        v[6] = grad.y * w;
+                        v[7] = grad.z * w;
+                        behind_r += cr * w;
+                        behind_g += cgr * w;
+                        behind_b += cbl * w;
+                        if (alpha_unclamped < SP_MAX_ALPHA) {
+                            v[8] = d_alpha * gaussian;
+                            const float d_power = d_alpha * opacity * gaussian;
+                            v[0] = -d_power * (a.z * dx + a.w * dy);
+                            v[1] = -d_power * (a.w * dx + b.x * dy);
+                            v[2] = -0.5f * d_power * dx * dx;
+                            v[3] = -d_power * dx * dy;
+                            v[4] = -0.5f * d_power * dy * dy;
+                        }
+                    }
+                }
+            }
+            if (__ballot_sync(0xffffffffu, active)) {
+#pragma unroll
+                for (int c = 0; c < 9; ++c) {
+#pragma unroll
+                    for (int o = 16; o > 0; o >>= 1) v[c] += __shfl_down_sync(0xffffffffu, v[c], o);
+                }
+                if (lane == 0) {
+                    if (MODE == SP_BWD_ATOMIC) {
+                        float4* out = gaussian_gradients + (size_t)s_g[kk] * 3;
+                        atomicAdd(out + 0, make_float4(v[0], v[1], v[2], v[3]));
+                        atomicAdd(out + 1, make_float4(v[4], v[5], v[6], v[7]));
+                        atomicAdd(reinterpret_cast<float*>(out + 2), v[8]);
+                    } else {
+#pragma unroll
+                        for (int c = 0; c < 9; ++c) s_part[kk][warp][c] = v[c];
+                    }
+                }
+            } else if (MODE == SP_BWD_DETERMINISTIC && lane == 0) {
+#pragma unroll
+                for (int c = 0; c < 9; ++c) s_part[kk][warp][c] = 0.0f;
+            }
+        }
+        if (MODE == SP_BWD_DETERMINISTIC) {
+            // One write per (Gaussian, tile) slot: the warps' sums in warp order.
+            __syncthreads();
+            for (uint32_t i = t; i < n * SP_GRAD_STRIDE; i += kTilePixels) {
+                const uint32_t kk = i / SP_GRAD_STRIDE, c = i % SP_GRAD_STRIDE;
+                float s = 0.0f;
+                if (c < 9)
+#pragma unroll
+                    for (int w = 0; w < kWarps; ++w) s += s_part[kk][w][c];
+                slot_gradients[slot_of(records, offsets, s_g[kk], gx, gy) * SP_GRAD_STRIDE + c] = s;
+            }
+        }
+    }
+    if (MODE == SP_BWD_DETERMINISTIC) {
+        // Entries past every pixel's last contributor get zero slots, as the reference
+        // writes every entry of the tile.
+        for (uint32_t i = t; i < (count - limit) * SP_GRAD_STRIDE; i += kTilePixels) {
+            const uint32_t j = limit + i / SP_GRAD_STRIDE, c = i % SP_GRAD_STRIDE;
+            const uint32_t g = sorted[range.x + j];
+            slot_gradients[slot_of(records, offsets, g, gx, gy) * SP_GRAD_STRIDE + c] = 0.0f;
+        }
+    }
+}
+
+}  // namespace
+
+cudaError_t launch_blend_forward(const float4* records, const uint32_t* sorted_gaussians, const uint2* ranges,
+                                 const sp_camera_uniform& cam, float4* image, uint32_t* contributions,
+                                 cudaStream_t stream) {
+    const unsigned tiles = cam.tiles_x * cam.tiles_y;
+    k_blend_forward<<<tiles, kTilePixels, 0, stream>>>(records, sorted_gaussians, ranges, cam, image, contributions);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_blend_backward(int mode, const float4* records, const uint32_t* sorted_gaussians,
+                                  const uint2* ranges, const uint32_t* offsets, const sp_camera_uniform& cam,
+                                  const float4* image, const uint32_t* contributions, const float4* loss_gradient,
+                                  float* slot_gradients, float4* gaussian_gradients, cudaStream_t stream) {
+    const unsigned tiles = cam.tiles_x * cam.tiles_y;
+    if (mode == SP_BWD_DETERMINISTIC)
+        k_blend_backward<SP_BWD_DETERMINISTIC><<<tiles, kTilePixels, 0, stream>>>(
+            records, sorted_gaussians, ranges, offsets, cam, image, contributions, loss_gradient, slot_gradients,
+            gaussian_gradients);
+    else
+        k_blend_backward<SP_BWD_ATOMIC><<<tiles, kTilePixels, 0, stream>>>(
+            records, sorted_gaussians, ranges, offsets, cam, image, contributions, loss_gradient, slot_gradients,
+            gaussian_gradients);
+    return cudaGetLastError();
+}
+
+}  // namespace splat

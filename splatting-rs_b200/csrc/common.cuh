@@ -1,0 +1,71 @@
+// Shared device-side declarations of libsplat_b200: record layouts, launch helpers and
+// the small warp primitives the kernels use. Written for sm_100a only.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/splat.h"
+#include "../../include/splat_constants.h"
+#include "../../include/splat_math.h"
+
+namespace splat {
+
+constexpr int kBlock = 256;                 // threads of every 1-D kernel
+constexpr int kTilePixels = SP_TILE * SP_TILE;
+
+// Per-Gaussian blend record written by the projection, 3 float4 (48 B, 16-B aligned):
+//   [0] mean.x, mean.y, conic.a, conic.b
+//   [1] conic.c, opacity, colour.r, colour.g
+//   [2] colour.b, depth, tile_min (x | y << 16), tile_max (x | y << 16)  (bit patterns)
+// The fields of the reference's 80-B `Projected` (common.wgsl:49-61) that the blend and
+// binning read, without its padding; the radius lives in its own array. A culled Gaussian
+// has an all-zero record and radius 0, as the reference's zeroed `Projected`.
+constexpr int kRecord = 3;
+
+// Device-side bookkeeping of one forward pass (the reference's IntersectionMeta and
+// ScanControl, rasterizer.rs:29-44), plus the status word device code raises errors in.
+struct DeviceMeta {
+    uint32_t count;             // entries in the intersection list: min(total, capacity)
+    uint32_t sort_blocks;       // ceil(count / 1024), as the reference reports it
+    uint32_t histogram_length;  // 16 * sort_blocks, as the reference reports it
+    uint32_t overflow;          // total > capacity
+    uint32_t capacity;
+    uint32_t partitions;        // sort partitions of this forward pass
+    uint32_t status;            // SP_ERR_* raised on the device, 0 when fine
+    uint32_t total_hi;          // high word of the uncapped total
+    uint32_t total_lo;
+    uint32_t pad[7];
+};
+
+// Sort geometry decided on the host from the tile grid.
+struct SortPlan {
+    int key_bits;      // significant bits of the keys
+    int key64;         // keys need 64 bits
+    int passes;        // ceil(key_bits / 8)
+    int tile_shift;    // key >> tile_shift = tile index
+};
+
+constexpr int kSortThreads = 256;
+constexpr int kSortItems = 16;
+constexpr int kSortPartition = kSortThreads * kSortItems;  // 4096 keys per partition
+constexpr int kSortMaxPasses = 8;
+constexpr int kSortRadix = 256;
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+__device__ __forceinline__ uint32_t lane_id() { return threadIdx.x & 31u; }
+
+__device__ __forceinline__ void raise_status(DeviceMeta* meta, uint32_t status) {
+    atomicCAS(&meta->status, 0u, status);
+}
+
+inline unsigned grid_for(uint64_t items, unsigned per_block) {
+    return (unsigned)((items + per_block - 1) / per_block);
+}
+
+}  // namespace splat

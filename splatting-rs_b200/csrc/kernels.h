@@ -1,0 +1,86 @@
+// Host-side launchers of the kernels of libsplat_b200 (one .cu file each group). The
+// C ABI (api.cu) calls only these. Every launcher enqueues on `stream` and returns the
+// launch error, if any.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "common.cuh"
+
+namespace splat {
+
+// ---- project.cu (compiled with -fmad=false: the tile decisions match the oracle's bits)
+
+// project_forward.wgsl:19-93 with the scan's first level (scan.wgsl:27-62) fused: per
+// block of 256 Gaussians the exclusive prefix of the tile counts and the block total.
+cudaError_t launch_project(const float* params, uint64_t n, int sh_degree, const sp_camera_uniform& cam,
+                           float4* records, uint32_t* radii, uint32_t* local_offsets, uint32_t* block_totals,
+                           cudaStream_t stream);
+// scan_tile_counts (scan.wgsl:64-81): scans the block totals into 64-bit block offsets,
+// fills the meta (count, overflow, sort partitions) and zeroes the sort's histograms and
+// partition tickets for this forward pass.
+cudaError_t launch_scan_blocks(const uint32_t* block_totals, unsigned long long* block_offsets, uint32_t blocks,
+                               uint64_t capacity, DeviceMeta* meta, uint32_t* sort_histograms, uint32_t* sort_tickets,
+                               cudaStream_t stream);
+// project_backward.wgsl:30-227 + reduce_camera_gradient.wgsl:10-34, fused (last block
+// done). Blend sums come per Gaussian (atomic mode) or per slot (deterministic mode).
+cudaError_t launch_project_backward(const float* params, uint64_t n, int sh_degree, int mode,
+                                    const sp_camera_uniform& cam,
+                                    const float4* records, const uint32_t* radii, const uint32_t* offsets,
+                                    const float* slot_gradients, uint64_t capacity, const float4* gaussian_gradients,
+                                    float* param_gradients, int accumulate, float* camera_partials,
+                                    uint32_t* camera_done, float* camera_gradient, float4* densify_stats,
+                                    cudaStream_t stream);
+// The reference's 80-B Projected records (diagnostics).
+cudaError_t launch_to_projected(const float4* records, const uint32_t* radii, uint64_t n, sp_projected* out,
+                                cudaStream_t stream);
+
+// ---- sort.cu
+
+// emit_tile_keys.wgsl:13-36: adds the block offsets into the tile offsets, writes one key
+// and Gaussian index per covered tile, and accumulates every sort pass's digit histogram.
+cudaError_t launch_emit(const float4* records, uint32_t* offsets, const unsigned long long* block_offsets, uint64_t n,
+                        const sp_camera_uniform& cam, int key_mode, const SortPlan& plan, const DeviceMeta* meta,
+                        void* keys, uint32_t* values, uint32_t* sort_histograms, cudaStream_t stream);
+// One onesweep pass (stable, 8-bit digit): keys/values in -> out.
+cudaError_t launch_sort_pass(const SortPlan& plan, int pass, uint32_t sequence, const void* keys_in,
+                             const uint32_t* values_in, void* keys_out, uint32_t* values_out,
+                             const uint32_t* sort_histograms, uint32_t* sort_tickets,
+                             unsigned long long* lookback, uint32_t max_partitions, DeviceMeta* meta,
+                             cudaStream_t stream);
+// tile_ranges.wgsl:9-22 over a zeroed range array.
+cudaError_t launch_ranges(const SortPlan& plan, const void* keys, const DeviceMeta* meta, uint64_t capacity,
+                          uint2* ranges, uint32_t tiles, cudaStream_t stream);
+
+// ---- blend.cu
+
+// rasterize_forward.wgsl:22-88.
+cudaError_t launch_blend_forward(const float4* records, const uint32_t* sorted_gaussians, const uint2* ranges,
+                                 const sp_camera_uniform& cam, float4* image, uint32_t* contributions,
+                                 cudaStream_t stream);
+// rasterize_backward.wgsl:30-133. mode SP_BWD_*: slot sums (deterministic) or atomics
+// into gaussian_gradients (3 float4 per Gaussian, zeroed by the caller).
+cudaError_t launch_blend_backward(int mode, const float4* records, const uint32_t* sorted_gaussians,
+                                  const uint2* ranges, const uint32_t* offsets, const sp_camera_uniform& cam,
+                                  const float4* image, const uint32_t* contributions, const float4* loss_gradient,
+                                  float* slot_gradients, float4* gaussian_gradients, cudaStream_t stream);
+
+// ---- loss.cu
+
+// ssim_forward.wgsl:34-91 (separable window sums in shared memory).
+cudaError_t launch_ssim(const float4* image, const float4* ground_truth, uint32_t width, uint32_t height,
+                        float4* partials, cudaStream_t stream);
+// loss.wgsl:35-97.
+cudaError_t launch_loss(const float4* image, const float4* ground_truth, const float4* partials, uint32_t width,
+                        uint32_t height, const sp_loss_weights& weights, float4* loss_gradient, float4* pixel_loss,
+                        cudaStream_t stream);
+
+// ---- adam.cu
+
+// adam.wgsl:20-37 + clamp_scales.wgsl:15-29, fused, over Gaussians [first, first + count).
+cudaError_t launch_adam(float* params, const float* gradients, float* first_moment, float* second_moment,
+                        uint64_t first, uint64_t count, int stride, const float* lr_by_slot_host, float bias1,
+                        float bias2, float max_log_scale, float max_log_anisotropy, cudaStream_t stream);
+
+}  // namespace splat

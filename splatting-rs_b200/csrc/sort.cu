@@ -1,0 +1,294 @@
+// Tile binning: key emission (K3), a onesweep LSD radix sort of the (tile, depth) keys
+// (K4) and the per-tile ranges (K5).
+//
+// The order is the reference's: a stable sort of the keys emitted in slot order
+// (emit_tile_keys.wgsl:13-36, sort.rs:1-3), so entries with equal keys keep ascending
+// Gaussian index. The reference sorts 4 bits a pass over 8 passes with a single-workgroup
+// scan between; here each pass moves 8 bits and needs no scan pass: the digit histograms
+// of every pass are accumulated while the keys are emitted, and each partition of 4096
+// keys finds its output offsets by decoupled look-back on its predecessors (the
+// "onesweep" radix sort of Adinets & Merrill, 2022). Passes only cover the significant
+// bits of the key (ceil(log2 tiles) + 20).
+#include <algorithm>
+
+#include <cuda/atomic>
+
+#include "kernels.h"
+
+namespace splat {
+namespace {
+
+constexpr uint32_t kFlagAggregate = 1u;
+constexpr uint32_t kFlagInclusive = 2u;
+// Look-back polls before a partition gives up and raises SP_ERR_TIMEOUT. Each poll
+// sleeps ~100 ns, so the limit is far above any legitimate wait (a predecessor partition
+// takes microseconds) and bounds a stuck wait to well under a second.
+constexpr uint32_t kLookbackSpinLimit = 1u << 22;
+
+template <typename Key>
+__device__ __forceinline__ Key make_key(int key_mode, uint32_t tile, float depth) {
+    const uint32_t bits = __float_as_uint(depth);
+    if (key_mode == SP_KEYS_FULL32) return (Key)(((unsigned long long)tile << 32) | bits);
+    return (Key)(((unsigned long long)tile << SP_DEPTH_BITS) | (bits >> (32 - SP_DEPTH_BITS)));
+}
+
+template <typename Key>
+__global__ void __launch_bounds__(kBlock) k_emit(const float4* __restrict__ records, uint32_t* __restrict__ offsets,
+                                                 const unsigned long long* __restrict__ block_offsets, uint32_t n,
+                                                 uint32_t tiles_x, int key_mode, int passes,
+                                                 const DeviceMeta* __restrict__ meta, Key* __restrict__ keys,
+                                                 uint32_t* __restrict__ values, uint32_t* __restrict__ histograms) {
+    __shared__ uint32_t hist[kSortMaxPasses][kSortRadix];
+    const uint32_t t = threadIdx.x;
+    for (uint32_t i = t; i < (uint32_t)passes * kSortRadix; i += kBlock) (&hist[0][0])[i] = 0;
+    __syncthreads();
+    const uint32_t g = blockIdx.x * kBlock + t;
+    if (g < n) {
+        const float4 r2 = records[(size_t)g * kRecord + 2];
+        const uint32_t lo = __float_as_uint(r2.z), hi = __float_as_uint(r2.w);
+        const uint32_t x0 = lo & 0xffffu, y0 = lo >> 16, x1 = hi & 0xffffu, y1 = hi >> 16;
+        unsigned long long index = block_offsets[blockIdx.x] + offsets[g];
+        offsets[g] = (uint32_t)index;
+        const unsigned long long capacity = meta->capacity;
+        for (uint32_t ty = y0; ty < y1; ++ty)
+            for (uint32_t tx = x0; tx < x1; ++tx) {
+                if (index < capacity) {
+                    const Key key = make_key<Key>(key_mode, ty * tiles_x + tx, r2.y);
+                    keys[index] = key;
+                    values[index] = g;
+                    for (int p = 0; p < passes; ++p) atomicAdd(&hist[p][(uint32_t)(key >> (8 * p)) & 255u], 1u);
+                }
+                ++index;
+            }
+    }
+    __syncthreads();
+    for (uint32_t i = t; i < (uint32_t)passes * kSortRadix; i += kBlock) {
+        const uint32_t c = (&hist[0][0])[i];
+        if (c) atomicAdd(histograms + i, c);
+    }
+}
+
+// One pass of the onesweep sort. A persistent grid: each block takes partitions of
+// kSortPartition keys in ticket order, ranks its keys stably by digit, publishes its digit
+// counts, sums its predecessors' (decoupled look-back) and scatters, digit-sorted through
+// shared memory so that the global writes of each digit are contiguous.
+template <typename Key>
+__global__ void __launch_bounds__(kSortThreads, 2)
+    k_sort_pass(int shift, uint32_t sequence, const Key* __restrict__ keys_in, const uint32_t* __restrict__ values_in,
+                Key* __restrict__ keys_out, uint32_t* __restrict__ values_out, const uint32_t* __restrict__ histogram,
+                uint32_t* ticket, unsigned long long* lookback, DeviceMeta* meta) {
+    extern __shared__ float4 smem4[];
+    Key* s_keys = reinterpret_cast<Key*>(smem4);
+    uint32_t* s_values = reinterpret_cast<uint32_t*>(s_keys + kSortPartition);
+    __shared__ uint32_t s_warp[kSortThreads / 32][kSortRadix];
+    __shared__ uint32_t s_global_base[kSortRadix];
+    __shared__ uint32_t s_block_start[kSortRadix];
+    __shared__ uint32_t s_out_base[kSortRadix];
+    __shared__ uint32_t s_scan_warp[kSortThreads / 32];
+    __shared__ uint32_t s_partition;
+
+    const uint32_t t = threadIdx.x, lane = lane_id(), warp = t / 32;
+    const uint32_t count = meta->count;
+    const uint32_t partitions = meta->partitions;
+    const uint32_t lanes_below = (1u << lane) - 1u;
+
+    // Exclusive scan over the digits of this pass's global histogram (thread t = digit t).
+    auto block_exclusive = [&](uint32_t v) -> uint32_t {
+        uint32_t inc = v;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const uint32_t up = __shfl_up_sync(0xffffffffu, inc, o);
+            if (lane >= (uint32_t)o) inc += up;
+        }
+        if (lane == 31) s_scan_warp[warp] = inc;
+        __syncthreads();
+        uint32_t before = 0;
+#pragma unroll
+        for (int w = 0; w < kSortThreads / 32; ++w)
+            if ((uint32_t)w < warp) before += s_scan_warp[w];
+        __syncthreads();
+        return before + inc - v;
+    };
+    s_global_base[t] = block_exclusive(histogram[t]);
+
+    for (;;) {
+        if (t == 0) s_partition = atomicAdd(ticket, 1u);
+#pragma unroll
+        for (int w = 0; w < kSortThreads / 32; ++w) s_warp[w][t] = 0;
+        __syncthreads();
+        const uint32_t part = s_partition;
+        if (part >= partitions) break;
+        const uint32_t base = part * kSortPartition;
+
+        // Load: warp w holds keys [base + 512 w, base + 512 (w + 1)), item k at lane + 32 k,
+        // so (warp, item, lane) order is the keys' original order.
+        Key key[kSortItems];
+        uint32_t value[kSortItems], digit[kSortItems], rank[kSortItems];
+#pragma unroll
+        for (int k = 0; k < kSortItems; ++k) {
+            const uint32_t i = base + warp * (32 * kSortItems) + k * 32 + lane;
+            const bool valid = i < count;
+            key[k] = valid ? keys_in[i] : (Key)0;
+            value[k] = valid ? values_in[i] : 0u;
+            digit[k] = valid ? ((uint32_t)(key[k] >> shift) & 255u) : 0xffffu;
+        }
+        // Stable rank within the warp, item by item.
+#pragma unroll
+        for (int k = 0; k < kSortItems; ++k) {
+            const uint32_t peers = __match_any_sync(0xffffffffu, digit[k]);
+            const bool valid = digit[k] < 256u;
+            uint32_t before = 0;
+            if (valid) before = s_warp[warp][digit[k]];
+            rank[k] = before + __popc(peers & lanes_below);
+            __syncwarp();
+            if (valid && (__ffs(peers) - 1) == (int)lane) s_warp[warp][digit[k]] = before + __popc(peers);
+            __syncwarp();
+        }
+        __syncthreads();
+        // Thread t = digit t: the warps' offsets within the partition and its total.
+        uint32_t total = 0;
+#pragma unroll
+        for (int w = 0; w < kSortThreads / 32; ++w) {
+            const uint32_t c = s_warp[w][t];
+            s_warp[w][t] = total;
+            total += c;
+        }
+        // Decoupled look-back for digit t.
+        {
+            cuda::atomic_ref<unsigned long long, cuda::thread_scope_device> mine(
+                lookback[(size_t)part * kSortRadix + t]);
+            const unsigned long long tag = (unsigned long long)sequence << 32;
+            uint32_t prefix = 0;
+            if (part == 0) {
+                mine.store(tag | ((unsigned long long)kFlagInclusive << 30) | total, cuda::memory_order_relaxed);
+            } else {
+                mine.store(tag | ((unsigned long long)kFlagAggregate << 30) | total, cuda::memory_order_relaxed);
+                uint32_t spins = 0;
+                for (int64_t k = (int64_t)part - 1; k >= 0;) {
+                    cuda::atomic_ref<unsigned long long, cuda::thread_scope_device> other(
+                        lookback[(size_t)k * kSortRadix + t]);
+                    const unsigned long long e = other.load(cuda::memory_order_relaxed);
+                    const uint32_t flag = (uint32_t)(e >> 30) & 3u;
+                    if ((uint32_t)(e >> 32) != sequence || flag == 0u) {
+                        if (++spins > kLookbackSpinLimit) {
+                            raise_status(meta, SP_ERR_TIMEOUT);
+                            break;
+                        }
+                        __nanosleep(100);
+                        continue;
+                    }
+                    prefix += (uint32_t)(e & 0x3fffffffull);
+                    if (flag == kFlagInclusive) break;
+                    --k;
+                }
+                mine.store(tag | ((unsigned long long)kFlagInclusive << 30) | (prefix + total),
+                           cuda::memory_order_relaxed);
+            }
+            s_out_base[t] = s_global_base[t] + prefix;
+        }
+        s_block_start[t] = block_exclusive(total);
+        __syncthreads();
+        // Digit-sorted order in shared memory.
+#pragma unroll
+        for (int k = 0; k < kSortItems; ++k)
+            if (digit[k] < 256u) {
+                const uint32_t pos = s_block_start[digit[k]] + s_warp[warp][digit[k]] + rank[k];
+                s_keys[pos] = key[k];
+                s_values[pos] = value[k];
+            }
+        __syncthreads();
+        const uint32_t valid_here = min((uint32_t)kSortPartition, count - base);
+        for (uint32_t i = t; i < valid_here; i += kSortThreads) {
+            const Key k = s_keys[i];
+            const uint32_t d = (uint32_t)(k >> shift) & 255u;
+            const uint32_t dst = s_out_base[d] + (i - s_block_start[d]);
+            keys_out[dst] = k;
+            values_out[dst] = s_values[i];
+        }
+        __syncthreads();
+    }
+}
+
+template <typename Key>
+__global__ void k_ranges(const Key* __restrict__ keys, const DeviceMeta* __restrict__ meta, int tile_shift,
+                         uint32_t tiles, uint2* __restrict__ ranges) {
+    const uint32_t count = meta->count;
+    for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < count; i += gridDim.x * blockDim.x) {
+        const uint32_t tile = (uint32_t)(keys[i] >> tile_shift);
+        if (tile >= tiles) continue;
+        uint32_t* r = reinterpret_cast<uint32_t*>(ranges + tile);
+        if (i == 0 || (uint32_t)(keys[i - 1] >> tile_shift) != tile) r[0] = i;
+        if (i + 1 == count || (uint32_t)(keys[i + 1] >> tile_shift) != tile) r[1] = i + 1;
+    }
+}
+
+int sort_grid() {
+    static int grid = 0;
+    if (grid == 0) {
+        int device = 0, sms = 0;
+        cudaGetDevice(&device);
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
+        grid = (sms > 0 ? sms : 148) * 2;
+    }
+    return grid;
+}
+
+}  // namespace
+
+cudaError_t launch_emit(const float4* records, uint32_t* offsets, const unsigned long long* block_offsets, uint64_t n,
+                        const sp_camera_uniform& cam, int key_mode, const SortPlan& plan, const DeviceMeta* meta,
+                        void* keys, uint32_t* values, uint32_t* sort_histograms, cudaStream_t stream) {
+    const unsigned grid = grid_for(n, kBlock);
+    if (plan.key64)
+        k_emit<unsigned long long><<<grid, kBlock, 0, stream>>>(records, offsets, block_offsets, (uint32_t)n,
+                                                                cam.tiles_x, key_mode, plan.passes, meta,
+                                                                static_cast<unsigned long long*>(keys), values,
+                                                                sort_histograms);
+    else
+        k_emit<uint32_t><<<grid, kBlock, 0, stream>>>(records, offsets, block_offsets, (uint32_t)n, cam.tiles_x,
+                                                      key_mode, plan.passes, meta, static_cast<uint32_t*>(keys),
+                                                      values, sort_histograms);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_sort_pass(const SortPlan& plan, int pass, uint32_t sequence, const void* keys_in,
+                             const uint32_t* values_in, void* keys_out, uint32_t* values_out,
+                             const uint32_t* sort_histograms, uint32_t* sort_tickets, unsigned long long* lookback,
+                             uint32_t max_partitions, DeviceMeta* meta, cudaStream_t stream) {
+    const unsigned grid = (unsigned)std::min<int>(sort_grid(), (int)std::max<uint32_t>(max_partitions, 1u));
+    const uint32_t* hist = sort_histograms + pass * kSortRadix;
+    if (plan.key64) {
+        using K = unsigned long long;
+        const size_t smem = kSortPartition * (sizeof(K) + sizeof(uint32_t));
+        cudaError_t err = cudaFuncSetAttribute(k_sort_pass<K>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (err != cudaSuccess) return err;
+        k_sort_pass<K><<<grid, kSortThreads, smem, stream>>>(8 * pass, sequence, static_cast<const K*>(keys_in),
+                                                             values_in, static_cast<K*>(keys_out), values_out, hist,
+                                                             sort_tickets + pass, lookback, meta);
+    } else {
+        using K = uint32_t;
+        const size_t smem = kSortPartition * (sizeof(K) + sizeof(uint32_t));
+        cudaError_t err = cudaFuncSetAttribute(k_sort_pass<K>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (err != cudaSuccess) return err;
+        k_sort_pass<K><<<grid, kSortThreads, smem, stream>>>(8 * pass, sequence, static_cast<const K*>(keys_in),
+                                                             values_in, static_cast<K*>(keys_out), values_out, hist,
+                                                             sort_tickets + pass, lookback, meta);
+    }
+    return cudaGetLastError();
+}
+
+cudaError_t launch_ranges(const SortPlan& plan, const void* keys, const DeviceMeta* meta, uint64_t capacity,
+                          uint2* ranges, uint32_t tiles, cudaStream_t stream) {
+    cudaError_t err = cudaMemsetAsync(ranges, 0, (size_t)tiles * sizeof(uint2), stream);
+    if (err != cudaSuccess) return err;
+    const unsigned grid = (unsigned)std::min<uint64_t>(std::max<uint64_t>(grid_for(capacity, kBlock), 1), 148 * 16);
+    if (plan.key64)
+        k_ranges<unsigned long long><<<grid, kBlock, 0, stream>>>(static_cast<const unsigned long long*>(keys), meta,
+                                                                   plan.tile_shift, tiles, ranges);
+    else
+        k_ranges<uint32_t><<<grid, kBlock, 0, stream>>>(static_cast<const uint32_t*>(keys), meta, plan.tile_shift,
+                                                         tiles, ranges);
+    return cudaGetLastError();
+}
+
+}  // namespace splat

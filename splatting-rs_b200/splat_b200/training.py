@@ -1,0 +1,108 @@
+"""The training step loop — a mirror of `Trainer` (instantsplat-rs/src/training.rs:86-443),
+the caller that switches its `Rasterizer` / `Adam` for libsplat_b200: one view per step,
+views cycled in order, the position rate decayed over the run, the camera gradient read
+back for the pose refinement when poses are refined. Densification (training.rs:238-266)
+is not part of this path."""
+
+from __future__ import annotations
+
+import numpy as np
+
+from .camera import PinholeCamera, cameras_extent
+from .gaussians import GaussianCloud
+from .optimizer import Adam, LearningRates, LEARNING_RATES_3DGS, position_rate_factor
+from .pose import PoseRefinement
+from .rasterizer import Context, LossTerms, Rasterizer, Rendered, default_options
+
+
+def ground_truth_rgba(rgb: np.ndarray, foreground: np.ndarray) -> np.ndarray:
+    """loss::ground_truth_rgba (loss.rs:95-104): rgb times the mask, then the mask."""
+    mask = np.asarray(foreground, np.float32).reshape(-1, 1)
+    rgb = np.asarray(rgb, np.float32).reshape(-1, 3)
+    return np.concatenate([rgb * mask, mask], axis=1).reshape(-1)
+
+
+class Trainer:
+    """Trainer::new / step / train_step / loss / render over one device."""
+
+    def __init__(
+        self,
+        cloud: GaussianCloud,
+        cameras: list[PinholeCamera],
+        ground_truth: np.ndarray,
+        learning_rates: LearningRates = LEARNING_RATES_3DGS,
+        refine_poses: bool = False,
+        ctx: Context | None = None,
+        backward_mode: int | None = None,
+    ):
+        import torch
+
+        if not cameras:
+            raise ValueError("no views")
+        width, height = cameras[0].width, cameras[0].height
+        for c in cameras:
+            if (c.width, c.height) != (width, height):
+                raise ValueError("every view must have the same size")
+        self.ctx = ctx or Context(0)
+        device = f"cuda:{self.ctx.device}"
+        self.cameras = list(cameras)
+        self.sh_degree = cloud.sh_degree
+        self.params = torch.from_numpy(cloud.to_packed()).to(device)
+        gt = np.ascontiguousarray(ground_truth, np.float32).reshape(-1)
+        if gt.size != len(cameras) * width * height * 4:
+            raise ValueError("ground truth buffer size")
+        self.ground_truth = torch.from_numpy(gt).to(device)
+        options = default_options(sh_degree=self.sh_degree)
+        if backward_mode is not None:
+            options.backward_mode = backward_mode
+        self.rasterizer = Rasterizer(
+            self.ctx, self.params, len(cloud), width, height, self.ground_truth, len(cameras), options
+        )
+        self.extent = cameras_extent(self.cameras)
+        if not self.extent > 0:
+            raise ValueError(f"camera extent {self.extent}: the views' cameras are all at the same position")
+        self.poses = PoseRefinement(self.cameras, learning_rates, self.extent) if refine_poses else None
+        self.adam = Adam(
+            self.ctx,
+            self.params,
+            self.rasterizer,
+            len(cloud),
+            learning_rates,
+            np.float32(self.extent),
+            sh_degree=self.sh_degree,
+        )
+
+    @property
+    def view_count(self) -> int:
+        return len(self.cameras)
+
+    def camera(self, view: int) -> PinholeCamera:
+        return self.poses.camera(view) if self.poses else self.cameras[view]
+
+    def step(self, view: int, rate_factor: float) -> None:
+        """Trainer::step_async (training.rs:197-209)."""
+        self.rasterizer.set_camera(self.camera(view))
+        self.rasterizer.encode_forward()
+        self.rasterizer.encode_loss(view)
+        self.rasterizer.encode_backward()
+        self.adam.encode_step(rate_factor)
+        if self.poses is not None:
+            gradient = self.rasterizer.read_camera_gradient()
+            self.poses.step(view, gradient, rate_factor)
+
+    def train_step(self, step: int, steps: int) -> None:
+        """Trainer::train_step_async (training.rs:221-229), without densification."""
+        self.step(step % self.view_count, position_rate_factor(step, steps))
+
+    def loss(self, view: int) -> LossTerms:
+        """Trainer::loss_async (training.rs:366-374)."""
+        self.rasterizer.set_camera(self.camera(view))
+        self.rasterizer.encode_forward()
+        self.rasterizer.encode_loss(view)
+        return self.rasterizer.read_loss()
+
+    def render(self, view: int) -> Rendered:
+        return self.rasterizer.render(self.camera(view))
+
+    def cloud(self) -> GaussianCloud:
+        return GaussianCloud.from_packed(self.params.cpu().numpy(), self.sh_degree)

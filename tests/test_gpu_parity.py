@@ -1,0 +1,235 @@
+"""Parity of the CUDA path (through the C ABI) with the CPU oracle on seeded inputs.
+
+Bars (the north star's):
+  - projection depth, radius and tile rectangle, tile lists, sort order and tile ranges:
+    bit-exact (the projection and the oracle share operation order and exp);
+  - images: within 1e-4 absolute (premultiplied colours and transmittance lie in [0, 1]),
+    with per-pixel contributor counts equal except at alpha/termination thresholds the
+    hardware exp lands on the other side of (< 0.5 % of pixels);
+  - gradients: |cuda - oracle| <= 1e-4 * max|oracle| + 1e-6 per parameter slot, over all
+    Gaussians (fp32 sums in a different order);
+  - Adam + clamp: bit-exact.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+import oracle
+import splat_b200 as sb
+from helpers import camera_at_origin, make_rasterizer, random_cloud
+from splat_b200 import scenes
+
+pytestmark = pytest.mark.gpu
+
+IMAGE_TOL = 1e-4
+GRAD_REL_TOL = 1e-4
+
+
+def scene_cases():
+    rng = np.random.default_rng(7)
+    cases = {
+        "random600_80x48": (random_cloud(600, rng), camera_at_origin(80, 48, 60.0)),
+        "random3000_sh3_256x192": (random_cloud(3000, np.random.default_rng(9), sh_degree=3),
+                                   camera_at_origin(256, 192, 180.0)),
+    }
+    s = scenes.config(0, scale=0.25)
+    cases["config0_5k_256"] = (s.cloud, s.cameras[1])
+    s = scenes.config(2, scale=0.01)
+    cases["config2_5k_sh3_1024x768"] = (s.cloud, s.cameras[3])
+    return cases
+
+
+CASES = scene_cases()
+
+
+def oracle_forward(cloud, camera, **kw):
+    return oracle.render(cloud.to_packed(), cloud.sh_degree, oracle.camera_array(camera.uniform()), **kw)
+
+
+@pytest.mark.parametrize("name", list(CASES))
+def test_projection_bit_exact(ctx, name):
+    cloud, camera = CASES[name]
+    rast, _, _ = make_rasterizer(ctx, cloud, camera)
+    rast.encode_forward()
+    got = rast.read_projected()
+    want = oracle_forward(cloud, camera)["proj"]
+    for field in ("radius", "tile_min", "tile_max", "depth", "mean", "conic", "opacity", "color"):
+        assert np.array_equal(got[field], want[field]), f"{name}: {field} differs"
+    fwd = oracle_forward(cloud, camera)
+    assert np.array_equal(rast.read_tile_offsets(), fwd["offsets"]), f"{name}: tile offsets differ"
+
+
+@pytest.mark.parametrize("name", list(CASES))
+def test_tile_lists_bit_exact(ctx, name):
+    cloud, camera = CASES[name]
+    rast, _, _ = make_rasterizer(ctx, cloud, camera)
+    rast.encode_forward()
+    meta = rast.read_intersections()
+    keys, gauss = rast.read_sorted_intersections()
+    want = oracle_forward(cloud, camera)
+    assert meta.count == len(want["keys"]) and meta.overflow == 0
+    assert np.array_equal(keys, want["keys"]), f"{name}: sorted keys differ"
+    assert np.array_equal(gauss, want["gauss"]), f"{name}: sort order differs"
+    assert np.array_equal(rast.read_tile_ranges(), want["ranges"]), f"{name}: tile ranges differ"
+
+
+@pytest.mark.parametrize("key_mode", [sb.SP_KEYS_REF20, sb.SP_KEYS_FULL32])
+def test_tile_lists_over_4096_tiles(ctx, key_mode):
+    """1920 x 1080 has 8160 tiles, which the reference's 32-bit keys refuse
+    (rasterizer.rs:188-192); the 64-bit keys keep the same order."""
+    s = scenes.config(3, scale=0.002)
+    cloud, camera = s.cloud, s.cameras[0]
+    rast, _, _ = make_rasterizer(ctx, cloud, camera, key_mode=key_mode)
+    rast.encode_forward()
+    keys, gauss = rast.read_sorted_intersections()
+    want = oracle_forward(cloud, camera, key_mode=key_mode)
+    assert len(keys) > 1000
+    assert np.array_equal(keys, want["keys"]) and np.array_equal(gauss, want["gauss"])
+    assert np.array_equal(rast.read_tile_ranges(), want["ranges"])
+
+
+@pytest.mark.parametrize("name", list(CASES))
+def test_image_matches(ctx, name):
+    cloud, camera = CASES[name]
+    rast, _, _ = make_rasterizer(ctx, cloud, camera)
+    rast.encode_forward()
+    image = rast.read_image().rgbt
+    contrib = rast.read_contributions()
+    want = oracle_forward(cloud, camera)
+    worst = float(np.max(np.abs(image - want["image"])))
+    assert worst < IMAGE_TOL, f"{name}: largest pixel difference {worst}"
+    mismatched = float(np.mean(contrib != want["contrib"]))
+    assert mismatched < 5e-3, f"{name}: {mismatched:.4%} of contributor counts differ"
+
+
+def test_loss_matches(ctx):
+    rng = np.random.default_rng(5)
+    width, height = 40, 24
+    pixels = width * height
+    mask = (rng.random(pixels) < 0.6).astype(np.float32)
+    gt = np.concatenate([rng.random((pixels, 3)).astype(np.float32) * mask[:, None], mask[:, None]], axis=1).reshape(-1)
+    rgbt = np.concatenate([rng.random((pixels, 3)), rng.uniform(0.1, 0.9, (pixels, 1))], axis=1).astype(np.float32).reshape(-1)
+    cloud = random_cloud(4, rng)
+    rast, _, _ = make_rasterizer(ctx, cloud, camera_at_origin(width, height, 40.0), ground_truth=gt)
+    rast.write_image(rgbt)
+    rast.encode_loss(0)
+    got_grad, got_loss = rast.read_loss_gradient(), rast.read_pixel_loss()
+    partials = oracle.ssim(rgbt, gt, width, height)
+    want_grad, want_loss = oracle.loss(rgbt, gt, partials, width, height)
+    assert np.max(np.abs(got_loss - want_loss)) < 1e-5
+    scale = np.max(np.abs(want_grad))
+    assert np.max(np.abs(got_grad - want_grad)) <= 1e-4 * scale
+    terms = rast.read_loss()
+    ref = sb.LossTerms.from_pixel_loss(want_loss)
+    assert abs(terms.total - ref.total) < 1e-6 and abs(terms.dssim - ref.dssim) < 1e-6
+
+
+def _check_gradients(name, got, want, stride):
+    got = got.reshape(-1, stride)
+    want = want.reshape(-1, stride)
+    for slot in range(stride):
+        scale = float(np.max(np.abs(want[:, slot])))
+        err = float(np.max(np.abs(got[:, slot] - want[:, slot])))
+        assert err <= GRAD_REL_TOL * scale + 1e-6, f"{name}: slot {slot} error {err:.3e} vs scale {scale:.3e}"
+
+
+@pytest.mark.parametrize("mode", [sb.SP_BWD_DETERMINISTIC, sb.SP_BWD_ATOMIC])
+@pytest.mark.parametrize("name", list(CASES))
+def test_backward_matches(ctx, name, mode):
+    cloud, camera = CASES[name]
+    rng = np.random.default_rng(11)
+    weights = rng.uniform(-1.0, 1.0, camera.width * camera.height * 4).astype(np.float32)
+    rast, _, _ = make_rasterizer(ctx, cloud, camera, backward_mode=mode)
+    rast.encode_forward()
+    rast.write_loss_gradient(weights)
+    rast.encode_backward()
+    got = rast.read_param_gradients()
+    got_camera = np.ctypeslib.as_array(rast.read_camera_gradient().world_to_camera_rotation_rows).reshape(-1)
+    cam = oracle.camera_array(camera.uniform())
+    packed = cloud.to_packed()
+    fwd = oracle.render(packed, cloud.sh_degree, cam)
+    bwd = oracle.backward(packed, cloud.sh_degree, cam, fwd, weights)
+    _check_gradients(name, got, bwd["param_gradients"], sb.param_stride(cloud.sh_degree))
+    cg = rast.read_camera_gradient()
+    got_cam = np.array(
+        [cg.world_to_camera_rotation_rows[r][c] for r in range(3) for c in range(3)]
+        + list(cg.world_to_camera_translation) + list(cg.focal), np.float32)
+    want_cam = bwd["camera_gradient"]
+    assert np.max(np.abs(got_cam - want_cam)) <= 1e-3 * np.max(np.abs(want_cam)) + 1e-6, (got_cam, want_cam)
+    stats = rast.read_densify_stats()
+    assert np.array_equal(stats[:, 1], bwd["stats"][:, 1]) and np.array_equal(stats[:, 2], bwd["stats"][:, 2])
+    assert np.max(np.abs(stats[:, 0] - bwd["stats"][:, 0])) <= 1e-3 * np.max(bwd["stats"][:, 0]) + 1e-6
+    del got_camera
+
+
+def test_deterministic_backward_is_bit_stable(ctx):
+    cloud, camera = CASES["config0_5k_256"]
+    weights = np.random.default_rng(3).uniform(-1, 1, camera.width * camera.height * 4).astype(np.float32)
+    rast, _, _ = make_rasterizer(ctx, cloud, camera, backward_mode=sb.SP_BWD_DETERMINISTIC)
+    runs = []
+    for _ in range(2):
+        rast.encode_forward()
+        rast.write_loss_gradient(weights)
+        rast.encode_backward()
+        runs.append(rast.read_param_gradients())
+    assert np.array_equal(runs[0], runs[1])
+
+
+@pytest.mark.parametrize("sh_degree", [0, 3])
+def test_adam_bit_exact(ctx, sh_degree):
+    import torch
+
+    rng = np.random.default_rng(21)
+    n = 1037
+    stride = sb.param_stride(sh_degree)
+    params = rng.normal(0, 1, n * stride).astype(np.float32)
+    params.reshape(n, stride)[:, 3:6] = rng.normal(-4, 1.5, (n, 3))
+    grads = rng.normal(0, 1e-3, n * stride).astype(np.float32)
+    p_dev = torch.from_numpy(params.copy()).cuda()
+    g_dev = torch.from_numpy(grads).cuda()
+    rates = sb.LEARNING_RATES_3DGS
+    extent = 3.3
+    adam = sb.Adam(ctx, p_dev, g_dev, n, rates, extent, sh_degree=sh_degree)
+    p_ref, m_ref, v_ref = params.copy(), np.zeros_like(params), np.zeros_like(params)
+    for step in range(1, 4):
+        factor = sb.position_rate_factor(step - 1, 10)
+        adam.encode_step(factor)
+        lr = oracle.learning_rates_by_slot(rates.to_c(), np.float32(extent) * np.float32(factor), stride)
+        oracle.adam_step(p_ref, grads, m_ref, v_ref, stride, lr, step, float(np.log(np.float32(0.02 * np.float32(extent)))),
+                         float(np.log(np.float32(10.0))))
+    ctx.sync()
+    m, v = adam.read_moments()
+    assert np.array_equal(m, m_ref) and np.array_equal(v, v_ref)
+    assert np.array_equal(p_dev.cpu().numpy(), p_ref)
+
+
+def test_overflow_is_reported(ctx):
+    """rasterizer.rs:536-544 panics; the C ABI returns SP_ERR_OVERFLOW."""
+    cloud, camera = CASES["config0_5k_256"]
+    rast, _, _ = make_rasterizer(ctx, cloud, camera, intersections_per_gaussian=1)
+    rast.encode_forward()
+    with pytest.raises(sb.SplatError) as err:
+        rast.read_intersections()
+    assert err.value.status == 3
+    meta = rast.read_intersections_unchecked()
+    assert meta.overflow == 1 and meta.count == meta.capacity == len(cloud)
+    # The capped list is still the oracle's prefix order.
+    keys, gauss = rast.read_sorted_intersections()
+    want = oracle_forward(cloud, camera, capacity=len(cloud))
+    assert np.array_equal(keys, want["keys"]) and np.array_equal(gauss, want["gauss"])
+
+
+def test_everything_culled(ctx):
+    cloud = random_cloud(50, np.random.default_rng(1))
+    cloud.positions[:, 2] *= -1.0  # behind the camera
+    camera = camera_at_origin(40, 30, 30.0)
+    rast, _, _ = make_rasterizer(ctx, cloud, camera)
+    rast.encode_forward()
+    assert rast.read_intersections().count == 0
+    img = rast.read_image().rgbt.reshape(-1, 4)
+    assert np.all(img[:, :3] == 0.0) and np.all(img[:, 3] == 1.0)
+    rast.write_loss_gradient(np.ones(40 * 30 * 4, np.float32))
+    rast.encode_backward()
+    assert np.all(rast.read_param_gradients() == 0.0)
