@@ -1,0 +1,472 @@
+#!/usr/bin/env python
+"""Benchmark of the B200-native splatting path: fwd+bwd views/s at 500k Gaussians (SH
+degree 3), 1024 x 768 — the training step of instantsplat-rs's `Trainer` (one view: forward,
+SSIM/L1 loss, backward, Adam + scale clamp) on the benchmark's config 2.
+
+    python bench.py [--gpus N --steps K --warmup W]          # this library (default)
+    python bench.py --impl reference [--steps K --warmup W]  # the CPU restatement, host cores
+
+One JSON line on rank 0. `value` is device-timed throughput with every input resident in
+HBM; `e2e` is the same step through the public API as the reference's caller runs it
+(camera from the host, pose refinement on: the 56-byte camera gradient and the loss read
+back every step). At N > 1 each rank trains its own views (weak scaling) and the
+parameter gradients are summed by an NCCL all-reduce before every Adam step.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import tempfile
+import time
+from datetime import timedelta
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path[:0] = [str(ROOT / "splatting-rs_b200"), str(ROOT / "oracle")]
+
+METRIC = "fwd+bwd views/sec @500k Gaussians 1024x768 (1/2/4/8 GPU); fwd Mpix/s @3M"
+UNIT = "views/s"
+CONFIG_INDEX = 2
+MEASURED_PEAKS = ROOT / "MEASURED_PEAKS.json"
+FALLBACK_HBM_GBS = 6650.0
+SMS = 148
+FP32_LANES_PER_SM = 128
+# FP32 instructions per (pixel, Gaussian) pair the blend kernels evaluate, counted from
+# their inner loops (rasterize_forward.wgsl:58-77, rasterize_backward.wgsl:166-200): an
+# FMA counts as one. The backward adds a 9-float warp reduction per (Gaussian, warp).
+FORWARD_OPS_PER_PAIR = 20
+BACKWARD_OPS_PER_PAIR = 48
+
+
+def parse_args():
+    p = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=240)
+    p.add_argument("--warmup", type=int, default=10)
+    p.add_argument("--impl", choices=["b200", "reference"], default="b200")
+    p.add_argument("--scale", type=float, default=1.0, help="Gaussian count scale (1.0 = the benchmark)")
+    p.add_argument("--e2e-steps", type=int, default=None)
+    p.add_argument("--cpu-seconds", type=float, default=20.0, help="CPU-baseline sample budget")
+    p.add_argument("--reference-seconds", type=float, default=150.0, help="--impl reference time budget")
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    return p.parse_args()
+
+
+def peaks() -> dict:
+    if MEASURED_PEAKS.exists():
+        data = json.loads(MEASURED_PEAKS.read_text())
+        return {"hbm_gbs": float(data["hbm_gbs"]), "source": "measured", "sm_max_mhz": float(data.get("sm_max_mhz", 1965))}
+    return {"hbm_gbs": FALLBACK_HBM_GBS, "source": "fallback", "sm_max_mhz": 1965.0}
+
+
+# ------------------------------------------------------------------------------ clocks
+
+
+class ClockSampler:
+    """nvidia-smi sampled every 200 ms during the timed region."""
+
+    QUERY = (
+        "index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+        "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+        "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap"
+    )
+
+    def __init__(self, device: int):
+        self.device = device
+        self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.device), f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
+                 "-lms", "200"],
+                stdout=self.file,
+                stderr=subprocess.DEVNULL,
+            )
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+        self.file.flush()
+
+    def summary(self) -> dict:
+        self.file.seek(0)
+        sm, sm_max, reasons = [], 0.0, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.file.read().splitlines():
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                sm_max = max(sm_max, float(parts[2]))
+            except ValueError:
+                continue
+            for name, flag in zip(names, parts[5:9]):
+                if flag.lower().startswith("active"):
+                    reasons.add(name)
+        os.unlink(self.file.name)
+        return {
+            "sm_mhz": float(np.median(sm)) if sm else None,
+            "sm_max_mhz": sm_max or None,
+            "samples": len(sm),
+            "reasons": sorted(reasons),
+        }
+
+
+# --------------------------------------------------------------------------- workload
+
+
+def build_ground_truth(ctx, scene, options_fn):
+    """Targets: the scene's ground-truth cloud rendered by this library, masked at
+    coverage 0.5 (pose_tests.rs:168-189), as loss::ground_truth_rgba lays them out."""
+    import torch
+
+    import splat_b200 as sb
+
+    cams = scene.cameras
+    w, h = cams[0].width, cams[0].height
+    truth = torch.from_numpy(scene.truth.to_packed()).cuda()
+    rast = sb.Rasterizer(ctx, truth, len(scene.truth), w, h, None, 0, options_fn())
+    gt = np.empty((len(cams), h * w, 4), np.float32)
+    for v, cam in enumerate(cams):
+        rgbt = rast.render(cam).rgbt.reshape(-1, 4)
+        mask = ((1.0 - rgbt[:, 3]) > 0.5).astype(np.float32)
+        gt[v, :, :3] = rgbt[:, :3] * mask[:, None]
+        gt[v, :, 3] = mask
+    rast.close()
+    del truth
+    return gt
+
+
+def cpu_baseline(scene, gt: np.ndarray, seconds: float, threads: int | None = None) -> dict:
+    """The CPU oracle's training step on the same workload, views in order, until the
+    sample budget is spent (at least 2 steps)."""
+    import oracle
+
+    import splat_b200 as sb
+
+    if threads:
+        oracle.set_threads(threads)
+    cams = scene.cameras
+    params = scene.cloud.to_packed().copy()
+    m = np.zeros_like(params)
+    v = np.zeros_like(params)
+    deg = scene.cloud.sh_degree
+    stride = sb.param_stride(deg)
+    extent = np.float32(sb.cameras_extent(cams))
+    max_log = float(np.log(np.float32(0.02) * extent))
+    aniso = float(np.log(np.float32(10.0)))
+    steps = 0
+    times = []
+    start = time.perf_counter()
+    while steps < 2 or (time.perf_counter() - start < seconds and steps < 64):
+        view = steps % len(cams)
+        lr = oracle.learning_rates_by_slot(sb.LEARNING_RATES_3DGS.to_c(), extent, stride)
+        t0 = time.perf_counter()
+        oracle.train_step(params, deg, oracle.camera_array(cams[view].uniform()), gt[view].reshape(-1), m, v, lr,
+                          steps + 1, max_log, aniso)
+        times.append(time.perf_counter() - t0)
+        steps += 1
+    total = sum(times)
+    return {
+        "steps": steps,
+        "value": steps / total,
+        "unit": UNIT,
+        "cores": oracle.threads(),
+        "kind": "port",
+        "sample": f"{steps} full training steps of the benchmark workload (views 0-{steps - 1}) "
+                  f"by the C++ oracle (OpenMP), {total:.1f} s",
+        "ms_per_step": 1000.0 * total / steps,
+    }
+
+
+def run_reference(args) -> None:
+    """--impl reference: the reference's CPU arithmetic (the oracle port: the reference
+    itself is Rust + WGSL on wgpu and has no CPU path that runs here) on the host cores."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    import oracle
+
+    from splat_b200 import scenes
+
+    scene = scenes.config(CONFIG_INDEX, scale=args.scale)
+    cams = scene.cameras
+    truth = scene.truth.to_packed()
+    deg = scene.truth.sh_degree
+    needed = min(len(cams), args.warmup + args.steps)
+    gt = np.zeros((len(cams), cams[0].width * cams[0].height, 4), np.float32)
+    for view in range(needed):
+        rgbt = oracle.render(truth, deg, oracle.camera_array(cams[view].uniform()))["image"].reshape(-1, 4)
+        mask = ((1.0 - rgbt[:, 3]) > 0.5).astype(np.float32)
+        gt[view, :, :3] = rgbt[:, :3] * mask[:, None]
+        gt[view, :, 3] = mask
+    # Warm-up steps, then timed steps within the time budget.
+    warm = cpu_baseline(scene, gt, 0.0) if args.warmup > 0 else None
+    del warm
+    result = cpu_baseline(scene, gt, args.reference_seconds)
+    line = {
+        "impl": "reference",
+        "metric": METRIC,
+        "value": result["value"],
+        "unit": UNIT,
+        "n_gpus": 1,
+        "steps": result["steps"],
+        "warmup": args.warmup,
+        "ms_per_step": result["ms_per_step"],
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "f32",
+        "data": "synthetic",
+        "config": config_dict(scene, 1),
+        "cpu_baseline": {k: result[k] for k in ("value", "unit", "cores", "kind", "sample")},
+        "e2e": {"value": result["value"], "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def config_dict(scene, world: int) -> dict:
+    cam = scene.cameras[0]
+    return {
+        "workload": f"config 2: {len(scene.cloud)} Gaussians SH{scene.cloud.sh_degree}, {cam.width}x{cam.height}, "
+                    f"{len(scene.cameras)} views; one step = forward + SSIM/L1 loss + backward + Adam per view",
+        "gaussians": len(scene.cloud),
+        "sh_degree": scene.cloud.sh_degree,
+        "width": cam.width,
+        "height": cam.height,
+        "views": len(scene.cameras),
+        "views_per_step": world,
+        "parallelism": f"view-sharded dp{world}" if world > 1 else "single GPU",
+        "l2": "working set (params, gradients, Adam moments: >0.4 GB) larger than the 126 MB L2",
+    }
+
+
+# ------------------------------------------------------------------------------- main
+
+
+def main() -> None:
+    args = parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+        return
+
+    import torch
+    import torch.distributed as dist
+
+    import splat_b200 as sb
+    from splat_b200 import scenes
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=180), device_id=torch.device("cuda", local))
+
+    scene = scenes.config(CONFIG_INDEX, scale=args.scale)
+    cloud, cams = scene.cloud, scene.cameras
+    deg = cloud.sh_degree
+    views = len(cams)
+    width, height = cams[0].width, cams[0].height
+    ctx = sb.Context(local)
+    options = lambda: sb.default_options(sh_degree=deg, backward_mode=sb.SP_BWD_ATOMIC)  # noqa: E731
+    gt_host = build_ground_truth(ctx, scene, options)
+    params = torch.from_numpy(cloud.to_packed()).cuda()
+    initial = params.clone()
+    gt = torch.from_numpy(gt_host.reshape(-1)).cuda()
+    rast = sb.Rasterizer(ctx, params, len(cloud), width, height, gt, views, options())
+    extent = np.float32(sb.cameras_extent(cams))
+    adam = sb.Adam(ctx, params, rast, len(cloud), sb.LEARNING_RATES_3DGS, extent, sh_degree=deg)
+    uniforms = [c.uniform() for c in cams]
+    grads = rast.param_gradients()
+    iterations = scene.iterations
+
+    def view_of(step: int) -> int:
+        return (step * world + rank) % views
+
+    def device_step(step: int) -> None:
+        v = view_of(step)
+        rast.set_camera(uniforms[v])
+        rast.encode_forward()
+        rast.encode_loss(v)
+        rast.encode_backward()
+        if world > 1:
+            dist.all_reduce(grads)
+        adam.encode_step(sb.position_rate_factor(step % iterations, iterations))
+
+    def barrier():
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+
+    def max_over_ranks(x: float) -> float:
+        if world == 1:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    for i in range(args.warmup):
+        device_step(i)
+    meta = rast.read_intersections_unchecked()
+
+    # ---- value: device-resident throughput.
+    barrier()
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        start.record()
+        for i in range(args.steps):
+            device_step(args.warmup + i)
+        stop.record()
+        torch.cuda.synchronize()
+    ms = max_over_ranks(start.elapsed_time(stop))
+    value = world * args.steps / (ms / 1000.0)
+    clock_summary = clocks.summary()
+
+    # ---- e2e: the reference caller's step through the public API, poses refined.
+    params.copy_(initial)
+    adam_e2e = sb.Adam(ctx, params, rast, len(cloud), sb.LEARNING_RATES_3DGS, extent, sh_degree=deg)
+    poses = sb.PoseRefinement(cams, sb.LEARNING_RATES_3DGS, float(extent))
+    e2e_steps = args.e2e_steps or args.steps
+
+    def api_step(step: int) -> None:
+        v = view_of(step)
+        factor = sb.position_rate_factor(step % iterations, iterations)
+        rast.set_camera(poses.camera(v))
+        rast.encode_forward()
+        rast.encode_loss(v)
+        rast.encode_backward()
+        if world > 1:
+            dist.all_reduce(grads)
+        adam_e2e.encode_step(factor)
+        gradient = rast.read_camera_gradient()
+        rast.read_loss()
+        poses.step(v, gradient, factor)
+
+    for i in range(min(args.warmup, 3)):
+        api_step(i)
+    barrier()
+    e_start, e_stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e_start.record()
+    for i in range(e2e_steps):
+        api_step(args.warmup + i)
+    e_stop.record()
+    torch.cuda.synchronize()
+    e2e_ms = max_over_ranks(e_start.elapsed_time(e_stop))
+    e2e_value = world * e2e_steps / (e2e_ms / 1000.0)
+
+    # ---- per-kernel device time over one pass of every view, and the blend work.
+    ctx.profile(True)
+    for i in range(views):
+        device_step(args.warmup + args.steps + i)
+    ctx.profile(False)
+    profile = ctx.read_profile()
+    fwd_pairs, bwd_pairs = 0, 0
+    for v in range(views):
+        rast.set_camera(uniforms[v])
+        rast.encode_forward()
+        f, b = rast.count_blend_work()
+        fwd_pairs += f
+        bwd_pairs += b
+    launches_per_step = sum(n for _, n in profile.values()) / views
+    pk = peaks()
+    fp32_peak = SMS * FP32_LANES_PER_SM * pk["sm_max_mhz"] * 1e6 / 1e12  # T FP32 instructions / s
+    n_params = len(cloud) * sb.param_stride(deg)
+    kernels = {}
+    for name, (kms, n) in profile.items():
+        if n == 0:
+            continue
+        entry = {"ms_per_launch": kms / n, "launches": n, "share": kms / max(sum(t for t, _ in profile.values()), 1e-9)}
+        if name == "blend_forward":
+            achieved = fwd_pairs / views * FORWARD_OPS_PER_PAIR / (kms / n * 1e-3) / 1e12
+            entry.update(bound="fp32", achieved=achieved, peak=fp32_peak, unit="T FP32 ops/s",
+                         frac=achieved / fp32_peak, pairs_per_launch=fwd_pairs / views)
+        elif name == "blend_backward":
+            achieved = bwd_pairs / views * BACKWARD_OPS_PER_PAIR / (kms / n * 1e-3) / 1e12
+            entry.update(bound="fp32", achieved=achieved, peak=fp32_peak, unit="T FP32 ops/s",
+                         frac=achieved / fp32_peak, pairs_per_launch=bwd_pairs / views)
+        elif name == "adam":
+            achieved = n_params * 28 / (kms / n * 1e-3) / 1e9
+            entry.update(bound="hbm", achieved=achieved, peak=pk["hbm_gbs"], unit="GB/s", frac=achieved / pk["hbm_gbs"],
+                         bytes_per_launch=n_params * 28)
+        elif name == "project":
+            b = len(cloud) * (4 * sb.param_stride(deg) + 52)
+            achieved = b / (kms / n * 1e-3) / 1e9
+            entry.update(bound="hbm", achieved=achieved, peak=pk["hbm_gbs"], unit="GB/s", frac=achieved / pk["hbm_gbs"],
+                         bytes_per_launch=b)
+        kernels[name] = entry
+    dominant = max(kernels, key=lambda k: kernels[k]["share"])
+    d = kernels[dominant]
+    roofline = {
+        "kernel": dominant,
+        "bound": d.get("bound"),
+        "achieved": d.get("achieved"),
+        "peak": d.get("peak"),
+        "unit": d.get("unit"),
+        "frac": d.get("frac"),
+        "traffic": None,
+        "peak_source": ("nominal FP32 issue rate: 148 SMs x 128 lanes x sm_max clock (FMA = 1 op)"
+                        if d.get("bound") == "fp32" else f"{pk['source']} HBM copy bandwidth"),
+    }
+
+    baseline = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        baseline = cpu_baseline(scene, gt_host, args.cpu_seconds)
+        baseline.pop("ms_per_step", None)
+        baseline.pop("steps", None)
+
+    if rank == 0:
+        line = {
+            "metric": METRIC,
+            "value": value,
+            "unit": UNIT,
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": ms / args.steps,
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "f32",
+            "data": "synthetic",
+            "config": config_dict(scene, world),
+            "clocks": clock_summary,
+            "e2e": {
+                "value": e2e_value,
+                "unit": UNIT,
+                "h2d_bytes_per_step": 80,
+                "d2h_bytes_per_step": 56 + 32,
+                "what": "set_camera (80-B camera uniform from the host) + forward + loss + backward + Adam, then the "
+                        "camera gradient (56 B) and the loss sums (32 B) read back and the host pose step",
+            },
+            "gpu_launches": int(round(launches_per_step * args.steps)),
+            "roofline": roofline,
+            "cpu_baseline": baseline,
+            "kernels": kernels,
+            "intersections": int(meta.count),
+            "mpix_per_s": value * width * height / 1e6,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -267,6 +267,36 @@ sp_status sp_read_tile_offsets(sp_rasterizer* r, uint32_t* host);
 sp_status sp_read_gaussian_blend_gradients(sp_rasterizer* r, float* host);
 /* Resets the densification statistics to zero (a fresh rasterizer starts at zero). */
 sp_status sp_clear_densify_stats(sp_rasterizer* r);
+/* Work of the blend kernels for the current camera and parameters (replays the forward
+ * pass's per-pixel decisions; no reference counterpart, used for roofline accounting):
+ * forward_pairs = sum over pixels of the tile-list entries the forward visits, up to and
+ * including the one that terminates the pixel; backward_pairs = sum over pixels of the
+ * contributor count (the entries the backward replays). */
+sp_status sp_count_blend_work(sp_rasterizer* r, uint64_t* forward_pairs, uint64_t* backward_pairs);
+
+/* ------------------------------------------------------------- per-kernel device timing */
+
+/* Kernels timed by the profiler (CUDA events on the context's stream around each launch;
+ * the reference has only wall-clock timing, training.rs:104,147,303). */
+enum {
+    SP_K_PROJECT = 0,
+    SP_K_SCAN = 1,
+    SP_K_EMIT = 2,
+    SP_K_SORT = 3,
+    SP_K_RANGES = 4,
+    SP_K_BLEND_FORWARD = 5,
+    SP_K_SSIM = 6,
+    SP_K_LOSS = 7,
+    SP_K_BLEND_BACKWARD = 8,
+    SP_K_PROJECT_BACKWARD = 9,
+    SP_K_ADAM = 10,
+    SP_K_COUNT = 11
+};
+/* Starts (1) or stops (0) recording events around every kernel launch of the context. */
+sp_status sp_profile_enable(sp_context* ctx, int enable);
+/* Waits for the recorded launches and adds their device milliseconds and launch counts
+ * per kernel into ms[SP_K_COUNT] and launches[SP_K_COUNT]; then forgets them. */
+sp_status sp_profile_read(sp_context* ctx, double* ms, uint64_t* launches);
 
 /* ---------------------------------------------------------------------------- Adam */
 

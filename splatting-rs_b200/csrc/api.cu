@@ -18,7 +18,49 @@ struct sp_context {
     cudaStream_t stream = nullptr;
     bool own_stream = false;
     std::string error;
+    // Per-kernel device timing (sp_profile_enable / sp_profile_read).
+    bool profiling = false;
+    std::vector<cudaEvent_t> event_pool;
+    std::vector<std::pair<cudaEvent_t, cudaEvent_t>> recorded[SP_K_COUNT];
+
+    cudaEvent_t take_event() {
+        if (!event_pool.empty()) {
+            cudaEvent_t e = event_pool.back();
+            event_pool.pop_back();
+            return e;
+        }
+        cudaEvent_t e = nullptr;
+        cudaEventCreate(&e);
+        return e;
+    }
 };
+
+namespace {
+
+// Records a pair of events around the launches in its scope when profiling is on.
+class KernelSpan {
+   public:
+    KernelSpan(sp_context* ctx, int kernel) : ctx_(ctx), kernel_(kernel) {
+        if (ctx_->profiling) {
+            start_ = ctx_->take_event();
+            cudaEventRecord(start_, ctx_->stream);
+        }
+    }
+    ~KernelSpan() {
+        if (start_) {
+            cudaEvent_t stop = ctx_->take_event();
+            cudaEventRecord(stop, ctx_->stream);
+            ctx_->recorded[kernel_].emplace_back(start_, stop);
+        }
+    }
+
+   private:
+    sp_context* ctx_;
+    int kernel_;
+    cudaEvent_t start_ = nullptr;
+};
+
+}  // namespace
 
 struct sp_rasterizer {
     sp_context* ctx = nullptr;
@@ -248,10 +290,14 @@ sp_status sp_context_create_on_stream(int device, void* stream, sp_context** out
 void sp_context_destroy(sp_context* ctx) {
     if (!ctx) return;
     cudaSetDevice(ctx->device);
-    if (ctx->own_stream) {
-        cudaStreamSynchronize(ctx->stream);
-        cudaStreamDestroy(ctx->stream);
-    }
+    cudaStreamSynchronize(ctx->stream);
+    for (int k = 0; k < SP_K_COUNT; ++k)
+        for (auto& pair : ctx->recorded[k]) {
+            cudaEventDestroy(pair.first);
+            cudaEventDestroy(pair.second);
+        }
+    for (cudaEvent_t e : ctx->event_pool) cudaEventDestroy(e);
+    if (ctx->own_stream) cudaStreamDestroy(ctx->stream);
     delete ctx;
 }
 
@@ -428,22 +474,40 @@ sp_status sp_forward(sp_rasterizer* r) {
     sp_context* ctx = r->ctx;
     SP_CHECK(select_device(ctx));
     cudaStream_t st = ctx->stream;
-    SP_CUDA(ctx, launch_project(r->params, r->n, (int)r->options.sh_degree, r->camera, r->records, r->radii,
-                                r->offsets, r->block_totals, st));
-    SP_CUDA(ctx, launch_scan_blocks(r->block_totals, r->block_offsets, r->blocks, r->capacity, r->meta,
-                                    r->sort_histograms, r->sort_tickets, st));
-    SP_CUDA(ctx, launch_emit(r->records, r->offsets, r->block_offsets, r->n, r->camera, (int)r->options.key_mode,
-                             r->plan, r->meta, r->keys[0], r->values[0], r->sort_histograms, st));
+    {
+        KernelSpan span(ctx, SP_K_PROJECT);
+        SP_CUDA(ctx, launch_project(r->params, r->n, (int)r->options.sh_degree, r->camera, r->records, r->radii,
+                                    r->offsets, r->block_totals, st));
+    }
+    {
+        KernelSpan span(ctx, SP_K_SCAN);
+        SP_CUDA(ctx, launch_scan_blocks(r->block_totals, r->block_offsets, r->blocks, r->capacity, r->meta,
+                                        r->sort_histograms, r->sort_tickets, st));
+    }
+    {
+        KernelSpan span(ctx, SP_K_EMIT);
+        SP_CUDA(ctx, launch_emit(r->records, r->offsets, r->block_offsets, r->n, r->camera,
+                                 (int)r->options.key_mode, r->plan, r->meta, r->keys[0], r->values[0],
+                                 r->sort_histograms, st));
+    }
     for (int pass = 0; pass < r->plan.passes; ++pass) {
         const int from = pass & 1, to = from ^ 1;
+        KernelSpan span(ctx, SP_K_SORT);
         SP_CUDA(ctx, launch_sort_pass(r->plan, pass, ++r->sequence, r->keys[from], r->values[from], r->keys[to],
                                       r->values[to], r->sort_histograms, r->sort_tickets, r->lookback,
                                       r->max_partitions, r->meta, st));
     }
     r->sorted_buffer = r->plan.passes & 1;
-    SP_CUDA(ctx, launch_ranges(r->plan, r->keys[r->sorted_buffer], r->meta, r->capacity, r->ranges, r->tiles, st));
-    SP_CUDA(ctx, launch_blend_forward(r->records, r->values[r->sorted_buffer], r->ranges, r->camera, r->image,
-                                      r->contributions, st));
+    {
+        KernelSpan span(ctx, SP_K_RANGES);
+        SP_CUDA(ctx,
+                launch_ranges(r->plan, r->keys[r->sorted_buffer], r->meta, r->capacity, r->ranges, r->tiles, st));
+    }
+    {
+        KernelSpan span(ctx, SP_K_BLEND_FORWARD);
+        SP_CUDA(ctx, launch_blend_forward(r->records, r->values[r->sorted_buffer], r->ranges, r->camera, r->image,
+                                          r->contributions, st));
+    }
     r->forward_done = true;
     return SP_OK;
 }
@@ -453,9 +517,15 @@ sp_status sp_loss(sp_rasterizer* r, uint32_t view) {
     SP_REQUIRE(r->ctx, view < r->views, SP_ERR_INVALID, "view index out of range");
     SP_CHECK(select_device(r->ctx));
     const float4* gt = reinterpret_cast<const float4*>(r->ground_truth) + (size_t)view * r->pixels();
-    SP_CUDA(r->ctx, launch_ssim(r->image, gt, r->width, r->height, r->ssim_partials, r->ctx->stream));
-    SP_CUDA(r->ctx, launch_loss(r->image, gt, r->ssim_partials, r->width, r->height, r->options.loss_weights,
-                                r->loss_gradient, r->pixel_loss, r->ctx->stream));
+    {
+        KernelSpan span(r->ctx, SP_K_SSIM);
+        SP_CUDA(r->ctx, launch_ssim(r->image, gt, r->width, r->height, r->ssim_partials, r->ctx->stream));
+    }
+    {
+        KernelSpan span(r->ctx, SP_K_LOSS);
+        SP_CUDA(r->ctx, launch_loss(r->image, gt, r->ssim_partials, r->width, r->height, r->options.loss_weights,
+                                    r->loss_gradient, r->pixel_loss, r->ctx->stream));
+    }
     return SP_OK;
 }
 
@@ -464,16 +534,23 @@ sp_status sp_backward(sp_rasterizer* r) {
     SP_REQUIRE(r->ctx, r->forward_done, SP_ERR_INVALID, "backward before any forward pass");
     SP_CHECK(select_device(r->ctx));
     cudaStream_t st = r->ctx->stream;
-    if (r->options.backward_mode == SP_BWD_ATOMIC)
-        SP_CUDA(r->ctx, cudaMemsetAsync(r->gaussian_gradients, 0, r->n * 3 * sizeof(float4), st));
-    SP_CUDA(r->ctx, launch_blend_backward((int)r->options.backward_mode, r->records, r->values[r->sorted_buffer],
-                                          r->ranges, r->offsets, r->camera, r->image, r->contributions,
-                                          r->loss_gradient, r->slot_gradients, r->gaussian_gradients, st));
-    SP_CUDA(r->ctx, launch_project_backward(r->params, r->n, (int)r->options.sh_degree, (int)r->options.backward_mode,
-                                            r->camera, r->records, r->radii, r->offsets, r->slot_gradients,
-                                            r->capacity, r->gaussian_gradients, r->param_gradients,
-                                            (int)r->options.accumulate_gradients, r->camera_partials, r->camera_done,
-                                            r->camera_gradient, r->densify_stats, st));
+    {
+        KernelSpan span(r->ctx, SP_K_BLEND_BACKWARD);
+        if (r->options.backward_mode == SP_BWD_ATOMIC)
+            SP_CUDA(r->ctx, cudaMemsetAsync(r->gaussian_gradients, 0, r->n * 3 * sizeof(float4), st));
+        SP_CUDA(r->ctx, launch_blend_backward((int)r->options.backward_mode, r->records,
+                                              r->values[r->sorted_buffer], r->ranges, r->offsets, r->camera,
+                                              r->image, r->contributions, r->loss_gradient, r->slot_gradients,
+                                              r->gaussian_gradients, st));
+    }
+    {
+        KernelSpan span(r->ctx, SP_K_PROJECT_BACKWARD);
+        SP_CUDA(r->ctx, launch_project_backward(
+                            r->params, r->n, (int)r->options.sh_degree, (int)r->options.backward_mode, r->camera,
+                            r->records, r->radii, r->offsets, r->slot_gradients, r->capacity, r->gaussian_gradients,
+                            r->param_gradients, (int)r->options.accumulate_gradients, r->camera_partials,
+                            r->camera_done, r->camera_gradient, r->densify_stats, st));
+    }
     return SP_OK;
 }
 
@@ -669,6 +746,51 @@ sp_status sp_read_gaussian_blend_gradients(sp_rasterizer* r, float* host) {
     return SP_OK;
 }
 
+sp_status sp_count_blend_work(sp_rasterizer* r, uint64_t* forward_pairs, uint64_t* backward_pairs) {
+    if (!r || !forward_pairs || !backward_pairs) return SP_ERR_INVALID;
+    SP_REQUIRE(r->ctx, r->forward_done, SP_ERR_INVALID, "count before any forward pass");
+    SP_CHECK(select_device(r->ctx));
+    unsigned long long* counts = nullptr;
+    SP_CUDA(r->ctx, cudaMallocAsync((void**)&counts, 2 * sizeof(unsigned long long), r->ctx->stream));
+    cudaError_t err = cudaMemsetAsync(counts, 0, 2 * sizeof(unsigned long long), r->ctx->stream);
+    if (err == cudaSuccess)
+        err = launch_count_blend(r->records, r->values[r->sorted_buffer], r->ranges, r->camera, r->contributions,
+                                 counts, r->ctx->stream);
+    unsigned long long host[2] = {0, 0};
+    sp_status s = err == cudaSuccess ? read_device(r->ctx, host, counts, sizeof(host))
+                                     : cuda_fail(r->ctx, err, "launch_count_blend");
+    cudaFreeAsync(counts, r->ctx->stream);
+    cudaStreamSynchronize(r->ctx->stream);
+    *forward_pairs = host[0];
+    *backward_pairs = host[1];
+    return s;
+}
+
+sp_status sp_profile_enable(sp_context* ctx, int enable) {
+    if (!ctx) return SP_ERR_INVALID;
+    SP_CHECK(select_device(ctx));
+    ctx->profiling = enable != 0;
+    return SP_OK;
+}
+
+sp_status sp_profile_read(sp_context* ctx, double* ms, uint64_t* launches) {
+    if (!ctx || !ms || !launches) return SP_ERR_INVALID;
+    SP_CHECK(select_device(ctx));
+    SP_CHECK(sync_stream(ctx));
+    for (int k = 0; k < SP_K_COUNT; ++k) {
+        for (auto& pair : ctx->recorded[k]) {
+            float elapsed = 0.0f;
+            SP_CUDA(ctx, cudaEventElapsedTime(&elapsed, pair.first, pair.second));
+            ms[k] += elapsed;
+            launches[k] += 1;
+            ctx->event_pool.push_back(pair.first);
+            ctx->event_pool.push_back(pair.second);
+        }
+        ctx->recorded[k].clear();
+    }
+    return SP_OK;
+}
+
 // ------------------------------------------------------------------------------- Adam
 
 static sp_status adam_make(sp_context* ctx, float* d_params, const float* d_gradients, uint64_t n, uint32_t sh_degree,
@@ -757,6 +879,7 @@ sp_status sp_adam_step_range(sp_adam* a, uint64_t first, uint64_t count) {
     SP_REQUIRE(a->ctx, a->step > 0 && !a->lr_by_slot.empty(), SP_ERR_INVALID, "sp_adam_advance first");
     SP_REQUIRE(a->ctx, first <= a->n && count <= a->n - first, SP_ERR_INVALID, "range outside the Gaussians");
     SP_CHECK(select_device(a->ctx));
+    KernelSpan span(a->ctx, SP_K_ADAM);
     SP_CUDA(a->ctx, launch_adam(a->params, a->gradients, a->first_moment, a->second_moment, first, count, (int)a->stride,
                                 a->lr_by_slot.data(), a->bias1, a->bias2, a->max_log_scale, a->max_log_anisotropy,
                                 a->ctx->stream));

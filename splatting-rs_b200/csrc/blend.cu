@@ -233,7 +233,55 @@ __global__ void __launch_bounds__(kTilePixels) k_blend_backward(
     }
 }
 
+// The forward's per-pixel walk without the colour, counting the entries visited (up to
+// and including the terminating one), plus the contributor counts the backward replays.
+__global__ void __launch_bounds__(kTilePixels) k_count_blend(const float4* __restrict__ records,
+                                                             const uint32_t* __restrict__ sorted,
+                                                             const uint2* __restrict__ ranges,
+                                                             const sp_camera_uniform cam,
+                                                             const uint32_t* __restrict__ contributions,
+                                                             unsigned long long* counts) {
+    const uint32_t tile = blockIdx.x;
+    const uint32_t gx = tile % cam.tiles_x, gy = tile / cam.tiles_x;
+    const uint32_t t = threadIdx.x;
+    const uint32_t px = gx * SP_TILE + (t % SP_TILE), py = gy * SP_TILE + (t / SP_TILE);
+    unsigned long long visited = 0, replayed = 0;
+    if (px < cam.width && py < cam.height) {
+        const uint2 range = ranges[tile];
+        const float fpx = (float)px, fpy = (float)py;
+        float transmittance = 1.0f;
+        for (uint32_t j = range.x; j < range.y; ++j) {
+            ++visited;
+            const float4* rec = records + (size_t)sorted[j] * kRecord;
+            const float4 a = rec[0], b = rec[1];
+            const float dx = a.x - fpx, dy = a.y - fpy;
+            const float power = -0.5f * (a.z * dx * dx + b.x * dy * dy) - a.w * dx * dy;
+            if (power > 0.0f) continue;
+            const float alpha = fminf(SP_MAX_ALPHA, b.y * __expf(power));
+            if (alpha < SP_MIN_ALPHA) continue;
+            const float next = transmittance * (1.0f - alpha);
+            if (next < SP_MIN_TRANSMITTANCE) break;
+            transmittance = next;
+        }
+        replayed = contributions[(size_t)py * cam.width + px];
+    }
+    visited = __reduce_add_sync(0xffffffffu, (unsigned)visited);
+    replayed = __reduce_add_sync(0xffffffffu, (unsigned)replayed);
+    if (lane_id() == 0) {
+        atomicAdd(counts, visited);
+        atomicAdd(counts + 1, replayed);
+    }
+}
+
 }  // namespace
+
+cudaError_t launch_count_blend(const float4* records, const uint32_t* sorted_gaussians, const uint2* ranges,
+                               const sp_camera_uniform& cam, const uint32_t* contributions,
+                               unsigned long long* counts, cudaStream_t stream) {
+    k_count_blend<<<cam.tiles_x * cam.tiles_y, kTilePixels, 0, stream>>>(records, sorted_gaussians, ranges, cam,
+                                                                          contributions, counts);
+    return cudaGetLastError();
+}
 
 cudaError_t launch_blend_forward(const float4* records, const uint32_t* sorted_gaussians, const uint2* ranges,
                                  const sp_camera_uniform& cam, float4* image, uint32_t* contributions,

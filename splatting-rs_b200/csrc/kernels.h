@@ -66,6 +66,12 @@ cudaError_t launch_blend_backward(int mode, const float4* records, const uint32_
                                   const float4* image, const uint32_t* contributions, const float4* loss_gradient,
                                   float* slot_gradients, float4* gaussian_gradients, cudaStream_t stream);
 
+// The work the blend kernels do for the current state: counts[0] += entries the forward
+// visits per pixel (through the terminating one), counts[1] += contributors per pixel.
+cudaError_t launch_count_blend(const float4* records, const uint32_t* sorted_gaussians, const uint2* ranges,
+                               const sp_camera_uniform& cam, const uint32_t* contributions,
+                               unsigned long long* counts, cudaStream_t stream);
+
 // ---- loss.cu
 
 // ssim_forward.wgsl:34-91 (separable window sums in shared memory).

@@ -30,6 +30,21 @@ SP_KEYS_FULL32 = 1
 SP_BWD_DETERMINISTIC = 0
 SP_BWD_ATOMIC = 1
 
+# Kernels of the per-kernel profiler (SP_K_*), in enum order.
+KERNEL_NAMES = (
+    "project",
+    "scan",
+    "emit",
+    "sort",
+    "ranges",
+    "blend_forward",
+    "ssim",
+    "loss",
+    "blend_backward",
+    "project_backward",
+    "adam",
+)
+
 
 class CameraUniform(ctypes.Structure):
     """CameraUniform (camera.rs:23-31), 80 bytes."""
@@ -190,6 +205,9 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "sp_read_tile_offsets": (c_int, [_P, _P]),
     "sp_read_gaussian_blend_gradients": (c_int, [_P, _P]),
     "sp_clear_densify_stats": (c_int, [_P]),
+    "sp_count_blend_work": (c_int, [_P, POINTER(c_uint64), POINTER(c_uint64)]),
+    "sp_profile_enable": (c_int, [_P, c_int]),
+    "sp_profile_read": (c_int, [_P, POINTER(c_double), POINTER(c_uint64)]),
     "sp_adam_create": (c_int, [_P, _P, _P, c_uint64, c_uint32, POINTER(LearningRatesC), c_float, POINTER(_P)]),
     "sp_adam_resume": (c_int, [_P, _P, _P, c_uint64, _P, _P, POINTER(_P)]),
     "sp_adam_destroy": (None, [_P]),

@@ -74,6 +74,18 @@ class Context:
     def sync(self) -> None:
         _lib.check(self.lib.sp_context_sync(self.handle), self.handle, "sync")
 
+    def profile(self, enable: bool) -> None:
+        """Starts or stops CUDA-event timing around every kernel launch."""
+        _lib.check(self.lib.sp_profile_enable(self.handle, 1 if enable else 0), self.handle, "profile")
+
+    def read_profile(self) -> dict[str, tuple[float, int]]:
+        """{kernel: (device ms, launches)} of the launches recorded since the last read."""
+        k = len(_lib.KERNEL_NAMES)
+        ms = (ctypes.c_double * k)()
+        launches = (ctypes.c_uint64 * k)()
+        _lib.check(self.lib.sp_profile_read(self.handle, ms, launches), self.handle, "read_profile")
+        return {name: (ms[i], int(launches[i])) for i, name in enumerate(_lib.KERNEL_NAMES)}
+
     def close(self) -> None:
         if getattr(self, "handle", None):
             self.lib.sp_context_destroy(self.handle)
@@ -382,6 +394,12 @@ class Rasterizer:
 
     def read_tile_offsets(self) -> np.ndarray:
         return self._read(self.lib.sp_read_tile_offsets, self.gaussian_count, np.uint32, "read_tile_offsets")
+
+    def count_blend_work(self) -> tuple[int, int]:
+        """(forward pairs visited, backward pairs replayed) of the last forward pass."""
+        fwd, bwd = ctypes.c_uint64(), ctypes.c_uint64()
+        self._check(self.lib.sp_count_blend_work(self.handle, ctypes.byref(fwd), ctypes.byref(bwd)), "count")
+        return int(fwd.value), int(bwd.value)
 
     def read_gaussian_blend_gradients(self) -> np.ndarray:
         return self._read(
