@@ -126,13 +126,81 @@ def test_loss_matches(ctx):
     assert abs(terms.total - ref.total) < 1e-6 and abs(terms.dssim - ref.dssim) < 1e-6
 
 
+# The rotation slots (6-9) go through d_q = (d_unit - q <q, d_unit>) / |q| over differences
+# of near-equal products (project_backward.wgsl:182-188), which amplifies the last-bit
+# differences of the fp32 blend sums (summed in another order) by up to ~100x on a few
+# Gaussians; their bar is 1e-3 of the slot's largest gradient. Both halves of the chain
+# are pinned tighter on their own: the per-Gaussian blend sums within 1e-4
+# (test_blend_sums_match) and the projection backward bit-exact given the same blend sums
+# (test_projection_backward_bit_exact).
+ROTATION_REL_TOL = 1e-3
+
+
 def _check_gradients(name, got, want, stride):
     got = got.reshape(-1, stride)
     want = want.reshape(-1, stride)
     for slot in range(stride):
+        tol = ROTATION_REL_TOL if 6 <= slot < 10 else GRAD_REL_TOL
         scale = float(np.max(np.abs(want[:, slot])))
         err = float(np.max(np.abs(got[:, slot] - want[:, slot])))
-        assert err <= GRAD_REL_TOL * scale + 1e-6, f"{name}: slot {slot} error {err:.3e} vs scale {scale:.3e}"
+        assert err <= tol * scale + 1e-6, f"{name}: slot {slot} error {err:.3e} vs scale {scale:.3e}"
+
+
+def _oracle_blend_sums(cloud, fwd, slot_gradients):
+    """Per Gaussian, the sum of its slots in slot order (project_backward.wgsl:38-55)."""
+    slots = slot_gradients.reshape(-1, 10)
+    out = np.zeros((len(cloud), 10), np.float32)
+    proj = fwd["proj"]
+    for g in np.nonzero(proj["radius"])[0]:
+        span = proj["tile_max"][g].astype(np.int64) - proj["tile_min"][g].astype(np.int64)
+        o = int(fwd["offsets"][g])
+        for row in slots[o : o + int(span[0] * span[1])]:
+            out[g] += row
+    return out
+
+
+@pytest.mark.parametrize("mode", [sb.SP_BWD_DETERMINISTIC, sb.SP_BWD_ATOMIC])
+@pytest.mark.parametrize("name", ["random600_80x48", "config2_5k_sh3_1024x768"])
+def test_blend_sums_match(ctx, name, mode):
+    cloud, camera = CASES[name]
+    weights = np.random.default_rng(11).uniform(-1.0, 1.0, camera.width * camera.height * 4).astype(np.float32)
+    rast, _, _ = make_rasterizer(ctx, cloud, camera, backward_mode=mode)
+    rast.encode_forward()
+    rast.write_loss_gradient(weights)
+    rast.encode_backward()
+    got = rast.read_gaussian_blend_gradients()
+    cam = oracle.camera_array(camera.uniform())
+    packed = cloud.to_packed()
+    fwd = oracle.render(packed, cloud.sh_degree, cam)
+    want = _oracle_blend_sums(cloud, fwd, oracle.backward(packed, cloud.sh_degree, cam, fwd, weights)["slot_gradients"])
+    for c in range(9):
+        scale = float(np.max(np.abs(want[:, c])))
+        err = float(np.max(np.abs(got[:, c] - want[:, c])))
+        assert err <= GRAD_REL_TOL * scale + 1e-7, f"{name}: blend sum {c} error {err:.3e} vs scale {scale:.3e}"
+
+
+@pytest.mark.parametrize("name", list(CASES))
+def test_projection_backward_bit_exact(ctx, name):
+    """Given the same per-Gaussian blend sums, the CUDA projection backward (compiled
+    without FMA contraction) reproduces the oracle's parameter gradients bit for bit."""
+    cloud, camera = CASES[name]
+    weights = np.random.default_rng(13).uniform(-1.0, 1.0, camera.width * camera.height * 4).astype(np.float32)
+    rast, _, _ = make_rasterizer(ctx, cloud, camera, backward_mode=sb.SP_BWD_ATOMIC)
+    rast.encode_forward()
+    rast.write_loss_gradient(weights)
+    rast.encode_backward()
+    got = rast.read_param_gradients()
+    sums = rast.read_gaussian_blend_gradients()
+    cam = oracle.camera_array(camera.uniform())
+    packed = cloud.to_packed()
+    fwd = oracle.render(packed, cloud.sh_degree, cam)
+    count = int(fwd["meta"]["count"])
+    slots = np.zeros((max(count, 1), 10), np.float32)
+    for g in np.nonzero(fwd["proj"]["radius"])[0]:
+        slots[int(fwd["offsets"][g])] = sums[g]  # the whole sum in the Gaussian's first slot
+    want, _, _ = oracle.project_backward(packed, cloud.sh_degree, cam, fwd["proj"], fwd["offsets"], slots.reshape(-1),
+                                         count)
+    assert np.array_equal(got, want)
 
 
 @pytest.mark.parametrize("mode", [sb.SP_BWD_DETERMINISTIC, sb.SP_BWD_ATOMIC])
