@@ -245,6 +245,22 @@ sp_status sp_read_camera_gradient(sp_rasterizer* r, sp_camera_gradient* host);
 sp_status sp_read_image(sp_rasterizer* r, float* host_rgbt);         /* P * 4 */
 sp_status sp_read_pixel_loss(sp_rasterizer* r, float* host);         /* P * 4 */
 sp_status sp_read_loss(sp_rasterizer* r, sp_loss_terms* out);        /* read_loss */
+
+/* Largest pixel_count sp_loss_sums_noalloc accepts: 1024 blocks of 4096 pixels. */
+#define SP_NOALLOC_MAX_PIXELS 4194304ull
+/* No counterpart in the reference. The sums over pixels of the 4 per-pixel loss terms
+ * (L1, alpha error, 1 - SSIM, weighted total: what sp_read_loss divides by the pixel count)
+ * of `d_pixel_loss` (pixel_count x 4 floats, device) into `d_sums` (4 doubles, device), on
+ * `stream` of device `device`, without allocating anything: for callers whose device memory
+ * is owned by their own allocator or who cannot afford the device-wide synchronisation of a
+ * cudaMalloc / cudaFree. Its scratch is a fixed 8 KiB array in the library that every GPU
+ * loading the library keeps until exit; hence the limit: SP_ERR_INVALID for pixel_count 0
+ * or above SP_NOALLOC_MAX_PIXELS. The first call on a device looks the array's device
+ * address up (cudaGetSymbolAddress); make that first call before any stream capture. Every
+ * call shares the array, so calls that overlap on the GPU race: order them on one stream.
+ * Enqueues only; the sums are ready when the stream reaches them. */
+sp_status sp_loss_sums_noalloc(int device, const float* d_pixel_loss, uint64_t pixel_count, double* d_sums,
+                               void* stream);
 /* read_intersections (rasterizer.rs:536-544): fills `out` and returns SP_ERR_OVERFLOW when
  * the list overflowed (where the reference panics). */
 sp_status sp_read_intersections(sp_rasterizer* r, sp_intersection_meta* out);

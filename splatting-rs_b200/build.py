@@ -27,7 +27,7 @@ LIBRARY = HERE / "splat_b200" / "libsplat_b200.so"
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", f"-I{INCLUDE}", "--expt-relaxed-constexpr"]
 EXACT = {"project.cu", "adam.cu"}
-SOURCES = ["project.cu", "sort.cu", "blend.cu", "loss.cu", "adam.cu", "api.cu", "pose.cpp"]
+SOURCES = ["project.cu", "sort.cu", "blend.cu", "loss.cu", "adam.cu", "api.cu", "pose.cpp", "noalloc.cu"]
 
 
 def nvcc() -> str:

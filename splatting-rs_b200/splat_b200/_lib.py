@@ -196,6 +196,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "sp_read_image": (c_int, [_P, _P]),
     "sp_read_pixel_loss": (c_int, [_P, _P]),
     "sp_read_loss": (c_int, [_P, POINTER(LossTermsC)]),
+    "sp_loss_sums_noalloc": (c_int, [c_int, _P, c_uint64, _P, _P]),
     "sp_read_intersections": (c_int, [_P, POINTER(IntersectionMeta)]),
     "sp_render": (c_int, [_P, POINTER(CameraUniform), _P]),
     "sp_read_projected": (c_int, [_P, _P]),
