@@ -1,11 +1,17 @@
 // Alpha blending: forward (K6, rasterize_forward.wgsl:22-88) and backward (K8,
-// rasterize_backward.wgsl:30-133). One block of 16 x 16 threads per tile, one pixel per
-// thread; the tile's Gaussians are gathered (sorted list -> Gaussian -> 48-B record, an
-// L2-resident array) into shared memory a batch at a time and read back as broadcasts.
+// rasterize_backward.wgsl:30-133). One block of 256 threads per 16 x 16 tile, one pixel per
+// thread; each warp owns an 8 x 4 block of the tile. The tile's Gaussians are gathered
+// (sorted list -> Gaussian -> 48-B record, an L2-resident array) into shared memory a batch
+// at a time and read back as broadcasts.
+//
+// With each record the batch loader stores the pixel rectangle outside of which the
+// Gaussian's alpha is below 1/255 (the exact per-pixel test rejects it there), padded; a
+// warp whose 8 x 4 pixels miss that rectangle skips the Gaussian as a whole. This changes
+// no result: only pairs the exact test would reject are skipped.
 //
 // The arithmetic per (pixel, Gaussian) is the reference's. exp is the hardware
-// approximation (__expf, MUFU.EX2), so images and gradients match the oracle within a
-// tolerance rather than bit for bit.
+// approximation (__expf), and the backward divides by (1 - alpha) through one reciprocal,
+// so images and gradients match the oracle within a tolerance rather than bit for bit.
 #include "kernels.h"
 
 namespace splat {
@@ -13,19 +19,46 @@ namespace {
 
 constexpr int kForwardBatch = 256;
 constexpr int kBackwardBatch = 32;
+constexpr int kWarps = kTilePixels / 32;
+constexpr uint32_t kFull = 0xffffffffu;
+
+// Pixel of thread (warp, lane) within the tile: warps tile it as 2 x 4 blocks of 8 x 4.
+__device__ __forceinline__ uint32_t local_x(uint32_t warp, uint32_t lane) { return ((warp & 1u) << 3) | (lane & 7u); }
+__device__ __forceinline__ uint32_t local_y(uint32_t warp, uint32_t lane) { return ((warp >> 1) << 2) | (lane >> 3); }
+
+// {xmin, xmax, ymin, ymax}: where op * exp(power) >= 1/255 can hold, i.e. the ellipse
+// d^T C d <= 2 ln(255 op) of the conic C, padded by 1 % in the level and 0.05 px.
+__device__ __forceinline__ float4 alpha_box(float4 a, float4 b) {
+    const float level = b.y * 255.0f;
+    if (!(level > 1.0f)) return make_float4(INFINITY, -INFINITY, INFINITY, -INFINITY);
+    const float q = 2.02f * __logf(level) + 0.02f;
+    const float det = a.z * b.x - a.w * a.w;
+    if (!(det > 0.0f) || !(a.z > 0.0f) || !(b.x > 0.0f))
+        return make_float4(-INFINITY, INFINITY, -INFINITY, INFINITY);
+    const float ex = sqrtf(q * b.x / det) + 0.05f;
+    const float ey = sqrtf(q * a.z / det) + 0.05f;
+    return make_float4(a.x - ex, a.x + ex, a.y - ey, a.y + ey);
+}
+
+__device__ __forceinline__ bool misses(float4 box, float x0, float x1, float y0, float y1) {
+    return box.y < x0 || box.x > x1 || box.w < y0 || box.z > y1;
+}
 
 __global__ void __launch_bounds__(kTilePixels) k_blend_forward(const float4* __restrict__ records,
                                                                const uint32_t* __restrict__ sorted,
                                                                const uint2* __restrict__ ranges,
                                                                const sp_camera_uniform cam, float4* __restrict__ image,
                                                                uint32_t* __restrict__ contributions) {
-    __shared__ float4 s_a[kForwardBatch];  // mean.x, mean.y, conic.a, conic.b
-    __shared__ float4 s_b[kForwardBatch];  // conic.c, opacity, colour.r, colour.g
-    __shared__ float s_c[kForwardBatch];   // colour.b
+    __shared__ float4 s_a[kForwardBatch];    // mean.x, mean.y, conic.a, conic.b
+    __shared__ float4 s_b[kForwardBatch];    // conic.c, opacity, colour.r, colour.g
+    __shared__ float4 s_box[kForwardBatch];  // alpha_box
+    __shared__ float s_c[kForwardBatch];     // colour.b
     const uint32_t tile = blockIdx.x;
     const uint32_t gx = tile % cam.tiles_x, gy = tile / cam.tiles_x;
-    const uint32_t t = threadIdx.x;
-    const uint32_t px = gx * SP_TILE + (t % SP_TILE), py = gy * SP_TILE + (t / SP_TILE);
+    const uint32_t t = threadIdx.x, warp = t / 32, lane = lane_id();
+    const uint32_t px = gx * SP_TILE + local_x(warp, lane), py = gy * SP_TILE + local_y(warp, lane);
+    const float wx0 = (float)(gx * SP_TILE + ((warp & 1u) << 3)), wx1 = wx0 + 7.0f;
+    const float wy0 = (float)(gy * SP_TILE + ((warp >> 1) << 2)), wy1 = wy0 + 3.0f;
     const bool inside = px < cam.width && py < cam.height;
     const float fpx = (float)px, fpy = (float)py;
     const uint2 range = ranges[tile];
@@ -40,14 +73,17 @@ __global__ void __launch_bounds__(kTilePixels) k_blend_forward(const float4* __r
         const uint32_t j = base + t;
         if (j < count) {
             const float4* rec = records + (size_t)sorted[range.x + j] * kRecord;
-            s_a[t] = rec[0];
-            s_b[t] = rec[1];
+            const float4 a = rec[0], b = rec[1];
+            s_a[t] = a;
+            s_b[t] = b;
             s_c[t] = rec[2].x;
+            s_box[t] = alpha_box(a, b);
         }
         __syncthreads();
         if (!done) {
             const uint32_t n = min((uint32_t)kForwardBatch, count - base);
             for (uint32_t k = 0; k < n; ++k) {
+                if (misses(s_box[k], wx0, wx1, wy0, wy1)) continue;
                 const float4 a = s_a[k];
                 const float4 b = s_b[k];
                 const float dx = a.x - fpx, dy = a.y - fpy;
@@ -87,6 +123,32 @@ __device__ __forceinline__ uint64_t slot_of(const float4* __restrict__ records, 
     return (uint64_t)offsets[g] + (uint64_t)(gy - y0) * (x1 - x0) + (gx - x0);
 }
 
+// Warp sums of 8 values with 9 shuffles instead of 40: at each of the first three levels
+// a lane keeps half of its values and trades the other half with its partner, so that
+// after them lane l holds a partial of value (l >> 2) & 7 only; two full levels finish.
+// Returns the warp total of value (lane >> 2) & 7.
+__device__ __forceinline__ float reduce8_transposed(const float v[8], uint32_t lane) {
+    const bool b4 = lane & 16u, b3 = lane & 8u, b2 = lane & 4u;
+    float x[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const float keep = b4 ? v[i + 4] : v[i];
+        const float send = b4 ? v[i] : v[i + 4];
+        x[i] = keep + __shfl_xor_sync(kFull, send, 16);
+    }
+    float y[2];
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+        const float keep = b3 ? x[i + 2] : x[i];
+        const float send = b3 ? x[i] : x[i + 2];
+        y[i] = keep + __shfl_xor_sync(kFull, send, 8);
+    }
+    float z = (b2 ? y[1] : y[0]) + __shfl_xor_sync(kFull, b2 ? y[0] : y[1], 4);
+    z += __shfl_xor_sync(kFull, z, 2);
+    z += __shfl_xor_sync(kFull, z, 1);
+    return z;
+}
+
 template <int MODE>
 __global__ void __launch_bounds__(kTilePixels) k_blend_backward(
     const float4* __restrict__ records, const uint32_t* __restrict__ sorted, const uint2* __restrict__ ranges,
@@ -94,9 +156,9 @@ __global__ void __launch_bounds__(kTilePixels) k_blend_backward(
     const uint32_t* __restrict__ contributions, const float4* __restrict__ loss_gradient,
     float* __restrict__ slot_gradients, float4* __restrict__ gaussian_gradients) {
     constexpr int B = kBackwardBatch;
-    constexpr int kWarps = kTilePixels / 32;
     __shared__ float4 s_a[B];
     __shared__ float4 s_b[B];
+    __shared__ float4 s_box[B];
     __shared__ float s_c[B];
     __shared__ uint32_t s_g[B];
     __shared__ float s_part[MODE == SP_BWD_DETERMINISTIC ? B : 1][kWarps][9];
@@ -105,7 +167,9 @@ __global__ void __launch_bounds__(kTilePixels) k_blend_backward(
     const uint32_t tile = blockIdx.x;
     const uint32_t gx = tile % cam.tiles_x, gy = tile / cam.tiles_x;
     const uint32_t t = threadIdx.x, lane = lane_id(), warp = t / 32;
-    const uint32_t px = gx * SP_TILE + (t % SP_TILE), py = gy * SP_TILE + (t / SP_TILE);
+    const uint32_t px = gx * SP_TILE + local_x(warp, lane), py = gy * SP_TILE + local_y(warp, lane);
+    const float wx0 = (float)(gx * SP_TILE + ((warp & 1u) << 3)), wx1 = wx0 + 7.0f;
+    const float wy0 = (float)(gy * SP_TILE + ((warp >> 1) << 2)), wy1 = wy0 + 3.0f;
     const bool inside = px < cam.width && py < cam.height;
     const float fpx = (float)px, fpy = (float)py;
     const uint2 range = ranges[tile];
@@ -120,11 +184,12 @@ __global__ void __launch_bounds__(kTilePixels) k_blend_backward(
         contributed = contributions[index];
         grad = loss_gradient[index];
     }
-    // No pixel of the tile replays past the largest contributor count.
+    // No pixel replays past its contributor count: the warp stops at its largest, the
+    // block at the largest of all.
     if (t == 0) s_limit = 0;
     __syncthreads();
-    const uint32_t warp_max = __reduce_max_sync(0xffffffffu, contributed);
-    if (lane == 0) atomicMax(&s_limit, warp_max);
+    const uint32_t warp_limit = __reduce_max_sync(kFull, contributed);
+    if (lane == 0) atomicMax(&s_limit, warp_limit);
     __syncthreads();
     const uint32_t limit = min(s_limit, count);
 
@@ -136,15 +201,21 @@ __global__ void __launch_bounds__(kTilePixels) k_blend_backward(
         if (t < (uint32_t)B && base + t < limit) {
             const uint32_t g = sorted[range.x + base + t];
             const float4* rec = records + (size_t)g * kRecord;
+            const float4 a = rec[0], b = rec[1];
             s_g[t] = g;
-            s_a[t] = rec[0];
-            s_b[t] = rec[1];
+            s_a[t] = a;
+            s_b[t] = b;
             s_c[t] = rec[2].x;
+            s_box[t] = alpha_box(a, b);
         }
         __syncthreads();
         const uint32_t n = min((uint32_t)B, limit - base);
         for (int kk = (int)n - 1; kk >= 0; --kk) {
             const uint32_t j = base + kk;
+            if (j >= warp_limit || misses(s_box[kk], wx0, wx1, wy0, wy1)) {
+                if (MODE == SP_BWD_DETERMINISTIC && lane < 9) s_part[kk][warp][lane] = 0.0f;
+                continue;
+            }
             float v[9];
 #pragma unroll
             for (int c = 0; c < 9; ++c) v[c] = 0.0f;
@@ -161,13 +232,13 @@ __global__ void __launch_bounds__(kTilePixels) k_blend_backward(
                     const float alpha = fminf(SP_MAX_ALPHA, alpha_unclamped);
                     if (alpha >= SP_MIN_ALPHA) {
                         active = true;
-                        const float one_minus = 1.0f - alpha;
-                        transmittance = transmittance / one_minus;
+                        const float inv = __fdividef(1.0f, 1.0f - alpha);
+                        transmittance = transmittance * inv;
                         const float cr = b.z, cgr = b.w, cbl = s_c[kk];
-                        const float d_alpha = grad.x * (cr * transmittance - behind_r / one_minus) +
-                                              grad.y * (cgr * transmittance - behind_g / one_minus) +
-                                              grad.z * (cbl * transmittance - behind_b / one_minus) +
-                                              grad.w * (0.0f * transmittance - behind_t / one_minus);
+                        const float d_alpha = grad.x * (cr * transmittance - behind_r * inv) +
+                                              grad.y * (cgr * transmittance - behind_g * inv) +
+                                              grad.z * (cbl * transmittance - behind_b * inv) -
+                                              grad.w * (behind_t * inv);
                         const float w = alpha * transmittance;
                         v[5] = grad.x * w;
                         v[6] = grad.y * w;
@@ -187,26 +258,20 @@ __global__ void __launch_bounds__(kTilePixels) k_blend_backward(
                     }
                 }
             }
-            if (__ballot_sync(0xffffffffu, active)) {
-#pragma unroll
-                for (int c = 0; c < 9; ++c) {
-#pragma unroll
-                    for (int o = 16; o > 0; o >>= 1) v[c] += __shfl_down_sync(0xffffffffu, v[c], o);
+            if (__ballot_sync(kFull, active)) {
+                const float total = reduce8_transposed(v, lane);
+                const float opacity_total = warp_sum(v[8]);
+                const uint32_t which = (lane >> 2) & 7u;
+                if (MODE == SP_BWD_ATOMIC) {
+                    float* out = reinterpret_cast<float*>(gaussian_gradients + (size_t)s_g[kk] * 3);
+                    if ((lane & 3u) == 0) atomicAdd(out + which, total);
+                    if (lane == 0) atomicAdd(out + 8, opacity_total);
+                } else {
+                    if ((lane & 3u) == 0) s_part[kk][warp][which] = total;
+                    if (lane == 0) s_part[kk][warp][8] = opacity_total;
                 }
-                if (lane == 0) {
-                    if (MODE == SP_BWD_ATOMIC) {
-                        float4* out = gaussian_gradients + (size_t)s_g[kk] * 3;
-                        atomicAdd(out + 0, make_float4(v[0], v[1], v[2], v[3]));
-                        atomicAdd(out + 1, make_float4(v[4], v[5], v[6], v[7]));
-                        atomicAdd(reinterpret_cast<float*>(out + 2), v[8]);
-                    } else {
-#pragma unroll
-                        for (int c = 0; c < 9; ++c) s_part[kk][warp][c] = v[c];
-                    }
-                }
-            } else if (MODE == SP_BWD_DETERMINISTIC && lane == 0) {
-#pragma unroll
-                for (int c = 0; c < 9; ++c) s_part[kk][warp][c] = 0.0f;
+            } else if (MODE == SP_BWD_DETERMINISTIC && lane < 9) {
+                s_part[kk][warp][lane] = 0.0f;
             }
         }
         if (MODE == SP_BWD_DETERMINISTIC) {
@@ -244,7 +309,7 @@ __global__ void __launch_bounds__(kTilePixels) k_count_blend(const float4* __res
     const uint32_t tile = blockIdx.x;
     const uint32_t gx = tile % cam.tiles_x, gy = tile / cam.tiles_x;
     const uint32_t t = threadIdx.x;
-    const uint32_t px = gx * SP_TILE + (t % SP_TILE), py = gy * SP_TILE + (t / SP_TILE);
+    const uint32_t px = gx * SP_TILE + local_x(t / 32, lane_id()), py = gy * SP_TILE + local_y(t / 32, lane_id());
     unsigned long long visited = 0, replayed = 0;
     if (px < cam.width && py < cam.height) {
         const uint2 range = ranges[tile];
@@ -265,8 +330,8 @@ __global__ void __launch_bounds__(kTilePixels) k_count_blend(const float4* __res
         }
         replayed = contributions[(size_t)py * cam.width + px];
     }
-    visited = __reduce_add_sync(0xffffffffu, (unsigned)visited);
-    replayed = __reduce_add_sync(0xffffffffu, (unsigned)replayed);
+    visited = __reduce_add_sync(kFull, (unsigned)visited);
+    replayed = __reduce_add_sync(kFull, (unsigned)replayed);
     if (lane_id() == 0) {
         atomicAdd(counts, visited);
         atomicAdd(counts + 1, replayed);
