@@ -51,6 +51,7 @@ def parse_args():
     p.add_argument("--warmup", type=int, default=10)
     p.add_argument("--impl", choices=["b200", "reference"], default="b200")
     p.add_argument("--scale", type=float, default=1.0, help="Gaussian count scale (1.0 = the benchmark)")
+    p.add_argument("--views", type=int, default=None, help="use only the first V views (small profiling cases)")
     p.add_argument("--e2e-steps", type=int, default=300)
     p.add_argument("--cpu-seconds", type=float, default=20.0, help="CPU-baseline sample budget")
     p.add_argument("--reference-seconds", type=float, default=150.0, help="--impl reference time budget")
@@ -280,6 +281,8 @@ def main() -> None:
         dist.init_process_group("nccl", timeout=timedelta(seconds=180), device_id=torch.device("cuda", local))
 
     scene = scenes.config(CONFIG_INDEX, scale=args.scale)
+    if args.views:
+        scene.cameras = scene.cameras[: args.views]
     cloud, cams = scene.cloud, scene.cameras
     deg = cloud.sh_degree
     views = len(cams)
