@@ -2,12 +2,13 @@
 // rasterize_backward.wgsl:30-133). One block of 256 threads per 16 x 16 tile, one pixel per
 // thread; each warp owns an 8 x 4 block of the tile. The tile's Gaussians are gathered
 // (sorted list -> Gaussian -> 48-B record, an L2-resident array) into shared memory a batch
-// at a time and read back as broadcasts.
+// at a time, one Gaussian per thread, and read back as broadcasts.
 //
-// With each record the batch loader stores the pixel rectangle outside of which the
-// Gaussian's alpha is below 1/255 (the exact per-pixel test rejects it there), padded; a
-// warp whose 8 x 4 pixels miss that rectangle skips the Gaussian as a whole. This changes
-// no result: only pairs the exact test would reject are skipped.
+// With each record the loading thread works out which of the tile's eight 8 x 4 warp blocks
+// the Gaussian can reach: the pixel rectangle outside of which its alpha is below 1/255
+// (where the exact per-pixel test rejects it), padded. Each warp then compacts the batch
+// into its own list of the Gaussians that reach it and walks only that list. This changes
+// no result: only pairs the exact test would reject are left out.
 //
 // The arithmetic per (pixel, Gaussian) is the reference's. exp is the hardware
 // approximation (__expf), and the backward divides by (1 - alpha) through one reciprocal,
@@ -17,8 +18,8 @@
 namespace splat {
 namespace {
 
-constexpr int kForwardBatch = 256;
-constexpr int kBackwardBatch = 32;
+constexpr int kBatch = 256;                  // records per batch (forward, backward atomic mode)
+constexpr int kDeterministicBatch = 32;      // backward deterministic mode (per-warp partials)
 constexpr int kWarps = kTilePixels / 32;
 constexpr uint32_t kFull = 0xffffffffu;
 
@@ -26,22 +27,52 @@ constexpr uint32_t kFull = 0xffffffffu;
 __device__ __forceinline__ uint32_t local_x(uint32_t warp, uint32_t lane) { return ((warp & 1u) << 3) | (lane & 7u); }
 __device__ __forceinline__ uint32_t local_y(uint32_t warp, uint32_t lane) { return ((warp >> 1) << 2) | (lane >> 3); }
 
-// {xmin, xmax, ymin, ymax}: where op * exp(power) >= 1/255 can hold, i.e. the ellipse
-// d^T C d <= 2 ln(255 op) of the conic C, padded by 1 % in the level and 0.05 px.
-__device__ __forceinline__ float4 alpha_box(float4 a, float4 b) {
+// The warp blocks of tile (gx, gy) that a Gaussian can reach, one bit per warp: where
+// op * exp(power) >= 1/255 can hold, i.e. inside the ellipse d^T C d <= 2 ln(255 op) of the
+// conic C, whose bounding rectangle is padded by 1 % in the level and 0.05 px.
+__device__ __forceinline__ uint32_t warp_mask(float4 a, float4 b, uint32_t gx, uint32_t gy) {
     const float level = b.y * 255.0f;
-    if (!(level > 1.0f)) return make_float4(INFINITY, -INFINITY, INFINITY, -INFINITY);
-    const float q = 2.02f * __logf(level) + 0.02f;
+    if (!(level > 1.0f)) return 0u;
     const float det = a.z * b.x - a.w * a.w;
-    if (!(det > 0.0f) || !(a.z > 0.0f) || !(b.x > 0.0f))
-        return make_float4(-INFINITY, INFINITY, -INFINITY, INFINITY);
+    if (!(det > 0.0f) || !(a.z > 0.0f) || !(b.x > 0.0f)) return 0xffu;
+    const float q = 2.02f * __logf(level) + 0.02f;
     const float ex = sqrtf(q * b.x / det) + 0.05f;
     const float ey = sqrtf(q * a.z / det) + 0.05f;
-    return make_float4(a.x - ex, a.x + ex, a.y - ey, a.y + ey);
+    const float x0 = (float)(gx * SP_TILE), y0 = (float)(gy * SP_TILE);
+    uint32_t cols = 0, rows = 0;
+#pragma unroll
+    for (int c = 0; c < 2; ++c) {
+        const float lo = x0 + 8.0f * c;
+        if (a.x + ex >= lo && a.x - ex <= lo + 7.0f) cols |= 1u << c;
+    }
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+        const float lo = y0 + 4.0f * r;
+        if (a.y + ey >= lo && a.y - ey <= lo + 3.0f) rows |= 1u << r;
+    }
+    uint32_t mask = 0;
+#pragma unroll
+    for (int r = 0; r < 4; ++r)
+        if (rows & (1u << r)) mask |= cols << (2 * r);
+    return mask;
 }
 
-__device__ __forceinline__ bool misses(float4 box, float x0, float x1, float y0, float y1) {
-    return box.y < x0 || box.x > x1 || box.w < y0 || box.z > y1;
+// This warp's list of batch entries k < n whose mask has its bit (and that pass `keep`),
+// in increasing k, written to `list`; returns its length.
+template <int B, typename Keep>
+__device__ __forceinline__ uint32_t compact(const uint8_t* masks, uint32_t n, uint32_t warp, uint32_t lane,
+                                            uint16_t* list, Keep keep) {
+    uint32_t length = 0;
+#pragma unroll
+    for (int chunk = 0; chunk < B / 32; ++chunk) {
+        const uint32_t k = chunk * 32 + lane;
+        const bool take = k < n && ((masks[k] >> warp) & 1u) && keep(k);
+        const uint32_t ballot = __ballot_sync(kFull, take);
+        if (take) list[length + __popc(ballot & ((1u << lane) - 1u))] = (uint16_t)k;
+        length += __popc(ballot);
+    }
+    __syncwarp();
+    return length;
 }
 
 __global__ void __launch_bounds__(kTilePixels) k_blend_forward(const float4* __restrict__ records,
@@ -49,25 +80,25 @@ __global__ void __launch_bounds__(kTilePixels) k_blend_forward(const float4* __r
                                                                const uint2* __restrict__ ranges,
                                                                const sp_camera_uniform cam, float4* __restrict__ image,
                                                                uint32_t* __restrict__ contributions) {
-    __shared__ float4 s_a[kForwardBatch];    // mean.x, mean.y, conic.a, conic.b
-    __shared__ float4 s_b[kForwardBatch];    // conic.c, opacity, colour.r, colour.g
-    __shared__ float4 s_box[kForwardBatch];  // alpha_box
-    __shared__ float s_c[kForwardBatch];     // colour.b
+    __shared__ float4 s_a[kBatch];  // mean.x, mean.y, conic.a, conic.b
+    __shared__ float4 s_b[kBatch];  // conic.c, opacity, colour.r, colour.g
+    __shared__ float s_c[kBatch];   // colour.b
+    __shared__ uint8_t s_mask[kBatch];
+    __shared__ uint16_t s_list[kWarps][kBatch];
     const uint32_t tile = blockIdx.x;
     const uint32_t gx = tile % cam.tiles_x, gy = tile / cam.tiles_x;
     const uint32_t t = threadIdx.x, warp = t / 32, lane = lane_id();
     const uint32_t px = gx * SP_TILE + local_x(warp, lane), py = gy * SP_TILE + local_y(warp, lane);
-    const float wx0 = (float)(gx * SP_TILE + ((warp & 1u) << 3)), wx1 = wx0 + 7.0f;
-    const float wy0 = (float)(gy * SP_TILE + ((warp >> 1) << 2)), wy1 = wy0 + 3.0f;
     const bool inside = px < cam.width && py < cam.height;
     const float fpx = (float)px, fpy = (float)py;
     const uint2 range = ranges[tile];
     const uint32_t count = range.y - range.x;
+    uint16_t* list = s_list[warp];
 
     float transmittance = 1.0f, cr = 0.0f, cg = 0.0f, cb = 0.0f;
     uint32_t contributed = 0;
     bool done = !inside;
-    for (uint32_t base = 0; base < count; base += kForwardBatch) {
+    for (uint32_t base = 0; base < count; base += kBatch) {
         // Also the barrier before the batch buffers are overwritten.
         if (__syncthreads_count(!done) == 0) break;
         const uint32_t j = base + t;
@@ -77,32 +108,32 @@ __global__ void __launch_bounds__(kTilePixels) k_blend_forward(const float4* __r
             s_a[t] = a;
             s_b[t] = b;
             s_c[t] = rec[2].x;
-            s_box[t] = alpha_box(a, b);
+            s_mask[t] = (uint8_t)warp_mask(a, b, gx, gy);
         }
         __syncthreads();
-        if (!done) {
-            const uint32_t n = min((uint32_t)kForwardBatch, count - base);
-            for (uint32_t k = 0; k < n; ++k) {
-                if (misses(s_box[k], wx0, wx1, wy0, wy1)) continue;
-                const float4 a = s_a[k];
-                const float4 b = s_b[k];
-                const float dx = a.x - fpx, dy = a.y - fpy;
-                const float power = -0.5f * (a.z * dx * dx + b.x * dy * dy) - a.w * dx * dy;
-                if (power > 0.0f) continue;
-                const float alpha = fminf(SP_MAX_ALPHA, b.y * __expf(power));
-                if (alpha < SP_MIN_ALPHA) continue;
-                const float next = transmittance * (1.0f - alpha);
-                if (next < SP_MIN_TRANSMITTANCE) {
-                    done = true;
-                    break;
-                }
-                const float w = alpha * transmittance;
-                cr += b.z * w;
-                cg += b.w * w;
-                cb += s_c[k] * w;
-                transmittance = next;
-                contributed = base + k + 1;
+        const uint32_t n = min((uint32_t)kBatch, count - base);
+        const uint32_t length = compact<kBatch>(s_mask, n, warp, lane, list, [](uint32_t) { return true; });
+        if (done) continue;
+        for (uint32_t i = 0; i < length; ++i) {
+            const uint32_t k = list[i];
+            const float4 a = s_a[k];
+            const float4 b = s_b[k];
+            const float dx = a.x - fpx, dy = a.y - fpy;
+            const float power = -0.5f * (a.z * dx * dx + b.x * dy * dy) - a.w * dx * dy;
+            if (power > 0.0f) continue;
+            const float alpha = fminf(SP_MAX_ALPHA, b.y * __expf(power));
+            if (alpha < SP_MIN_ALPHA) continue;
+            const float next = transmittance * (1.0f - alpha);
+            if (next < SP_MIN_TRANSMITTANCE) {
+                done = true;
+                break;
             }
+            const float w = alpha * transmittance;
+            cr += b.z * w;
+            cg += b.w * w;
+            cb += s_c[k] * w;
+            transmittance = next;
+            contributed = base + k + 1;
         }
     }
     if (inside) {
@@ -155,25 +186,26 @@ __global__ void __launch_bounds__(kTilePixels) k_blend_backward(
     const uint32_t* __restrict__ offsets, const sp_camera_uniform cam, const float4* __restrict__ image,
     const uint32_t* __restrict__ contributions, const float4* __restrict__ loss_gradient,
     float* __restrict__ slot_gradients, float4* __restrict__ gaussian_gradients) {
-    constexpr int B = kBackwardBatch;
+    constexpr bool kDet = MODE == SP_BWD_DETERMINISTIC;
+    constexpr int B = kDet ? kDeterministicBatch : kBatch;
     __shared__ float4 s_a[B];
     __shared__ float4 s_b[B];
-    __shared__ float4 s_box[B];
     __shared__ float s_c[B];
     __shared__ uint32_t s_g[B];
-    __shared__ float s_part[MODE == SP_BWD_DETERMINISTIC ? B : 1][kWarps][9];
+    __shared__ uint8_t s_mask[B];
+    __shared__ uint16_t s_list[kWarps][B];
+    __shared__ float s_part[kDet ? B : 1][kWarps][9];
     __shared__ uint32_t s_limit;
 
     const uint32_t tile = blockIdx.x;
     const uint32_t gx = tile % cam.tiles_x, gy = tile / cam.tiles_x;
     const uint32_t t = threadIdx.x, lane = lane_id(), warp = t / 32;
     const uint32_t px = gx * SP_TILE + local_x(warp, lane), py = gy * SP_TILE + local_y(warp, lane);
-    const float wx0 = (float)(gx * SP_TILE + ((warp & 1u) << 3)), wx1 = wx0 + 7.0f;
-    const float wy0 = (float)(gy * SP_TILE + ((warp >> 1) << 2)), wy1 = wy0 + 3.0f;
     const bool inside = px < cam.width && py < cam.height;
     const float fpx = (float)px, fpy = (float)py;
     const uint2 range = ranges[tile];
     const uint32_t count = range.y - range.x;
+    uint16_t* list = s_list[warp];
 
     float transmittance = 0.0f;
     uint32_t contributed = 0;
@@ -184,8 +216,8 @@ __global__ void __launch_bounds__(kTilePixels) k_blend_backward(
         contributed = contributions[index];
         grad = loss_gradient[index];
     }
-    // No pixel replays past its contributor count: the warp stops at its largest, the
-    // block at the largest of all.
+    // No pixel replays past its contributor count: the warp's list stops at its largest,
+    // the block's batches at the largest of all.
     if (t == 0) s_limit = 0;
     __syncthreads();
     const uint32_t warp_limit = __reduce_max_sync(kFull, contributed);
@@ -206,23 +238,24 @@ __global__ void __launch_bounds__(kTilePixels) k_blend_backward(
             s_a[t] = a;
             s_b[t] = b;
             s_c[t] = rec[2].x;
-            s_box[t] = alpha_box(a, b);
+            s_mask[t] = (uint8_t)warp_mask(a, b, gx, gy);
         }
+        if (kDet)
+            for (uint32_t i = lane; i < (uint32_t)B * 9; i += 32) s_part[i / 9][warp][i % 9] = 0.0f;
         __syncthreads();
         const uint32_t n = min((uint32_t)B, limit - base);
-        for (int kk = (int)n - 1; kk >= 0; --kk) {
-            const uint32_t j = base + kk;
-            if (j >= warp_limit || misses(s_box[kk], wx0, wx1, wy0, wy1)) {
-                if (MODE == SP_BWD_DETERMINISTIC && lane < 9) s_part[kk][warp][lane] = 0.0f;
-                continue;
-            }
+        const uint32_t length =
+            compact<B>(s_mask, n, warp, lane, list, [&](uint32_t k) { return base + k < warp_limit; });
+        for (int i = (int)length - 1; i >= 0; --i) {
+            const uint32_t k = list[i];
+            const uint32_t j = base + k;
             float v[9];
 #pragma unroll
             for (int c = 0; c < 9; ++c) v[c] = 0.0f;
             bool active = false;
             if (j < contributed) {
-                const float4 a = s_a[kk];
-                const float4 b = s_b[kk];
+                const float4 a = s_a[k];
+                const float4 b = s_b[k];
                 const float dx = a.x - fpx, dy = a.y - fpy;
                 const float power = -0.5f * (a.z * dx * dx + b.x * dy * dy) - a.w * dx * dy;
                 if (power <= 0.0f) {
@@ -234,7 +267,7 @@ __global__ void __launch_bounds__(kTilePixels) k_blend_backward(
                         active = true;
                         const float inv = __fdividef(1.0f, 1.0f - alpha);
                         transmittance = transmittance * inv;
-                        const float cr = b.z, cgr = b.w, cbl = s_c[kk];
+                        const float cr = b.z, cgr = b.w, cbl = s_c[k];
                         const float d_alpha = grad.x * (cr * transmittance - behind_r * inv) +
                                               grad.y * (cgr * transmittance - behind_g * inv) +
                                               grad.z * (cbl * transmittance - behind_b * inv) -
@@ -262,32 +295,30 @@ __global__ void __launch_bounds__(kTilePixels) k_blend_backward(
                 const float total = reduce8_transposed(v, lane);
                 const float opacity_total = warp_sum(v[8]);
                 const uint32_t which = (lane >> 2) & 7u;
-                if (MODE == SP_BWD_ATOMIC) {
-                    float* out = reinterpret_cast<float*>(gaussian_gradients + (size_t)s_g[kk] * 3);
+                if (!kDet) {
+                    float* out = reinterpret_cast<float*>(gaussian_gradients + (size_t)s_g[k] * 3);
                     if ((lane & 3u) == 0) atomicAdd(out + which, total);
                     if (lane == 0) atomicAdd(out + 8, opacity_total);
                 } else {
-                    if ((lane & 3u) == 0) s_part[kk][warp][which] = total;
-                    if (lane == 0) s_part[kk][warp][8] = opacity_total;
+                    if ((lane & 3u) == 0) s_part[k][warp][which] = total;
+                    if (lane == 0) s_part[k][warp][8] = opacity_total;
                 }
-            } else if (MODE == SP_BWD_DETERMINISTIC && lane < 9) {
-                s_part[kk][warp][lane] = 0.0f;
             }
         }
-        if (MODE == SP_BWD_DETERMINISTIC) {
+        if (kDet) {
             // One write per (Gaussian, tile) slot: the warps' sums in warp order.
             __syncthreads();
             for (uint32_t i = t; i < n * SP_GRAD_STRIDE; i += kTilePixels) {
-                const uint32_t kk = i / SP_GRAD_STRIDE, c = i % SP_GRAD_STRIDE;
+                const uint32_t k = i / SP_GRAD_STRIDE, c = i % SP_GRAD_STRIDE;
                 float s = 0.0f;
                 if (c < 9)
 #pragma unroll
-                    for (int w = 0; w < kWarps; ++w) s += s_part[kk][w][c];
-                slot_gradients[slot_of(records, offsets, s_g[kk], gx, gy) * SP_GRAD_STRIDE + c] = s;
+                    for (int w = 0; w < kWarps; ++w) s += s_part[k][w][c];
+                slot_gradients[slot_of(records, offsets, s_g[k], gx, gy) * SP_GRAD_STRIDE + c] = s;
             }
         }
     }
-    if (MODE == SP_BWD_DETERMINISTIC) {
+    if (kDet) {
         // Entries past every pixel's last contributor get zero slots, as the reference
         // writes every entry of the tile.
         for (uint32_t i = t; i < (count - limit) * SP_GRAD_STRIDE; i += kTilePixels) {
