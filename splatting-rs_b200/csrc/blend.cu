@@ -27,9 +27,31 @@ constexpr uint32_t kFull = 0xffffffffu;
 __device__ __forceinline__ uint32_t local_x(uint32_t warp, uint32_t lane) { return ((warp & 1u) << 3) | (lane & 7u); }
 __device__ __forceinline__ uint32_t local_y(uint32_t warp, uint32_t lane) { return ((warp >> 1) << 2) | (lane >> 3); }
 
+// Whether the ellipse a x^2 + 2 b x y + c y^2 <= q (a, c > 0, ac > b^2) meets the rectangle
+// [x0, x1] x [y0, y1] (coordinates relative to its centre): the minimum of the convex form
+// over the rectangle is 0 if the centre is inside, else on an edge, where it is a clamped
+// 1-D quadratic.
+__device__ __forceinline__ bool ellipse_meets_rect(float a, float b, float c, float q, float x0, float x1, float y0,
+                                                   float y1) {
+    if (x0 <= 0.0f && x1 >= 0.0f && y0 <= 0.0f && y1 >= 0.0f) return true;
+    float best = INFINITY;
+    const float xs[2] = {x0, x1}, ys[2] = {y0, y1};
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+        const float x = xs[e];
+        const float y = fminf(fmaxf(-b * x / c, y0), y1);
+        best = fminf(best, a * x * x + 2.0f * b * x * y + c * y * y);
+        const float yy = ys[e];
+        const float xx = fminf(fmaxf(-b * yy / a, x0), x1);
+        best = fminf(best, a * xx * xx + 2.0f * b * xx * yy + c * yy * yy);
+    }
+    return best <= q;
+}
+
 // The warp blocks of tile (gx, gy) that a Gaussian can reach, one bit per warp: where
 // op * exp(power) >= 1/255 can hold, i.e. inside the ellipse d^T C d <= 2 ln(255 op) of the
-// conic C, whose bounding rectangle is padded by 1 % in the level and 0.05 px.
+// conic C, padded by 1 % in the level; each block's rectangle of pixel centres is padded
+// by 0.05 px. A bounding-box test first, then the exact ellipse test.
 __device__ __forceinline__ uint32_t warp_mask(float4 a, float4 b, uint32_t gx, uint32_t gy) {
     const float level = b.y * 255.0f;
     if (!(level > 1.0f)) return 0u;
@@ -38,22 +60,19 @@ __device__ __forceinline__ uint32_t warp_mask(float4 a, float4 b, uint32_t gx, u
     const float q = 2.02f * __logf(level) + 0.02f;
     const float ex = sqrtf(q * b.x / det) + 0.05f;
     const float ey = sqrtf(q * a.z / det) + 0.05f;
-    const float x0 = (float)(gx * SP_TILE), y0 = (float)(gy * SP_TILE);
-    uint32_t cols = 0, rows = 0;
-#pragma unroll
-    for (int c = 0; c < 2; ++c) {
-        const float lo = x0 + 8.0f * c;
-        if (a.x + ex >= lo && a.x - ex <= lo + 7.0f) cols |= 1u << c;
-    }
-#pragma unroll
-    for (int r = 0; r < 4; ++r) {
-        const float lo = y0 + 4.0f * r;
-        if (a.y + ey >= lo && a.y - ey <= lo + 3.0f) rows |= 1u << r;
-    }
+    const float x0 = (float)(gx * SP_TILE) - a.x, y0 = (float)(gy * SP_TILE) - a.y;
     uint32_t mask = 0;
 #pragma unroll
-    for (int r = 0; r < 4; ++r)
-        if (rows & (1u << r)) mask |= cols << (2 * r);
+    for (int r = 0; r < 4; ++r) {
+        const float lo_y = y0 + 4.0f * r - 0.05f, hi_y = lo_y + 3.1f;
+        if (ey < lo_y || -ey > hi_y) continue;
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
+            const float lo_x = x0 + 8.0f * c - 0.05f, hi_x = lo_x + 7.1f;
+            if (ex < lo_x || -ex > hi_x) continue;
+            if (ellipse_meets_rect(a.z, a.w, b.x, q, lo_x, hi_x, lo_y, hi_y)) mask |= 1u << (2 * r + c);
+        }
+    }
     return mask;
 }
 
@@ -75,7 +94,7 @@ __device__ __forceinline__ uint32_t compact(const uint8_t* masks, uint32_t n, ui
     return length;
 }
 
-__global__ void __launch_bounds__(kTilePixels) k_blend_forward(const float4* __restrict__ records,
+__global__ void __launch_bounds__(kTilePixels, 5) k_blend_forward(const float4* __restrict__ records,
                                                                const uint32_t* __restrict__ sorted,
                                                                const uint2* __restrict__ ranges,
                                                                const sp_camera_uniform cam, float4* __restrict__ image,
@@ -114,26 +133,40 @@ __global__ void __launch_bounds__(kTilePixels) k_blend_forward(const float4* __r
         const uint32_t n = min((uint32_t)kBatch, count - base);
         const uint32_t length = compact<kBatch>(s_mask, n, warp, lane, list, [](uint32_t) { return true; });
         if (done) continue;
-        for (uint32_t i = 0; i < length; ++i) {
-            const uint32_t k = list[i];
-            const float4 a = s_a[k];
-            const float4 b = s_b[k];
+        // rasterize_forward.wgsl:58-77. Two Gaussians per iteration: their alphas are
+        // independent, only the compositing is sequential.
+        auto alpha_at = [&](float4 a, float4 b) {
             const float dx = a.x - fpx, dy = a.y - fpy;
             const float power = -0.5f * (a.z * dx * dx + b.x * dy * dy) - a.w * dx * dy;
-            if (power > 0.0f) continue;
-            const float alpha = fminf(SP_MAX_ALPHA, b.y * __expf(power));
-            if (alpha < SP_MIN_ALPHA) continue;
+            return power > 0.0f ? 0.0f : fminf(SP_MAX_ALPHA, b.y * __expf(power));
+        };
+        // Returns false when the pixel ends here.
+        auto composite = [&](float alpha, float4 b, uint32_t k) {
+            if (alpha < SP_MIN_ALPHA) return true;
             const float next = transmittance * (1.0f - alpha);
-            if (next < SP_MIN_TRANSMITTANCE) {
-                done = true;
-                break;
-            }
+            if (next < SP_MIN_TRANSMITTANCE) return false;
             const float w = alpha * transmittance;
             cr += b.z * w;
             cg += b.w * w;
             cb += s_c[k] * w;
             transmittance = next;
             contributed = base + k + 1;
+            return true;
+        };
+        uint32_t i = 0;
+        for (; i + 1 < length; i += 2) {
+            const uint32_t k0 = list[i], k1 = list[i + 1];
+            const float4 a0 = s_a[k0], b0 = s_b[k0], a1 = s_a[k1], b1 = s_b[k1];
+            const float alpha0 = alpha_at(a0, b0), alpha1 = alpha_at(a1, b1);
+            if (!composite(alpha0, b0, k0) || !composite(alpha1, b1, k1)) {
+                done = true;
+                break;
+            }
+        }
+        if (!done && i < length) {
+            const uint32_t k = list[i];
+            const float4 b = s_b[k];
+            if (!composite(alpha_at(s_a[k], b), b, k)) done = true;
         }
     }
     if (inside) {
