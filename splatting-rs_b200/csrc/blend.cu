@@ -94,80 +94,128 @@ __device__ __forceinline__ uint32_t compact(const uint8_t* masks, uint32_t n, ui
     return length;
 }
 
+// Whether a Gaussian can reach the rectangle of pixel centres [x0, x0 + 7] x [y0, y0 + 3]:
+// op * exp(power) >= 1/255 somewhere in it, i.e. the ellipse d^T C d <= 2 ln(255 op) of the
+// conic C (padded by 1 % in the level) meets the rectangle (padded by 0.05 px). A
+// bounding-box test first, then the exact one.
+__device__ __forceinline__ bool reaches(float4 a, float4 b, float x0, float y0) {
+    const float level = b.y * 255.0f;
+    if (!(level > 1.0f)) return false;
+    const float det = a.z * b.x - a.w * a.w;
+    if (!(det > 0.0f) || !(a.z > 0.0f) || !(b.x > 0.0f)) return true;
+    const float q = 2.02f * __logf(level) + 0.02f;
+    const float lo_x = x0 - a.x - 0.05f, hi_x = lo_x + 7.1f;
+    const float lo_y = y0 - a.y - 0.05f, hi_y = lo_y + 3.1f;
+    const float ex = sqrtf(q * b.x / det) + 0.05f;
+    const float ey = sqrtf(q * a.z / det) + 0.05f;
+    if (ex < lo_x || -ex > hi_x || ey < lo_y || -ey > hi_y) return false;
+    return ellipse_meets_rect(a.z, a.w, b.x, q, lo_x, hi_x, lo_y, hi_y);
+}
+
+// One warp's staging area: the records of a 32-entry chunk of the tile list that reach the
+// warp's 8 x 4 pixels, compacted in list order.
+struct WarpStage {
+    float4 a[32];     // mean.x, mean.y, conic.a, conic.b
+    float4 b[32];     // conic.c, opacity, colour.r, colour.g
+    float c[32];      // colour.b
+    uint32_t j[32];   // index in the tile list
+    uint32_t g[32];   // Gaussian
+};
+
+// Loads entries base .. base + 31 (below `end`) of the tile list, one per lane, keeps those
+// that reach the warp's pixels, compacted into `st`; returns how many.
+__device__ __forceinline__ uint32_t stage_chunk(const float4* __restrict__ records, const uint32_t* __restrict__ sorted,
+                                                uint32_t first, uint32_t base, uint32_t end, float x0, float y0,
+                                                uint32_t lane, WarpStage& st) {
+    const uint32_t j = base + lane;
+    bool take = false;
+    float4 a, b;
+    float c = 0.0f;
+    uint32_t g = 0;
+    if (j < end) {
+        g = sorted[first + j];
+        const float4* rec = records + (size_t)g * kRecord;
+        a = rec[0];
+        b = rec[1];
+        c = rec[2].x;
+        take = reaches(a, b, x0, y0);
+    }
+    const uint32_t ballot = __ballot_sync(kFull, take);
+    if (take) {
+        const uint32_t p = __popc(ballot & ((1u << lane) - 1u));
+        st.a[p] = a;
+        st.b[p] = b;
+        st.c[p] = c;
+        st.j[p] = j;
+        st.g[p] = g;
+    }
+    __syncwarp();
+    return __popc(ballot);
+}
+
+// Each warp walks the tile's list on its own, 32 entries at a time, over only the
+// Gaussians that reach its 8 x 4 pixels; no block barrier, and a warp whose pixels are all
+// done leaves.
 __global__ void __launch_bounds__(kTilePixels, 5) k_blend_forward(const float4* __restrict__ records,
-                                                               const uint32_t* __restrict__ sorted,
-                                                               const uint2* __restrict__ ranges,
-                                                               const sp_camera_uniform cam, float4* __restrict__ image,
-                                                               uint32_t* __restrict__ contributions) {
-    __shared__ float4 s_a[kBatch];  // mean.x, mean.y, conic.a, conic.b
-    __shared__ float4 s_b[kBatch];  // conic.c, opacity, colour.r, colour.g
-    __shared__ float s_c[kBatch];   // colour.b
-    __shared__ uint8_t s_mask[kBatch];
-    __shared__ uint16_t s_list[kWarps][kBatch];
+                                                                  const uint32_t* __restrict__ sorted,
+                                                                  const uint2* __restrict__ ranges,
+                                                                  const sp_camera_uniform cam,
+                                                                  float4* __restrict__ image,
+                                                                  uint32_t* __restrict__ contributions) {
+    __shared__ WarpStage s_stage[kWarps];
     const uint32_t tile = blockIdx.x;
     const uint32_t gx = tile % cam.tiles_x, gy = tile / cam.tiles_x;
     const uint32_t t = threadIdx.x, warp = t / 32, lane = lane_id();
     const uint32_t px = gx * SP_TILE + local_x(warp, lane), py = gy * SP_TILE + local_y(warp, lane);
+    const float x0 = (float)(gx * SP_TILE + ((warp & 1u) << 3)), y0 = (float)(gy * SP_TILE + ((warp >> 1) << 2));
     const bool inside = px < cam.width && py < cam.height;
     const float fpx = (float)px, fpy = (float)py;
     const uint2 range = ranges[tile];
     const uint32_t count = range.y - range.x;
-    uint16_t* list = s_list[warp];
+    WarpStage& st = s_stage[warp];
 
     float transmittance = 1.0f, cr = 0.0f, cg = 0.0f, cb = 0.0f;
     uint32_t contributed = 0;
     bool done = !inside;
-    for (uint32_t base = 0; base < count; base += kBatch) {
-        // Also the barrier before the batch buffers are overwritten.
-        if (__syncthreads_count(!done) == 0) break;
-        const uint32_t j = base + t;
-        if (j < count) {
-            const float4* rec = records + (size_t)sorted[range.x + j] * kRecord;
-            const float4 a = rec[0], b = rec[1];
-            s_a[t] = a;
-            s_b[t] = b;
-            s_c[t] = rec[2].x;
-            s_mask[t] = (uint8_t)warp_mask(a, b, gx, gy);
-        }
-        __syncthreads();
-        const uint32_t n = min((uint32_t)kBatch, count - base);
-        const uint32_t length = compact<kBatch>(s_mask, n, warp, lane, list, [](uint32_t) { return true; });
-        if (done) continue;
-        // rasterize_forward.wgsl:58-77. Two Gaussians per iteration: their alphas are
-        // independent, only the compositing is sequential.
-        auto alpha_at = [&](float4 a, float4 b) {
-            const float dx = a.x - fpx, dy = a.y - fpy;
-            const float power = -0.5f * (a.z * dx * dx + b.x * dy * dy) - a.w * dx * dy;
-            return power > 0.0f ? 0.0f : fminf(SP_MAX_ALPHA, b.y * __expf(power));
-        };
-        // Returns false when the pixel ends here.
-        auto composite = [&](float alpha, float4 b, uint32_t k) {
-            if (alpha < SP_MIN_ALPHA) return true;
-            const float next = transmittance * (1.0f - alpha);
-            if (next < SP_MIN_TRANSMITTANCE) return false;
-            const float w = alpha * transmittance;
-            cr += b.z * w;
-            cg += b.w * w;
-            cb += s_c[k] * w;
-            transmittance = next;
-            contributed = base + k + 1;
-            return true;
-        };
-        uint32_t i = 0;
-        for (; i + 1 < length; i += 2) {
-            const uint32_t k0 = list[i], k1 = list[i + 1];
-            const float4 a0 = s_a[k0], b0 = s_b[k0], a1 = s_a[k1], b1 = s_b[k1];
-            const float alpha0 = alpha_at(a0, b0), alpha1 = alpha_at(a1, b1);
-            if (!composite(alpha0, b0, k0) || !composite(alpha1, b1, k1)) {
-                done = true;
-                break;
+    // rasterize_forward.wgsl:58-77, two Gaussians per iteration: their alphas are
+    // independent, only the compositing is sequential.
+    auto alpha_at = [&](float4 a, float4 b) {
+        const float dx = a.x - fpx, dy = a.y - fpy;
+        const float power = -0.5f * (a.z * dx * dx + b.x * dy * dy) - a.w * dx * dy;
+        return power > 0.0f ? 0.0f : fminf(SP_MAX_ALPHA, b.y * __expf(power));
+    };
+    // Returns false when the pixel ends here.
+    auto composite = [&](float alpha, float4 b, float c, uint32_t j) {
+        if (alpha < SP_MIN_ALPHA) return true;
+        const float next = transmittance * (1.0f - alpha);
+        if (next < SP_MIN_TRANSMITTANCE) return false;
+        const float w = alpha * transmittance;
+        cr += b.z * w;
+        cg += b.w * w;
+        cb += c * w;
+        transmittance = next;
+        contributed = j + 1;
+        return true;
+    };
+    for (uint32_t base = 0; base < count; base += 32) {
+        if (__all_sync(kFull, done)) break;
+        const uint32_t n = stage_chunk(records, sorted, range.x, base, count, x0, y0, lane, st);
+        if (!done) {
+            uint32_t i = 0;
+            for (; i + 1 < n; i += 2) {
+                const float4 a0 = st.a[i], b0 = st.b[i], a1 = st.a[i + 1], b1 = st.b[i + 1];
+                const float alpha0 = alpha_at(a0, b0), alpha1 = alpha_at(a1, b1);
+                if (!composite(alpha0, b0, st.c[i], st.j[i]) || !composite(alpha1, b1, st.c[i + 1], st.j[i + 1])) {
+                    done = true;
+                    break;
+                }
+            }
+            if (!done && i < n) {
+                const float4 b = st.b[i];
+                if (!composite(alpha_at(st.a[i], b), b, st.c[i], st.j[i])) done = true;
             }
         }
-        if (!done && i < length) {
-            const uint32_t k = list[i];
-            const float4 b = s_b[k];
-            if (!composite(alpha_at(s_a[k], b), b, k)) done = true;
-        }
+        __syncwarp();
     }
     if (inside) {
         const size_t index = (size_t)py * cam.width + px;
@@ -362,6 +410,95 @@ __global__ void __launch_bounds__(kTilePixels) k_blend_backward(
     }
 }
 
+// The backward with per-Gaussian sums by float atomics (SP_BWD_ATOMIC): each
+// warp walks the tile's list on its own, back to front from its pixels' largest contributor
+// count, 32 entries at a time, over only the Gaussians that reach its 8 x 4 pixels. Per
+// (Gaussian, warp) the 9 gradient terms are summed over the lanes (reduce8_transposed plus
+// one butterfly) and added into the Gaussian's sums by up to 9 lanes at once.
+__global__ void __launch_bounds__(kTilePixels, 4) k_blend_backward_atomic(
+    const float4* __restrict__ records, const uint32_t* __restrict__ sorted, const uint2* __restrict__ ranges,
+    const sp_camera_uniform cam, const float4* __restrict__ image, const uint32_t* __restrict__ contributions,
+    const float4* __restrict__ loss_gradient, float4* __restrict__ gaussian_gradients) {
+    __shared__ WarpStage s_stage[kWarps];
+    const uint32_t tile = blockIdx.x;
+    const uint32_t gx = tile % cam.tiles_x, gy = tile / cam.tiles_x;
+    const uint32_t t = threadIdx.x, lane = lane_id(), warp = t / 32;
+    const uint32_t px = gx * SP_TILE + local_x(warp, lane), py = gy * SP_TILE + local_y(warp, lane);
+    const float x0 = (float)(gx * SP_TILE + ((warp & 1u) << 3)), y0 = (float)(gy * SP_TILE + ((warp >> 1) << 2));
+    const bool inside = px < cam.width && py < cam.height;
+    const float fpx = (float)px, fpy = (float)py;
+    const uint2 range = ranges[tile];
+    WarpStage& st = s_stage[warp];
+
+    float transmittance = 0.0f;
+    uint32_t contributed = 0;
+    float4 grad = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    if (inside) {
+        const size_t index = (size_t)py * cam.width + px;
+        transmittance = image[index].w;
+        contributed = contributions[index];
+        grad = loss_gradient[index];
+    }
+    const uint32_t end = min(__reduce_max_sync(kFull, contributed), range.y - range.x);
+    float behind_r = 0.0f, behind_g = 0.0f, behind_b = 0.0f;
+    const float behind_t = transmittance;
+    for (int base = end ? (int)((end - 1) & ~31u) : -32; base >= 0; base -= 32) {
+        const uint32_t n = stage_chunk(records, sorted, range.x, (uint32_t)base, end, x0, y0, lane, st);
+        for (int i = (int)n - 1; i >= 0; --i) {
+            float v[9];
+#pragma unroll
+            for (int c = 0; c < 9; ++c) v[c] = 0.0f;
+            bool active = false;
+            if (st.j[i] < contributed) {
+                const float4 a = st.a[i];
+                const float4 b = st.b[i];
+                const float dx = a.x - fpx, dy = a.y - fpy;
+                const float power = -0.5f * (a.z * dx * dx + b.x * dy * dy) - a.w * dx * dy;
+                if (power <= 0.0f) {
+                    const float gaussian = __expf(power);
+                    const float opacity = b.y;
+                    const float alpha_unclamped = opacity * gaussian;
+                    const float alpha = fminf(SP_MAX_ALPHA, alpha_unclamped);
+                    if (alpha >= SP_MIN_ALPHA) {
+                        active = true;
+                        const float inv = __fdividef(1.0f, 1.0f - alpha);
+                        transmittance = transmittance * inv;
+                        const float cr = b.z, cgr = b.w, cbl = st.c[i];
+                        const float d_alpha = grad.x * (cr * transmittance - behind_r * inv) +
+                                              grad.y * (cgr * transmittance - behind_g * inv) +
+                                              grad.z * (cbl * transmittance - behind_b * inv) -
+                                              grad.w * (behind_t * inv);
+                        const float w = alpha * transmittance;
+                        v[5] = grad.x * w;
+                        v[6] = grad.y * w;
+                        v[7] = grad.z * w;
+                        behind_r += cr * w;
+                        behind_g += cgr * w;
+                        behind_b += cbl * w;
+                        if (alpha_unclamped < SP_MAX_ALPHA) {
+                            v[8] = d_alpha * gaussian;
+                            const float d_power = d_alpha * opacity * gaussian;
+                            v[0] = -d_power * (a.z * dx + a.w * dy);
+                            v[1] = -d_power * (a.w * dx + b.x * dy);
+                            v[2] = -0.5f * d_power * dx * dx;
+                            v[3] = -d_power * dx * dy;
+                            v[4] = -0.5f * d_power * dy * dy;
+                        }
+                    }
+                }
+            }
+            if (__ballot_sync(kFull, active)) {
+                const float total = reduce8_transposed(v, lane);
+                const float opacity_total = warp_sum(v[8]);
+                float* out = reinterpret_cast<float*>(gaussian_gradients + (size_t)st.g[i] * 3);
+                if ((lane & 3u) == 0) atomicAdd(out + ((lane >> 2) & 7u), total);
+                if (lane == 0) atomicAdd(out + 8, opacity_total);
+            }
+        }
+        __syncwarp();
+    }
+}
+
 // The forward's per-pixel walk without the colour, counting the entries visited (up to
 // and including the terminating one), plus the contributor counts the backward replays.
 __global__ void __launch_bounds__(kTilePixels) k_count_blend(const float4* __restrict__ records,
@@ -430,9 +567,8 @@ cudaError_t launch_blend_backward(int mode, const float4* records, const uint32_
             records, sorted_gaussians, ranges, offsets, cam, image, contributions, loss_gradient, slot_gradients,
             gaussian_gradients);
     else
-        k_blend_backward<SP_BWD_ATOMIC><<<tiles, kTilePixels, 0, stream>>>(
-            records, sorted_gaussians, ranges, offsets, cam, image, contributions, loss_gradient, slot_gradients,
-            gaussian_gradients);
+        k_blend_backward_atomic<<<tiles, kTilePixels, 0, stream>>>(records, sorted_gaussians, ranges, cam, image,
+                                                                    contributions, loss_gradient, gaussian_gradients);
     return cudaGetLastError();
 }
 
