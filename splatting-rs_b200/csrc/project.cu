@@ -75,7 +75,7 @@ __device__ __forceinline__ void project_one(const float* p, const sp_camera_unif
     const float cnt = (tmax0 - tmin0) * (tmax1 - tmin1);
     if (cnt <= 0.0f) return;
     float col[3];
-    raw_color<DEG>(p, cam, col);
+    raw_color<DEG>(p, p + SP_SLOT_SH, cam, col);
     const float opacity = sp_sigmoid(p[SP_SLOT_OPACITY]);
     const uint32_t rect_lo = (uint32_t)tmin0 | ((uint32_t)tmin1 << 16);
     const uint32_t rect_hi = (uint32_t)tmax0 | ((uint32_t)tmax1 << 16);
@@ -174,13 +174,23 @@ __device__ __forceinline__ void project_backward_one(float* p, uint32_t g, const
                                                      const float4* __restrict__ gaussian_gradients,
                                                      float4* __restrict__ densify_stats, float cgrad[14]) {
     constexpr int S = SP_PARAM_STRIDE(DEG);
-    float prm[S];
+    // Position, log scale, rotation and opacity logit in registers; the SH coefficients
+    // stay in shared memory, each read before its gradient overwrites it.
+    float prm[SP_SLOT_SH];
 #pragma unroll
-    for (int k = 0; k < S; ++k) {
+    for (int k = 0; k < SP_SLOT_SH; ++k) {
         prm[k] = p[k];
         p[k] = 0.0f;
     }
-    if (radius == 0) return;
+    float* sh = p + SP_SLOT_SH;
+    auto zero_sh = [&]() {
+#pragma unroll
+        for (int k = SP_SLOT_SH; k < S; ++k) p[k] = 0.0f;
+    };
+    if (radius == 0) {
+        zero_sh();
+        return;
+    }
     const float4 r0 = records[(size_t)g * kRecord + 0];
     const float4 r1 = records[(size_t)g * kRecord + 1];
     const float4 r2 = records[(size_t)g * kRecord + 2];
@@ -231,7 +241,10 @@ __device__ __forceinline__ void project_backward_one(float* p, uint32_t g, const
     }
     Geometry geo;
     geometry(prm, cam, geo);
-    if (geo.det <= 0.0f) return;
+    if (geo.det <= 0.0f) {
+        zero_sh();
+        return;
+    }
     const float fx = cam.focal[0], fy = cam.focal[1];
     const float* pc = geo.pc;
     const float z3 = geo.z2 * pc[2];
@@ -239,31 +252,33 @@ __device__ __forceinline__ void project_backward_one(float* p, uint32_t g, const
     const float opacity = r1.y;
     p[SP_SLOT_OPACITY] = d_opacity * opacity * (1.0f - opacity);
     float color_raw[3];
-    raw_color<DEG>(prm, cam, color_raw);
+    raw_color<DEG>(prm, sh, cam, color_raw);
     float d_position_sh[3] = {0.0f, 0.0f, 0.0f};
     if (DEG == 0) {
 #pragma unroll
-        for (int c = 0; c < 3; ++c) p[SP_SLOT_SH + c] = SP_SH_C0 * d_color[c] * (color_raw[c] > 0.0f ? 1.0f : 0.0f);
+        for (int c = 0; c < 3; ++c) sh[c] = SP_SH_C0 * d_color[c] * (color_raw[c] > 0.0f ? 1.0f : 0.0f);
     } else {
         float d_col[3];
 #pragma unroll
         for (int c = 0; c < 3; ++c) d_col[c] = color_raw[c] > 0.0f ? d_color[c] : 0.0f;
         float dir[3], len;
         view_direction(cam, prm, dir, &len);
-        float b[16], bg[16][3];
+        float b[16];
         sh_basis<DEG>(dir[0], dir[1], dir[2], b);
-        sh_basis_gradient<DEG>(dir[0], dir[1], dir[2], bg);
         constexpr int kCount = (DEG + 1) * (DEG + 1);
         float d_dir[3] = {0.0f, 0.0f, 0.0f};
 #pragma unroll
-        for (int k = 0; k < kCount; ++k)
+        for (int k = 0; k < kCount; ++k) {
+            float bg[3];
+            sh_basis_gradient_of<DEG>(k, dir[0], dir[1], dir[2], bg);
 #pragma unroll
             for (int c = 0; c < 3; ++c) {
-                p[SP_SLOT_SH + 3 * k + c] = b[k] * d_col[c];
-                const float w = d_col[c] * prm[SP_SLOT_SH + 3 * k + c];
+                const float w = d_col[c] * sh[3 * k + c];
+                sh[3 * k + c] = b[k] * d_col[c];
 #pragma unroll
-                for (int a = 0; a < 3; ++a) d_dir[a] += w * bg[k][a];
+                for (int a = 0; a < 3; ++a) d_dir[a] += w * bg[a];
             }
+        }
         const float dd = dir[0] * d_dir[0] + dir[1] * d_dir[1] + dir[2] * d_dir[2];
 #pragma unroll
         for (int a = 0; a < 3; ++a) d_position_sh[a] = (d_dir[a] - dir[a] * dd) / len;
@@ -376,7 +391,7 @@ __device__ __forceinline__ void project_backward_one(float* p, uint32_t g, const
 }
 
 template <int DEG, int MODE>
-__global__ void __launch_bounds__(kBlock) k_project_backward(
+__global__ void __launch_bounds__(kBlock, 3) k_project_backward(
     const float* __restrict__ params, uint32_t n, const sp_camera_uniform cam, const float4* __restrict__ records,
     const uint32_t* __restrict__ radii, const uint32_t* __restrict__ offsets, const float* __restrict__ slot_gradients,
     unsigned long long capacity, const float4* __restrict__ gaussian_gradients, float* __restrict__ param_gradients,
@@ -386,7 +401,6 @@ __global__ void __launch_bounds__(kBlock) k_project_backward(
     extern __shared__ float4 smem4[];
     float* sp = reinterpret_cast<float*>(smem4);
     __shared__ float warp_camera[kBlock / 32][SP_CAMERA_GRAD_STRIDE];
-    __shared__ float reduce[kBlock][SP_CAMERA_GRAD_STRIDE + 1];
     __shared__ bool last_block;
     const uint32_t g0 = blockIdx.x * kBlock;
     const uint32_t here = min((uint32_t)kBlock, n - g0);
@@ -433,6 +447,8 @@ __global__ void __launch_bounds__(kBlock) k_project_backward(
     for (uint32_t b = t; b < gridDim.x; b += kBlock)
 #pragma unroll
         for (int c = 0; c < SP_CAMERA_GRAD_STRIDE; ++c) sums[c] += __ldcg(camera_partials + (size_t)b * SP_CAMERA_GRAD_STRIDE + c);
+    // The staging buffer (at least 14 floats per thread) is free again: reuse it.
+    float (*reduce)[SP_CAMERA_GRAD_STRIDE] = reinterpret_cast<float (*)[SP_CAMERA_GRAD_STRIDE]>(sp);
 #pragma unroll
     for (int c = 0; c < SP_CAMERA_GRAD_STRIDE; ++c) reduce[t][c] = sums[c];
     __syncthreads();

@@ -151,54 +151,49 @@ __device__ __forceinline__ void sh_basis(float x, float y, float z, float* b) {
     b[15] = SP_SH_C3_6 * x * (xx - 3.0f * yy);
 }
 
-// d basis_k / d(x, y, z), k >= 1.
+// d basis_k / d(x, y, z) for one k (the rows of sh_basis_gradient), so that a caller
+// looping over k need not hold the whole table.
 template <int DEG>
-__device__ __forceinline__ void sh_basis_gradient(float x, float y, float z, float (*g)[3]) {
-#pragma unroll
-    for (int k = 0; k < 16; ++k) g[k][0] = g[k][1] = g[k][2] = 0.0f;
-    if (DEG < 1) return;
-    g[1][1] = -SP_SH_C1;
-    g[2][2] = SP_SH_C1;
-    g[3][0] = -SP_SH_C1;
-    if (DEG < 2) return;
+__device__ __forceinline__ void sh_basis_gradient_of(int k, float x, float y, float z, float g[3]) {
+    g[0] = g[1] = g[2] = 0.0f;
     const float xx = x * x, yy = y * y, zz = z * z;
-    g[4][0] = SP_SH_C2_0 * y;
-    g[4][1] = SP_SH_C2_0 * x;
-    g[5][1] = SP_SH_C2_1 * z;
-    g[5][2] = SP_SH_C2_1 * y;
-    g[6][0] = -2.0f * SP_SH_C2_2 * x;
-    g[6][1] = -2.0f * SP_SH_C2_2 * y;
-    g[6][2] = 4.0f * SP_SH_C2_2 * z;
-    g[7][0] = SP_SH_C2_3 * z;
-    g[7][2] = SP_SH_C2_3 * x;
-    g[8][0] = 2.0f * SP_SH_C2_4 * x;
-    g[8][1] = -2.0f * SP_SH_C2_4 * y;
-    if (DEG < 3) return;
-    g[9][0] = SP_SH_C3_0 * 6.0f * x * y;
-    g[9][1] = SP_SH_C3_0 * (3.0f * xx - 3.0f * yy);
-    g[10][0] = SP_SH_C3_1 * y * z;
-    g[10][1] = SP_SH_C3_1 * x * z;
-    g[10][2] = SP_SH_C3_1 * x * y;
-    g[11][0] = SP_SH_C3_2 * -2.0f * x * y;
-    g[11][1] = SP_SH_C3_2 * (4.0f * zz - xx - 3.0f * yy);
-    g[11][2] = SP_SH_C3_2 * 8.0f * y * z;
-    g[12][0] = SP_SH_C3_3 * -6.0f * x * z;
-    g[12][1] = SP_SH_C3_3 * -6.0f * y * z;
-    g[12][2] = SP_SH_C3_3 * (6.0f * zz - 3.0f * xx - 3.0f * yy);
-    g[13][0] = SP_SH_C3_4 * (4.0f * zz - 3.0f * xx - yy);
-    g[13][1] = SP_SH_C3_4 * -2.0f * x * y;
-    g[13][2] = SP_SH_C3_4 * 8.0f * x * z;
-    g[14][0] = SP_SH_C3_5 * 2.0f * x * z;
-    g[14][1] = SP_SH_C3_5 * -2.0f * y * z;
-    g[14][2] = SP_SH_C3_5 * (xx - yy);
-    g[15][0] = SP_SH_C3_6 * (3.0f * xx - 3.0f * yy);
-    g[15][1] = SP_SH_C3_6 * -6.0f * x * y;
+    switch (k) {
+        case 1: g[1] = -SP_SH_C1; break;
+        case 2: g[2] = SP_SH_C1; break;
+        case 3: g[0] = -SP_SH_C1; break;
+        case 4: g[0] = SP_SH_C2_0 * y; g[1] = SP_SH_C2_0 * x; break;
+        case 5: g[1] = SP_SH_C2_1 * z; g[2] = SP_SH_C2_1 * y; break;
+        case 6: g[0] = -2.0f * SP_SH_C2_2 * x; g[1] = -2.0f * SP_SH_C2_2 * y; g[2] = 4.0f * SP_SH_C2_2 * z; break;
+        case 7: g[0] = SP_SH_C2_3 * z; g[2] = SP_SH_C2_3 * x; break;
+        case 8: g[0] = 2.0f * SP_SH_C2_4 * x; g[1] = -2.0f * SP_SH_C2_4 * y; break;
+        case 9: g[0] = SP_SH_C3_0 * 6.0f * x * y; g[1] = SP_SH_C3_0 * (3.0f * xx - 3.0f * yy); break;
+        case 10: g[0] = SP_SH_C3_1 * y * z; g[1] = SP_SH_C3_1 * x * z; g[2] = SP_SH_C3_1 * x * y; break;
+        case 11:
+            g[0] = SP_SH_C3_2 * -2.0f * x * y;
+            g[1] = SP_SH_C3_2 * (4.0f * zz - xx - 3.0f * yy);
+            g[2] = SP_SH_C3_2 * 8.0f * y * z;
+            break;
+        case 12:
+            g[0] = SP_SH_C3_3 * -6.0f * x * z;
+            g[1] = SP_SH_C3_3 * -6.0f * y * z;
+            g[2] = SP_SH_C3_3 * (6.0f * zz - 3.0f * xx - 3.0f * yy);
+            break;
+        case 13:
+            g[0] = SP_SH_C3_4 * (4.0f * zz - 3.0f * xx - yy);
+            g[1] = SP_SH_C3_4 * -2.0f * x * y;
+            g[2] = SP_SH_C3_4 * 8.0f * x * z;
+            break;
+        case 14: g[0] = SP_SH_C3_5 * 2.0f * x * z; g[1] = SP_SH_C3_5 * -2.0f * y * z; g[2] = SP_SH_C3_5 * (xx - yy); break;
+        case 15: g[0] = SP_SH_C3_6 * (3.0f * xx - 3.0f * yy); g[1] = SP_SH_C3_6 * -6.0f * x * y; break;
+        default: break;
+    }
 }
 
-// Colour before the clamp at zero (project_forward.wgsl:83-86 at degree 0).
+// Colour before the clamp at zero (project_forward.wgsl:83-86 at degree 0): `params` holds
+// at least the position, `sh` the SH coefficients.
 template <int DEG>
-__device__ __forceinline__ void raw_color(const float* params, const sp_camera_uniform& cam, float out[3]) {
-    const float* sh = params + SP_SLOT_SH;
+__device__ __forceinline__ void raw_color(const float* params, const float* sh, const sp_camera_uniform& cam,
+                                          float out[3]) {
     if (DEG == 0) {
 #pragma unroll
         for (int c = 0; c < 3; ++c) out[c] = SP_SH_C0 * sh[c] + 0.5f;
