@@ -5,7 +5,7 @@
 // (emit_tile_keys.wgsl:13-36, sort.rs:1-3), so entries with equal keys keep ascending
 // Gaussian index. The reference sorts 4 bits a pass over 8 passes with a single-workgroup
 // scan between; here each pass moves 8 bits and needs no scan pass: the digit histograms
-// of every pass are accumulated while the keys are emitted, and each partition of 4096
+// of every pass are accumulated while the keys are emitted, and each partition of 2048
 // keys finds its output offsets by decoupled look-back on its predecessors (the
 // "onesweep" radix sort of Adinets & Merrill, 2022). Passes only cover the significant
 // bits of the key (ceil(log2 tiles) + 20).
@@ -32,6 +32,11 @@ __device__ __forceinline__ Key make_key(int key_mode, uint32_t tile, float depth
     return (Key)(((unsigned long long)tile << SP_DEPTH_BITS) | (bits >> (32 - SP_DEPTH_BITS)));
 }
 
+// Key emission, one warp per 32 Gaussians: the warp's slots are contiguous (the tile
+// offsets are an exclusive scan in Gaussian order), so its lanes write them together, key by
+// key, whatever the rectangles' sizes: balanced work and coalesced stores. The sort's digit
+// histograms are accumulated on the way: per Gaussian (weighted by its tile count) for the
+// passes whose digit holds depth bits only, per key for the others.
 template <typename Key>
 __global__ void __launch_bounds__(kBlock) k_emit(const float4* __restrict__ records, uint32_t* __restrict__ offsets,
                                                  const unsigned long long* __restrict__ block_offsets, uint32_t n,
@@ -39,27 +44,66 @@ __global__ void __launch_bounds__(kBlock) k_emit(const float4* __restrict__ reco
                                                  const DeviceMeta* __restrict__ meta, Key* __restrict__ keys,
                                                  uint32_t* __restrict__ values, uint32_t* __restrict__ histograms) {
     __shared__ uint32_t hist[kSortMaxPasses][kSortRadix];
-    const uint32_t t = threadIdx.x;
+    const uint32_t t = threadIdx.x, lane = lane_id();
     for (uint32_t i = t; i < (uint32_t)passes * kSortRadix; i += kBlock) (&hist[0][0])[i] = 0;
     __syncthreads();
+    const int tile_shift = key_mode == SP_KEYS_FULL32 ? 32 : SP_DEPTH_BITS;
+    const unsigned long long capacity = meta->capacity;
     const uint32_t g = blockIdx.x * kBlock + t;
+    uint32_t x0 = 0, y0 = 0, w = 1, count = 0;
+    float depth = 0.0f;
+    unsigned long long index = 0;
     if (g < n) {
         const float4 r2 = records[(size_t)g * kRecord + 2];
         const uint32_t lo = __float_as_uint(r2.z), hi = __float_as_uint(r2.w);
-        const uint32_t x0 = lo & 0xffffu, y0 = lo >> 16, x1 = hi & 0xffffu, y1 = hi >> 16;
-        unsigned long long index = block_offsets[blockIdx.x] + offsets[g];
+        x0 = lo & 0xffffu;
+        y0 = lo >> 16;
+        const uint32_t x1 = hi & 0xffffu, y1 = hi >> 16;
+        w = max(x1 - x0, 1u);
+        count = (x1 - x0) * (y1 - y0);
+        depth = r2.y;
+        index = block_offsets[blockIdx.x] + offsets[g];
         offsets[g] = (uint32_t)index;
-        const unsigned long long capacity = meta->capacity;
-        for (uint32_t ty = y0; ty < y1; ++ty)
-            for (uint32_t tx = x0; tx < x1; ++tx) {
-                if (index < capacity) {
-                    const Key key = make_key<Key>(key_mode, ty * tiles_x + tx, r2.y);
-                    keys[index] = key;
-                    values[index] = g;
-                    for (int p = 0; p < passes; ++p) atomicAdd(&hist[p][(uint32_t)(key >> (8 * p)) & 255u], 1u);
-                }
-                ++index;
-            }
+        // Depth-only digits: the same for every key of the Gaussian.
+        const unsigned long long kept = index >= capacity ? 0ull : min((unsigned long long)count, capacity - index);
+        if (kept) {
+            const Key depth_key = make_key<Key>(key_mode, 0u, depth);
+            for (int p = 0; p < passes && 8 * p + 8 <= tile_shift; ++p)
+                atomicAdd(&hist[p][(uint32_t)(depth_key >> (8 * p)) & 255u], (uint32_t)kept);
+        }
+    }
+    // Exclusive scan of the counts over the warp.
+    uint32_t inclusive = count;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const uint32_t up = __shfl_up_sync(0xffffffffu, inclusive, o);
+        if (lane >= (uint32_t)o) inclusive += up;
+    }
+    const uint32_t exclusive = inclusive - count;
+    const uint32_t total = __shfl_sync(0xffffffffu, inclusive, 31);
+    const unsigned long long start = __shfl_sync(0xffffffffu, index, 0);
+    const int first_tile_pass = tile_shift / 8;
+    for (uint32_t round = 0; round * 32 < total; ++round) {
+        const uint32_t e = round * 32 + lane;
+        // The lane whose slots hold e: the last with exclusive <= e.
+        uint32_t owner = 0;
+#pragma unroll
+        for (uint32_t step = 16; step > 0; step >>= 1)
+            if (__shfl_sync(0xffffffffu, exclusive, owner + step) <= e) owner += step;
+        const uint32_t local = e - __shfl_sync(0xffffffffu, exclusive, owner);
+        const uint32_t ox0 = __shfl_sync(0xffffffffu, x0, owner), oy0 = __shfl_sync(0xffffffffu, y0, owner);
+        const uint32_t ow = __shfl_sync(0xffffffffu, w, owner);
+        const float odepth = __shfl_sync(0xffffffffu, depth, owner);
+        const uint32_t og = __shfl_sync(0xffffffffu, g, owner);
+        const unsigned long long slot = start + e;
+        if (e < total && slot < capacity) {
+            const uint32_t row = local / ow;
+            const Key key = make_key<Key>(key_mode, (oy0 + row) * tiles_x + ox0 + (local - row * ow), odepth);
+            keys[slot] = key;
+            values[slot] = og;
+            for (int p = first_tile_pass; p < passes; ++p)
+                atomicAdd(&hist[p][(uint32_t)(key >> (8 * p)) & 255u], 1u);
+        }
     }
     __syncthreads();
     for (uint32_t i = t; i < (uint32_t)passes * kSortRadix; i += kBlock) {
@@ -73,7 +117,7 @@ __global__ void __launch_bounds__(kBlock) k_emit(const float4* __restrict__ reco
 // counts, sums its predecessors' (decoupled look-back) and scatters, digit-sorted through
 // shared memory so that the global writes of each digit are contiguous.
 template <typename Key>
-__global__ void __launch_bounds__(kSortThreads, 2)
+__global__ void __launch_bounds__(kSortThreads, kSortBlocksPerSM)
     k_sort_pass(int shift, uint32_t sequence, const Key* __restrict__ keys_in, const uint32_t* __restrict__ values_in,
                 Key* __restrict__ keys_out, uint32_t* __restrict__ values_out, const uint32_t* __restrict__ histogram,
                 uint32_t* ticket, unsigned long long* lookback, DeviceMeta* meta) {
@@ -120,7 +164,7 @@ __global__ void __launch_bounds__(kSortThreads, 2)
         if (part >= partitions) break;
         const uint32_t base = part * kSortPartition;
 
-        // Load: warp w holds keys [base + 512 w, base + 512 (w + 1)), item k at lane + 32 k,
+        // Load: warp w holds keys [base + 32 kSortItems w, base + 32 kSortItems (w + 1)), item k at lane + 32 k,
         // so (warp, item, lane) order is the keys' original order.
         Key key[kSortItems];
         uint32_t value[kSortItems], digit[kSortItems], rank[kSortItems];
@@ -228,7 +272,7 @@ int sort_grid() {
         int device = 0, sms = 0;
         cudaGetDevice(&device);
         cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
-        grid = (sms > 0 ? sms : 148) * 2;
+        grid = (sms > 0 ? sms : 148) * kSortBlocksPerSM;
     }
     return grid;
 }
