@@ -368,15 +368,18 @@ def main() -> None:
     def api_step(step: int) -> None:
         v = view_of(step)
         factor = sb.position_rate_factor(step % iterations, iterations)
-        rast.set_camera(poses.camera(v))
-        rast.encode_forward()
-        rast.encode_loss(v)
-        rast.encode_backward()
-        if world > 1:
+        if world == 1:
+            # One library call: the step and its 88-byte read-back.
+            gradient, _ = rast.train_step(adam_e2e, poses.camera(v), v, factor)
+        else:
+            rast.set_camera(poses.camera(v))
+            rast.encode_forward()
+            rast.encode_loss(v)
+            rast.encode_backward()
             dist.all_reduce(grads)
-        adam_e2e.encode_step(factor)
-        gradient = rast.read_camera_gradient()
-        rast.read_loss()
+            adam_e2e.encode_step(factor)
+            gradient = rast.read_camera_gradient()
+            rast.read_loss()
         poses.step(v, gradient, factor)
 
     for i in range(min(args.warmup, 3)):

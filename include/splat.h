@@ -264,6 +264,13 @@ sp_status sp_loss_sums_noalloc(int device, const float* d_pixel_loss, uint64_t p
 /* read_intersections (rasterizer.rs:536-544): fills `out` and returns SP_ERR_OVERFLOW when
  * the list overflowed (where the reference panics). */
 sp_status sp_read_intersections(sp_rasterizer* r, sp_intersection_meta* out);
+/* Trainer::step_async (training.rs:197-209) in one call: set the camera, forward, loss
+ * against `view`, backward, one Adam step at `position_rate_factor`; then, if either
+ * output is non-NULL, the camera gradient (56 B) and the loss terms (32 B) are copied to
+ * pinned host memory and the stream is synchronised once — the per-step read-back the
+ * reference's pose refinement does (training.rs:205-208). */
+sp_status sp_train_step(sp_rasterizer* r, sp_adam* adam, const sp_camera_uniform* camera, uint32_t view,
+                        float position_rate_factor, sp_camera_gradient* camera_gradient_out, sp_loss_terms* loss_out);
 /* Rasterizer::render (rasterizer.rs:552-564): set_camera, forward, overflow check, image. */
 sp_status sp_render(sp_rasterizer* r, const sp_camera_uniform* camera, float* host_rgbt);
 /* Diagnostics, as the reference's `Projected` mirror "for tests and diagnostics"

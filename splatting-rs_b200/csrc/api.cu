@@ -107,6 +107,14 @@ struct sp_rasterizer {
     uint32_t* camera_done = nullptr;
     float* camera_gradient = nullptr;
     float4* densify_stats = nullptr;
+    // Pinned host staging of the per-step read-back (sp_train_step).
+    struct StepReadback {
+        float camera[SP_CAMERA_GRAD_STRIDE];
+        uint32_t status;  // DeviceMeta::status of the step
+        uint32_t pad;
+        double loss[4];
+    };
+    StepReadback* readback = nullptr;
 
     uint64_t pixels() const { return (uint64_t)width * height; }
 };
@@ -353,6 +361,7 @@ void sp_rasterizer_destroy(sp_rasterizer* r) {
     cudaSetDevice(r->ctx->device);
     cudaStreamSynchronize(r->ctx->stream);
     for (void* p : r->allocations) cudaFree(p);
+    if (r->readback) cudaFreeHost(r->readback);
     delete r;
 }
 
@@ -449,6 +458,13 @@ sp_status sp_rasterizer_create(sp_context* ctx, const float* d_params, uint64_t 
     SP_ALLOC(r->camera_gradient, SP_CAMERA_GRAD_STRIDE);
     SP_ALLOC(r->densify_stats, n);
 #undef SP_ALLOC
+    {
+        const cudaError_t err = cudaMallocHost(&r->readback, sizeof(sp_rasterizer::StepReadback));
+        if (err != cudaSuccess) {
+            sp_rasterizer_destroy(r);
+            return cuda_fail(ctx, err, "cudaMallocHost");
+        }
+    }
     // The default camera of rasterizer.rs:202-213: identity pose, unit focal.
     const double identity[9] = {1, 0, 0, 0, 1, 0, 0, 0, 1}, zero[3] = {0, 0, 0}, unit[2] = {1, 1}, origin[2] = {0, 0};
     sp_camera_uniform_from_pinhole(identity, zero, unit, origin, width, height, &r->camera);
@@ -650,6 +666,38 @@ sp_status sp_read_intersections(sp_rasterizer* r, sp_intersection_meta* out) {
         return fail(r->ctx, SP_ERR_OVERFLOW,
                     "intersection list overflow: more than " + std::to_string(r->capacity) +
                         " (Gaussian, tile) pairs; Gaussians are too large for the image");
+    return SP_OK;
+}
+
+sp_status sp_train_step(sp_rasterizer* r, sp_adam* adam, const sp_camera_uniform* camera, uint32_t view,
+                        float position_rate_factor, sp_camera_gradient* camera_gradient_out, sp_loss_terms* loss_out) {
+    if (!r || !adam || !camera) return SP_ERR_INVALID;
+    SP_CHECK(sp_set_camera(r, camera));
+    SP_CHECK(sp_forward(r));
+    SP_CHECK(sp_loss(r, view));
+    SP_CHECK(sp_backward(r));
+    SP_CHECK(sp_adam_step(adam, position_rate_factor));
+    if (!camera_gradient_out && !loss_out) return SP_OK;
+    cudaStream_t st = r->ctx->stream;
+    SP_CUDA(r->ctx, cudaMemcpyAsync(&r->readback->status, &r->meta->status, sizeof(uint32_t), cudaMemcpyDeviceToHost,
+                                    st));
+    if (loss_out) SP_CUDA(r->ctx, launch_loss_sums(r->pixel_loss, r->pixels(), r->loss_sums, st));
+    if (camera_gradient_out)
+        SP_CUDA(r->ctx, cudaMemcpyAsync(r->readback->camera, r->camera_gradient, sizeof(r->readback->camera),
+                                        cudaMemcpyDeviceToHost, st));
+    if (loss_out)
+        SP_CUDA(r->ctx,
+                cudaMemcpyAsync(r->readback->loss, r->loss_sums, sizeof(r->readback->loss), cudaMemcpyDeviceToHost, st));
+    SP_CHECK(sync_stream(r->ctx));
+    if (r->readback->status != 0) return device_status(r, nullptr);
+    if (camera_gradient_out) std::memcpy(camera_gradient_out, r->readback->camera, sizeof(sp_camera_gradient));
+    if (loss_out) {
+        const double pixels = (double)r->pixels();
+        loss_out->l1 = (float)(r->readback->loss[0] / pixels);
+        loss_out->alpha = (float)(r->readback->loss[1] / pixels);
+        loss_out->dssim = (float)(r->readback->loss[2] / pixels);
+        loss_out->total = (float)(r->readback->loss[3] / pixels);
+    }
     return SP_OK;
 }
 

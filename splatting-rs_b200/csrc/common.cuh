@@ -47,9 +47,9 @@ struct SortPlan {
 };
 
 constexpr int kSortThreads = 256;
-constexpr int kSortItems = 8;
-constexpr int kSortBlocksPerSM = 4;
-constexpr int kSortPartition = kSortThreads * kSortItems;  // 2048 keys per partition
+constexpr int kSortItems = 16;
+constexpr int kSortBlocksPerSM = 2;
+constexpr int kSortPartition = kSortThreads * kSortItems;  // 4096 keys per partition
 constexpr int kSortMaxPasses = 8;
 constexpr int kSortRadix = 256;
 

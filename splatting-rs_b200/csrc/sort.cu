@@ -5,7 +5,7 @@
 // (emit_tile_keys.wgsl:13-36, sort.rs:1-3), so entries with equal keys keep ascending
 // Gaussian index. The reference sorts 4 bits a pass over 8 passes with a single-workgroup
 // scan between; here each pass moves 8 bits and needs no scan pass: the digit histograms
-// of every pass are accumulated while the keys are emitted, and each partition of 2048
+// of every pass are accumulated while the keys are emitted, and each partition of 4096
 // keys finds its output offsets by decoupled look-back on its predecessors (the
 // "onesweep" radix sort of Adinets & Merrill, 2022). Passes only cover the significant
 // bits of the key (ceil(log2 tiles) + 20).

@@ -199,6 +199,9 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "sp_loss_sums_noalloc": (c_int, [c_int, _P, c_uint64, _P, _P]),
     "sp_read_intersections": (c_int, [_P, POINTER(IntersectionMeta)]),
     "sp_render": (c_int, [_P, POINTER(CameraUniform), _P]),
+    "sp_train_step": (
+        c_int, [_P, _P, POINTER(CameraUniform), c_uint32, c_float, POINTER(CameraGradient), POINTER(LossTermsC)]
+    ),
     "sp_read_projected": (c_int, [_P, _P]),
     "sp_read_sorted_intersections": (c_int, [_P, _P, _P]),
     "sp_read_tile_ranges": (c_int, [_P, _P]),

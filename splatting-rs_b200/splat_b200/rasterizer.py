@@ -343,6 +343,20 @@ class Rasterizer:
             self._check(status, "read_intersections")
         return out
 
+    def train_step(self, adam, camera: PinholeCamera | CameraUniform, view: int, rate_factor: float,
+                   read_back: bool = True):
+        """One whole training step (Trainer::step_async, training.rs:197-209) in one call;
+        with `read_back`, returns (camera gradient, loss terms) read back together."""
+        uniform = camera.uniform() if isinstance(camera, PinholeCamera) else camera
+        if not read_back:
+            self._check(self.lib.sp_train_step(self.handle, adam.handle, ctypes.byref(uniform), view,
+                                               float(rate_factor), None, None), "train_step")
+            return None
+        gradient, loss = CameraGradient(), LossTermsC()
+        self._check(self.lib.sp_train_step(self.handle, adam.handle, ctypes.byref(uniform), view, float(rate_factor),
+                                           ctypes.byref(gradient), ctypes.byref(loss)), "train_step")
+        return gradient, LossTerms(loss.l1, loss.alpha, loss.dssim, loss.total)
+
     def render(self, camera: PinholeCamera | CameraUniform) -> Rendered:
         """Rasterizer::render (rasterizer.rs:552-564)."""
         uniform = camera.uniform() if isinstance(camera, PinholeCamera) else camera

@@ -80,15 +80,12 @@ class Trainer:
         return self.poses.camera(view) if self.poses else self.cameras[view]
 
     def step(self, view: int, rate_factor: float) -> None:
-        """Trainer::step_async (training.rs:197-209)."""
-        self.rasterizer.set_camera(self.camera(view))
-        self.rasterizer.encode_forward()
-        self.rasterizer.encode_loss(view)
-        self.rasterizer.encode_backward()
-        self.adam.encode_step(rate_factor)
+        """Trainer::step_async (training.rs:197-209), one library call (sp_train_step);
+        with pose refinement its camera gradient comes back in the same call."""
+        result = self.rasterizer.train_step(self.adam, self.camera(view), view, rate_factor,
+                                            read_back=self.poses is not None)
         if self.poses is not None:
-            gradient = self.rasterizer.read_camera_gradient()
-            self.poses.step(view, gradient, rate_factor)
+            self.poses.step(view, result[0], rate_factor)
 
     def train_step(self, step: int, steps: int) -> None:
         """Trainer::train_step_async (training.rs:221-229), without densification."""

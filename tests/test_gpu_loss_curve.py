@@ -1,0 +1,107 @@
+"""Loss-curve parity (the benchmark's config 0): 20k Gaussians, SH degree 0, 3 views of
+256 x 256, 100 training steps (forward, loss, backward, Adam with the scale clamp) on the
+CUDA path through the C ABI against the CPU oracle's full training step on the same
+seeded inputs. Bar: every step's mean total loss within 1e-3 relative."""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+import oracle
+import splat_b200 as sb
+from splat_b200 import scenes
+
+pytestmark = pytest.mark.gpu
+
+STEPS = 100
+
+
+def ground_truth(scene):
+    gts = []
+    for cam in scene.cameras:
+        rgbt = oracle.render(scene.truth.to_packed(), 0, oracle.camera_array(cam.uniform()))["image"].reshape(-1, 4)
+        mask = ((1.0 - rgbt[:, 3]) > 0.5).astype(np.float32)
+        gts.append(np.concatenate([rgbt[:, :3] * mask[:, None], mask[:, None]], axis=1))
+    return np.stack(gts).astype(np.float32)
+
+
+@pytest.mark.parametrize("mode", [sb.SP_BWD_DETERMINISTIC, sb.SP_BWD_ATOMIC])
+def test_loss_curve_matches_the_oracle(ctx, mode):
+    import torch
+
+    scene = scenes.config(0)
+    cams = scene.cameras
+    gt = ground_truth(scene)
+    extent = np.float32(sb.cameras_extent(cams))
+    rates = sb.LEARNING_RATES_3DGS
+
+    params = torch.from_numpy(scene.cloud.to_packed()).cuda()
+    gt_dev = torch.from_numpy(gt.reshape(-1)).cuda()
+    rast = sb.Rasterizer(ctx, params, len(scene.cloud), 256, 256, gt_dev, len(cams),
+                         sb.default_options(backward_mode=mode))
+    adam = sb.Adam(ctx, params, rast, len(scene.cloud), rates, extent)
+    gpu_losses = []
+    for step in range(STEPS):
+        view = step % len(cams)
+        rast.set_camera(cams[view])
+        rast.encode_forward()
+        rast.encode_loss(view)
+        rast.encode_backward()
+        adam.encode_step(sb.position_rate_factor(step, STEPS))
+        gpu_losses.append(rast.read_loss().total)
+
+    packed = scene.cloud.to_packed().copy()
+    m, v = np.zeros_like(packed), np.zeros_like(packed)
+    max_log = float(np.log(np.float32(0.02) * extent))
+    aniso = float(np.log(np.float32(10.0)))
+    oracle_losses = []
+    for step in range(STEPS):
+        view = step % len(cams)
+        factor = np.float32(sb.position_rate_factor(step, STEPS))
+        lr = oracle.learning_rates_by_slot(rates.to_c(), np.float32(extent * factor), 14)
+        loss, _ = oracle.train_step(packed, 0, oracle.camera_array(cams[view].uniform()), gt[view].reshape(-1), m, v, lr,
+                                    step + 1, max_log, aniso)
+        oracle_losses.append(loss)
+
+    gpu_losses, oracle_losses = np.array(gpu_losses), np.array(oracle_losses)
+    rel = np.abs(gpu_losses - oracle_losses) / np.abs(oracle_losses)
+    assert rel.max() < 1e-3, f"step {rel.argmax()}: {gpu_losses[rel.argmax()]} vs {oracle_losses[rel.argmax()]}"
+    # The run trains: the loss falls.
+    assert gpu_losses[-3:].mean() < gpu_losses[:3].mean()
+
+
+def test_fused_train_step_equals_the_separate_calls(ctx):
+    """sp_train_step (one call with its 88-byte read-back) against set_camera, forward, loss,
+    backward, Adam and the two reads issued one by one: bit-identical parameters, camera
+    gradients and losses over 10 steps (deterministic backward)."""
+    import torch
+
+    scene = scenes.config(0)
+    cams = scene.cameras
+    gt_dev = torch.from_numpy(ground_truth(scene).reshape(-1)).cuda()
+    extent = np.float32(sb.cameras_extent(cams))
+    runs = []
+    for fused in (False, True):
+        params = torch.from_numpy(scene.cloud.to_packed()).cuda()
+        rast = sb.Rasterizer(ctx, params, len(scene.cloud), 256, 256, gt_dev, len(cams),
+                             sb.default_options(backward_mode=sb.SP_BWD_DETERMINISTIC))
+        adam = sb.Adam(ctx, params, rast, len(scene.cloud), sb.LEARNING_RATES_3DGS, extent)
+        trace = []
+        for step in range(10):
+            view, factor = step % len(cams), sb.position_rate_factor(step, 10)
+            if fused:
+                gradient, loss = rast.train_step(adam, cams[view], view, factor)
+            else:
+                rast.set_camera(cams[view])
+                rast.encode_forward()
+                rast.encode_loss(view)
+                rast.encode_backward()
+                adam.encode_step(factor)
+                gradient, loss = rast.read_camera_gradient(), rast.read_loss()
+            trace.append((bytes(gradient), loss.total, loss.l1, loss.dssim, loss.alpha))
+        ctx.sync()
+        runs.append((trace, params.cpu().numpy().copy()))
+        del adam, rast
+    assert runs[0][0] == runs[1][0]
+    assert np.array_equal(runs[0][1].view(np.uint32), runs[1][1].view(np.uint32))
