@@ -1,18 +1,22 @@
 // Alpha blending: forward (K6, rasterize_forward.wgsl:22-88) and backward (K8,
-// rasterize_backward.wgsl:30-133). One block of 256 threads per 16 x 16 tile, one pixel per
-// thread; each warp owns an 8 x 4 block of the tile. The tile's Gaussians are gathered
-// (sorted list -> Gaussian -> 48-B record, an L2-resident array) into shared memory a batch
-// at a time, one Gaussian per thread, and read back as broadcasts.
+// rasterize_backward.wgsl:30-133).
 //
-// With each record the loading thread works out which of the tile's eight 8 x 4 warp blocks
-// the Gaussian can reach: the pixel rectangle outside of which its alpha is below 1/255
-// (where the exact per-pixel test rejects it), padded. Each warp then compacts the batch
-// into its own list of the Gaussians that reach it and walks only that list. This changes
-// no result: only pairs the exact test would reject are left out.
+// Forward and atomic backward: one block of 128 threads per 16 x 16 tile; each warp owns an
+// 8 x 8 block of it and each lane two pixels of that block, (x, y) and (x, y + 4), whose
+// arithmetic runs as packed f32x2 instructions (FFMA2 / FMUL2 / FADD2 of sm_100). Each warp
+// walks the tile's sorted list on its own, 32 entries at a time: the entries' 48-B records
+// (an L2-resident array) are gathered one per lane, those that can reach the warp's pixels
+// are kept, compacted into the warp's shared-memory stage, and read back as broadcasts.
+// "Can reach": the Gaussian's alpha is at least 1/255 somewhere in the block's rectangle of
+// pixel centres (the exact ellipse-rectangle test, padded), so only pairs the exact
+// per-pixel test rejects are left out and no result changes.
 //
-// The arithmetic per (pixel, Gaussian) is the reference's. exp is the hardware
-// approximation (__expf), and the backward divides by (1 - alpha) through one reciprocal,
-// so images and gradients match the oracle within a tolerance rather than bit for bit.
+// The deterministic backward keeps one pixel per thread (256 threads, 8 x 4 pixels per
+// warp) and block-synchronous batches, because it writes per-(Gaussian, tile) slots.
+//
+// The arithmetic per (pixel, Gaussian) is the reference's; exp is the hardware 2^x
+// approximation of e^x, and the backward divides by (1 - alpha) through one reciprocal, so
+// images and gradients match the oracle within a tolerance rather than bit for bit.
 #include "kernels.h"
 
 namespace splat {
@@ -94,10 +98,11 @@ __device__ __forceinline__ uint32_t compact(const uint8_t* masks, uint32_t n, ui
     return length;
 }
 
-// Whether a Gaussian can reach the rectangle of pixel centres [x0, x0 + 7] x [y0, y0 + 3]:
+// Whether a Gaussian can reach the rectangle of pixel centres [x0, x0 + 7] x [y0, y0 + ROWS - 1]:
 // op * exp(power) >= 1/255 somewhere in it, i.e. the ellipse d^T C d <= 2 ln(255 op) of the
 // conic C (padded by 1 % in the level) meets the rectangle (padded by 0.05 px). A
 // bounding-box test first, then the exact one.
+template <int ROWS>
 __device__ __forceinline__ bool reaches(float4 a, float4 b, float x0, float y0) {
     const float level = b.y * 255.0f;
     if (!(level > 1.0f)) return false;
@@ -105,7 +110,7 @@ __device__ __forceinline__ bool reaches(float4 a, float4 b, float x0, float y0) 
     if (!(det > 0.0f) || !(a.z > 0.0f) || !(b.x > 0.0f)) return true;
     const float q = 2.02f * __logf(level) + 0.02f;
     const float lo_x = x0 - a.x - 0.05f, hi_x = lo_x + 7.1f;
-    const float lo_y = y0 - a.y - 0.05f, hi_y = lo_y + 3.1f;
+    const float lo_y = y0 - a.y - 0.05f, hi_y = lo_y + (float)(ROWS - 1) + 0.1f;
     const float ex = sqrtf(q * b.x / det) + 0.05f;
     const float ey = sqrtf(q * a.z / det) + 0.05f;
     if (ex < lo_x || -ex > hi_x || ey < lo_y || -ey > hi_y) return false;
@@ -123,7 +128,8 @@ struct WarpStage {
 };
 
 // Loads entries base .. base + 31 (below `end`) of the tile list, one per lane, keeps those
-// that reach the warp's pixels, compacted into `st`; returns how many.
+// that reach the warp's 8 x ROWS pixels at (x0, y0), compacted into `st`; returns how many.
+template <int ROWS>
 __device__ __forceinline__ uint32_t stage_chunk(const float4* __restrict__ records, const uint32_t* __restrict__ sorted,
                                                 uint32_t first, uint32_t base, uint32_t end, float x0, float y0,
                                                 uint32_t lane, WarpStage& st) {
@@ -138,7 +144,7 @@ __device__ __forceinline__ uint32_t stage_chunk(const float4* __restrict__ recor
         a = rec[0];
         b = rec[1];
         c = rec[2].x;
-        take = reaches(a, b, x0, y0);
+        take = reaches<ROWS>(a, b, x0, y0);
     }
     const uint32_t ballot = __ballot_sync(kFull, take);
     if (take) {
@@ -153,74 +159,129 @@ __device__ __forceinline__ uint32_t stage_chunk(const float4* __restrict__ recor
     return __popc(ballot);
 }
 
+// Packed f32x2 arithmetic (sm_100).
+__device__ __forceinline__ float2 splat(float v) { return make_float2(v, v); }
+__device__ __forceinline__ float2 add2(float2 a, float2 b) { return __fadd2_rn(a, b); }
+__device__ __forceinline__ float2 mul2(float2 a, float2 b) { return __fmul2_rn(a, b); }
+__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) { return __ffma2_rn(a, b, c); }
+__device__ __forceinline__ float2 neg2(float2 a) { return make_float2(-a.x, -a.y); }
+
+// 2^x by the hardware approximation (PTX ex2.approx).
+__device__ __forceinline__ float exp2_approx(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr int kPairWarps = 4;                     // forward / atomic backward: 8 x 8 pixels per warp
+constexpr int kPairThreads = kPairWarps * 32;
+
+// The falloff of one Gaussian at a lane's two pixels (fpx, fpy.x) and (fpx, fpy.y)
+// (rasterize_forward.wgsl:60-66): power = -1/2 (a dx^2 + c dy^2) - b dx dy of the conic
+// (a, b, c), d = mean - pixel; gaussian = e^power, evaluated as 2^(power log2 e).
+struct Falloff {
+    float dx;
+    float2 dy, dxdy, dy2;
+    float2 gaussian;
+    bool below0, below1;  // power <= 0
+};
+
+__device__ __forceinline__ Falloff falloff(float4 a, float4 b, float fpx, float2 fpy) {
+    Falloff f;
+    f.dx = a.x - fpx;
+    f.dy = add2(splat(a.y), neg2(fpy));
+    f.dxdy = mul2(splat(f.dx), f.dy);
+    f.dy2 = mul2(f.dy, f.dy);
+    const float2 quad = fma2(splat(b.x), f.dy2, splat(a.z * f.dx * f.dx));  // a dx^2 + c dy^2
+    const float2 power2 = fma2(splat(-0.5f * kLog2e), quad, mul2(splat(-kLog2e * a.w), f.dxdy));
+    f.below0 = power2.x <= 0.0f;
+    f.below1 = power2.y <= 0.0f;
+    f.gaussian = make_float2(exp2_approx(power2.x), exp2_approx(power2.y));
+    return f;
+}
+
+// falloff() at one pixel, with the same roundings (for the one-pixel-per-thread kernels).
+__device__ __forceinline__ float falloff1(float4 a, float4 b, float fpx, float fpy, float& dx, float& dy,
+                                          bool& below) {
+    dx = a.x - fpx;
+    dy = __fadd_rn(a.y, -fpy);
+    const float dxdy = __fmul_rn(dx, dy);
+    const float quad = __fmaf_rn(b.x, __fmul_rn(dy, dy), a.z * dx * dx);
+    const float power2 = __fmaf_rn(-0.5f * kLog2e, quad, __fmul_rn(-kLog2e * a.w, dxdy));
+    below = power2 <= 0.0f;
+    return exp2_approx(power2);
+}
+
 // Each warp walks the tile's list on its own, 32 entries at a time, over only the
-// Gaussians that reach its 8 x 4 pixels; no block barrier, and a warp whose pixels are all
+// Gaussians that reach its 8 x 8 pixels; no block barrier, and a warp whose pixels are all
 // done leaves.
-__global__ void __launch_bounds__(kTilePixels, 5) k_blend_forward(const float4* __restrict__ records,
-                                                                  const uint32_t* __restrict__ sorted,
-                                                                  const uint2* __restrict__ ranges,
-                                                                  const sp_camera_uniform cam,
-                                                                  float4* __restrict__ image,
-                                                                  uint32_t* __restrict__ contributions) {
-    __shared__ WarpStage s_stage[kWarps];
+__global__ void __launch_bounds__(kPairThreads, 8) k_blend_forward(const float4* __restrict__ records,
+                                                                   const uint32_t* __restrict__ sorted,
+                                                                   const uint2* __restrict__ ranges,
+                                                                   const sp_camera_uniform cam,
+                                                                   float4* __restrict__ image,
+                                                                   uint32_t* __restrict__ contributions) {
+    __shared__ WarpStage s_stage[kPairWarps];
     const uint32_t tile = blockIdx.x;
     const uint32_t gx = tile % cam.tiles_x, gy = tile / cam.tiles_x;
-    const uint32_t t = threadIdx.x, warp = t / 32, lane = lane_id();
-    const uint32_t px = gx * SP_TILE + local_x(warp, lane), py = gy * SP_TILE + local_y(warp, lane);
-    const float x0 = (float)(gx * SP_TILE + ((warp & 1u) << 3)), y0 = (float)(gy * SP_TILE + ((warp >> 1) << 2));
-    const bool inside = px < cam.width && py < cam.height;
-    const float fpx = (float)px, fpy = (float)py;
+    const uint32_t warp = threadIdx.x / 32, lane = lane_id();
+    const uint32_t bx = gx * SP_TILE + ((warp & 1u) << 3), by = gy * SP_TILE + ((warp >> 1) << 3);
+    const uint32_t px = bx + (lane & 7u), py = by + (lane >> 3);
+    const bool inside0 = px < cam.width && py < cam.height, inside1 = px < cam.width && py + 4 < cam.height;
+    const float fpx = (float)px;
+    const float2 fpy = make_float2((float)py, (float)(py + 4));
     const uint2 range = ranges[tile];
     const uint32_t count = range.y - range.x;
     WarpStage& st = s_stage[warp];
 
-    float transmittance = 1.0f, cr = 0.0f, cg = 0.0f, cb = 0.0f;
-    uint32_t contributed = 0;
-    bool done = !inside;
-    // rasterize_forward.wgsl:58-77, two Gaussians per iteration: their alphas are
-    // independent, only the compositing is sequential.
-    auto alpha_at = [&](float4 a, float4 b) {
-        const float dx = a.x - fpx, dy = a.y - fpy;
-        const float power = -0.5f * (a.z * dx * dx + b.x * dy * dy) - a.w * dx * dy;
-        return power > 0.0f ? 0.0f : fminf(SP_MAX_ALPHA, b.y * __expf(power));
-    };
-    // Returns false when the pixel ends here.
-    auto composite = [&](float alpha, float4 b, float c, uint32_t j) {
-        if (alpha < SP_MIN_ALPHA) return true;
-        const float next = transmittance * (1.0f - alpha);
-        if (next < SP_MIN_TRANSMITTANCE) return false;
-        const float w = alpha * transmittance;
-        cr += b.z * w;
-        cg += b.w * w;
-        cb += c * w;
-        transmittance = next;
-        contributed = j + 1;
-        return true;
-    };
+    // rasterize_forward.wgsl:58-77 at both pixels.
+    float2 transmittance = splat(1.0f), cr = splat(0.0f), cg = splat(0.0f), cb = splat(0.0f);
+    uint32_t contributed0 = 0, contributed1 = 0;
+    bool done0 = !inside0, done1 = !inside1;
     for (uint32_t base = 0; base < count; base += 32) {
-        if (__all_sync(kFull, done)) break;
-        const uint32_t n = stage_chunk(records, sorted, range.x, base, count, x0, y0, lane, st);
-        if (!done) {
-            uint32_t i = 0;
-            for (; i + 1 < n; i += 2) {
-                const float4 a0 = st.a[i], b0 = st.b[i], a1 = st.a[i + 1], b1 = st.b[i + 1];
-                const float alpha0 = alpha_at(a0, b0), alpha1 = alpha_at(a1, b1);
-                if (!composite(alpha0, b0, st.c[i], st.j[i]) || !composite(alpha1, b1, st.c[i + 1], st.j[i + 1])) {
-                    done = true;
-                    break;
-                }
+        if (__all_sync(kFull, done0 && done1)) break;
+        const uint32_t n = stage_chunk<8>(records, sorted, range.x, base, count, (float)bx, (float)by, lane, st);
+        for (uint32_t i = 0; i < n && !(done0 && done1); ++i) {
+            const float4 a = st.a[i], b = st.b[i];
+            const Falloff f = falloff(a, b, fpx, fpy);
+            const float2 unclamped = mul2(splat(b.y), f.gaussian);
+            const float2 alpha = make_float2(fminf(SP_MAX_ALPHA, unclamped.x), fminf(SP_MAX_ALPHA, unclamped.y));
+            bool take0 = !done0 && f.below0 && alpha.x >= SP_MIN_ALPHA;
+            bool take1 = !done1 && f.below1 && alpha.y >= SP_MIN_ALPHA;
+            const float2 next = mul2(transmittance, add2(splat(1.0f), neg2(alpha)));
+            // A pixel whose transmittance would fall below the floor ends before this one.
+            const bool end0 = take0 && next.x < SP_MIN_TRANSMITTANCE, end1 = take1 && next.y < SP_MIN_TRANSMITTANCE;
+            take0 = take0 && !end0;
+            take1 = take1 && !end1;
+            done0 = done0 || end0;
+            done1 = done1 || end1;
+            float2 w = mul2(alpha, transmittance);
+            w.x = take0 ? w.x : 0.0f;
+            w.y = take1 ? w.y : 0.0f;
+            cr = fma2(splat(b.z), w, cr);
+            cg = fma2(splat(b.w), w, cg);
+            cb = fma2(splat(st.c[i]), w, cb);
+            const uint32_t j1 = st.j[i] + 1;
+            if (take0) {
+                transmittance.x = next.x;
+                contributed0 = j1;
             }
-            if (!done && i < n) {
-                const float4 b = st.b[i];
-                if (!composite(alpha_at(st.a[i], b), b, st.c[i], st.j[i])) done = true;
+            if (take1) {
+                transmittance.y = next.y;
+                contributed1 = j1;
             }
         }
         __syncwarp();
     }
-    if (inside) {
-        const size_t index = (size_t)py * cam.width + px;
-        image[index] = make_float4(cr, cg, cb, transmittance);
-        contributions[index] = contributed;
+    const size_t index = (size_t)py * cam.width + px;
+    if (inside0) {
+        image[index] = make_float4(cr.x, cg.x, cb.x, transmittance.x);
+        contributions[index] = contributed0;
+    }
+    if (inside1) {
+        image[index + 4 * (size_t)cam.width] = make_float4(cr.y, cg.y, cb.y, transmittance.y);
+        contributions[index + 4 * (size_t)cam.width] = contributed1;
     }
 }
 
@@ -337,10 +398,10 @@ __global__ void __launch_bounds__(kTilePixels) k_blend_backward(
             if (j < contributed) {
                 const float4 a = s_a[k];
                 const float4 b = s_b[k];
-                const float dx = a.x - fpx, dy = a.y - fpy;
-                const float power = -0.5f * (a.z * dx * dx + b.x * dy * dy) - a.w * dx * dy;
-                if (power <= 0.0f) {
-                    const float gaussian = __expf(power);
+                float dx, dy;
+                bool below;
+                const float gaussian = falloff1(a, b, fpx, fpy, dx, dy, below);
+                if (below) {
                     const float opacity = b.y;
                     const float alpha_unclamped = opacity * gaussian;
                     const float alpha = fminf(SP_MAX_ALPHA, alpha_unclamped);
@@ -410,90 +471,96 @@ __global__ void __launch_bounds__(kTilePixels) k_blend_backward(
     }
 }
 
-// The backward with per-Gaussian sums by float atomics (SP_BWD_ATOMIC): each
-// warp walks the tile's list on its own, back to front from its pixels' largest contributor
-// count, 32 entries at a time, over only the Gaussians that reach its 8 x 4 pixels. Per
-// (Gaussian, warp) the 9 gradient terms are summed over the lanes (reduce8_transposed plus
-// one butterfly) and added into the Gaussian's sums by up to 9 lanes at once.
-__global__ void __launch_bounds__(kTilePixels, 4) k_blend_backward_atomic(
+// The backward with per-Gaussian sums by float atomics (SP_BWD_ATOMIC): each warp walks
+// the tile's list on its own, back to front from its pixels' largest contributor count, 32
+// entries at a time, over only the Gaussians that reach its 8 x 8 pixels. Per (Gaussian,
+// warp) a lane adds its two pixels' 9 gradient terms, the lanes' sums are reduced
+// (reduce8_transposed plus one butterfly) and added into the Gaussian's sums by up to 9
+// lanes at once.
+__global__ void __launch_bounds__(kPairThreads, 6) k_blend_backward_atomic(
     const float4* __restrict__ records, const uint32_t* __restrict__ sorted, const uint2* __restrict__ ranges,
     const sp_camera_uniform cam, const float4* __restrict__ image, const uint32_t* __restrict__ contributions,
     const float4* __restrict__ loss_gradient, float4* __restrict__ gaussian_gradients) {
-    __shared__ WarpStage s_stage[kWarps];
+    __shared__ WarpStage s_stage[kPairWarps];
     const uint32_t tile = blockIdx.x;
     const uint32_t gx = tile % cam.tiles_x, gy = tile / cam.tiles_x;
-    const uint32_t t = threadIdx.x, lane = lane_id(), warp = t / 32;
-    const uint32_t px = gx * SP_TILE + local_x(warp, lane), py = gy * SP_TILE + local_y(warp, lane);
-    const float x0 = (float)(gx * SP_TILE + ((warp & 1u) << 3)), y0 = (float)(gy * SP_TILE + ((warp >> 1) << 2));
-    const bool inside = px < cam.width && py < cam.height;
-    const float fpx = (float)px, fpy = (float)py;
+    const uint32_t warp = threadIdx.x / 32, lane = lane_id();
+    const uint32_t bx = gx * SP_TILE + ((warp & 1u) << 3), by = gy * SP_TILE + ((warp >> 1) << 3);
+    const uint32_t px = bx + (lane & 7u), py = by + (lane >> 3);
+    const bool inside0 = px < cam.width && py < cam.height, inside1 = px < cam.width && py + 4 < cam.height;
+    const float fpx = (float)px;
+    const float2 fpy = make_float2((float)py, (float)(py + 4));
     const uint2 range = ranges[tile];
     WarpStage& st = s_stage[warp];
 
-    float transmittance = 0.0f;
-    uint32_t contributed = 0;
-    float4 grad = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-    if (inside) {
-        const size_t index = (size_t)py * cam.width + px;
-        transmittance = image[index].w;
-        contributed = contributions[index];
-        grad = loss_gradient[index];
+    // Per pixel: final transmittance, contributor count, dL/d(rgb, transmittance).
+    float2 transmittance = splat(0.0f), gr = splat(0.0f), gg = splat(0.0f), gb = splat(0.0f), gt = splat(0.0f);
+    uint32_t contributed0 = 0, contributed1 = 0;
+    const size_t index = (size_t)py * cam.width + px;
+    if (inside0) {
+        const float4 g = loss_gradient[index];
+        transmittance.x = image[index].w;
+        contributed0 = contributions[index];
+        gr.x = g.x, gg.x = g.y, gb.x = g.z, gt.x = g.w;
     }
-    const uint32_t end = min(__reduce_max_sync(kFull, contributed), range.y - range.x);
-    float behind_r = 0.0f, behind_g = 0.0f, behind_b = 0.0f;
-    const float behind_t = transmittance;
+    if (inside1) {
+        const size_t i1 = index + 4 * (size_t)cam.width;
+        const float4 g = loss_gradient[i1];
+        transmittance.y = image[i1].w;
+        contributed1 = contributions[i1];
+        gr.y = g.x, gg.y = g.y, gb.y = g.z, gt.y = g.w;
+    }
+    const uint32_t end = min(__reduce_max_sync(kFull, max(contributed0, contributed1)), range.y - range.x);
+    // rasterize_backward.wgsl:166-200. The colour behind each entry accumulates back to
+    // front; dL/dalpha = T (g . c) - (g . behind + g_T T_final) / (1 - alpha), with T the
+    // transmittance in front of the entry.
+    float2 behind_r = splat(0.0f), behind_g = splat(0.0f), behind_b = splat(0.0f);
+    const float2 behind_t = mul2(gt, transmittance);
     for (int base = end ? (int)((end - 1) & ~31u) : -32; base >= 0; base -= 32) {
-        const uint32_t n = stage_chunk(records, sorted, range.x, (uint32_t)base, end, x0, y0, lane, st);
+        const uint32_t n =
+            stage_chunk<8>(records, sorted, range.x, (uint32_t)base, end, (float)bx, (float)by, lane, st);
         for (int i = (int)n - 1; i >= 0; --i) {
-            float v[9];
-#pragma unroll
-            for (int c = 0; c < 9; ++c) v[c] = 0.0f;
-            bool active = false;
-            if (st.j[i] < contributed) {
-                const float4 a = st.a[i];
-                const float4 b = st.b[i];
-                const float dx = a.x - fpx, dy = a.y - fpy;
-                const float power = -0.5f * (a.z * dx * dx + b.x * dy * dy) - a.w * dx * dy;
-                if (power <= 0.0f) {
-                    const float gaussian = __expf(power);
-                    const float opacity = b.y;
-                    const float alpha_unclamped = opacity * gaussian;
-                    const float alpha = fminf(SP_MAX_ALPHA, alpha_unclamped);
-                    if (alpha >= SP_MIN_ALPHA) {
-                        active = true;
-                        const float inv = __fdividef(1.0f, 1.0f - alpha);
-                        transmittance = transmittance * inv;
-                        const float cr = b.z, cgr = b.w, cbl = st.c[i];
-                        const float d_alpha = grad.x * (cr * transmittance - behind_r * inv) +
-                                              grad.y * (cgr * transmittance - behind_g * inv) +
-                                              grad.z * (cbl * transmittance - behind_b * inv) -
-                                              grad.w * (behind_t * inv);
-                        const float w = alpha * transmittance;
-                        v[5] = grad.x * w;
-                        v[6] = grad.y * w;
-                        v[7] = grad.z * w;
-                        behind_r += cr * w;
-                        behind_g += cgr * w;
-                        behind_b += cbl * w;
-                        if (alpha_unclamped < SP_MAX_ALPHA) {
-                            v[8] = d_alpha * gaussian;
-                            const float d_power = d_alpha * opacity * gaussian;
-                            v[0] = -d_power * (a.z * dx + a.w * dy);
-                            v[1] = -d_power * (a.w * dx + b.x * dy);
-                            v[2] = -0.5f * d_power * dx * dx;
-                            v[3] = -d_power * dx * dy;
-                            v[4] = -0.5f * d_power * dy * dy;
-                        }
-                    }
-                }
-            }
-            if (__ballot_sync(kFull, active)) {
-                const float total = reduce8_transposed(v, lane);
-                const float opacity_total = warp_sum(v[8]);
-                float* out = reinterpret_cast<float*>(gaussian_gradients + (size_t)st.g[i] * 3);
-                if ((lane & 3u) == 0) atomicAdd(out + ((lane >> 2) & 7u), total);
-                if (lane == 0) atomicAdd(out + 8, opacity_total);
-            }
+            const uint32_t j = st.j[i];
+            const float4 a = st.a[i], b = st.b[i];
+            const Falloff f = falloff(a, b, fpx, fpy);
+            const float2 unclamped = mul2(splat(b.y), f.gaussian);
+            float2 alpha = make_float2(fminf(SP_MAX_ALPHA, unclamped.x), fminf(SP_MAX_ALPHA, unclamped.y));
+            const bool take0 = j < contributed0 && f.below0 && alpha.x >= SP_MIN_ALPHA;
+            const bool take1 = j < contributed1 && f.below1 && alpha.y >= SP_MIN_ALPHA;
+            if (!__any_sync(kFull, take0 || take1)) continue;
+            alpha.x = take0 ? alpha.x : 0.0f;
+            alpha.y = take1 ? alpha.y : 0.0f;
+            const float2 one_minus = add2(splat(1.0f), neg2(alpha));
+            const float2 inv = make_float2(__fdividef(1.0f, one_minus.x), __fdividef(1.0f, one_minus.y));
+            const float2 divided = mul2(transmittance, inv);
+            transmittance.x = take0 ? divided.x : transmittance.x;
+            transmittance.y = take1 ? divided.y : transmittance.y;
+            const float cbl = st.c[i];
+            const float2 g_dot_c = fma2(gb, splat(cbl), fma2(gg, splat(b.w), mul2(gr, splat(b.z))));
+            const float2 g_dot_behind = fma2(gb, behind_b, fma2(gg, behind_g, fma2(gr, behind_r, behind_t)));
+            const float2 d_alpha = fma2(neg2(inv), g_dot_behind, mul2(transmittance, g_dot_c));
+            const float2 w = mul2(alpha, transmittance);
+            const float2 d_r = mul2(gr, w), d_g = mul2(gg, w), d_b = mul2(gb, w);
+            behind_r = fma2(splat(b.z), w, behind_r);
+            behind_g = fma2(splat(b.w), w, behind_g);
+            behind_b = fma2(splat(cbl), w, behind_b);
+            // The clamp at 0.99 passes no gradient to opacity or the falloff.
+            const float2 gate = make_float2(take0 && unclamped.x < SP_MAX_ALPHA ? f.gaussian.x : 0.0f,
+                                            take1 && unclamped.y < SP_MAX_ALPHA ? f.gaussian.y : 0.0f);
+            const float2 d_opacity = mul2(d_alpha, gate);
+            const float2 nd_power = mul2(d_opacity, splat(-b.y));  // -dL/dpower
+            const float2 d_mx = mul2(nd_power, fma2(splat(a.w), f.dy, splat(a.z * f.dx)));
+            const float2 d_my = mul2(nd_power, fma2(splat(b.x), f.dy, splat(a.w * f.dx)));
+            const float2 d_ca = mul2(nd_power, splat(0.5f * f.dx * f.dx));
+            const float2 d_cb = mul2(nd_power, f.dxdy);
+            const float2 d_cc = mul2(nd_power, mul2(splat(0.5f), f.dy2));
+            const float v[8] = {d_mx.x + d_mx.y, d_my.x + d_my.y, d_ca.x + d_ca.y, d_cb.x + d_cb.y,
+                                d_cc.x + d_cc.y, d_r.x + d_r.y,   d_g.x + d_g.y,   d_b.x + d_b.y};
+            const float total = reduce8_transposed(v, lane);
+            const float opacity_total = warp_sum(d_opacity.x + d_opacity.y);
+            float* out = reinterpret_cast<float*>(gaussian_gradients + (size_t)st.g[i] * 3);
+            if ((lane & 3u) == 0) atomicAdd(out + ((lane >> 2) & 7u), total);
+            if (lane == 0) atomicAdd(out + 8, opacity_total);
         }
         __syncwarp();
     }
@@ -520,10 +587,11 @@ __global__ void __launch_bounds__(kTilePixels) k_count_blend(const float4* __res
             ++visited;
             const float4* rec = records + (size_t)sorted[j] * kRecord;
             const float4 a = rec[0], b = rec[1];
-            const float dx = a.x - fpx, dy = a.y - fpy;
-            const float power = -0.5f * (a.z * dx * dx + b.x * dy * dy) - a.w * dx * dy;
-            if (power > 0.0f) continue;
-            const float alpha = fminf(SP_MAX_ALPHA, b.y * __expf(power));
+            float dx, dy;
+            bool below;
+            const float gaussian = falloff1(a, b, fpx, fpy, dx, dy, below);
+            if (!below) continue;
+            const float alpha = fminf(SP_MAX_ALPHA, b.y * gaussian);
             if (alpha < SP_MIN_ALPHA) continue;
             const float next = transmittance * (1.0f - alpha);
             if (next < SP_MIN_TRANSMITTANCE) break;
@@ -553,7 +621,7 @@ cudaError_t launch_blend_forward(const float4* records, const uint32_t* sorted_g
                                  const sp_camera_uniform& cam, float4* image, uint32_t* contributions,
                                  cudaStream_t stream) {
     const unsigned tiles = cam.tiles_x * cam.tiles_y;
-    k_blend_forward<<<tiles, kTilePixels, 0, stream>>>(records, sorted_gaussians, ranges, cam, image, contributions);
+    k_blend_forward<<<tiles, kPairThreads, 0, stream>>>(records, sorted_gaussians, ranges, cam, image, contributions);
     return cudaGetLastError();
 }
 
@@ -567,7 +635,7 @@ cudaError_t launch_blend_backward(int mode, const float4* records, const uint32_
             records, sorted_gaussians, ranges, offsets, cam, image, contributions, loss_gradient, slot_gradients,
             gaussian_gradients);
     else
-        k_blend_backward_atomic<<<tiles, kTilePixels, 0, stream>>>(records, sorted_gaussians, ranges, cam, image,
+        k_blend_backward_atomic<<<tiles, kPairThreads, 0, stream>>>(records, sorted_gaussians, ranges, cam, image,
                                                                     contributions, loss_gradient, gaussian_gradients);
     return cudaGetLastError();
 }
