@@ -179,10 +179,12 @@ constexpr int kPairThreads = kPairWarps * 32;
 
 // The falloff of one Gaussian at a lane's two pixels (fpx, fpy.x) and (fpx, fpy.y)
 // (rasterize_forward.wgsl:60-66): power = -1/2 (a dx^2 + c dy^2) - b dx dy of the conic
-// (a, b, c), d = mean - pixel; gaussian = e^power, evaluated as 2^(power log2 e).
+// (a, b, c), d = mean - pixel, rounded operation by operation in the reference's order
+// (no fused multiply-adds), so that power is the oracle's bit for bit; gaussian = e^power,
+// evaluated as 2^(power log2 e).
 struct Falloff {
     float dx;
-    float2 dy, dxdy, dy2;
+    float2 dy;
     float2 gaussian;
     bool below0, below1;  // power <= 0
 };
@@ -191,12 +193,11 @@ __device__ __forceinline__ Falloff falloff(float4 a, float4 b, float fpx, float2
     Falloff f;
     f.dx = a.x - fpx;
     f.dy = add2(splat(a.y), neg2(fpy));
-    f.dxdy = mul2(splat(f.dx), f.dy);
-    f.dy2 = mul2(f.dy, f.dy);
-    const float2 quad = fma2(splat(b.x), f.dy2, splat(a.z * f.dx * f.dx));  // a dx^2 + c dy^2
-    const float2 power2 = fma2(splat(-0.5f * kLog2e), quad, mul2(splat(-kLog2e * a.w), f.dxdy));
-    f.below0 = power2.x <= 0.0f;
-    f.below1 = power2.y <= 0.0f;
+    const float2 quad = add2(splat(__fmul_rn(__fmul_rn(a.z, f.dx), f.dx)), mul2(mul2(splat(b.x), f.dy), f.dy));
+    const float2 power = add2(mul2(splat(-0.5f), quad), neg2(mul2(splat(__fmul_rn(a.w, f.dx)), f.dy)));
+    f.below0 = power.x <= 0.0f;
+    f.below1 = power.y <= 0.0f;
+    const float2 power2 = mul2(power, splat(kLog2e));
     f.gaussian = make_float2(exp2_approx(power2.x), exp2_approx(power2.y));
     return f;
 }
@@ -206,11 +207,10 @@ __device__ __forceinline__ float falloff1(float4 a, float4 b, float fpx, float f
                                           bool& below) {
     dx = a.x - fpx;
     dy = __fadd_rn(a.y, -fpy);
-    const float dxdy = __fmul_rn(dx, dy);
-    const float quad = __fmaf_rn(b.x, __fmul_rn(dy, dy), a.z * dx * dx);
-    const float power2 = __fmaf_rn(-0.5f * kLog2e, quad, __fmul_rn(-kLog2e * a.w, dxdy));
-    below = power2 <= 0.0f;
-    return exp2_approx(power2);
+    const float quad = __fadd_rn(__fmul_rn(__fmul_rn(a.z, dx), dx), __fmul_rn(__fmul_rn(b.x, dy), dy));
+    const float power = __fadd_rn(__fmul_rn(-0.5f, quad), -__fmul_rn(__fmul_rn(a.w, dx), dy));
+    below = power <= 0.0f;
+    return exp2_approx(__fmul_rn(power, kLog2e));
 }
 
 // Each warp walks the tile's list on its own, 32 entries at a time, over only the
@@ -552,8 +552,8 @@ __global__ void __launch_bounds__(kPairThreads, 6) k_blend_backward_atomic(
             const float2 d_mx = mul2(nd_power, fma2(splat(a.w), f.dy, splat(a.z * f.dx)));
             const float2 d_my = mul2(nd_power, fma2(splat(b.x), f.dy, splat(a.w * f.dx)));
             const float2 d_ca = mul2(nd_power, splat(0.5f * f.dx * f.dx));
-            const float2 d_cb = mul2(nd_power, f.dxdy);
-            const float2 d_cc = mul2(nd_power, mul2(splat(0.5f), f.dy2));
+            const float2 d_cb = mul2(mul2(nd_power, splat(f.dx)), f.dy);
+            const float2 d_cc = mul2(mul2(nd_power, mul2(splat(0.5f), f.dy)), f.dy);
             const float v[8] = {d_mx.x + d_mx.y, d_my.x + d_my.y, d_ca.x + d_ca.y, d_cb.x + d_cb.y,
                                 d_cc.x + d_cc.y, d_r.x + d_r.y,   d_g.x + d_g.y,   d_b.x + d_b.y};
             const float total = reduce8_transposed(v, lane);
