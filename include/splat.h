@@ -313,7 +313,8 @@ enum {
     SP_K_BLEND_BACKWARD = 8,
     SP_K_PROJECT_BACKWARD = 9,
     SP_K_ADAM = 10,
-    SP_K_COUNT = 11
+    SP_K_TILE_ORDER = 11, /* the blend kernels' tile schedule (no counterpart in the reference) */
+    SP_K_COUNT = 12
 };
 /* Starts (1) or stops (0) recording events around every kernel launch of the context. */
 sp_status sp_profile_enable(sp_context* ctx, int enable);

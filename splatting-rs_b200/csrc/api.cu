@@ -94,6 +94,7 @@ struct sp_rasterizer {
     uint32_t* sort_tickets = nullptr;
     unsigned long long* lookback = nullptr;
     uint2* ranges = nullptr;
+    uint32_t* tile_order = nullptr;
     float4* image = nullptr;
     uint32_t* contributions = nullptr;
     float4* ssim_partials = nullptr;
@@ -441,6 +442,7 @@ sp_status sp_rasterizer_create(sp_context* ctx, const float* d_params, uint64_t 
     SP_ALLOC(r->sort_tickets, kSortMaxPasses);
     SP_ALLOC(r->lookback, (size_t)std::max<uint32_t>(r->max_partitions, 1) * kSortRadix);
     SP_ALLOC(r->ranges, r->tiles);
+    SP_ALLOC(r->tile_order, r->tiles);
     SP_ALLOC(r->image, p);
     SP_ALLOC(r->contributions, p);
     SP_ALLOC(r->ssim_partials, p * 3);
@@ -520,9 +522,13 @@ sp_status sp_forward(sp_rasterizer* r) {
                 launch_ranges(r->plan, r->keys[r->sorted_buffer], r->meta, r->capacity, r->ranges, r->tiles, st));
     }
     {
+        KernelSpan span(ctx, SP_K_TILE_ORDER);
+        SP_CUDA(ctx, launch_tile_order(r->ranges, r->tiles, r->tile_order, st));
+    }
+    {
         KernelSpan span(ctx, SP_K_BLEND_FORWARD);
-        SP_CUDA(ctx, launch_blend_forward(r->records, r->values[r->sorted_buffer], r->ranges, r->camera, r->image,
-                                          r->contributions, st));
+        SP_CUDA(ctx, launch_blend_forward(r->records, r->values[r->sorted_buffer], r->ranges, r->tile_order,
+                                          r->camera, r->image, r->contributions, st));
     }
     r->forward_done = true;
     return SP_OK;
@@ -555,7 +561,8 @@ sp_status sp_backward(sp_rasterizer* r) {
         if (r->options.backward_mode == SP_BWD_ATOMIC)
             SP_CUDA(r->ctx, cudaMemsetAsync(r->gaussian_gradients, 0, r->n * 3 * sizeof(float4), st));
         SP_CUDA(r->ctx, launch_blend_backward((int)r->options.backward_mode, r->records,
-                                              r->values[r->sorted_buffer], r->ranges, r->offsets, r->camera,
+                                              r->values[r->sorted_buffer], r->ranges, r->tile_order, r->offsets,
+                                              r->camera,
                                               r->image, r->contributions, r->loss_gradient, r->slot_gradients,
                                               r->gaussian_gradients, st));
     }

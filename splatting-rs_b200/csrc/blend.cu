@@ -219,11 +219,12 @@ __device__ __forceinline__ float falloff1(float4 a, float4 b, float fpx, float f
 __global__ void __launch_bounds__(kPairThreads, 8) k_blend_forward(const float4* __restrict__ records,
                                                                    const uint32_t* __restrict__ sorted,
                                                                    const uint2* __restrict__ ranges,
+                                                                   const uint32_t* __restrict__ order,
                                                                    const sp_camera_uniform cam,
                                                                    float4* __restrict__ image,
                                                                    uint32_t* __restrict__ contributions) {
     __shared__ WarpStage s_stage[kPairWarps];
-    const uint32_t tile = blockIdx.x;
+    const uint32_t tile = order[blockIdx.x];
     const uint32_t gx = tile % cam.tiles_x, gy = tile / cam.tiles_x;
     const uint32_t warp = threadIdx.x / 32, lane = lane_id();
     const uint32_t bx = gx * SP_TILE + ((warp & 1u) << 3), by = gy * SP_TILE + ((warp >> 1) << 3);
@@ -325,7 +326,8 @@ __device__ __forceinline__ float reduce8_transposed(const float v[8], uint32_t l
 template <int MODE>
 __global__ void __launch_bounds__(kTilePixels) k_blend_backward(
     const float4* __restrict__ records, const uint32_t* __restrict__ sorted, const uint2* __restrict__ ranges,
-    const uint32_t* __restrict__ offsets, const sp_camera_uniform cam, const float4* __restrict__ image,
+    const uint32_t* __restrict__ order, const uint32_t* __restrict__ offsets, const sp_camera_uniform cam,
+    const float4* __restrict__ image,
     const uint32_t* __restrict__ contributions, const float4* __restrict__ loss_gradient,
     float* __restrict__ slot_gradients, float4* __restrict__ gaussian_gradients) {
     constexpr bool kDet = MODE == SP_BWD_DETERMINISTIC;
@@ -339,7 +341,7 @@ __global__ void __launch_bounds__(kTilePixels) k_blend_backward(
     __shared__ float s_part[kDet ? B : 1][kWarps][9];
     __shared__ uint32_t s_limit;
 
-    const uint32_t tile = blockIdx.x;
+    const uint32_t tile = order[blockIdx.x];
     const uint32_t gx = tile % cam.tiles_x, gy = tile / cam.tiles_x;
     const uint32_t t = threadIdx.x, lane = lane_id(), warp = t / 32;
     const uint32_t px = gx * SP_TILE + local_x(warp, lane), py = gy * SP_TILE + local_y(warp, lane);
@@ -479,10 +481,11 @@ __global__ void __launch_bounds__(kTilePixels) k_blend_backward(
 // lanes at once.
 __global__ void __launch_bounds__(kPairThreads, 6) k_blend_backward_atomic(
     const float4* __restrict__ records, const uint32_t* __restrict__ sorted, const uint2* __restrict__ ranges,
-    const sp_camera_uniform cam, const float4* __restrict__ image, const uint32_t* __restrict__ contributions,
-    const float4* __restrict__ loss_gradient, float4* __restrict__ gaussian_gradients) {
+    const uint32_t* __restrict__ order, const sp_camera_uniform cam, const float4* __restrict__ image,
+    const uint32_t* __restrict__ contributions, const float4* __restrict__ loss_gradient,
+    float4* __restrict__ gaussian_gradients) {
     __shared__ WarpStage s_stage[kPairWarps];
-    const uint32_t tile = blockIdx.x;
+    const uint32_t tile = order[blockIdx.x];
     const uint32_t gx = tile % cam.tiles_x, gy = tile / cam.tiles_x;
     const uint32_t warp = threadIdx.x / 32, lane = lane_id();
     const uint32_t bx = gx * SP_TILE + ((warp & 1u) << 3), by = gy * SP_TILE + ((warp >> 1) << 3);
@@ -566,6 +569,57 @@ __global__ void __launch_bounds__(kPairThreads, 6) k_blend_backward_atomic(
     }
 }
 
+// Tiles in decreasing order of list length: a counting sort on the length's quarter-octave
+// bucket (the bit length and the two bits below the leading one), by one block; the order
+// within a bucket is the atomics' and does not matter, each tile's results being its own.
+constexpr int kOrderThreads = 1024;
+constexpr int kOrderBuckets = 129;  // 128 for lengths 1 .. 2^32 - 1, the last for empty tiles
+
+__device__ __forceinline__ uint32_t order_bucket(uint2 range) {
+    const uint32_t count = range.y - range.x;
+    if (count == 0) return kOrderBuckets - 1;
+    const uint32_t msb = 31u - __clz(count);
+    const uint32_t below = msb >= 2 ? (count >> (msb - 2)) & 3u : (count << (2 - msb)) & 3u;
+    return 127u - (msb * 4u + below);
+}
+
+__global__ void __launch_bounds__(kOrderThreads) k_tile_order(const uint2* __restrict__ ranges, uint32_t tiles,
+                                                              uint32_t* __restrict__ order) {
+    __shared__ uint32_t s_next[kOrderBuckets];
+    const uint32_t t = threadIdx.x;
+    for (uint32_t b = t; b < kOrderBuckets; b += kOrderThreads) s_next[b] = 0;
+    __syncthreads();
+    for (uint32_t tile = t; tile < tiles; tile += kOrderThreads) atomicAdd(&s_next[order_bucket(ranges[tile])], 1u);
+    __syncthreads();
+    if (t < 32) {
+        // Exclusive scan of the bucket sizes: 5 consecutive buckets per lane, then the lanes.
+        constexpr int kPer = (kOrderBuckets + 31) / 32;
+        uint32_t own[kPer], total = 0;
+#pragma unroll
+        for (int k = 0; k < kPer; ++k) {
+            const uint32_t b = t * kPer + k;
+            own[k] = b < kOrderBuckets ? s_next[b] : 0u;
+            total += own[k];
+        }
+        uint32_t inclusive = total;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const uint32_t v = __shfl_up_sync(kFull, inclusive, o);
+            if (t >= (uint32_t)o) inclusive += v;
+        }
+        uint32_t start = inclusive - total;
+#pragma unroll
+        for (int k = 0; k < kPer; ++k) {
+            const uint32_t b = t * kPer + k;
+            if (b < kOrderBuckets) s_next[b] = start;
+            start += own[k];
+        }
+    }
+    __syncthreads();
+    for (uint32_t tile = t; tile < tiles; tile += kOrderThreads)
+        order[atomicAdd(&s_next[order_bucket(ranges[tile])], 1u)] = tile;
+}
+
 // The forward's per-pixel walk without the colour, counting the entries visited (up to
 // and including the terminating one), plus the contributor counts the backward replays.
 __global__ void __launch_bounds__(kTilePixels) k_count_blend(const float4* __restrict__ records,
@@ -617,26 +671,34 @@ cudaError_t launch_count_blend(const float4* records, const uint32_t* sorted_gau
     return cudaGetLastError();
 }
 
+cudaError_t launch_tile_order(const uint2* ranges, uint32_t tiles, uint32_t* order, cudaStream_t stream) {
+    k_tile_order<<<1, kOrderThreads, 0, stream>>>(ranges, tiles, order);
+    return cudaGetLastError();
+}
+
 cudaError_t launch_blend_forward(const float4* records, const uint32_t* sorted_gaussians, const uint2* ranges,
-                                 const sp_camera_uniform& cam, float4* image, uint32_t* contributions,
-                                 cudaStream_t stream) {
+                                 const uint32_t* order, const sp_camera_uniform& cam, float4* image,
+                                 uint32_t* contributions, cudaStream_t stream) {
     const unsigned tiles = cam.tiles_x * cam.tiles_y;
-    k_blend_forward<<<tiles, kPairThreads, 0, stream>>>(records, sorted_gaussians, ranges, cam, image, contributions);
+    k_blend_forward<<<tiles, kPairThreads, 0, stream>>>(records, sorted_gaussians, ranges, order, cam, image,
+                                                        contributions);
     return cudaGetLastError();
 }
 
 cudaError_t launch_blend_backward(int mode, const float4* records, const uint32_t* sorted_gaussians,
-                                  const uint2* ranges, const uint32_t* offsets, const sp_camera_uniform& cam,
-                                  const float4* image, const uint32_t* contributions, const float4* loss_gradient,
-                                  float* slot_gradients, float4* gaussian_gradients, cudaStream_t stream) {
+                                  const uint2* ranges, const uint32_t* order, const uint32_t* offsets,
+                                  const sp_camera_uniform& cam, const float4* image, const uint32_t* contributions,
+                                  const float4* loss_gradient, float* slot_gradients, float4* gaussian_gradients,
+                                  cudaStream_t stream) {
     const unsigned tiles = cam.tiles_x * cam.tiles_y;
     if (mode == SP_BWD_DETERMINISTIC)
         k_blend_backward<SP_BWD_DETERMINISTIC><<<tiles, kTilePixels, 0, stream>>>(
-            records, sorted_gaussians, ranges, offsets, cam, image, contributions, loss_gradient, slot_gradients,
-            gaussian_gradients);
+            records, sorted_gaussians, ranges, order, offsets, cam, image, contributions, loss_gradient,
+            slot_gradients, gaussian_gradients);
     else
-        k_blend_backward_atomic<<<tiles, kPairThreads, 0, stream>>>(records, sorted_gaussians, ranges, cam, image,
-                                                                    contributions, loss_gradient, gaussian_gradients);
+        k_blend_backward_atomic<<<tiles, kPairThreads, 0, stream>>>(records, sorted_gaussians, ranges, order, cam,
+                                                                    image, contributions, loss_gradient,
+                                                                    gaussian_gradients);
     return cudaGetLastError();
 }
 

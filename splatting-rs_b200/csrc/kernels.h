@@ -55,16 +55,20 @@ cudaError_t launch_ranges(const SortPlan& plan, const void* keys, const DeviceMe
 
 // ---- blend.cu
 
-// rasterize_forward.wgsl:22-88.
+// The blend kernels' schedule: the tiles in decreasing order of list length (to a quarter
+// octave), so that the longest tiles start first and the short ones fill the last wave.
+cudaError_t launch_tile_order(const uint2* ranges, uint32_t tiles, uint32_t* order, cudaStream_t stream);
+// rasterize_forward.wgsl:22-88; block b blends tile order[b].
 cudaError_t launch_blend_forward(const float4* records, const uint32_t* sorted_gaussians, const uint2* ranges,
-                                 const sp_camera_uniform& cam, float4* image, uint32_t* contributions,
-                                 cudaStream_t stream);
+                                 const uint32_t* order, const sp_camera_uniform& cam, float4* image,
+                                 uint32_t* contributions, cudaStream_t stream);
 // rasterize_backward.wgsl:30-133. mode SP_BWD_*: slot sums (deterministic) or atomics
 // into gaussian_gradients (3 float4 per Gaussian, zeroed by the caller).
 cudaError_t launch_blend_backward(int mode, const float4* records, const uint32_t* sorted_gaussians,
-                                  const uint2* ranges, const uint32_t* offsets, const sp_camera_uniform& cam,
-                                  const float4* image, const uint32_t* contributions, const float4* loss_gradient,
-                                  float* slot_gradients, float4* gaussian_gradients, cudaStream_t stream);
+                                  const uint2* ranges, const uint32_t* order, const uint32_t* offsets,
+                                  const sp_camera_uniform& cam, const float4* image, const uint32_t* contributions,
+                                  const float4* loss_gradient, float* slot_gradients, float4* gaussian_gradients,
+                                  cudaStream_t stream);
 
 // The work the blend kernels do for the current state: counts[0] += entries the forward
 // visits per pixel (through the terminating one), counts[1] += contributors per pixel.

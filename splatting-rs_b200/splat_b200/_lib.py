@@ -43,6 +43,7 @@ KERNEL_NAMES = (
     "blend_backward",
     "project_backward",
     "adam",
+    "tile_order",
 )
 
 

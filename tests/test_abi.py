@@ -113,3 +113,12 @@ def test_python_mirror_refuses_host_tensors():
 
     with pytest.raises(ValueError):
         sb.Rasterizer._pointer(torch.zeros(4))
+
+
+def test_profiler_kernel_names_follow_the_header_enum():
+    """KERNEL_NAMES indexes sp_profile_read's arrays: one name per SP_K_* value, in order."""
+    text = (ROOT / "include" / "splat.h").read_text()
+    values = {m.group(1).lower(): int(m.group(2)) for m in re.finditer(r"SP_K_(\w+) = (\d+)", text)}
+    count = values.pop("count")
+    assert count == len(_lib.KERNEL_NAMES)
+    assert [name for name, _ in sorted(values.items(), key=lambda kv: kv[1])] == list(_lib.KERNEL_NAMES)
