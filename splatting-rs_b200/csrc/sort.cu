@@ -20,10 +20,12 @@ namespace {
 
 constexpr uint32_t kFlagAggregate = 1u;
 constexpr uint32_t kFlagInclusive = 2u;
-// Look-back polls before a partition gives up and raises SP_ERR_TIMEOUT. Each poll
-// sleeps ~100 ns, so the limit is far above any legitimate wait (a predecessor partition
-// takes microseconds) and bounds a stuck wait to well under a second.
-constexpr uint32_t kLookbackSpinLimit = 1u << 22;
+// Look-back polls that find a predecessor not yet posted before a partition gives up and
+// raises SP_ERR_TIMEOUT. Each such poll costs an L2 round trip plus a ~32 ns sleep, so the
+// limit is far above any legitimate wait (a predecessor partition takes microseconds) and
+// bounds a stuck wait to well under a second.
+constexpr uint32_t kLookbackSpinLimit = 1u << 21;
+constexpr int kLookbackWindow = 8;
 
 template <typename Key>
 __device__ __forceinline__ Key make_key(int key_mode, uint32_t tile, float depth) {
@@ -207,23 +209,44 @@ __global__ void __launch_bounds__(kSortThreads, kSortBlocksPerSM)
                 mine.store(tag | ((unsigned long long)kFlagInclusive << 30) | total, cuda::memory_order_relaxed);
             } else {
                 mine.store(tag | ((unsigned long long)kFlagAggregate << 30) | total, cuda::memory_order_relaxed);
+                // Walk back kLookbackWindow predecessors per round trip: read them all, then
+                // add in order up to the first inclusive prefix or the first not yet posted.
                 uint32_t spins = 0;
-                for (int64_t k = (int64_t)part - 1; k >= 0;) {
-                    cuda::atomic_ref<unsigned long long, cuda::thread_scope_device> other(
-                        lookback[(size_t)k * kSortRadix + t]);
-                    const unsigned long long e = other.load(cuda::memory_order_relaxed);
-                    const uint32_t flag = (uint32_t)(e >> 30) & 3u;
-                    if ((uint32_t)(e >> 32) != sequence || flag == 0u) {
+                int64_t k = (int64_t)part - 1;
+                for (;;) {
+                    unsigned long long e[kLookbackWindow];
+#pragma unroll
+                    for (int w = 0; w < kLookbackWindow; ++w) {
+                        e[w] = 0ull;
+                        if (k - w >= 0) {
+                            cuda::atomic_ref<unsigned long long, cuda::thread_scope_device> other(
+                                lookback[(size_t)(k - w) * kSortRadix + t]);
+                            e[w] = other.load(cuda::memory_order_relaxed);
+                        }
+                    }
+                    int taken = 0;
+                    bool inclusive = false, waiting = false;
+#pragma unroll
+                    for (int w = 0; w < kLookbackWindow; ++w) {
+                        if (inclusive || waiting) continue;
+                        const uint32_t flag = (uint32_t)(e[w] >> 30) & 3u;
+                        if (k - w < 0 || (uint32_t)(e[w] >> 32) != sequence || flag == 0u) {
+                            waiting = true;
+                            continue;
+                        }
+                        prefix += (uint32_t)(e[w] & 0x3fffffffull);
+                        ++taken;
+                        inclusive = flag == kFlagInclusive;
+                    }
+                    if (inclusive) break;
+                    k -= taken;
+                    if (waiting) {
                         if (++spins > kLookbackSpinLimit) {
                             raise_status(meta, SP_ERR_TIMEOUT);
                             break;
                         }
-                        __nanosleep(100);
-                        continue;
+                        __nanosleep(32);
                     }
-                    prefix += (uint32_t)(e & 0x3fffffffull);
-                    if (flag == kFlagInclusive) break;
-                    --k;
                 }
                 mine.store(tag | ((unsigned long long)kFlagInclusive << 30) | (prefix + total),
                            cuda::memory_order_relaxed);
