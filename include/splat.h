@@ -264,8 +264,20 @@ sp_status sp_loss_sums_noalloc(int device, const float* d_pixel_loss, uint64_t p
 /* read_intersections (rasterizer.rs:536-544): fills `out` and returns SP_ERR_OVERFLOW when
  * the list overflowed (where the reference panics). */
 sp_status sp_read_intersections(sp_rasterizer* r, sp_intersection_meta* out);
+/* sp_backward then sp_adam_step(adam, position_rate_factor) in one pass over the
+ * parameters: the projection backward applies the Adam update and the scale clamp to each
+ * Gaussian as soon as its gradient is complete, so the parameter gradients are not written
+ * (sp_param_gradients / sp_read_param_gradients then hold stale values). The camera
+ * gradient, densify statistics and blend sums are produced as by sp_backward. `adam` must
+ * be over this rasterizer's own parameters and gradient buffer, and the rasterizer must not
+ * accumulate gradients. Parameters and moments equal those of the two separate calls bit for
+ * bit. No counterpart in the reference, whose Trainer::step_async (training.rs:203-204)
+ * encodes the two passes one after the other. */
+sp_status sp_backward_adam(sp_rasterizer* r, sp_adam* adam, float position_rate_factor);
 /* Trainer::step_async (training.rs:197-209) in one call: set the camera, forward, loss
- * against `view`, backward, one Adam step at `position_rate_factor`; then, if either
+ * against `view`, backward, one Adam step at `position_rate_factor` (the last two fused as
+ * by sp_backward_adam unless the rasterizer accumulates gradients or `adam` is over other
+ * buffers); then, if either
  * output is non-NULL, the camera gradient (56 B) and the loss terms (32 B) are copied to
  * pinned host memory and the stream is synchronised once — the per-step read-back the
  * reference's pose refinement does (training.rs:205-208). */
@@ -314,7 +326,8 @@ enum {
     SP_K_PROJECT_BACKWARD = 9,
     SP_K_ADAM = 10,
     SP_K_TILE_ORDER = 11, /* the blend kernels' tile schedule (no counterpart in the reference) */
-    SP_K_COUNT = 12
+    SP_K_BACKWARD_ADAM = 12, /* projection backward with the Adam step fused (sp_backward_adam) */
+    SP_K_COUNT = 13
 };
 /* Starts (1) or stops (0) recording events around every kernel launch of the context. */
 sp_status sp_profile_enable(sp_context* ctx, int enable);

@@ -551,28 +551,59 @@ sp_status sp_loss(sp_rasterizer* r, uint32_t view) {
     return SP_OK;
 }
 
+namespace {
+
+// The blend backward (K8) of sp_backward and sp_backward_adam.
+sp_status blend_backward(sp_rasterizer* r) {
+    cudaStream_t st = r->ctx->stream;
+    KernelSpan span(r->ctx, SP_K_BLEND_BACKWARD);
+    if (r->options.backward_mode == SP_BWD_ATOMIC)
+        SP_CUDA(r->ctx, cudaMemsetAsync(r->gaussian_gradients, 0, r->n * 3 * sizeof(float4), st));
+    SP_CUDA(r->ctx, launch_blend_backward((int)r->options.backward_mode, r->records, r->values[r->sorted_buffer],
+                                          r->ranges, r->tile_order, r->offsets, r->camera, r->image,
+                                          r->contributions, r->loss_gradient, r->slot_gradients,
+                                          r->gaussian_gradients, st));
+    return SP_OK;
+}
+
+}  // namespace
+
+sp_status sp_backward_adam(sp_rasterizer* r, sp_adam* adam, float position_rate_factor) {
+    if (!r || !adam) return SP_ERR_INVALID;
+    SP_REQUIRE(r->ctx, r->forward_done, SP_ERR_INVALID, "backward before any forward pass");
+    SP_REQUIRE(r->ctx,
+               adam->params == r->params && adam->gradients == r->param_gradients && adam->n == r->n &&
+                   adam->stride == r->stride,
+               SP_ERR_INVALID, "the Adam state does not belong to this rasterizer's parameters");
+    SP_REQUIRE(r->ctx, !r->options.accumulate_gradients, SP_ERR_INVALID,
+               "a fused step cannot accumulate gradients over views");
+    SP_CHECK(select_device(r->ctx));
+    SP_CHECK(sp_adam_advance(adam, position_rate_factor));
+    SP_CHECK(blend_backward(r));
+    AdamLaunch step{adam->params, adam->first_moment, adam->second_moment, adam->lr_by_slot.data(),
+                    adam->bias1, adam->bias2, adam->max_log_scale, adam->max_log_anisotropy};
+    KernelSpan span(r->ctx, SP_K_BACKWARD_ADAM);
+    SP_CUDA(r->ctx, launch_project_backward(r->params, r->n, (int)r->options.sh_degree, (int)r->options.backward_mode,
+                                            r->camera, r->records, r->radii, r->offsets, r->slot_gradients,
+                                            r->capacity, r->gaussian_gradients, r->param_gradients, 0,
+                                            r->camera_partials, r->camera_done, r->camera_gradient,
+                                            r->densify_stats, &step, r->ctx->stream));
+    return SP_OK;
+}
+
 sp_status sp_backward(sp_rasterizer* r) {
     if (!r) return SP_ERR_INVALID;
     SP_REQUIRE(r->ctx, r->forward_done, SP_ERR_INVALID, "backward before any forward pass");
     SP_CHECK(select_device(r->ctx));
     cudaStream_t st = r->ctx->stream;
-    {
-        KernelSpan span(r->ctx, SP_K_BLEND_BACKWARD);
-        if (r->options.backward_mode == SP_BWD_ATOMIC)
-            SP_CUDA(r->ctx, cudaMemsetAsync(r->gaussian_gradients, 0, r->n * 3 * sizeof(float4), st));
-        SP_CUDA(r->ctx, launch_blend_backward((int)r->options.backward_mode, r->records,
-                                              r->values[r->sorted_buffer], r->ranges, r->tile_order, r->offsets,
-                                              r->camera,
-                                              r->image, r->contributions, r->loss_gradient, r->slot_gradients,
-                                              r->gaussian_gradients, st));
-    }
+    SP_CHECK(blend_backward(r));
     {
         KernelSpan span(r->ctx, SP_K_PROJECT_BACKWARD);
         SP_CUDA(r->ctx, launch_project_backward(
                             r->params, r->n, (int)r->options.sh_degree, (int)r->options.backward_mode, r->camera,
                             r->records, r->radii, r->offsets, r->slot_gradients, r->capacity, r->gaussian_gradients,
                             r->param_gradients, (int)r->options.accumulate_gradients, r->camera_partials,
-                            r->camera_done, r->camera_gradient, r->densify_stats, st));
+                            r->camera_done, r->camera_gradient, r->densify_stats, nullptr, st));
     }
     return SP_OK;
 }
@@ -682,8 +713,12 @@ sp_status sp_train_step(sp_rasterizer* r, sp_adam* adam, const sp_camera_uniform
     SP_CHECK(sp_set_camera(r, camera));
     SP_CHECK(sp_forward(r));
     SP_CHECK(sp_loss(r, view));
-    SP_CHECK(sp_backward(r));
-    SP_CHECK(sp_adam_step(adam, position_rate_factor));
+    if (!r->options.accumulate_gradients && adam->params == r->params && adam->gradients == r->param_gradients) {
+        SP_CHECK(sp_backward_adam(r, adam, position_rate_factor));
+    } else {
+        SP_CHECK(sp_backward(r));
+        SP_CHECK(sp_adam_step(adam, position_rate_factor));
+    }
     if (!camera_gradient_out && !loss_out) return SP_OK;
     cudaStream_t st = r->ctx->stream;
     SP_CUDA(r->ctx, cudaMemcpyAsync(&r->readback->status, &r->meta->status, sizeof(uint32_t), cudaMemcpyDeviceToHost,

@@ -25,13 +25,25 @@ cudaError_t launch_scan_blocks(const uint32_t* block_totals, unsigned long long*
                                cudaStream_t stream);
 // project_backward.wgsl:30-227 + reduce_camera_gradient.wgsl:10-34, fused (last block
 // done). Blend sums come per Gaussian (atomic mode) or per slot (deterministic mode).
+// One Adam step for the projection backward to apply in place of writing the parameter
+// gradients (the parameters are the projection's own).
+struct AdamLaunch {
+    float* params;
+    float* first_moment;
+    float* second_moment;
+    const float* lr_by_slot;  // host, one rate per parameter slot
+    float bias1, bias2, max_log_scale, max_log_anisotropy;
+};
+// project_backward.wgsl plus reduce_camera_gradient.wgsl; with `adam` non-null the
+// parameter gradients are not written but consumed by that Adam step (adam.wgsl,
+// clamp_scales.wgsl) in the same kernel.
 cudaError_t launch_project_backward(const float* params, uint64_t n, int sh_degree, int mode,
                                     const sp_camera_uniform& cam,
                                     const float4* records, const uint32_t* radii, const uint32_t* offsets,
                                     const float* slot_gradients, uint64_t capacity, const float4* gaussian_gradients,
                                     float* param_gradients, int accumulate, float* camera_partials,
                                     uint32_t* camera_done, float* camera_gradient, float4* densify_stats,
-                                    cudaStream_t stream);
+                                    const AdamLaunch* adam, cudaStream_t stream);
 // The reference's 80-B Projected records (diagnostics).
 cudaError_t launch_to_projected(const float4* records, const uint32_t* radii, uint64_t n, sp_projected* out,
                                 cudaStream_t stream);

@@ -5,6 +5,7 @@
 // exactly), and the backward shares the same forward recomputation.
 #include <cuda/atomic>
 
+#include "adam_math.cuh"
 #include "kernels.h"
 #include "project_math.cuh"
 
@@ -390,21 +391,34 @@ __device__ __forceinline__ void project_backward_one(float* p, uint32_t g, const
     for (int k = 0; k < 4; ++k) p[SP_SLOT_ROTATION + k] = (du[k] - geo.q[k] * qdu) / geo.q_length;
 }
 
-template <int DEG, int MODE>
+// FUSED: Adam and the scale clamp are applied to the block's Gaussians as soon as their
+// gradients are complete (adam_block), instead of writing the gradients out for a separate
+// Adam pass; `adam` then holds the parameters (the same buffer as `params`, written after
+// every read of it) and the moments.
+struct FusedAdam {
+    float* params;
+    float* first_moment;
+    float* second_moment;
+    AdamStep step;
+};
+
+template <int DEG, int MODE, bool FUSED>
 __global__ void __launch_bounds__(kBlock, 3) k_project_backward(
-    const float* __restrict__ params, uint32_t n, const sp_camera_uniform cam, const float4* __restrict__ records,
+    const float* params, uint32_t n, const sp_camera_uniform cam, const float4* __restrict__ records,
     const uint32_t* __restrict__ radii, const uint32_t* __restrict__ offsets, const float* __restrict__ slot_gradients,
     unsigned long long capacity, const float4* __restrict__ gaussian_gradients, float* __restrict__ param_gradients,
     int accumulate, float* __restrict__ camera_partials, uint32_t* camera_done, float* __restrict__ camera_gradient,
-    float4* __restrict__ densify_stats) {
+    float4* __restrict__ densify_stats, const FusedAdam adam) {
     constexpr int S = SP_PARAM_STRIDE(DEG);
     extern __shared__ float4 smem4[];
     float* sp = reinterpret_cast<float*>(smem4);
     __shared__ float warp_camera[kBlock / 32][SP_CAMERA_GRAD_STRIDE];
+    __shared__ float s_lr[FUSED ? S : 1];
     __shared__ bool last_block;
     const uint32_t g0 = blockIdx.x * kBlock;
     const uint32_t here = min((uint32_t)kBlock, n - g0);
     stage_in(params + (size_t)g0 * S, here * S, sp);
+    if (FUSED && threadIdx.x < (uint32_t)S) s_lr[threadIdx.x] = adam.step.lr[threadIdx.x];
     __syncthreads();
     const uint32_t t = threadIdx.x;
     float cgrad[SP_CAMERA_GRAD_STRIDE];
@@ -414,9 +428,14 @@ __global__ void __launch_bounds__(kBlock, 3) k_project_backward(
         project_backward_one<DEG, MODE>(sp + t * S, g0 + t, cam, records, radii[g0 + t], offsets, slot_gradients,
                                         capacity, gaussian_gradients, densify_stats, cgrad);
     __syncthreads();
-    // The gradients, coalesced out of shared memory.
-    float* out = param_gradients + (size_t)g0 * S;
-    for (uint32_t i = t; i < here * S; i += kBlock) out[i] = accumulate ? out[i] + sp[i] : sp[i];
+    if constexpr (FUSED) {
+        adam_block<S>(adam.params, adam.first_moment, adam.second_moment, g0, here, sp, s_lr, adam.step);
+        __syncthreads();  // sp is reused by the last block below
+    } else {
+        // The gradients, coalesced out of shared memory.
+        float* out = param_gradients + (size_t)g0 * S;
+        for (uint32_t i = t; i < here * S; i += kBlock) out[i] = accumulate ? out[i] + sp[i] : sp[i];
+    }
     // The block's camera partial: warp sums, then the 8 warps in order.
     const uint32_t lane = lane_id(), warp = t / 32;
 #pragma unroll
@@ -535,17 +554,34 @@ cudaError_t launch_project_backward(const float* params, uint64_t n, int sh_degr
                                     const uint32_t* offsets, const float* slot_gradients, uint64_t capacity,
                                     const float4* gaussian_gradients, float* param_gradients, int accumulate,
                                     float* camera_partials, uint32_t* camera_done, float* camera_gradient,
-                                    float4* densify_stats, cudaStream_t stream) {
+                                    float4* densify_stats, const AdamLaunch* adam, cudaStream_t stream) {
     const unsigned grid = grid_for(n, kBlock);
     const size_t smem = (size_t)kBlock * SP_PARAM_STRIDE(sh_degree) * sizeof(float);
     cudaError_t err = cudaSuccess;
-#define SPLAT_PB(D, M)                                                                                      \
-    if (sh_degree == D && mode == M) {                                                                      \
-        if ((err = set_smem(k_project_backward<D, M>, smem)) != cudaSuccess) return err;                    \
-        k_project_backward<D, M><<<grid, kBlock, smem, stream>>>(                                           \
-            params, (uint32_t)n, cam, records, radii, offsets, slot_gradients, capacity, gaussian_gradients, \
-            param_gradients, accumulate, camera_partials, camera_done, camera_gradient, densify_stats);     \
-        return cudaGetLastError();                                                                          \
+    FusedAdam fused{};
+    if (adam) {
+        fused.params = adam->params;
+        fused.first_moment = adam->first_moment;
+        fused.second_moment = adam->second_moment;
+        for (int k = 0; k < SP_PARAM_STRIDE(sh_degree); ++k) fused.step.lr[k] = adam->lr_by_slot[k];
+        fused.step.bias1 = adam->bias1;
+        fused.step.bias2 = adam->bias2;
+        fused.step.max_log_scale = adam->max_log_scale;
+        fused.step.max_log_anisotropy = adam->max_log_anisotropy;
+    }
+#define SPLAT_PB_ONE(D, M, F)                                                                                   \
+    if ((err = set_smem(k_project_backward<D, M, F>, smem)) != cudaSuccess) return err;                         \
+    k_project_backward<D, M, F><<<grid, kBlock, smem, stream>>>(                                                \
+        params, (uint32_t)n, cam, records, radii, offsets, slot_gradients, capacity, gaussian_gradients,         \
+        param_gradients, accumulate, camera_partials, camera_done, camera_gradient, densify_stats, fused);      \
+    return cudaGetLastError();
+#define SPLAT_PB(D, M)                    \
+    if (sh_degree == D && mode == M) {    \
+        if (adam) {                       \
+            SPLAT_PB_ONE(D, M, true)      \
+        } else {                          \
+            SPLAT_PB_ONE(D, M, false)     \
+        }                                 \
     }
     SPLAT_PB(0, SP_BWD_DETERMINISTIC)
     SPLAT_PB(0, SP_BWD_ATOMIC)
@@ -556,6 +592,7 @@ cudaError_t launch_project_backward(const float* params, uint64_t n, int sh_degr
     SPLAT_PB(3, SP_BWD_DETERMINISTIC)
     SPLAT_PB(3, SP_BWD_ATOMIC)
 #undef SPLAT_PB
+#undef SPLAT_PB_ONE
     return cudaErrorInvalidValue;
 }
 

@@ -44,6 +44,7 @@ KERNEL_NAMES = (
     "project_backward",
     "adam",
     "tile_order",
+    "backward_adam",
 )
 
 
@@ -200,6 +201,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "sp_loss_sums_noalloc": (c_int, [c_int, _P, c_uint64, _P, _P]),
     "sp_read_intersections": (c_int, [_P, POINTER(IntersectionMeta)]),
     "sp_render": (c_int, [_P, POINTER(CameraUniform), _P]),
+    "sp_backward_adam": (c_int, [_P, _P, c_float]),
     "sp_train_step": (
         c_int, [_P, _P, POINTER(CameraUniform), c_uint32, c_float, POINTER(CameraGradient), POINTER(LossTermsC)]
     ),

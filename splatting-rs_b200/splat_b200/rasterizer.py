@@ -343,6 +343,11 @@ class Rasterizer:
             self._check(status, "read_intersections")
         return out
 
+    def encode_backward_adam(self, adam, rate_factor: float) -> None:
+        """encode_backward then adam.encode_step(rate_factor) as one fused pass
+        (sp_backward_adam); the parameter gradients are consumed, not written."""
+        self._check(self.lib.sp_backward_adam(self.handle, adam.handle, float(rate_factor)), "backward_adam")
+
     def train_step(self, adam, camera: PinholeCamera | CameraUniform, view: int, rate_factor: float,
                    read_back: bool = True):
         """One whole training step (Trainer::step_async, training.rs:197-209) in one call;

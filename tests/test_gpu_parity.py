@@ -301,3 +301,55 @@ def test_everything_culled(ctx):
     rast.write_loss_gradient(np.ones(40 * 30 * 4, np.float32))
     rast.encode_backward()
     assert np.all(rast.read_param_gradients() == 0.0)
+
+
+@pytest.mark.parametrize("sh_degree", [0, 3])
+def test_fused_backward_adam_equals_backward_then_adam(ctx, sh_degree):
+    """sp_backward_adam against sp_backward then sp_adam_step (deterministic backward, 3
+    steps): parameters, both moments, camera gradient and densify statistics bit for bit."""
+    import torch
+
+    rng = np.random.default_rng(5 + sh_degree)
+    cloud = random_cloud(3000, rng, sh_degree=sh_degree)
+    camera = camera_at_origin(160, 120, 120.0)
+    gt = np.random.default_rng(2).uniform(0, 1, 160 * 120 * 4).astype(np.float32)
+    runs = []
+    for fused in (False, True):
+        rast, params, _ = make_rasterizer(ctx, cloud, camera, ground_truth=gt,
+                                          backward_mode=sb.SP_BWD_DETERMINISTIC)
+        adam = sb.Adam(ctx, params, rast, len(cloud), sb.LEARNING_RATES_3DGS, 2.5, sh_degree=sh_degree)
+        cams = []
+        for step in range(3):
+            factor = sb.position_rate_factor(step, 10)
+            rast.encode_forward()
+            rast.encode_loss(0)
+            if fused:
+                rast.encode_backward_adam(adam, factor)
+            else:
+                rast.encode_backward()
+                adam.encode_step(factor)
+            cams.append(bytes(rast.read_camera_gradient()))
+        m, v = adam.read_moments()
+        runs.append((params.cpu().numpy().copy(), m, v, cams, rast.read_densify_stats().copy()))
+        assert adam.steps_taken() == 3
+        del adam, rast
+    for a, b in zip(runs[0], runs[1]):
+        if isinstance(a, list):
+            assert a == b
+        else:
+            assert np.array_equal(np.asarray(a).view(np.uint32), np.asarray(b).view(np.uint32))
+
+
+def test_fused_backward_adam_rejects_foreign_state(ctx):
+    import torch
+
+    cloud = random_cloud(200, np.random.default_rng(3))
+    camera = camera_at_origin(64, 48, 50.0)
+    rast, params, _ = make_rasterizer(ctx, cloud, camera)
+    other = torch.zeros_like(params)
+    adam = sb.Adam(ctx, other, rast, len(cloud), sb.LEARNING_RATES_3DGS, 2.5)
+    rast.encode_forward()
+    rast.encode_loss(0)
+    with pytest.raises(sb.SplatError) as err:
+        rast.encode_backward_adam(adam, 1.0)
+    assert err.value.status == sb._lib.SP_ERR_INVALID
