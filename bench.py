@@ -43,6 +43,12 @@ FP32_LANES_PER_SM = 128
 FORWARD_OPS_PER_PAIR = 20
 BACKWARD_OPS_PER_PAIR = 48
 
+# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) per launch of the heaviest kernels,
+# from one ncu --set full capture of this workload each (profiles/blend_kernels_config2.txt,
+# profiles/project_backward_adam_config2.txt; cold caches, so an upper bound on the in-bench
+# traffic).
+NCU_TRAFFIC_BYTES = {"blend_backward": 80.1e6, "blend_forward": 30.0e6, "backward_adam": 836.7e6}
+
 
 def parse_args():
     p = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
@@ -441,7 +447,7 @@ def main() -> None:
         "peak": d.get("peak"),
         "unit": d.get("unit"),
         "frac": d.get("frac"),
-        "traffic": None,
+        "traffic": NCU_TRAFFIC_BYTES.get(dominant),
         "peak_source": ("nominal FP32 issue rate: 148 SMs x 128 lanes x sm_max clock (FMA = 1 op)"
                         if d.get("bound") == "fp32" else f"{pk['source']} HBM copy bandwidth"),
     }
