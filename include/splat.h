@@ -185,7 +185,9 @@ const char* sp_status_string(sp_status status);
 /* Replaces Gpu::request / request_async (gpu.rs:29-66): device `device`, its own stream. */
 sp_status sp_context_create(int device, sp_context** out);
 /* As sp_context_create, but enqueues on `stream` (a cudaStream_t the caller keeps alive),
- * so that the work orders with the caller's own (e.g. a torch stream). */
+ * so that the work orders with the caller's own (e.g. a torch stream). NULL gives the
+ * context a stream of its own, as sp_context_create; the legacy default stream is passed
+ * as cudaStreamLegacy. */
 sp_status sp_context_create_on_stream(int device, void* stream, sp_context** out);
 void sp_context_destroy(sp_context* ctx);
 /* Waits for every call enqueued on the context's stream (Gpu::submit + poll). */

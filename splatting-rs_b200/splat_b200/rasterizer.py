@@ -53,10 +53,15 @@ def _torch():
     return torch
 
 
+# CUDA's handle of the legacy default stream (cudaStreamLegacy). torch reports its default
+# stream as handle 0, which the C ABI reads as "give the context a stream of its own".
+CUDA_STREAM_LEGACY = 0x1
+
+
 class Context:
     """One CUDA device and the stream the library enqueues on (Gpu, gpu.rs:13-66). By
     default the current torch stream of the device, so that the library's work orders with
-    the tensors' copies."""
+    torch's: tensor copies, CUDA events and NCCL collectives on that stream see it."""
 
     def __init__(self, device: int = 0, stream: int | None = None):
         self.lib = _lib.load()
@@ -65,11 +70,16 @@ class Context:
             torch = _torch()
             if not torch.cuda.is_available():
                 raise _lib.SplatError(_lib.SP_ERR_NO_DEVICE, "no CUDA device")
-            stream = torch.cuda.current_stream(device).cuda_stream
+            stream = torch.cuda.current_stream(device).cuda_stream or CUDA_STREAM_LEGACY
         status = self.lib.sp_context_create_on_stream(device, ctypes.c_void_p(stream), ctypes.byref(handle))
         _lib.check(status, None, "sp_context_create")
         self.handle = handle.value
         self.device = device
+
+    @property
+    def stream(self) -> int:
+        """The handle of the stream the library enqueues on."""
+        return int(self.lib.sp_context_stream(self.handle) or 0)
 
     def sync(self) -> None:
         _lib.check(self.lib.sp_context_sync(self.handle), self.handle, "sync")

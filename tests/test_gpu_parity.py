@@ -353,3 +353,33 @@ def test_fused_backward_adam_rejects_foreign_state(ctx):
     with pytest.raises(sb.SplatError) as err:
         rast.encode_backward_adam(adam, 1.0)
     assert err.value.status == sb._lib.SP_ERR_INVALID
+
+
+def test_context_enqueues_on_the_current_torch_stream():
+    """The library's work orders with torch's: on torch's default stream (handle 0) the
+    context enqueues on the legacy default stream, on any other stream on that stream, so
+    CUDA events, tensor copies and NCCL collectives on it see the library's work."""
+    import torch
+
+    assert torch.cuda.current_stream(0).cuda_stream == 0
+    ctx = sb.Context(0)
+    assert ctx.stream == sb.rasterizer.CUDA_STREAM_LEGACY
+    side = torch.cuda.Stream(0)
+    with torch.cuda.stream(side):
+        other = sb.Context(0)
+        assert other.stream == side.cuda_stream
+    # A torch event pair brackets the library's work: a forward of config 0 takes time.
+    cloud, camera = CASES["config0_5k_256"]
+    rast, _, _ = make_rasterizer(ctx, cloud, camera)
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    start.record()
+    for _ in range(20):
+        rast.encode_forward()
+    stop.record()
+    stop.synchronize()
+    # Without the ordering the pair would close before the forwards ran.
+    assert ctx.lib.sp_context_sync(ctx.handle) == 0
+    image = rast.read_image().rgbt
+    assert np.isfinite(image).all()
+    assert start.elapsed_time(stop) > 0.01
