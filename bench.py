@@ -259,7 +259,8 @@ def config_dict(scene, world: int) -> dict:
         "height": cam.height,
         "views": len(scene.cameras),
         "views_per_step": world,
-        "parallelism": f"view-sharded dp{world}" if world > 1 else "single GPU",
+        "parallelism": (f"view-sharded dp{world}: gradients reduce-scattered, Adam sharded by Gaussians, "
+                        f"parameters all-gathered (NCCL)" if world > 1 else "single GPU"),
         "l2": "working set (params, gradients, Adam moments: >0.4 GB) larger than the 126 MB L2",
     }
 
@@ -277,7 +278,8 @@ def main() -> None:
     import torch.distributed as dist
 
     import splat_b200 as sb
-    from splat_b200 import scenes
+    from splat_b200 import scenes, sharding
+    from splat_b200.sharding import GradientExchange, ViewShardedStep
 
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -303,26 +305,16 @@ def main() -> None:
     extent = np.float32(sb.cameras_extent(cams))
     adam = sb.Adam(ctx, params, rast, len(cloud), sb.LEARNING_RATES_3DGS, extent, sh_degree=deg)
     uniforms = [c.uniform() for c in cams]
-    grads = rast.param_gradients()
     iterations = scene.iterations
+    # One GPU: backward with the Adam step fused. N GPUs: gradients reduce-scattered, Adam on
+    # this rank's share of the Gaussians, parameters all-gathered (splat_b200/sharding.py).
+    train_step = ViewShardedStep(rast, adam, params, uniforms, rank, world)
 
     def view_of(step: int) -> int:
-        return (step * world + rank) % views
+        return sharding.view_of(step, rank, world, views)
 
     def device_step(step: int) -> None:
-        v = view_of(step)
-        rast.set_camera(uniforms[v])
-        rast.encode_forward()
-        rast.encode_loss(v)
-        factor = sb.position_rate_factor(step % iterations, iterations)
-        if world == 1:
-            # Backward with the Adam step fused into the projection backward.
-            rast.encode_backward_adam(adam, factor)
-        else:
-            # The gradients are summed over the ranks before the Adam step.
-            rast.encode_backward()
-            dist.all_reduce(grads)
-            adam.encode_step(factor)
+        train_step(step, sb.position_rate_factor(step % iterations, iterations))
 
     def barrier():
         torch.cuda.synchronize()
@@ -373,6 +365,7 @@ def main() -> None:
     # ---- e2e: the reference caller's step through the public API, poses refined.
     params.copy_(initial)
     adam_e2e = sb.Adam(ctx, params, rast, len(cloud), sb.LEARNING_RATES_3DGS, extent, sh_degree=deg)
+    exchange_e2e = GradientExchange(adam_e2e, params, rast.param_gradients(), len(cloud), rast.stride, rank, world)
     poses = sb.PoseRefinement(cams, sb.LEARNING_RATES_3DGS, float(extent))
     e2e_steps = args.e2e_steps or args.steps
 
@@ -387,8 +380,7 @@ def main() -> None:
             rast.encode_forward()
             rast.encode_loss(v)
             rast.encode_backward()
-            dist.all_reduce(grads)
-            adam_e2e.encode_step(factor)
+            exchange_e2e(factor)
             gradient = rast.read_camera_gradient()
             rast.read_loss()
         poses.step(v, gradient, factor)

@@ -59,27 +59,53 @@ def _gradient(oracle, cloud, camera, gt_view, packed):
     return oracle.backward(packed, 0, cam, fwd, loss_gradient)["param_gradients"]
 
 
-def _rank_main(rank: int, world: int, port: int, out_dir: str) -> None:
+class _OracleAdam:
+    """The CPU oracle's Adam behind the interface GradientExchange drives (encode_step,
+    advance + step_range), over numpy views of the exchange's tensors."""
+
+    def __init__(self, oracle, params, gradients, lr):
+        self.oracle, self.params, self.gradients, self.lr = oracle, params, gradients, lr
+        self.m, self.v = np.zeros_like(params), np.zeros_like(params)
+        self.step = 0
+
+    def _apply(self, first: int, count: int) -> None:
+        lo, hi = first * 14, (first + count) * 14
+        self.oracle.adam_step(self.params[lo:hi], self.gradients[lo:hi], self.m[lo:hi], self.v[lo:hi], 14, self.lr,
+                              self.step, float(np.log(np.float32(0.02))), float(np.log(np.float32(10.0))))
+
+    def encode_step(self, rate_factor: float) -> None:
+        self.advance(rate_factor)
+        self._apply(0, len(self.params) // 14)
+
+    def advance(self, rate_factor: float) -> None:
+        self.step += 1
+
+    def step_range(self, first: int, count: int) -> None:
+        self._apply(first, count)
+
+
+def _rank_main(rank: int, world: int, port: int, out_dir: str, mode: str) -> None:
     import torch
     import torch.distributed as dist
 
     sys.path[:0] = [str(ROOT / "splatting-rs_b200"), str(ROOT / "oracle")]
     import oracle
     import splat_b200 as sb
+    from splat_b200.sharding import GradientExchange
 
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=world)
     cloud, cams, gt = _scene()
-    packed = cloud.to_packed().copy()
-    m, v = np.zeros_like(packed), np.zeros_like(packed)
+    params = torch.from_numpy(cloud.to_packed().copy())
+    gradients = torch.zeros_like(params)
     lr = sb.LEARNING_RATES_3DGS.by_slot(np.float32(1.0), 14)
+    adam = _OracleAdam(oracle, params.numpy(), gradients.numpy(), lr)
+    exchange = GradientExchange(adam, params, gradients, len(cloud), 14, rank, world, mode)
     for step in range(2):
         view = view_of(step, rank, world, len(cams))
-        grad = torch.from_numpy(_gradient(oracle, cloud, cams[view], gt[view], packed))
-        dist.all_reduce(grad)
-        oracle.adam_step(packed, grad.numpy(), m, v, 14, lr, step + 1, float(np.log(np.float32(0.02))),
-                         float(np.log(np.float32(10.0))))
-    np.save(os.path.join(out_dir, f"rank{rank}.npy"), packed)
+        gradients.copy_(torch.from_numpy(_gradient(oracle, cloud, cams[view], gt[view], params.numpy())))
+        exchange(1.0)
+    np.save(os.path.join(out_dir, f"rank{rank}.npy"), params.numpy())
     dist.barrier()
     dist.destroy_process_group()
 
@@ -90,14 +116,18 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
-def test_two_gloo_ranks_equal_one_process_summing_their_views(tmp_path):
+@pytest.mark.parametrize("mode", ["allreduce", "sharded"])
+def test_two_gloo_ranks_equal_one_process_summing_their_views(tmp_path, mode):
+    """Two ranks, each the gradient of its own view, exchanged by an all-reduce or by a
+    reduce-scatter + Adam on each rank's half + all-gather (in place, as on the GPUs): the
+    same parameters on both ranks, equal to one process summing both views' gradients."""
     import torch.multiprocessing as mp
 
     import oracle
     import splat_b200 as sb
 
     world = 2
-    mp.start_processes(_rank_main, args=(world, _free_port(), str(tmp_path)), nprocs=world, join=True,
+    mp.start_processes(_rank_main, args=(world, _free_port(), str(tmp_path), mode), nprocs=world, join=True,
                        start_method="spawn")
     ranks = [np.load(tmp_path / f"rank{r}.npy") for r in range(world)]
     assert np.array_equal(ranks[0], ranks[1]), "ranks diverged"
