@@ -412,6 +412,35 @@ sp_status sp_pose_refinement_correction(const sp_pose_refinement* p, uint32_t vi
 double sp_pose_refinement_focal_scale(const sp_pose_refinement* p);
 sp_status sp_pose_refinement_last_gradient(const sp_pose_refinement* p, sp_pose_gradient* out);
 
+/* The pose refinement on the device (no counterpart in the reference, whose
+ * pose_refinement.rs:113-163 runs on the host after reading back the camera gradient every
+ * step, training.rs:205-208). A copy of a host refinement's state (sp_pose_refinement) bound
+ * to a rasterizer: each step the refinement of the view just trained runs in a one-thread
+ * kernel on the camera gradient the backward left in device memory, and writes the camera
+ * of the next view for the next forward, so a training loop needs no host synchronisation.
+ * The arithmetic is the host refinement's (f64, the same source); results agree with it to
+ * the rounding of sin, cos, exp and pow. */
+typedef struct sp_device_poses sp_device_poses;
+sp_status sp_device_poses_create(sp_rasterizer* r, const sp_pose_refinement* from, sp_device_poses** out);
+void sp_device_poses_destroy(sp_device_poses* dp);
+/* Enqueues: the rasterizer's camera := view's corrected camera (instead of sp_set_camera). */
+sp_status sp_device_poses_set_camera(sp_device_poses* dp, uint32_t view);
+/* Enqueues: the refinement step of `view` (after its backward; rate_factor in (0, 1]), then
+ * the rasterizer's camera := next_view's corrected camera. */
+sp_status sp_device_poses_step(sp_device_poses* dp, uint32_t view, uint32_t next_view, float rate_factor);
+/* Synchronises and copies the device state into `into` (a refinement over the same views);
+ * SP_ERR_NONFINITE if a step met a non-finite pose gradient (that step changed nothing). */
+sp_status sp_device_poses_download(sp_device_poses* dp, sp_pose_refinement* into);
+/* Trainer::step_async with the poses refined on the device, without synchronising: forward
+ * with the camera already in place (sp_device_poses_set_camera, or the previous step), loss
+ * against `view`, backward + Adam (fused when `adam` steps the rasterizer's own
+ * parameters), the pose step of `view` and the camera of next_view; if pinned_loss_sums
+ * (page-locked host memory, 4 doubles) is not NULL, the loss sums (L1, alpha, D-SSIM, total;
+ * divide by the pixel count for the means) are copied into it asynchronously. */
+sp_status sp_train_step_device_poses(sp_rasterizer* r, sp_adam* adam, sp_device_poses* dp, uint32_t view,
+                                     uint32_t next_view, float position_rate_factor, double* pinned_loss_sums);
+
+
 #ifdef __cplusplus
 }
 #endif

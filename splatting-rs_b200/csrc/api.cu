@@ -10,6 +10,8 @@
 #include <vector>
 
 #include "kernels.h"
+#include "pose_math.h"
+#include "pose_state.h"
 
 using namespace splat;
 
@@ -95,6 +97,9 @@ struct sp_rasterizer {
     unsigned long long* lookback = nullptr;
     uint2* ranges = nullptr;
     uint32_t* tile_order = nullptr;
+    // The camera the projection kernels read: written by sp_set_camera (an asynchronous copy)
+    // or by the device pose step (sp_device_poses_step).
+    sp_camera_uniform* camera_dev = nullptr;
     float4* image = nullptr;
     uint32_t* contributions = nullptr;
     float4* ssim_partials = nullptr;
@@ -324,23 +329,8 @@ sp_status sp_camera_uniform_from_pinhole(const double rotation_c2w[9], const dou
                                          const double focal[2], const double principal_point[2], uint32_t width,
                                          uint32_t height, sp_camera_uniform* out) {
     if (!rotation_c2w || !translation || !focal || !principal_point || !out) return SP_ERR_INVALID;
-    // camera.rs:46-70: W = R^T, t = -W C, rows (W | t) to f32.
-    double w[3][3], t[3];
-    for (int r = 0; r < 3; ++r)
-        for (int c = 0; c < 3; ++c) w[r][c] = rotation_c2w[c * 3 + r];
-    for (int r = 0; r < 3; ++r) t[r] = -(w[r][0] * translation[0] + w[r][1] * translation[1] + w[r][2] * translation[2]);
-    for (int r = 0; r < 3; ++r) {
-        for (int c = 0; c < 3; ++c) out->world_to_camera_rows[r][c] = (float)w[r][c];
-        out->world_to_camera_rows[r][3] = (float)t[r];
-    }
-    out->focal[0] = (float)focal[0];
-    out->focal[1] = (float)focal[1];
-    out->principal_point[0] = (float)principal_point[0];
-    out->principal_point[1] = (float)principal_point[1];
-    out->width = width;
-    out->height = height;
-    out->tiles_x = (width + SP_TILE - 1) / SP_TILE;
-    out->tiles_y = (height + SP_TILE - 1) / SP_TILE;
+    // camera.rs:46-70 (pose_math.h, shared with the device pose step).
+    *out = splat::pose::uniform_of(rotation_c2w, translation, focal, principal_point, width, height);
     return SP_OK;
 }
 
@@ -443,6 +433,7 @@ sp_status sp_rasterizer_create(sp_context* ctx, const float* d_params, uint64_t 
     SP_ALLOC(r->lookback, (size_t)std::max<uint32_t>(r->max_partitions, 1) * kSortRadix);
     SP_ALLOC(r->ranges, r->tiles);
     SP_ALLOC(r->tile_order, r->tiles);
+    SP_ALLOC(r->camera_dev, 1);
     SP_ALLOC(r->image, p);
     SP_ALLOC(r->contributions, p);
     SP_ALLOC(r->ssim_partials, p * 3);
@@ -470,6 +461,13 @@ sp_status sp_rasterizer_create(sp_context* ctx, const float* d_params, uint64_t 
     // The default camera of rasterizer.rs:202-213: identity pose, unit focal.
     const double identity[9] = {1, 0, 0, 0, 1, 0, 0, 0, 1}, zero[3] = {0, 0, 0}, unit[2] = {1, 1}, origin[2] = {0, 0};
     sp_camera_uniform_from_pinhole(identity, zero, unit, origin, width, height, &r->camera);
+    {
+        const cudaError_t err = cudaMemcpy(r->camera_dev, &r->camera, sizeof(sp_camera_uniform), cudaMemcpyHostToDevice);
+        if (err != cudaSuccess) {
+            sp_rasterizer_destroy(r);
+            return cuda_fail(ctx, err, "camera upload");
+        }
+    }
     r->has_camera = true;
     *out = r;
     return SP_OK;
@@ -483,7 +481,11 @@ sp_status sp_set_camera(sp_rasterizer* r, const sp_camera_uniform* camera) {
     SP_REQUIRE(r->ctx, camera->width == r->width && camera->height == r->height, SP_ERR_INVALID, "camera image size");
     SP_REQUIRE(r->ctx, camera->tiles_x == r->tiles_x && camera->tiles_y == r->tiles_y, SP_ERR_INVALID,
                "camera tile grid");
+    SP_CHECK(select_device(r->ctx));
     r->camera = *camera;
+    // From pageable memory: the copy is staged before the call returns.
+    SP_CUDA(r->ctx, cudaMemcpyAsync(r->camera_dev, camera, sizeof(sp_camera_uniform), cudaMemcpyHostToDevice,
+                                    r->ctx->stream));
     return SP_OK;
 }
 
@@ -494,7 +496,7 @@ sp_status sp_forward(sp_rasterizer* r) {
     cudaStream_t st = ctx->stream;
     {
         KernelSpan span(ctx, SP_K_PROJECT);
-        SP_CUDA(ctx, launch_project(r->params, r->n, (int)r->options.sh_degree, r->camera, r->records, r->radii,
+        SP_CUDA(ctx, launch_project(r->params, r->n, (int)r->options.sh_degree, r->camera_dev, r->records, r->radii,
                                     r->offsets, r->block_totals, st));
     }
     {
@@ -584,7 +586,7 @@ sp_status sp_backward_adam(sp_rasterizer* r, sp_adam* adam, float position_rate_
                     adam->bias1, adam->bias2, adam->max_log_scale, adam->max_log_anisotropy};
     KernelSpan span(r->ctx, SP_K_BACKWARD_ADAM);
     SP_CUDA(r->ctx, launch_project_backward(r->params, r->n, (int)r->options.sh_degree, (int)r->options.backward_mode,
-                                            r->camera, r->records, r->radii, r->offsets, r->slot_gradients,
+                                            r->camera_dev, r->records, r->radii, r->offsets, r->slot_gradients,
                                             r->capacity, r->gaussian_gradients, r->param_gradients, 0,
                                             r->camera_partials, r->camera_done, r->camera_gradient,
                                             r->densify_stats, &step, r->ctx->stream));
@@ -600,7 +602,7 @@ sp_status sp_backward(sp_rasterizer* r) {
     {
         KernelSpan span(r->ctx, SP_K_PROJECT_BACKWARD);
         SP_CUDA(r->ctx, launch_project_backward(
-                            r->params, r->n, (int)r->options.sh_degree, (int)r->options.backward_mode, r->camera,
+                            r->params, r->n, (int)r->options.sh_degree, (int)r->options.backward_mode, r->camera_dev,
                             r->records, r->radii, r->offsets, r->slot_gradients, r->capacity, r->gaussian_gradients,
                             r->param_gradients, (int)r->options.accumulate_gradients, r->camera_partials,
                             r->camera_done, r->camera_gradient, r->densify_stats, nullptr, st));
@@ -739,6 +741,109 @@ sp_status sp_train_step(sp_rasterizer* r, sp_adam* adam, const sp_camera_uniform
         loss_out->alpha = (float)(r->readback->loss[1] / pixels);
         loss_out->dssim = (float)(r->readback->loss[2] / pixels);
         loss_out->total = (float)(r->readback->loss[3] / pixels);
+    }
+    return SP_OK;
+}
+
+// ------------------------------------------------------------------ device pose refinement
+
+struct sp_device_poses {
+    sp_rasterizer* r = nullptr;
+    uint32_t views = 0;
+    sp_pinhole_camera* initial = nullptr;
+    splat::pose::ViewState* states = nullptr;
+    splat::pose::SharedState* shared = nullptr;
+};
+
+void sp_device_poses_destroy(sp_device_poses* dp) {
+    if (!dp) return;
+    cudaSetDevice(dp->r->ctx->device);
+    cudaStreamSynchronize(dp->r->ctx->stream);
+    cudaFree(dp->initial);
+    cudaFree(dp->states);
+    cudaFree(dp->shared);
+    delete dp;
+}
+
+sp_status sp_device_poses_create(sp_rasterizer* r, const sp_pose_refinement* from, sp_device_poses** out) {
+    if (!r || !from || !out) return SP_ERR_INVALID;
+    *out = nullptr;
+    const uint32_t views = (uint32_t)from->initial.size();
+    SP_REQUIRE(r->ctx, views > 0, SP_ERR_INVALID, "no views");
+    for (const sp_pinhole_camera& c : from->initial)
+        SP_REQUIRE(r->ctx, c.width == r->width && c.height == r->height, SP_ERR_INVALID, "camera image size");
+    SP_CHECK(select_device(r->ctx));
+    sp_device_poses* dp = new sp_device_poses();
+    dp->r = r;
+    dp->views = views;
+    cudaError_t err = cudaMalloc(&dp->initial, views * sizeof(sp_pinhole_camera));
+    if (err == cudaSuccess) err = cudaMalloc(&dp->states, views * sizeof(splat::pose::ViewState));
+    if (err == cudaSuccess) err = cudaMalloc(&dp->shared, sizeof(splat::pose::SharedState));
+    if (err == cudaSuccess)
+        err = cudaMemcpy(dp->initial, from->initial.data(), views * sizeof(sp_pinhole_camera), cudaMemcpyHostToDevice);
+    if (err == cudaSuccess)
+        err = cudaMemcpy(dp->states, from->views.data(), views * sizeof(splat::pose::ViewState), cudaMemcpyHostToDevice);
+    if (err == cudaSuccess)
+        err = cudaMemcpy(dp->shared, &from->shared, sizeof(splat::pose::SharedState), cudaMemcpyHostToDevice);
+    if (err != cudaSuccess) {
+        sp_device_poses_destroy(dp);
+        return cuda_fail(r->ctx, err, "device pose state");
+    }
+    *out = dp;
+    return SP_OK;
+}
+
+sp_status sp_device_poses_set_camera(sp_device_poses* dp, uint32_t view) {
+    if (!dp) return SP_ERR_INVALID;
+    sp_rasterizer* r = dp->r;
+    SP_REQUIRE(r->ctx, view < dp->views, SP_ERR_INVALID, "view index out of range");
+    SP_CHECK(select_device(r->ctx));
+    SP_CUDA(r->ctx, launch_pose_step(dp->initial, dp->states, dp->shared, r->camera_gradient, dp->views, dp->views,
+                                     view, 0.0, r->camera_dev, r->ctx->stream));
+    return SP_OK;
+}
+
+sp_status sp_device_poses_step(sp_device_poses* dp, uint32_t view, uint32_t next_view, float rate_factor) {
+    if (!dp) return SP_ERR_INVALID;
+    sp_rasterizer* r = dp->r;
+    SP_REQUIRE(r->ctx, view < dp->views && next_view < dp->views, SP_ERR_INVALID, "view index out of range");
+    // pose_refinement.rs:113-163.
+    SP_REQUIRE(r->ctx, rate_factor > 0.0f && rate_factor <= 1.0f, SP_ERR_INVALID,
+               "position rate factor must be in (0, 1]");
+    SP_CHECK(select_device(r->ctx));
+    SP_CUDA(r->ctx, launch_pose_step(dp->initial, dp->states, dp->shared, r->camera_gradient, dp->views, view,
+                                     next_view, (double)rate_factor, r->camera_dev, r->ctx->stream));
+    return SP_OK;
+}
+
+sp_status sp_device_poses_download(sp_device_poses* dp, sp_pose_refinement* into) {
+    if (!dp || !into || into->initial.size() != dp->views) return SP_ERR_INVALID;
+    sp_rasterizer* r = dp->r;
+    SP_CHECK(select_device(r->ctx));
+    SP_CHECK(read_device(r->ctx, into->views.data(), dp->states, dp->views * sizeof(splat::pose::ViewState)));
+    splat::pose::SharedState shared;
+    SP_CHECK(read_device(r->ctx, &shared, dp->shared, sizeof(shared)));
+    into->shared = shared;
+    if (shared.status != 0) return fail(r->ctx, (sp_status)shared.status, "a device pose step met a non-finite gradient");
+    return SP_OK;
+}
+
+sp_status sp_train_step_device_poses(sp_rasterizer* r, sp_adam* adam, sp_device_poses* dp, uint32_t view,
+                                     uint32_t next_view, float position_rate_factor, double* pinned_loss_sums) {
+    if (!r || !adam || !dp || dp->r != r) return SP_ERR_INVALID;
+    SP_CHECK(sp_forward(r));
+    SP_CHECK(sp_loss(r, view));
+    if (adam->params == r->params && adam->gradients == r->param_gradients && adam->n == r->n) {
+        SP_CHECK(sp_backward_adam(r, adam, position_rate_factor));
+    } else {
+        SP_CHECK(sp_backward(r));
+        SP_CHECK(sp_adam_step(adam, position_rate_factor));
+    }
+    SP_CHECK(sp_device_poses_step(dp, view, next_view, position_rate_factor));
+    if (pinned_loss_sums) {
+        cudaStream_t st = r->ctx->stream;
+        SP_CUDA(r->ctx, launch_loss_sums(r->pixel_loss, r->pixels(), r->loss_sums, st));
+        SP_CUDA(r->ctx, cudaMemcpyAsync(pinned_loss_sums, r->loss_sums, 4 * sizeof(double), cudaMemcpyDeviceToHost, st));
     }
     return SP_OK;
 }

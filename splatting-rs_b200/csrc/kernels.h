@@ -14,7 +14,8 @@ namespace splat {
 
 // project_forward.wgsl:19-93 with the scan's first level (scan.wgsl:27-62) fused: per
 // block of 256 Gaussians the exclusive prefix of the tile counts and the block total.
-cudaError_t launch_project(const float* params, uint64_t n, int sh_degree, const sp_camera_uniform& cam,
+// `cam`: the camera in device memory (sp_camera_uniform, 80 B).
+cudaError_t launch_project(const float* params, uint64_t n, int sh_degree, const sp_camera_uniform* cam,
                            float4* records, uint32_t* radii, uint32_t* local_offsets, uint32_t* block_totals,
                            cudaStream_t stream);
 // scan_tile_counts (scan.wgsl:64-81): scans the block totals into 64-bit block offsets,
@@ -38,7 +39,7 @@ struct AdamLaunch {
 // parameter gradients are not written but consumed by that Adam step (adam.wgsl,
 // clamp_scales.wgsl) in the same kernel.
 cudaError_t launch_project_backward(const float* params, uint64_t n, int sh_degree, int mode,
-                                    const sp_camera_uniform& cam,
+                                    const sp_camera_uniform* cam,
                                     const float4* records, const uint32_t* radii, const uint32_t* offsets,
                                     const float* slot_gradients, uint64_t capacity, const float4* gaussian_gradients,
                                     float* param_gradients, int accumulate, float* camera_partials,
@@ -104,5 +105,18 @@ cudaError_t launch_loss(const float4* image, const float4* ground_truth, const f
 cudaError_t launch_adam(float* params, const float* gradients, float* first_moment, float* second_moment,
                         uint64_t first, uint64_t count, int stride, const float* lr_by_slot_host, float bias1,
                         float bias2, float max_log_scale, float max_log_anisotropy, cudaStream_t stream);
+
+// ---- pose_device.cu
+
+namespace pose {
+struct ViewState;
+struct SharedState;
+}  // namespace pose
+// The device pose refinement: if view < views, the refinement step of `view` from the
+// camera gradient (14 floats); then, if next_view < views, the camera uniform of next_view
+// into camera_out. One thread.
+cudaError_t launch_pose_step(const sp_pinhole_camera* initial, pose::ViewState* states, pose::SharedState* shared,
+                             const float* camera_gradient, uint32_t views, uint32_t view, uint32_t next_view,
+                             double factor, sp_camera_uniform* camera_out, cudaStream_t stream);
 
 }  // namespace splat

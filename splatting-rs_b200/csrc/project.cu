@@ -87,16 +87,28 @@ __device__ __forceinline__ void project_one(const float* p, const sp_camera_unif
     *count_out = (uint32_t)cnt;
 }
 
+// The camera of the pass, copied from device memory (where sp_set_camera or the device
+// pose step put it) into shared memory by the first threads; visible after the next barrier.
+__device__ __forceinline__ void load_camera(const sp_camera_uniform* __restrict__ camera, sp_camera_uniform& s_cam) {
+    constexpr uint32_t kWords = sizeof(sp_camera_uniform) / sizeof(uint32_t);
+    if (threadIdx.x < kWords)
+        reinterpret_cast<uint32_t*>(&s_cam)[threadIdx.x] = reinterpret_cast<const uint32_t*>(camera)[threadIdx.x];
+}
+
 template <int DEG>
 __global__ void __launch_bounds__(kBlock) k_project(const float* __restrict__ params, uint32_t n,
-                                                    const sp_camera_uniform cam, float4* __restrict__ records,
-                                                    uint32_t* __restrict__ radii, uint32_t* __restrict__ local_offsets,
+                                                    const sp_camera_uniform* __restrict__ camera,
+                                                    float4* __restrict__ records, uint32_t* __restrict__ radii,
+                                                    uint32_t* __restrict__ local_offsets,
                                                     uint32_t* __restrict__ block_totals) {
     constexpr int S = SP_PARAM_STRIDE(DEG);
     extern __shared__ float4 smem4[];
+    __shared__ sp_camera_uniform s_cam;
+    const sp_camera_uniform& cam = s_cam;
     float* sp = reinterpret_cast<float*>(smem4);
     const uint32_t g0 = blockIdx.x * kBlock;
     const uint32_t here = min((uint32_t)kBlock, n - g0);
+    load_camera(camera, s_cam);
     stage_in(params + (size_t)g0 * S, here * S, sp);
     __syncthreads();
     const uint32_t t = threadIdx.x;
@@ -404,12 +416,15 @@ struct FusedAdam {
 
 template <int DEG, int MODE, bool FUSED>
 __global__ void __launch_bounds__(kBlock, 3) k_project_backward(
-    const float* params, uint32_t n, const sp_camera_uniform cam, const float4* __restrict__ records,
+    const float* params, uint32_t n, const sp_camera_uniform* __restrict__ camera, const float4* __restrict__ records,
     const uint32_t* __restrict__ radii, const uint32_t* __restrict__ offsets, const float* __restrict__ slot_gradients,
     unsigned long long capacity, const float4* __restrict__ gaussian_gradients, float* __restrict__ param_gradients,
     int accumulate, float* __restrict__ camera_partials, uint32_t* camera_done, float* __restrict__ camera_gradient,
     float4* __restrict__ densify_stats, const FusedAdam adam) {
     constexpr int S = SP_PARAM_STRIDE(DEG);
+    __shared__ sp_camera_uniform s_cam;
+    const sp_camera_uniform& cam = s_cam;
+    load_camera(camera, s_cam);
     extern __shared__ float4 smem4[];
     float* sp = reinterpret_cast<float*>(smem4);
     __shared__ float warp_camera[kBlock / 32][SP_CAMERA_GRAD_STRIDE];
@@ -517,7 +532,7 @@ cudaError_t set_smem(Kernel kernel, size_t bytes) {
 
 }  // namespace
 
-cudaError_t launch_project(const float* params, uint64_t n, int sh_degree, const sp_camera_uniform& cam,
+cudaError_t launch_project(const float* params, uint64_t n, int sh_degree, const sp_camera_uniform* cam,
                            float4* records, uint32_t* radii, uint32_t* local_offsets, uint32_t* block_totals,
                            cudaStream_t stream) {
     const unsigned grid = grid_for(n, kBlock);
@@ -550,7 +565,7 @@ cudaError_t launch_scan_blocks(const uint32_t* block_totals, unsigned long long*
 }
 
 cudaError_t launch_project_backward(const float* params, uint64_t n, int sh_degree, int mode,
-                                    const sp_camera_uniform& cam, const float4* records, const uint32_t* radii,
+                                    const sp_camera_uniform* cam, const float4* records, const uint32_t* radii,
                                     const uint32_t* offsets, const float* slot_gradients, uint64_t capacity,
                                     const float4* gaussian_gradients, float* param_gradients, int accumulate,
                                     float* camera_partials, uint32_t* camera_done, float* camera_gradient,

@@ -18,7 +18,7 @@ from .optimizer import (  # noqa: F401
     LearningRates,
     position_rate_factor,
 )
-from .pose import PoseCorrection, PoseRefinement, corrected_camera, pose_gradient  # noqa: F401
+from .pose import DevicePoses, PoseCorrection, PoseRefinement, corrected_camera, pose_gradient  # noqa: F401
 from .rasterizer import (  # noqa: F401
     BACKGROUND,
     Context,

@@ -132,3 +132,42 @@ class PoseRefinement:
 
     def __del__(self):
         self.close()
+
+
+class DevicePoses:
+    """The pose refinement on the GPU (sp_device_poses): a copy of a host PoseRefinement's
+    state bound to a rasterizer. Each training step refines the pose of the view it trained
+    from the camera gradient in device memory and sets the camera of the next view, with no
+    host synchronisation; download() brings the state back into the host refinement."""
+
+    def __init__(self, rasterizer, refinement: PoseRefinement):
+        self.lib = _lib.load()
+        self.rasterizer = rasterizer
+        self.refinement = refinement
+        handle = ctypes.c_void_p()
+        _lib.check(self.lib.sp_device_poses_create(rasterizer.handle, refinement.handle, ctypes.byref(handle)),
+                   rasterizer.ctx.handle, "DevicePoses")
+        self.handle = handle.value
+
+    def set_camera(self, view: int) -> None:
+        """The rasterizer's camera := view's corrected camera (enqueued)."""
+        _lib.check(self.lib.sp_device_poses_set_camera(self.handle, view), self.rasterizer.ctx.handle, "set_camera")
+
+    def step(self, view: int, next_view: int, rate_factor: float) -> None:
+        """The refinement step of `view`, then the camera of `next_view` (enqueued)."""
+        _lib.check(self.lib.sp_device_poses_step(self.handle, view, next_view, float(rate_factor)),
+                   self.rasterizer.ctx.handle, "pose step")
+
+    def download(self) -> PoseRefinement:
+        """Synchronises and copies the device state into the host refinement (returned)."""
+        _lib.check(self.lib.sp_device_poses_download(self.handle, self.refinement.handle), self.rasterizer.ctx.handle,
+                   "download")
+        return self.refinement
+
+    def close(self) -> None:
+        if getattr(self, "handle", None):
+            self.lib.sp_device_poses_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        self.close()

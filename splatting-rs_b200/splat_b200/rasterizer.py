@@ -372,6 +372,15 @@ class Rasterizer:
                                            ctypes.byref(gradient), ctypes.byref(loss)), "train_step")
         return gradient, LossTerms(loss.l1, loss.alpha, loss.dssim, loss.total)
 
+    def train_step_device_poses(self, adam, poses, view: int, next_view: int, rate_factor: float,
+                                loss_sums=None) -> None:
+        """One training step with the poses refined on the device (sp_train_step_device_poses),
+        enqueued without synchronising; `loss_sums`, a pinned float64 tensor of 4, receives the
+        loss sums asynchronously."""
+        ptr = ctypes.c_void_p(loss_sums.data_ptr() if loss_sums is not None else 0)
+        self._check(self.lib.sp_train_step_device_poses(self.handle, adam.handle, poses.handle, view, next_view,
+                                                         float(rate_factor), ptr), "train_step_device_poses")
+
     def render(self, camera: PinholeCamera | CameraUniform) -> Rendered:
         """Rasterizer::render (rasterizer.rs:552-564)."""
         uniform = camera.uniform() if isinstance(camera, PinholeCamera) else camera

@@ -105,3 +105,55 @@ def test_fused_train_step_equals_the_separate_calls(ctx):
         del adam, rast
     assert runs[0][0] == runs[1][0]
     assert np.array_equal(runs[0][1].view(np.uint32), runs[1][1].view(np.uint32))
+
+
+def test_device_poses_equal_host_poses(ctx):
+    """The pose refinement on the device (sp_device_poses, no host synchronisation per step)
+    against the host refinement fed the read-back camera gradient (the reference's
+    Trainer::step_async, training.rs:197-209): 20 steps of config 0 with poses refined, the
+    deterministic backward. The corrections, the focal scale and every step's loss agree to
+    f64 rounding of the math library (1e-9 relative)."""
+    import torch
+
+    scene = scenes.config(0)
+    cams = scene.cameras
+    gt_dev = torch.from_numpy(ground_truth(scene).reshape(-1)).cuda()
+    extent = np.float32(sb.cameras_extent(cams))
+    rates = sb.LEARNING_RATES_3DGS
+    steps = 20
+    runs = []
+    for device in (False, True):
+        params = torch.from_numpy(scene.cloud.to_packed()).cuda()
+        rast = sb.Rasterizer(ctx, params, len(scene.cloud), 256, 256, gt_dev, len(cams),
+                             sb.default_options(backward_mode=sb.SP_BWD_DETERMINISTIC))
+        adam = sb.Adam(ctx, params, rast, len(scene.cloud), rates, extent)
+        poses = sb.PoseRefinement(cams, rates, float(extent))
+        losses = []
+        if device:
+            dp = sb.DevicePoses(rast, poses)
+            sums = torch.zeros(4, dtype=torch.float64).pin_memory()
+            dp.set_camera(0)
+            for step in range(steps):
+                view, nxt = step % len(cams), (step + 1) % len(cams)
+                rast.train_step_device_poses(adam, dp, view, nxt, sb.position_rate_factor(step, steps), sums)
+                ctx.sync()
+                losses.append(float(sums[3]) / (256 * 256))
+            dp.download()
+        else:
+            for step in range(steps):
+                view = step % len(cams)
+                factor = sb.position_rate_factor(step, steps)
+                gradient, loss = rast.train_step(adam, poses.camera(view), view, factor)
+                poses.step(view, gradient, factor)
+                losses.append(loss.total)
+        corrections = [poses.correction(v) for v in range(len(cams))]
+        runs.append((np.array(losses), corrections, poses.focal_scale()))
+        del adam, rast
+    (l0, c0, f0), (l1, c1, f1) = runs
+    np.testing.assert_allclose(l1, l0, rtol=1e-6)
+    assert abs(f1 - f0) <= 1e-9 * abs(f0)
+    for a, b in zip(c0, c1):
+        np.testing.assert_allclose(b.rotation, a.rotation, rtol=1e-9, atol=1e-15)
+        np.testing.assert_allclose(b.translation, a.translation, rtol=1e-9, atol=1e-15)
+    # The refinement moved the poses of every view but the fixed first one.
+    assert np.all(c0[0].rotation == 0.0) and np.any(c0[1].rotation != 0.0)
