@@ -397,6 +397,45 @@ def main() -> None:
     e2e_ms = max_over_ranks(e_start.elapsed_time(e_stop))
     e2e_value = world * e2e_steps / (e2e_ms / 1000.0)
 
+    # ---- e2e with the poses refined on the device (one GPU): the same steps through
+    # sp_train_step_device_poses, no host synchronisation per step; each step's loss sums
+    # (32 B) are copied asynchronously into its own slot of a pinned host ring.
+    e2e_device = None
+    if world == 1:
+        params.copy_(initial)
+        adam_dp = sb.Adam(ctx, params, rast, len(cloud), sb.LEARNING_RATES_3DGS, extent, sh_degree=deg)
+        device_poses = sb.DevicePoses(rast, sb.PoseRefinement(cams, sb.LEARNING_RATES_3DGS, float(extent)))
+        ring = torch.zeros((64, 4), dtype=torch.float64).pin_memory()
+
+        def device_pose_step(step: int) -> None:
+            factor = sb.position_rate_factor(step % iterations, iterations)
+            rast.train_step_device_poses(adam_dp, device_poses, view_of(step), view_of(step + 1), factor,
+                                         ring[step % len(ring)])
+
+        device_poses.set_camera(view_of(0))
+        for i in range(min(args.warmup, 3)):
+            device_pose_step(i)
+        barrier()
+        d_start, d_stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        d_start.record()
+        for i in range(e2e_steps):
+            device_pose_step(args.warmup + i)
+        d_stop.record()
+        torch.cuda.synchronize()
+        device_poses.download()
+        d_ms = d_start.elapsed_time(d_stop)
+        e2e_device = {
+            "value": e2e_steps / (d_ms / 1000.0),
+            "unit": UNIT,
+            "h2d_bytes_per_step": 0,
+            "d2h_bytes_per_step": 32,
+            "what": "sp_train_step_device_poses: forward + loss + backward + Adam + the pose step on the device, "
+                    "the next view's camera written on the device, the loss sums (32 B) copied asynchronously "
+                    "to pinned host memory; no host synchronisation per step",
+        }
+        device_poses.close()
+        del adam_dp
+
     launches_per_step = sum(n for _, n in profile.values()) / views
     pk = peaks()
     fp32_peak = SMS * FP32_LANES_PER_SM * pk["sm_max_mhz"] * 1e6 / 1e12  # T FP32 instructions / s
@@ -474,6 +513,7 @@ def main() -> None:
                 "what": "set_camera (80-B camera uniform from the host) + forward + loss + backward + Adam, then the "
                         "camera gradient (56 B) and the loss sums (32 B) read back and the host pose step",
             },
+            "e2e_device_poses": e2e_device,
             "gpu_launches": int(round(launches_per_step * args.steps)),
             "roofline": roofline,
             "cpu_baseline": baseline,
