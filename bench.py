@@ -62,6 +62,8 @@ def parse_args():
     p.add_argument("--cpu-seconds", type=float, default=20.0, help="CPU-baseline sample budget")
     p.add_argument("--reference-seconds", type=float, default=150.0, help="--impl reference time budget")
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--no-forward-3m", action="store_true", help="skip the forward-only config-3 measurement")
+    p.add_argument("--forward-batches", type=int, default=3, help="timed passes over config 3's 64 cameras")
     return p.parse_args()
 
 
@@ -266,6 +268,61 @@ def config_dict(scene, world: int) -> dict:
 
 
 # ------------------------------------------------------------------------------- main
+
+
+def forward_throughput(args, ctx, rank: int, world: int, max_over_ranks, barrier) -> dict:
+    """BASELINE's "fwd Mpix/s @3M": config 3 (3M Gaussians, SH degree 3, 64 cameras at
+    1920x1080), forward passes only (projection, binning, sort, blend), the cameras split
+    over the ranks (rank r renders cameras r, r + world, ...). Device-timed over
+    `forward_batches` passes of the camera batch after one untimed pass; the value is every
+    rank's pixels over the slowest rank's time."""
+    import torch
+
+    import splat_b200 as sb
+    from splat_b200 import scenes
+
+    scene = scenes.config(3)
+    cams = scene.cameras[rank::world]
+    w, h = cams[0].width, cams[0].height
+    params = torch.from_numpy(scene.cloud.to_packed()).cuda()
+    opts = sb.default_options(sh_degree=scene.cloud.sh_degree)
+    rast = sb.Rasterizer(ctx, params, len(scene.cloud), w, h, None, 0, opts)
+    uniforms = [c.uniform() for c in cams]
+
+    def batch() -> None:
+        for u in uniforms:
+            rast.set_camera(u)
+            rast.encode_forward()
+
+    batch()
+    meta = rast.read_intersections_unchecked()
+    ctx.profile(True)
+    batch()
+    ctx.profile(False)
+    profile = {k: v for k, v in ctx.read_profile().items() if v[1]}
+    barrier()
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(args.forward_batches):
+        batch()
+    stop.record()
+    torch.cuda.synchronize()
+    ms = max_over_ranks(start.elapsed_time(stop))
+    pixels = len(scene.cameras) * w * h * args.forward_batches
+    out = {
+        "value": pixels / (ms / 1000.0) / 1e6,
+        "unit": "Mpix/s",
+        "workload": f"config 3: {len(scene.cloud)} Gaussians SH{scene.cloud.sh_degree}, {len(scene.cameras)} cameras "
+                    f"{w}x{h}, forward only, cameras split over {world} GPU(s)",
+        "ms_per_view": ms / (len(scene.cameras) * args.forward_batches / world),
+        "intersections_last_view": int(meta.count),
+        "overflow": bool(meta.overflow),
+        "kernels_ms_per_view": {k: v[0] / len(uniforms) for k, v in profile.items()},
+    }
+    rast.close()
+    del params
+    torch.cuda.empty_cache()
+    return out
 
 
 def main() -> None:
@@ -483,6 +540,10 @@ def main() -> None:
                         if d.get("bound") == "fp32" else f"{pk['source']} HBM copy bandwidth"),
     }
 
+    forward_3m = None
+    if not args.no_forward_3m:
+        forward_3m = forward_throughput(args, ctx, rank, world, max_over_ranks, barrier)
+
     baseline = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         baseline = cpu_baseline(scene, gt_host, args.cpu_seconds)
@@ -520,6 +581,7 @@ def main() -> None:
             "kernels": kernels,
             "intersections": int(meta.count),
             "mpix_per_s": value * width * height / 1e6,
+            "fwd_mpix_per_s_3M": forward_3m,
         }
         print(json.dumps(line), flush=True)
     if world > 1:

@@ -399,7 +399,14 @@ sp_status sp_rasterizer_create(sp_context* ctx, const float* d_params, uint64_t 
     r->blocks = (uint32_t)((gaussian_count + kBlock - 1) / kBlock);
     r->max_partitions = (uint32_t)((capacity + kSortPartition - 1) / kSortPartition);
     const uint32_t tile_bits = ceil_log2(r->tiles);
-    r->plan.key_bits = (int)tile_bits + (opt.key_mode == SP_KEYS_FULL32 ? 32 : SP_DEPTH_BITS);
+    r->plan.tile_bits = (int)tile_bits;
+    // REF20 order: compressed 32-bit keys (tile << r) | (depth key - nearest), r the frame's
+    // depth-key range (< 2^19), wherever tile_bits + 19 fits 32 bits (up to 8192 tiles);
+    // beyond, and for FULL32, the reference's layout in 64 bits.
+    r->plan.compressed = opt.key_mode == SP_KEYS_REF20 && (int)tile_bits + kMaxDepthRangeBits <= 32;
+    r->plan.key_bits = (int)tile_bits + (r->plan.compressed            ? kMaxDepthRangeBits
+                                         : opt.key_mode == SP_KEYS_FULL32 ? 32
+                                                                          : SP_DEPTH_BITS);
     r->plan.key64 = r->plan.key_bits > 32 || opt.key_mode == SP_KEYS_FULL32;
     r->plan.passes = (r->plan.key_bits + 7) / 8;
     r->plan.tile_shift = opt.key_mode == SP_KEYS_FULL32 ? 32 : SP_DEPTH_BITS;
@@ -418,6 +425,15 @@ sp_status sp_rasterizer_create(sp_context* ctx, const float* d_params, uint64_t 
     SP_ALLOC(r->block_totals, r->blocks);
     SP_ALLOC(r->block_offsets, r->blocks);
     SP_ALLOC(r->meta, 1);
+    {
+        // An empty depth-key range for the first frame's projection to widen.
+        const uint32_t empty = 0xffffffffu;
+        const cudaError_t err = cudaMemcpy(&r->meta->depth_lo, &empty, sizeof(empty), cudaMemcpyHostToDevice);
+        if (err != cudaSuccess) {
+            sp_rasterizer_destroy(r);
+            return cuda_fail(ctx, err, "meta");
+        }
+    }
     {
         unsigned char* k0 = nullptr;
         unsigned char* k1 = nullptr;
@@ -497,24 +513,24 @@ sp_status sp_forward(sp_rasterizer* r) {
     {
         KernelSpan span(ctx, SP_K_PROJECT);
         SP_CUDA(ctx, launch_project(r->params, r->n, (int)r->options.sh_degree, r->camera_dev, r->records, r->radii,
-                                    r->offsets, r->block_totals, st));
+                                    r->offsets, r->block_totals, r->plan.compressed ? r->meta : nullptr, st));
     }
     {
         KernelSpan span(ctx, SP_K_SCAN);
         SP_CUDA(ctx, launch_scan_blocks(r->block_totals, r->block_offsets, r->blocks, r->capacity, r->meta,
-                                        r->sort_histograms, r->sort_tickets, st));
+                                        r->sort_histograms, r->sort_tickets, r->plan, st));
     }
     {
         KernelSpan span(ctx, SP_K_EMIT);
         SP_CUDA(ctx, launch_emit(r->records, r->offsets, r->block_offsets, r->n, r->camera,
-                                 (int)r->options.key_mode, r->plan, r->meta, r->keys[0], r->values[0],
-                                 r->sort_histograms, st));
+                                 (int)r->options.key_mode, r->plan, r->meta, r->keys[0], r->keys[1], r->values[0],
+                                 r->values[1], r->sort_histograms, st));
     }
+    // Passes past the frame's key width return at once; the result lands in buffer passes & 1.
     for (int pass = 0; pass < r->plan.passes; ++pass) {
-        const int from = pass & 1, to = from ^ 1;
         KernelSpan span(ctx, SP_K_SORT);
-        SP_CUDA(ctx, launch_sort_pass(r->plan, pass, ++r->sequence, r->keys[from], r->values[from], r->keys[to],
-                                      r->values[to], r->sort_histograms, r->sort_tickets, r->lookback,
+        SP_CUDA(ctx, launch_sort_pass(r->plan, pass, ++r->sequence, r->keys[0], r->values[0], r->keys[1],
+                                      r->values[1], r->sort_histograms, r->sort_tickets, r->lookback,
                                       r->max_partitions, r->meta, st));
     }
     r->sorted_buffer = r->plan.passes & 1;
@@ -881,7 +897,15 @@ sp_status sp_read_sorted_intersections(sp_rasterizer* r, uint64_t* keys_host, ui
     } else {
         std::vector<uint32_t> keys(count);
         SP_CHECK(read_device(r->ctx, keys.data(), r->keys[r->sorted_buffer], count * 4));
-        for (uint64_t i = 0; i < count; ++i) keys_host[i] = keys[i];
+        if (r->plan.compressed) {
+            // Back to the reference's layout: (tile << 20) | depth key.
+            const uint32_t mask = meta.key_shift ? (uint32_t)((1ull << meta.key_shift) - 1) : 0u;
+            for (uint64_t i = 0; i < count; ++i)
+                keys_host[i] = ((uint64_t)(keys[i] >> meta.key_shift) << SP_DEPTH_BITS) |
+                               (uint64_t)((keys[i] & mask) + meta.key_base);
+        } else {
+            for (uint64_t i = 0; i < count; ++i) keys_host[i] = keys[i];
+        }
     }
     return read_device(r->ctx, gaussians_host, r->values[r->sorted_buffer], count * 4);
 }

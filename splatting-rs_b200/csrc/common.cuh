@@ -35,16 +35,33 @@ struct DeviceMeta {
     uint32_t status;            // SP_ERR_* raised on the device, 0 when fine
     uint32_t total_hi;          // high word of the uncapped total
     uint32_t total_lo;
-    uint32_t pad[7];
+    // Compressed keys (SortPlan::compressed): the projection accumulates the range of the
+    // visible Gaussians' depth keys (bits(depth) >> 12) in depth_lo / depth_hi; the scan
+    // turns it into key = (tile << key_shift) | (depth key - key_base), a key as wide as the
+    // frame needs and ordered as the reference's (tile << 20) | depth key.
+    uint32_t depth_lo, depth_hi;
+    uint32_t key_shift;         // key >> key_shift = tile
+    uint32_t key_base;          // depth key of the nearest visible Gaussian
+    uint32_t passes;            // sort passes this frame needs (<= SortPlan::passes)
+    uint32_t first_buffer;      // the emission's ping-pong buffer, so that the last pass
+                                // lands in buffer SortPlan::passes & 1
+    uint32_t pad[1];
 };
 
 // Sort geometry decided on the host from the tile grid.
 struct SortPlan {
-    int key_bits;      // significant bits of the keys
+    int key_bits;      // significant bits of the keys (an upper bound when compressed)
     int key64;         // keys need 64 bits
-    int passes;        // ceil(key_bits / 8)
-    int tile_shift;    // key >> tile_shift = tile index
+    int passes;        // ceil(key_bits / 8): the passes launched
+    int tile_shift;    // key >> tile_shift = tile index (uncompressed keys)
+    int compressed;    // REF20 order in 32-bit keys whose width follows the frame's depth range
+    int tile_bits;     // ceil(log2 tiles)
 };
+
+// bits(0.01f) >> 12 and the largest depth key (NaN included) a visible Gaussian can have:
+// a frame's depth-key range is below 2^19, so compressed keys fit 32 bits up to 2^13 tiles.
+constexpr uint32_t kMinDepthKey = 0x3C23Du;
+constexpr int kMaxDepthRangeBits = 19;
 
 constexpr int kSortThreads = 256;
 constexpr int kSortItems = 16;

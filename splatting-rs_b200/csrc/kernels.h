@@ -15,15 +15,17 @@ namespace splat {
 // project_forward.wgsl:19-93 with the scan's first level (scan.wgsl:27-62) fused: per
 // block of 256 Gaussians the exclusive prefix of the tile counts and the block total.
 // `cam`: the camera in device memory (sp_camera_uniform, 80 B).
+// With `depth_range` non-null (compressed keys) the depth keys' range of the Gaussians that
+// emit keys is accumulated into its depth_lo / depth_hi.
 cudaError_t launch_project(const float* params, uint64_t n, int sh_degree, const sp_camera_uniform* cam,
                            float4* records, uint32_t* radii, uint32_t* local_offsets, uint32_t* block_totals,
-                           cudaStream_t stream);
+                           DeviceMeta* depth_range, cudaStream_t stream);
 // scan_tile_counts (scan.wgsl:64-81): scans the block totals into 64-bit block offsets,
-// fills the meta (count, overflow, sort partitions) and zeroes the sort's histograms and
-// partition tickets for this forward pass.
+// fills the meta (count, overflow, sort partitions, this frame's key geometry) and zeroes
+// the sort's histograms and partition tickets for this forward pass.
 cudaError_t launch_scan_blocks(const uint32_t* block_totals, unsigned long long* block_offsets, uint32_t blocks,
                                uint64_t capacity, DeviceMeta* meta, uint32_t* sort_histograms, uint32_t* sort_tickets,
-                               cudaStream_t stream);
+                               const SortPlan& plan, cudaStream_t stream);
 // project_backward.wgsl:30-227 + reduce_camera_gradient.wgsl:10-34, fused (last block
 // done). Blend sums come per Gaussian (atomic mode) or per slot (deterministic mode).
 // One Adam step for the projection backward to apply in place of writing the parameter
@@ -53,13 +55,16 @@ cudaError_t launch_to_projected(const float4* records, const uint32_t* radii, ui
 
 // emit_tile_keys.wgsl:13-36: adds the block offsets into the tile offsets, writes one key
 // and Gaussian index per covered tile, and accumulates every sort pass's digit histogram.
+// Keys and values go to ping-pong buffer meta->first_buffer, so that the frame's last sort
+// pass lands in buffer plan.passes & 1.
 cudaError_t launch_emit(const float4* records, uint32_t* offsets, const unsigned long long* block_offsets, uint64_t n,
                         const sp_camera_uniform& cam, int key_mode, const SortPlan& plan, const DeviceMeta* meta,
-                        void* keys, uint32_t* values, uint32_t* sort_histograms, cudaStream_t stream);
-// One onesweep pass (stable, 8-bit digit): keys/values in -> out.
-cudaError_t launch_sort_pass(const SortPlan& plan, int pass, uint32_t sequence, const void* keys_in,
-                             const uint32_t* values_in, void* keys_out, uint32_t* values_out,
-                             const uint32_t* sort_histograms, uint32_t* sort_tickets,
+                        void* keys0, void* keys1, uint32_t* values0, uint32_t* values1, uint32_t* sort_histograms,
+                        cudaStream_t stream);
+// One onesweep pass (stable, 8-bit digit `pass`) between the two ping-pong buffers; a pass at
+// or past the frame's meta->passes does nothing.
+cudaError_t launch_sort_pass(const SortPlan& plan, int pass, uint32_t sequence, void* keys0, uint32_t* values0,
+                             void* keys1, uint32_t* values1, const uint32_t* sort_histograms, uint32_t* sort_tickets,
                              unsigned long long* lookback, uint32_t max_partitions, DeviceMeta* meta,
                              cudaStream_t stream);
 // tile_ranges.wgsl:9-22 over a zeroed range array.

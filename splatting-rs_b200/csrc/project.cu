@@ -100,7 +100,7 @@ __global__ void __launch_bounds__(kBlock) k_project(const float* __restrict__ pa
                                                     const sp_camera_uniform* __restrict__ camera,
                                                     float4* __restrict__ records, uint32_t* __restrict__ radii,
                                                     uint32_t* __restrict__ local_offsets,
-                                                    uint32_t* __restrict__ block_totals) {
+                                                    uint32_t* __restrict__ block_totals, DeviceMeta* depth_range) {
     constexpr int S = SP_PARAM_STRIDE(DEG);
     extern __shared__ float4 smem4[];
     __shared__ sp_camera_uniform s_cam;
@@ -127,13 +127,40 @@ __global__ void __launch_bounds__(kBlock) k_project(const float* __restrict__ pa
     const uint32_t exclusive = block_exclusive_scan(count, &total);
     if (t < here) local_offsets[g0 + t] = exclusive;
     if (t == 0) block_totals[blockIdx.x] = total;
+    if (depth_range) {
+        // The range of the depth keys of the Gaussians that emit keys, for compressed keys.
+        __shared__ uint32_t s_lo[kBlock / 32], s_hi[kBlock / 32];
+        const bool emits = t < here && count > 0;
+        const uint32_t key =
+            emits ? __float_as_uint(records[(size_t)(g0 + t) * kRecord + 2].y) >> (32 - SP_DEPTH_BITS) : 0u;
+        const uint32_t lo = __reduce_min_sync(0xffffffffu, emits ? key : 0xffffffffu);
+        const uint32_t hi = __reduce_max_sync(0xffffffffu, key);
+        if ((t & 31u) == 0) {
+            s_lo[t / 32] = lo;
+            s_hi[t / 32] = hi;
+        }
+        __syncthreads();
+        if (t == 0) {
+            uint32_t block_lo = s_lo[0], block_hi = s_hi[0];
+#pragma unroll
+            for (int w = 1; w < kBlock / 32; ++w) {
+                block_lo = min(block_lo, s_lo[w]);
+                block_hi = max(block_hi, s_hi[w]);
+            }
+            if (block_lo <= block_hi) {
+                atomicMin(&depth_range->depth_lo, block_lo);
+                atomicMax(&depth_range->depth_hi, block_hi);
+            }
+        }
+    }
 }
 
 // scan.wgsl:64-81 over the block totals: one block of 1024 threads loops over chunks.
 __global__ void __launch_bounds__(1024) k_scan_blocks(const uint32_t* __restrict__ block_totals,
                                                       unsigned long long* __restrict__ block_offsets, uint32_t blocks,
                                                       unsigned long long capacity, DeviceMeta* meta,
-                                                      uint32_t* sort_histograms, uint32_t* sort_tickets) {
+                                                      uint32_t* sort_histograms, uint32_t* sort_tickets,
+                                                      const SortPlan plan) {
     __shared__ unsigned long long warp_sums[32];
     __shared__ unsigned long long carry;
     const uint32_t t = threadIdx.x, lane = t & 31u, warp = t >> 5;
@@ -174,6 +201,23 @@ __global__ void __launch_bounds__(1024) k_scan_blocks(const uint32_t* __restrict
         meta->partitions = (uint32_t)((count + kSortPartition - 1) / kSortPartition);
         meta->total_lo = (uint32_t)total;
         meta->total_hi = (uint32_t)(total >> 32);
+        // The key geometry of this frame.
+        uint32_t passes = (uint32_t)plan.passes, shift = (uint32_t)plan.tile_shift, base = 0;
+        if (plan.compressed) {
+            const uint32_t lo = meta->depth_lo, hi = meta->depth_hi;
+            base = lo <= hi ? lo : 0u;
+            const uint32_t range = lo <= hi ? hi - lo : 0u;  // largest key offset
+            shift = range ? 32u - __clz(range) : 0u;
+            const uint32_t bits = (uint32_t)plan.tile_bits + shift;
+            passes = max(1u, (bits + 7u) / 8u);
+            // Reset for the next frame's projection.
+            meta->depth_lo = 0xffffffffu;
+            meta->depth_hi = 0u;
+        }
+        meta->key_shift = shift;
+        meta->key_base = base;
+        meta->passes = passes;
+        meta->first_buffer = ((uint32_t)plan.passes ^ passes) & 1u;
     }
 }
 
@@ -534,7 +578,7 @@ cudaError_t set_smem(Kernel kernel, size_t bytes) {
 
 cudaError_t launch_project(const float* params, uint64_t n, int sh_degree, const sp_camera_uniform* cam,
                            float4* records, uint32_t* radii, uint32_t* local_offsets, uint32_t* block_totals,
-                           cudaStream_t stream) {
+                           DeviceMeta* depth_range, cudaStream_t stream) {
     const unsigned grid = grid_for(n, kBlock);
     const size_t smem = (size_t)kBlock * SP_PARAM_STRIDE(sh_degree) * sizeof(float);
     cudaError_t err = cudaSuccess;
@@ -542,7 +586,7 @@ cudaError_t launch_project(const float* params, uint64_t n, int sh_degree, const
     case D:                                                                                               \
         if ((err = set_smem(k_project<D>, smem)) != cudaSuccess) return err;                              \
         k_project<D><<<grid, kBlock, smem, stream>>>(params, (uint32_t)n, cam, records, radii, local_offsets, \
-                                                     block_totals);                                       \
+                                                     block_totals, depth_range);                          \
         break;
     switch (sh_degree) {
         SPLAT_PROJECT(0)
@@ -558,9 +602,9 @@ cudaError_t launch_project(const float* params, uint64_t n, int sh_degree, const
 
 cudaError_t launch_scan_blocks(const uint32_t* block_totals, unsigned long long* block_offsets, uint32_t blocks,
                                uint64_t capacity, DeviceMeta* meta, uint32_t* sort_histograms,
-                               uint32_t* sort_tickets, cudaStream_t stream) {
+                               uint32_t* sort_tickets, const SortPlan& plan, cudaStream_t stream) {
     k_scan_blocks<<<1, 1024, 0, stream>>>(block_totals, block_offsets, blocks, capacity, meta, sort_histograms,
-                                          sort_tickets);
+                                          sort_tickets, plan);
     return cudaGetLastError();
 }
 

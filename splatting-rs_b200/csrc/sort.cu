@@ -27,11 +27,17 @@ constexpr uint32_t kFlagInclusive = 2u;
 constexpr uint32_t kLookbackSpinLimit = 1u << 21;
 constexpr int kLookbackWindow = 8;
 
-template <typename Key>
-__device__ __forceinline__ Key make_key(int key_mode, uint32_t tile, float depth) {
+// The depth part of a key: the depth's float bits (FULL32), or its 20-bit depth key
+// bits >> 12 (the reference's, emit_tile_keys.wgsl:26-29) minus the frame's base (0 unless
+// the keys are compressed). The key is (tile << shift) | depth part.
+__device__ __forceinline__ uint32_t depth_part(int key_mode, float depth, uint32_t base) {
     const uint32_t bits = __float_as_uint(depth);
-    if (key_mode == SP_KEYS_FULL32) return (Key)(((unsigned long long)tile << 32) | bits);
-    return (Key)(((unsigned long long)tile << SP_DEPTH_BITS) | (bits >> (32 - SP_DEPTH_BITS)));
+    return key_mode == SP_KEYS_FULL32 ? bits : (bits >> (32 - SP_DEPTH_BITS)) - base;
+}
+
+template <typename Key>
+__device__ __forceinline__ Key compose_key(uint32_t tile, uint32_t shift, uint32_t depth_bits) {
+    return (Key)(((unsigned long long)tile << shift) | depth_bits);
 }
 
 // Key emission, one warp per 32 Gaussians: the warp's slots are contiguous (the tile
@@ -42,14 +48,20 @@ __device__ __forceinline__ Key make_key(int key_mode, uint32_t tile, float depth
 template <typename Key>
 __global__ void __launch_bounds__(kBlock) k_emit(const float4* __restrict__ records, uint32_t* __restrict__ offsets,
                                                  const unsigned long long* __restrict__ block_offsets, uint32_t n,
-                                                 uint32_t tiles_x, int key_mode, int passes,
-                                                 const DeviceMeta* __restrict__ meta, Key* __restrict__ keys,
-                                                 uint32_t* __restrict__ values, uint32_t* __restrict__ histograms) {
+                                                 uint32_t tiles_x, int key_mode, const DeviceMeta* __restrict__ meta,
+                                                 Key* __restrict__ keys0, Key* __restrict__ keys1,
+                                                 uint32_t* __restrict__ values0, uint32_t* __restrict__ values1,
+                                                 uint32_t* __restrict__ histograms) {
     __shared__ uint32_t hist[kSortMaxPasses][kSortRadix];
     const uint32_t t = threadIdx.x, lane = lane_id();
+    // This frame's key geometry (k_scan_blocks): the passes it sorts, the tile shift, the
+    // depth base, and the ping-pong buffer the keys start in.
+    const int passes = (int)meta->passes;
+    const uint32_t tile_shift = meta->key_shift, base = meta->key_base;
+    Key* __restrict__ keys = meta->first_buffer ? keys1 : keys0;
+    uint32_t* __restrict__ values = meta->first_buffer ? values1 : values0;
     for (uint32_t i = t; i < (uint32_t)passes * kSortRadix; i += kBlock) (&hist[0][0])[i] = 0;
     __syncthreads();
-    const int tile_shift = key_mode == SP_KEYS_FULL32 ? 32 : SP_DEPTH_BITS;
     const unsigned long long capacity = meta->capacity;
     const uint32_t g = blockIdx.x * kBlock + t;
     uint32_t x0 = 0, y0 = 0, w = 1, count = 0;
@@ -69,9 +81,9 @@ __global__ void __launch_bounds__(kBlock) k_emit(const float4* __restrict__ reco
         // Depth-only digits: the same for every key of the Gaussian.
         const unsigned long long kept = index >= capacity ? 0ull : min((unsigned long long)count, capacity - index);
         if (kept) {
-            const Key depth_key = make_key<Key>(key_mode, 0u, depth);
-            for (int p = 0; p < passes && 8 * p + 8 <= tile_shift; ++p)
-                atomicAdd(&hist[p][(uint32_t)(depth_key >> (8 * p)) & 255u], (uint32_t)kept);
+            const uint32_t depth_key = depth_part(key_mode, depth, base);
+            for (int p = 0; p < passes && 8 * p + 8 <= (int)tile_shift; ++p)
+                atomicAdd(&hist[p][(depth_key >> (8 * p)) & 255u], (uint32_t)kept);
         }
     }
     // Exclusive scan of the counts over the warp.
@@ -84,7 +96,7 @@ __global__ void __launch_bounds__(kBlock) k_emit(const float4* __restrict__ reco
     const uint32_t exclusive = inclusive - count;
     const uint32_t total = __shfl_sync(0xffffffffu, inclusive, 31);
     const unsigned long long start = __shfl_sync(0xffffffffu, index, 0);
-    const int first_tile_pass = tile_shift / 8;
+    const int first_tile_pass = (int)tile_shift / 8;
     for (uint32_t round = 0; round * 32 < total; ++round) {
         const uint32_t e = round * 32 + lane;
         // The lane whose slots hold e: the last with exclusive <= e.
@@ -100,7 +112,8 @@ __global__ void __launch_bounds__(kBlock) k_emit(const float4* __restrict__ reco
         const unsigned long long slot = start + e;
         if (e < total && slot < capacity) {
             const uint32_t row = local / ow;
-            const Key key = make_key<Key>(key_mode, (oy0 + row) * tiles_x + ox0 + (local - row * ow), odepth);
+            const Key key = compose_key<Key>((oy0 + row) * tiles_x + ox0 + (local - row * ow), tile_shift,
+                                             depth_part(key_mode, odepth, base));
             keys[slot] = key;
             values[slot] = og;
             for (int p = first_tile_pass; p < passes; ++p)
@@ -120,9 +133,18 @@ __global__ void __launch_bounds__(kBlock) k_emit(const float4* __restrict__ reco
 // shared memory so that the global writes of each digit are contiguous.
 template <typename Key>
 __global__ void __launch_bounds__(kSortThreads, kSortBlocksPerSM)
-    k_sort_pass(int shift, uint32_t sequence, const Key* __restrict__ keys_in, const uint32_t* __restrict__ values_in,
-                Key* __restrict__ keys_out, uint32_t* __restrict__ values_out, const uint32_t* __restrict__ histogram,
-                uint32_t* ticket, unsigned long long* lookback, DeviceMeta* meta) {
+    k_sort_pass(int pass, uint32_t sequence, Key* keys0, uint32_t* values0, Key* keys1, uint32_t* values1,
+                const uint32_t* __restrict__ histogram, uint32_t* ticket, unsigned long long* lookback,
+                DeviceMeta* meta) {
+    // Passes past the ones this frame's keys need do nothing; the others ping-pong from the
+    // buffer the emission started in.
+    if (pass >= (int)meta->passes) return;
+    const int shift = 8 * pass;
+    const bool from1 = (meta->first_buffer ^ (uint32_t)pass) & 1u;
+    const Key* __restrict__ keys_in = from1 ? keys1 : keys0;
+    const uint32_t* __restrict__ values_in = from1 ? values1 : values0;
+    Key* __restrict__ keys_out = from1 ? keys0 : keys1;
+    uint32_t* __restrict__ values_out = from1 ? values0 : values1;
     extern __shared__ float4 smem4[];
     Key* s_keys = reinterpret_cast<Key*>(smem4);
     uint32_t* s_values = reinterpret_cast<uint32_t*>(s_keys + kSortPartition);
@@ -277,9 +299,10 @@ __global__ void __launch_bounds__(kSortThreads, kSortBlocksPerSM)
 }
 
 template <typename Key>
-__global__ void k_ranges(const Key* __restrict__ keys, const DeviceMeta* __restrict__ meta, int tile_shift,
-                         uint32_t tiles, uint2* __restrict__ ranges) {
+__global__ void k_ranges(const Key* __restrict__ keys, const DeviceMeta* __restrict__ meta, uint32_t tiles,
+                         uint2* __restrict__ ranges) {
     const uint32_t count = meta->count;
+    const uint32_t tile_shift = meta->key_shift;
     for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < count; i += gridDim.x * blockDim.x) {
         const uint32_t tile = (uint32_t)(keys[i] >> tile_shift);
         if (tile >= tiles) continue;
@@ -304,41 +327,54 @@ int sort_grid() {
 
 cudaError_t launch_emit(const float4* records, uint32_t* offsets, const unsigned long long* block_offsets, uint64_t n,
                         const sp_camera_uniform& cam, int key_mode, const SortPlan& plan, const DeviceMeta* meta,
-                        void* keys, uint32_t* values, uint32_t* sort_histograms, cudaStream_t stream) {
+                        void* keys0, void* keys1, uint32_t* values0, uint32_t* values1, uint32_t* sort_histograms,
+                        cudaStream_t stream) {
     const unsigned grid = grid_for(n, kBlock);
-    if (plan.key64)
-        k_emit<unsigned long long><<<grid, kBlock, 0, stream>>>(records, offsets, block_offsets, (uint32_t)n,
-                                                                cam.tiles_x, key_mode, plan.passes, meta,
-                                                                static_cast<unsigned long long*>(keys), values,
-                                                                sort_histograms);
-    else
-        k_emit<uint32_t><<<grid, kBlock, 0, stream>>>(records, offsets, block_offsets, (uint32_t)n, cam.tiles_x,
-                                                      key_mode, plan.passes, meta, static_cast<uint32_t*>(keys),
-                                                      values, sort_histograms);
+    if (plan.key64) {
+        using K = unsigned long long;
+        k_emit<K><<<grid, kBlock, 0, stream>>>(records, offsets, block_offsets, (uint32_t)n, cam.tiles_x, key_mode,
+                                               meta, static_cast<K*>(keys0), static_cast<K*>(keys1), values0, values1,
+                                               sort_histograms);
+    } else {
+        using K = uint32_t;
+        k_emit<K><<<grid, kBlock, 0, stream>>>(records, offsets, block_offsets, (uint32_t)n, cam.tiles_x, key_mode,
+                                               meta, static_cast<K*>(keys0), static_cast<K*>(keys1), values0, values1,
+                                               sort_histograms);
+    }
     return cudaGetLastError();
 }
 
-cudaError_t launch_sort_pass(const SortPlan& plan, int pass, uint32_t sequence, const void* keys_in,
-                             const uint32_t* values_in, void* keys_out, uint32_t* values_out,
-                             const uint32_t* sort_histograms, uint32_t* sort_tickets, unsigned long long* lookback,
-                             uint32_t max_partitions, DeviceMeta* meta, cudaStream_t stream) {
+cudaError_t launch_sort_pass(const SortPlan& plan, int pass, uint32_t sequence, void* keys0, uint32_t* values0,
+                             void* keys1, uint32_t* values1, const uint32_t* sort_histograms, uint32_t* sort_tickets,
+                             unsigned long long* lookback, uint32_t max_partitions, DeviceMeta* meta,
+                             cudaStream_t stream) {
     const unsigned grid = (unsigned)std::min<int>(sort_grid(), (int)std::max<uint32_t>(max_partitions, 1u));
     const uint32_t* hist = sort_histograms + pass * kSortRadix;
     if (plan.key64) {
         using K = unsigned long long;
         const size_t smem = kSortPartition * (sizeof(K) + sizeof(uint32_t));
-        cudaError_t err = cudaFuncSetAttribute(k_sort_pass<K>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        if (err != cudaSuccess) return err;
-        k_sort_pass<K><<<grid, kSortThreads, smem, stream>>>(8 * pass, sequence, static_cast<const K*>(keys_in),
-                                                             values_in, static_cast<K*>(keys_out), values_out, hist,
+        static bool configured = false;
+        if (!configured) {
+            const cudaError_t err =
+                cudaFuncSetAttribute(k_sort_pass<K>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+            if (err != cudaSuccess) return err;
+            configured = true;
+        }
+        k_sort_pass<K><<<grid, kSortThreads, smem, stream>>>(pass, sequence, static_cast<K*>(keys0), values0,
+                                                             static_cast<K*>(keys1), values1, hist,
                                                              sort_tickets + pass, lookback, meta);
     } else {
         using K = uint32_t;
         const size_t smem = kSortPartition * (sizeof(K) + sizeof(uint32_t));
-        cudaError_t err = cudaFuncSetAttribute(k_sort_pass<K>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        if (err != cudaSuccess) return err;
-        k_sort_pass<K><<<grid, kSortThreads, smem, stream>>>(8 * pass, sequence, static_cast<const K*>(keys_in),
-                                                             values_in, static_cast<K*>(keys_out), values_out, hist,
+        static bool configured = false;
+        if (!configured) {
+            const cudaError_t err =
+                cudaFuncSetAttribute(k_sort_pass<K>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+            if (err != cudaSuccess) return err;
+            configured = true;
+        }
+        k_sort_pass<K><<<grid, kSortThreads, smem, stream>>>(pass, sequence, static_cast<K*>(keys0), values0,
+                                                             static_cast<K*>(keys1), values1, hist,
                                                              sort_tickets + pass, lookback, meta);
     }
     return cudaGetLastError();
@@ -351,10 +387,9 @@ cudaError_t launch_ranges(const SortPlan& plan, const void* keys, const DeviceMe
     const unsigned grid = (unsigned)std::min<uint64_t>(std::max<uint64_t>(grid_for(capacity, kBlock), 1), 148 * 16);
     if (plan.key64)
         k_ranges<unsigned long long><<<grid, kBlock, 0, stream>>>(static_cast<const unsigned long long*>(keys), meta,
-                                                                   plan.tile_shift, tiles, ranges);
+                                                                   tiles, ranges);
     else
-        k_ranges<uint32_t><<<grid, kBlock, 0, stream>>>(static_cast<const uint32_t*>(keys), meta, plan.tile_shift,
-                                                         tiles, ranges);
+        k_ranges<uint32_t><<<grid, kBlock, 0, stream>>>(static_cast<const uint32_t*>(keys), meta, tiles, ranges);
     return cudaGetLastError();
 }
 

@@ -38,11 +38,19 @@ def random_rotations(rng: np.random.Generator, n: int) -> np.ndarray:
     return q / np.linalg.norm(q, axis=1, keepdims=True)
 
 
-def _sh(rng: np.random.Generator, n: int, degree: int, rest_sigma: float) -> np.ndarray:
+def _sh(rng: np.random.Generator, n: int, degree: int, rest_sigma: float, single: bool = False) -> np.ndarray:
+    """DC from uniform colours, higher bands ~N(0, rest_sigma); `single` draws the higher
+    bands in float32 (the multi-million-Gaussian configs, where float64 draws are slow)."""
     sh = np.zeros((n, (degree + 1) ** 2, 3), np.float32)
     sh[:, 0, :] = rgb_to_sh_dc(rng.uniform(0.0, 1.0, (n, 3)))
     if degree > 0:
-        sh[:, 1:, :] = rng.normal(0.0, rest_sigma, (n, (degree + 1) ** 2 - 1, 3))
+        shape = (n, (degree + 1) ** 2 - 1, 3)
+        if single:
+            rest = rng.standard_normal(shape, dtype=np.float32)
+            rest *= np.float32(rest_sigma)
+            sh[:, 1:, :] = rest
+        else:
+            sh[:, 1:, :] = rng.normal(0.0, rest_sigma, shape)
     return sh
 
 
@@ -148,7 +156,7 @@ def config(index: int, scale: float = 1.0) -> Scene:
             rng.normal(-5.5, 0.8, (n, 3)),
             random_rotations(rng, n),
             rng.normal(0.5, 1.5, n),
-            _sh(rng, n, 3, 0.05),
+            _sh(rng, n, 3, 0.05, single=True),
         )
         if index == 3:
             cams = circle_cameras(64, 4.0, 1920, 1080, elevation=0.8)

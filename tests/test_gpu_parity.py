@@ -75,12 +75,19 @@ def test_tile_lists_bit_exact(ctx, name):
     assert np.array_equal(rast.read_tile_ranges(), want["ranges"]), f"{name}: tile ranges differ"
 
 
-@pytest.mark.parametrize("key_mode", [sb.SP_KEYS_REF20, sb.SP_KEYS_FULL32])
-def test_tile_lists_over_4096_tiles(ctx, key_mode):
+@pytest.mark.parametrize("key_mode,width,height", [(sb.SP_KEYS_REF20, 1920, 1080), (sb.SP_KEYS_FULL32, 1920, 1080),
+                                                    (sb.SP_KEYS_REF20, 2560, 1440)])
+def test_tile_lists_over_4096_tiles(ctx, key_mode, width, height):
     """1920 x 1080 has 8160 tiles, which the reference's 32-bit keys refuse
-    (rasterizer.rs:188-192); the 64-bit keys keep the same order."""
+    (rasterizer.rs:188-192): REF20 order in compressed 32-bit keys (the frame's depth-key
+    range), FULL32 in 64-bit keys; 2560 x 1440 (14400 tiles) in the reference's layout in 64
+    bits. The same order as the oracle's either way, read back in the reference's layout."""
     s = scenes.config(3, scale=0.002)
-    cloud, camera = s.cloud, s.cameras[0]
+    cloud = s.cloud
+    base = s.cameras[0]
+    camera = sb.PinholeCamera(base.rotation, base.translation,
+                              (base.focal[0] * width / base.width, base.focal[1] * width / base.width),
+                              (width / 2.0, height / 2.0), width, height)
     rast, _, _ = make_rasterizer(ctx, cloud, camera, key_mode=key_mode)
     rast.encode_forward()
     keys, gauss = rast.read_sorted_intersections()
