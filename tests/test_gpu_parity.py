@@ -33,6 +33,11 @@ def scene_cases():
         "random600_80x48": (random_cloud(600, rng), camera_at_origin(80, 48, 60.0)),
         "random3000_sh3_256x192": (random_cloud(3000, np.random.default_rng(9), sh_degree=3),
                                    camera_at_origin(256, 192, 180.0)),
+        # Ragged image sizes (partial tiles and partial 8 x 8 warp blocks) and SH 1, 2.
+        "random800_sh1_100x70": (random_cloud(800, np.random.default_rng(12), sh_degree=1),
+                                 camera_at_origin(100, 70, 70.0)),
+        "random500_sh2_37x29": (random_cloud(500, np.random.default_rng(13), sh_degree=2),
+                                camera_at_origin(37, 29, 30.0)),
     }
     s = scenes.config(0, scale=0.25)
     cases["config0_5k_256"] = (s.cloud, s.cameras[1])
