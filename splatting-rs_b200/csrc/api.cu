@@ -100,6 +100,7 @@ struct sp_rasterizer {
     // The camera the projection kernels read: written by sp_set_camera (an asynchronous copy)
     // or by the device pose step (sp_device_poses_step).
     sp_camera_uniform* camera_dev = nullptr;
+    bool camera_on_device = false;  // the last camera came from the device pose step
     float4* image = nullptr;
     uint32_t* contributions = nullptr;
     float4* ssim_partials = nullptr;
@@ -497,11 +498,8 @@ sp_status sp_set_camera(sp_rasterizer* r, const sp_camera_uniform* camera) {
     SP_REQUIRE(r->ctx, camera->width == r->width && camera->height == r->height, SP_ERR_INVALID, "camera image size");
     SP_REQUIRE(r->ctx, camera->tiles_x == r->tiles_x && camera->tiles_y == r->tiles_y, SP_ERR_INVALID,
                "camera tile grid");
-    SP_CHECK(select_device(r->ctx));
     r->camera = *camera;
-    // From pageable memory: the copy is staged before the call returns.
-    SP_CUDA(r->ctx, cudaMemcpyAsync(r->camera_dev, camera, sizeof(sp_camera_uniform), cudaMemcpyHostToDevice,
-                                    r->ctx->stream));
+    r->camera_on_device = false;
     return SP_OK;
 }
 
@@ -512,8 +510,9 @@ sp_status sp_forward(sp_rasterizer* r) {
     cudaStream_t st = ctx->stream;
     {
         KernelSpan span(ctx, SP_K_PROJECT);
-        SP_CUDA(ctx, launch_project(r->params, r->n, (int)r->options.sh_degree, r->camera_dev, r->records, r->radii,
-                                    r->offsets, r->block_totals, r->plan.compressed ? r->meta : nullptr, st));
+        SP_CUDA(ctx, launch_project(r->params, r->n, (int)r->options.sh_degree, r->camera,
+                                    r->camera_on_device ? r->camera_dev : nullptr, r->records, r->radii, r->offsets,
+                                    r->block_totals, r->plan.compressed ? r->meta : nullptr, st));
     }
     {
         KernelSpan span(ctx, SP_K_SCAN);
@@ -602,7 +601,8 @@ sp_status sp_backward_adam(sp_rasterizer* r, sp_adam* adam, float position_rate_
                     adam->bias1, adam->bias2, adam->max_log_scale, adam->max_log_anisotropy};
     KernelSpan span(r->ctx, SP_K_BACKWARD_ADAM);
     SP_CUDA(r->ctx, launch_project_backward(r->params, r->n, (int)r->options.sh_degree, (int)r->options.backward_mode,
-                                            r->camera_dev, r->records, r->radii, r->offsets, r->slot_gradients,
+                                            r->camera, r->camera_on_device ? r->camera_dev : nullptr, r->records,
+                                            r->radii, r->offsets, r->slot_gradients,
                                             r->capacity, r->gaussian_gradients, r->param_gradients, 0,
                                             r->camera_partials, r->camera_done, r->camera_gradient,
                                             r->densify_stats, &step, r->ctx->stream));
@@ -618,7 +618,8 @@ sp_status sp_backward(sp_rasterizer* r) {
     {
         KernelSpan span(r->ctx, SP_K_PROJECT_BACKWARD);
         SP_CUDA(r->ctx, launch_project_backward(
-                            r->params, r->n, (int)r->options.sh_degree, (int)r->options.backward_mode, r->camera_dev,
+                            r->params, r->n, (int)r->options.sh_degree, (int)r->options.backward_mode, r->camera,
+                            r->camera_on_device ? r->camera_dev : nullptr,
                             r->records, r->radii, r->offsets, r->slot_gradients, r->capacity, r->gaussian_gradients,
                             r->param_gradients, (int)r->options.accumulate_gradients, r->camera_partials,
                             r->camera_done, r->camera_gradient, r->densify_stats, nullptr, st));
@@ -816,6 +817,7 @@ sp_status sp_device_poses_set_camera(sp_device_poses* dp, uint32_t view) {
     SP_CHECK(select_device(r->ctx));
     SP_CUDA(r->ctx, launch_pose_step(dp->initial, dp->states, dp->shared, r->camera_gradient, dp->views, dp->views,
                                      view, 0.0, r->camera_dev, r->ctx->stream));
+    r->camera_on_device = true;
     return SP_OK;
 }
 
@@ -829,6 +831,7 @@ sp_status sp_device_poses_step(sp_device_poses* dp, uint32_t view, uint32_t next
     SP_CHECK(select_device(r->ctx));
     SP_CUDA(r->ctx, launch_pose_step(dp->initial, dp->states, dp->shared, r->camera_gradient, dp->views, view,
                                      next_view, (double)rate_factor, r->camera_dev, r->ctx->stream));
+    r->camera_on_device = true;
     return SP_OK;
 }
 

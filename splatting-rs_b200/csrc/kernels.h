@@ -14,12 +14,13 @@ namespace splat {
 
 // project_forward.wgsl:19-93 with the scan's first level (scan.wgsl:27-62) fused: per
 // block of 256 Gaussians the exclusive prefix of the tile counts and the block total.
-// `cam`: the camera in device memory (sp_camera_uniform, 80 B).
+// The camera is `cam`, or when `cam_device` is non-null the 80 B there (written on the device).
 // With `depth_range` non-null (compressed keys) the depth keys' range of the Gaussians that
 // emit keys is accumulated into its depth_lo / depth_hi.
-cudaError_t launch_project(const float* params, uint64_t n, int sh_degree, const sp_camera_uniform* cam,
-                           float4* records, uint32_t* radii, uint32_t* local_offsets, uint32_t* block_totals,
-                           DeviceMeta* depth_range, cudaStream_t stream);
+cudaError_t launch_project(const float* params, uint64_t n, int sh_degree, const sp_camera_uniform& cam,
+                           const sp_camera_uniform* cam_device, float4* records, uint32_t* radii,
+                           uint32_t* local_offsets, uint32_t* block_totals, DeviceMeta* depth_range,
+                           cudaStream_t stream);
 // scan_tile_counts (scan.wgsl:64-81): scans the block totals into 64-bit block offsets,
 // fills the meta (count, overflow, sort partitions, this frame's key geometry) and zeroes
 // the sort's histograms and partition tickets for this forward pass.
@@ -41,7 +42,7 @@ struct AdamLaunch {
 // parameter gradients are not written but consumed by that Adam step (adam.wgsl,
 // clamp_scales.wgsl) in the same kernel.
 cudaError_t launch_project_backward(const float* params, uint64_t n, int sh_degree, int mode,
-                                    const sp_camera_uniform* cam,
+                                    const sp_camera_uniform& cam, const sp_camera_uniform* cam_device,
                                     const float4* records, const uint32_t* radii, const uint32_t* offsets,
                                     const float* slot_gradients, uint64_t capacity, const float4* gaussian_gradients,
                                     float* param_gradients, int accumulate, float* camera_partials,

@@ -87,28 +87,38 @@ __device__ __forceinline__ void project_one(const float* p, const sp_camera_unif
     *count_out = (uint32_t)cnt;
 }
 
-// The camera of the pass, copied from device memory (where sp_set_camera or the device
-// pose step put it) into shared memory by the first threads; visible after the next barrier.
+// The camera of the pass. Set by the host (sp_set_camera) it is a kernel argument, whose
+// fields the instructions read as constant-bank operands; written on the device (the device
+// pose step: DEV) it is copied from device memory into shared memory by the first threads,
+// visible after the next barrier.
 __device__ __forceinline__ void load_camera(const sp_camera_uniform* __restrict__ camera, sp_camera_uniform& s_cam) {
     constexpr uint32_t kWords = sizeof(sp_camera_uniform) / sizeof(uint32_t);
     if (threadIdx.x < kWords)
         reinterpret_cast<uint32_t*>(&s_cam)[threadIdx.x] = reinterpret_cast<const uint32_t*>(camera)[threadIdx.x];
 }
 
-template <int DEG>
+template <bool DEV>
+__device__ __forceinline__ const sp_camera_uniform& pick_camera(const sp_camera_uniform& argument,
+                                                                const sp_camera_uniform& shared) {
+    if constexpr (DEV) return shared;
+    else return argument;
+}
+
+template <int DEG, bool DEV>
 __global__ void __launch_bounds__(kBlock) k_project(const float* __restrict__ params, uint32_t n,
-                                                    const sp_camera_uniform* __restrict__ camera,
+                                                    const sp_camera_uniform camera_argument,
+                                                    const sp_camera_uniform* __restrict__ camera_device,
                                                     float4* __restrict__ records, uint32_t* __restrict__ radii,
                                                     uint32_t* __restrict__ local_offsets,
                                                     uint32_t* __restrict__ block_totals, DeviceMeta* depth_range) {
     constexpr int S = SP_PARAM_STRIDE(DEG);
     extern __shared__ float4 smem4[];
     __shared__ sp_camera_uniform s_cam;
-    const sp_camera_uniform& cam = s_cam;
+    const sp_camera_uniform& cam = pick_camera<DEV>(camera_argument, s_cam);
     float* sp = reinterpret_cast<float*>(smem4);
     const uint32_t g0 = blockIdx.x * kBlock;
     const uint32_t here = min((uint32_t)kBlock, n - g0);
-    load_camera(camera, s_cam);
+    if constexpr (DEV) load_camera(camera_device, s_cam);
     stage_in(params + (size_t)g0 * S, here * S, sp);
     __syncthreads();
     const uint32_t t = threadIdx.x;
@@ -458,17 +468,18 @@ struct FusedAdam {
     AdamStep step;
 };
 
-template <int DEG, int MODE, bool FUSED>
+template <int DEG, int MODE, bool FUSED, bool DEV>
 __global__ void __launch_bounds__(kBlock, 3) k_project_backward(
-    const float* params, uint32_t n, const sp_camera_uniform* __restrict__ camera, const float4* __restrict__ records,
+    const float* params, uint32_t n, const sp_camera_uniform camera_argument,
+    const sp_camera_uniform* __restrict__ camera_device, const float4* __restrict__ records,
     const uint32_t* __restrict__ radii, const uint32_t* __restrict__ offsets, const float* __restrict__ slot_gradients,
     unsigned long long capacity, const float4* __restrict__ gaussian_gradients, float* __restrict__ param_gradients,
     int accumulate, float* __restrict__ camera_partials, uint32_t* camera_done, float* __restrict__ camera_gradient,
     float4* __restrict__ densify_stats, const FusedAdam adam) {
     constexpr int S = SP_PARAM_STRIDE(DEG);
     __shared__ sp_camera_uniform s_cam;
-    const sp_camera_uniform& cam = s_cam;
-    load_camera(camera, s_cam);
+    const sp_camera_uniform& cam = pick_camera<DEV>(camera_argument, s_cam);
+    if constexpr (DEV) load_camera(camera_device, s_cam);
     extern __shared__ float4 smem4[];
     float* sp = reinterpret_cast<float*>(smem4);
     __shared__ float warp_camera[kBlock / 32][SP_CAMERA_GRAD_STRIDE];
@@ -576,28 +587,33 @@ cudaError_t set_smem(Kernel kernel, size_t bytes) {
 
 }  // namespace
 
-cudaError_t launch_project(const float* params, uint64_t n, int sh_degree, const sp_camera_uniform* cam,
-                           float4* records, uint32_t* radii, uint32_t* local_offsets, uint32_t* block_totals,
-                           DeviceMeta* depth_range, cudaStream_t stream) {
+cudaError_t launch_project(const float* params, uint64_t n, int sh_degree, const sp_camera_uniform& cam,
+                           const sp_camera_uniform* cam_device, float4* records, uint32_t* radii,
+                           uint32_t* local_offsets, uint32_t* block_totals, DeviceMeta* depth_range,
+                           cudaStream_t stream) {
     const unsigned grid = grid_for(n, kBlock);
     const size_t smem = (size_t)kBlock * SP_PARAM_STRIDE(sh_degree) * sizeof(float);
     cudaError_t err = cudaSuccess;
-#define SPLAT_PROJECT(D)                                                                                  \
-    case D:                                                                                               \
-        if ((err = set_smem(k_project<D>, smem)) != cudaSuccess) return err;                              \
-        k_project<D><<<grid, kBlock, smem, stream>>>(params, (uint32_t)n, cam, records, radii, local_offsets, \
-                                                     block_totals, depth_range);                          \
-        break;
-    switch (sh_degree) {
-        SPLAT_PROJECT(0)
-        SPLAT_PROJECT(1)
-        SPLAT_PROJECT(2)
-        SPLAT_PROJECT(3)
-        default:
-            return cudaErrorInvalidValue;
-    }
-#undef SPLAT_PROJECT
+#define SPLAT_PROJECT_ONE(D, V)                                                                           \
+    if ((err = set_smem(k_project<D, V>, smem)) != cudaSuccess) return err;                                \
+    k_project<D, V><<<grid, kBlock, smem, stream>>>(params, (uint32_t)n, cam, cam_device, records, radii,  \
+                                                    local_offsets, block_totals, depth_range);            \
     return cudaGetLastError();
+#define SPLAT_PROJECT(D)                \
+    if (sh_degree == D) {               \
+        if (cam_device) {               \
+            SPLAT_PROJECT_ONE(D, true)  \
+        } else {                        \
+            SPLAT_PROJECT_ONE(D, false) \
+        }                               \
+    }
+    SPLAT_PROJECT(0)
+    SPLAT_PROJECT(1)
+    SPLAT_PROJECT(2)
+    SPLAT_PROJECT(3)
+#undef SPLAT_PROJECT
+#undef SPLAT_PROJECT_ONE
+    return cudaErrorInvalidValue;
 }
 
 cudaError_t launch_scan_blocks(const uint32_t* block_totals, unsigned long long* block_offsets, uint32_t blocks,
@@ -609,7 +625,8 @@ cudaError_t launch_scan_blocks(const uint32_t* block_totals, unsigned long long*
 }
 
 cudaError_t launch_project_backward(const float* params, uint64_t n, int sh_degree, int mode,
-                                    const sp_camera_uniform* cam, const float4* records, const uint32_t* radii,
+                                    const sp_camera_uniform& cam, const sp_camera_uniform* cam_device,
+                                    const float4* records, const uint32_t* radii,
                                     const uint32_t* offsets, const float* slot_gradients, uint64_t capacity,
                                     const float4* gaussian_gradients, float* param_gradients, int accumulate,
                                     float* camera_partials, uint32_t* camera_done, float* camera_gradient,
@@ -628,18 +645,25 @@ cudaError_t launch_project_backward(const float* params, uint64_t n, int sh_degr
         fused.step.max_log_scale = adam->max_log_scale;
         fused.step.max_log_anisotropy = adam->max_log_anisotropy;
     }
-#define SPLAT_PB_ONE(D, M, F)                                                                                   \
-    if ((err = set_smem(k_project_backward<D, M, F>, smem)) != cudaSuccess) return err;                         \
-    k_project_backward<D, M, F><<<grid, kBlock, smem, stream>>>(                                                \
-        params, (uint32_t)n, cam, records, radii, offsets, slot_gradients, capacity, gaussian_gradients,         \
-        param_gradients, accumulate, camera_partials, camera_done, camera_gradient, densify_stats, fused);      \
+#define SPLAT_PB_ONE(D, M, F, V)                                                                               \
+    if ((err = set_smem(k_project_backward<D, M, F, V>, smem)) != cudaSuccess) return err;                     \
+    k_project_backward<D, M, F, V><<<grid, kBlock, smem, stream>>>(                                            \
+        params, (uint32_t)n, cam, cam_device, records, radii, offsets, slot_gradients, capacity,               \
+        gaussian_gradients, param_gradients, accumulate, camera_partials, camera_done, camera_gradient,        \
+        densify_stats, fused);                                                                                 \
     return cudaGetLastError();
+#define SPLAT_PB_CAM(D, M, F)              \
+    if (cam_device) {                      \
+        SPLAT_PB_ONE(D, M, F, true)        \
+    } else {                               \
+        SPLAT_PB_ONE(D, M, F, false)       \
+    }
 #define SPLAT_PB(D, M)                    \
     if (sh_degree == D && mode == M) {    \
         if (adam) {                       \
-            SPLAT_PB_ONE(D, M, true)      \
+            SPLAT_PB_CAM(D, M, true)      \
         } else {                          \
-            SPLAT_PB_ONE(D, M, false)     \
+            SPLAT_PB_CAM(D, M, false)     \
         }                                 \
     }
     SPLAT_PB(0, SP_BWD_DETERMINISTIC)
@@ -651,6 +675,7 @@ cudaError_t launch_project_backward(const float* params, uint64_t n, int sh_degr
     SPLAT_PB(3, SP_BWD_DETERMINISTIC)
     SPLAT_PB(3, SP_BWD_ATOMIC)
 #undef SPLAT_PB
+#undef SPLAT_PB_CAM
 #undef SPLAT_PB_ONE
     return cudaErrorInvalidValue;
 }
