@@ -430,8 +430,10 @@ def main() -> None:
         v = view_of(step)
         factor = sb.position_rate_factor(step % iterations, iterations)
         if world == 1:
-            # One library call: the step and its 88-byte read-back.
-            gradient, _ = rast.train_step(adam_e2e, poses.camera(v), v, factor)
+            # One library call: the refinement's camera, the step, its 88-byte read-back and
+            # the host pose step.
+            rast.train_step_host_poses(adam_e2e, poses, v, factor)
+            return
         else:
             rast.set_camera(poses.camera(v))
             rast.encode_forward()

@@ -412,6 +412,12 @@ sp_status sp_pose_refinement_correction(const sp_pose_refinement* p, uint32_t vi
 double sp_pose_refinement_focal_scale(const sp_pose_refinement* p);
 sp_status sp_pose_refinement_last_gradient(const sp_pose_refinement* p, sp_pose_gradient* out);
 
+/* Trainer::step_async with pose refinement (training.rs:197-209) in one call: the camera of
+ * `view` from the host refinement, sp_train_step with its camera-gradient read-back, then the
+ * host pose step of `view` (pose_refinement.rs:113-163). Synchronises once. */
+sp_status sp_train_step_host_poses(sp_rasterizer* r, sp_adam* adam, sp_pose_refinement* poses, uint32_t view,
+                                   float position_rate_factor, sp_loss_terms* loss_out);
+
 /* The pose refinement on the device (no counterpart in the reference, whose
  * pose_refinement.rs:113-163 runs on the host after reading back the camera gradient every
  * step, training.rs:205-208). A copy of a host refinement's state (sp_pose_refinement) bound

@@ -762,6 +762,20 @@ sp_status sp_train_step(sp_rasterizer* r, sp_adam* adam, const sp_camera_uniform
     return SP_OK;
 }
 
+sp_status sp_train_step_host_poses(sp_rasterizer* r, sp_adam* adam, sp_pose_refinement* poses, uint32_t view,
+                                   float position_rate_factor, sp_loss_terms* loss_out) {
+    if (!r || !adam || !poses || view >= poses->initial.size()) return SP_ERR_INVALID;
+    // training.rs:197-209 with pose refinement: the view's corrected camera, the step, the
+    // camera gradient read back, the host pose step (pose_refinement.rs:113-163).
+    const sp_camera_uniform camera = splat::pose::uniform_of(
+        splat::pose::corrected(poses->initial[view], poses->views[view].correction, poses->shared.focal_log_scale));
+    sp_camera_gradient gradient;
+    SP_CHECK(sp_train_step(r, adam, &camera, view, position_rate_factor, &gradient, loss_out));
+    const sp_status status = sp_pose_refinement_step(poses, view, &gradient, position_rate_factor);
+    if (status != SP_OK) return fail(r->ctx, status, "pose step: non-finite pose gradient");
+    return SP_OK;
+}
+
 // ------------------------------------------------------------------ device pose refinement
 
 struct sp_device_poses {

@@ -241,6 +241,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "sp_pose_refinement_correction": (c_int, [_P, c_uint32, POINTER(PoseCorrectionC)]),
     "sp_pose_refinement_focal_scale": (c_double, [_P]),
     "sp_pose_refinement_last_gradient": (c_int, [_P, POINTER(PoseGradientC)]),
+    "sp_train_step_host_poses": (c_int, [_P, _P, _P, c_uint32, c_float, POINTER(LossTermsC)]),
     "sp_device_poses_create": (c_int, [_P, _P, POINTER(_P)]),
     "sp_device_poses_destroy": (None, [_P]),
     "sp_device_poses_set_camera": (c_int, [_P, c_uint32]),

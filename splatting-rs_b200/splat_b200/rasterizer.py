@@ -372,6 +372,15 @@ class Rasterizer:
                                            ctypes.byref(gradient), ctypes.byref(loss)), "train_step")
         return gradient, LossTerms(loss.l1, loss.alpha, loss.dssim, loss.total)
 
+    def train_step_host_poses(self, adam, poses, view: int, rate_factor: float) -> LossTerms:
+        """Trainer::step_async with pose refinement in one call (sp_train_step_host_poses):
+        the refinement's camera of `view`, the step, the camera gradient read back, the host
+        pose step. Returns the step's loss terms."""
+        loss = LossTermsC()
+        self._check(self.lib.sp_train_step_host_poses(self.handle, adam.handle, poses.handle, view, float(rate_factor),
+                                                       ctypes.byref(loss)), "train_step_host_poses")
+        return LossTerms(loss.l1, loss.alpha, loss.dssim, loss.total)
+
     def train_step_device_poses(self, adam, poses, view: int, next_view: int, rate_factor: float,
                                 loss_sums=None) -> None:
         """One training step with the poses refined on the device (sp_train_step_device_poses),

@@ -157,3 +157,36 @@ def test_device_poses_equal_host_poses(ctx):
         np.testing.assert_allclose(b.translation, a.translation, rtol=1e-9, atol=1e-15)
     # The refinement moved the poses of every view but the fixed first one.
     assert np.all(c0[0].rotation == 0.0) and np.any(c0[1].rotation != 0.0)
+
+
+def test_host_pose_step_in_one_call(ctx):
+    """sp_train_step_host_poses (camera from the refinement, step, read-back, host pose step in
+    one call) against the same sequence from Python: identical losses and corrections."""
+    import torch
+
+    scene = scenes.config(0)
+    cams = scene.cameras
+    gt_dev = torch.from_numpy(ground_truth(scene).reshape(-1)).cuda()
+    extent = np.float32(sb.cameras_extent(cams))
+    rates = sb.LEARNING_RATES_3DGS
+    runs = []
+    for one_call in (False, True):
+        params = torch.from_numpy(scene.cloud.to_packed()).cuda()
+        rast = sb.Rasterizer(ctx, params, len(scene.cloud), 256, 256, gt_dev, len(cams),
+                             sb.default_options(backward_mode=sb.SP_BWD_DETERMINISTIC))
+        adam = sb.Adam(ctx, params, rast, len(scene.cloud), rates, extent)
+        poses = sb.PoseRefinement(cams, rates, float(extent))
+        losses = []
+        for step in range(6):
+            view, factor = step % len(cams), sb.position_rate_factor(step, 6)
+            if one_call:
+                losses.append(rast.train_step_host_poses(adam, poses, view, factor).total)
+            else:
+                gradient, loss = rast.train_step(adam, poses.camera(view), view, factor)
+                poses.step(view, gradient, factor)
+                losses.append(loss.total)
+        runs.append((losses, [poses.correction(v) for v in range(len(cams))], poses.focal_scale()))
+        del adam, rast
+    assert runs[0][0] == runs[1][0] and runs[0][2] == runs[1][2]
+    for a, b in zip(runs[0][1], runs[1][1]):
+        assert np.array_equal(a.rotation, b.rotation) and np.array_equal(a.translation, b.translation)
