@@ -229,6 +229,13 @@ sp_status sp_forward(sp_rasterizer* r);
 sp_status sp_loss(sp_rasterizer* r, uint32_t view);
 /* Rasterizer::encode_backward (rasterizer.rs:429-442). */
 sp_status sp_backward(sp_rasterizer* r);
+/* sp_backward in parts (no counterpart in the reference), so that a collective on the
+ * gradients of some Gaussians can overlap the backward of the others: the blend backward
+ * (K8) once, then the projection backward (K9-K10) over ranges [first, first + count) of the
+ * Gaussians, first a multiple of 256, the ranges covering all of them once, in order; the
+ * camera gradient is complete after the last range. */
+sp_status sp_backward_blend(sp_rasterizer* r);
+sp_status sp_backward_project(sp_rasterizer* r, uint64_t first, uint64_t count);
 /* write_loss_gradient / write_image (rasterizer.rs:446-456): width*height*4 floats from
  * host memory (src_is_device = 0) or device memory (1). */
 sp_status sp_write_loss_gradient(sp_rasterizer* r, const float* src, int src_is_device);

@@ -605,7 +605,31 @@ sp_status sp_backward_adam(sp_rasterizer* r, sp_adam* adam, float position_rate_
                                             r->radii, r->offsets, r->slot_gradients,
                                             r->capacity, r->gaussian_gradients, r->param_gradients, 0,
                                             r->camera_partials, r->camera_done, r->camera_gradient,
-                                            r->densify_stats, &step, r->ctx->stream));
+                                            r->densify_stats, &step, 0, r->n, r->ctx->stream));
+    return SP_OK;
+}
+
+sp_status sp_backward_blend(sp_rasterizer* r) {
+    if (!r) return SP_ERR_INVALID;
+    SP_REQUIRE(r->ctx, r->forward_done, SP_ERR_INVALID, "backward before any forward pass");
+    SP_CHECK(select_device(r->ctx));
+    return blend_backward(r);
+}
+
+sp_status sp_backward_project(sp_rasterizer* r, uint64_t first, uint64_t count) {
+    if (!r) return SP_ERR_INVALID;
+    SP_REQUIRE(r->ctx, r->forward_done, SP_ERR_INVALID, "backward before any forward pass");
+    SP_REQUIRE(r->ctx, first % kBlock == 0 && first <= r->n && count <= r->n - first, SP_ERR_INVALID,
+               "range: first a multiple of 256, inside the Gaussians");
+    SP_CHECK(select_device(r->ctx));
+    KernelSpan span(r->ctx, SP_K_PROJECT_BACKWARD);
+    SP_CUDA(r->ctx, launch_project_backward(r->params, r->n, (int)r->options.sh_degree, (int)r->options.backward_mode,
+                                            r->camera, r->camera_on_device ? r->camera_dev : nullptr, r->records,
+                                            r->radii, r->offsets, r->slot_gradients, r->capacity,
+                                            r->gaussian_gradients, r->param_gradients,
+                                            (int)r->options.accumulate_gradients, r->camera_partials, r->camera_done,
+                                            r->camera_gradient, r->densify_stats, nullptr, first, count,
+                                            r->ctx->stream));
     return SP_OK;
 }
 
@@ -622,7 +646,7 @@ sp_status sp_backward(sp_rasterizer* r) {
                             r->camera_on_device ? r->camera_dev : nullptr,
                             r->records, r->radii, r->offsets, r->slot_gradients, r->capacity, r->gaussian_gradients,
                             r->param_gradients, (int)r->options.accumulate_gradients, r->camera_partials,
-                            r->camera_done, r->camera_gradient, r->densify_stats, nullptr, st));
+                            r->camera_done, r->camera_gradient, r->densify_stats, nullptr, 0, r->n, st));
     }
     return SP_OK;
 }

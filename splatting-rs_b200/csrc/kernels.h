@@ -38,8 +38,10 @@ struct AdamLaunch {
     const float* lr_by_slot;  // host, one rate per parameter slot
     float bias1, bias2, max_log_scale, max_log_anisotropy;
 };
-// project_backward.wgsl plus reduce_camera_gradient.wgsl; with `adam` non-null the
-// parameter gradients are not written but consumed by that Adam step (adam.wgsl,
+// project_backward.wgsl plus reduce_camera_gradient.wgsl over the Gaussians
+// [first, first + count) (first a multiple of 256; ranges that cover all n, launched in order
+// on one stream, the last block of all reducing the camera gradient); with `adam` non-null
+// the parameter gradients are not written but consumed by that Adam step (adam.wgsl,
 // clamp_scales.wgsl) in the same kernel.
 cudaError_t launch_project_backward(const float* params, uint64_t n, int sh_degree, int mode,
                                     const sp_camera_uniform& cam, const sp_camera_uniform* cam_device,
@@ -47,7 +49,7 @@ cudaError_t launch_project_backward(const float* params, uint64_t n, int sh_degr
                                     const float* slot_gradients, uint64_t capacity, const float4* gaussian_gradients,
                                     float* param_gradients, int accumulate, float* camera_partials,
                                     uint32_t* camera_done, float* camera_gradient, float4* densify_stats,
-                                    const AdamLaunch* adam, cudaStream_t stream);
+                                    const AdamLaunch* adam, uint64_t first, uint64_t count, cudaStream_t stream);
 // The reference's 80-B Projected records (diagnostics).
 cudaError_t launch_to_projected(const float4* records, const uint32_t* radii, uint64_t n, sp_projected* out,
                                 cudaStream_t stream);

@@ -475,7 +475,7 @@ __global__ void __launch_bounds__(kBlock, 3) k_project_backward(
     const uint32_t* __restrict__ radii, const uint32_t* __restrict__ offsets, const float* __restrict__ slot_gradients,
     unsigned long long capacity, const float4* __restrict__ gaussian_gradients, float* __restrict__ param_gradients,
     int accumulate, float* __restrict__ camera_partials, uint32_t* camera_done, float* __restrict__ camera_gradient,
-    float4* __restrict__ densify_stats, const FusedAdam adam) {
+    float4* __restrict__ densify_stats, const FusedAdam adam, uint32_t first_block, uint32_t total_blocks) {
     constexpr int S = SP_PARAM_STRIDE(DEG);
     __shared__ sp_camera_uniform s_cam;
     const sp_camera_uniform& cam = pick_camera<DEV>(camera_argument, s_cam);
@@ -485,7 +485,11 @@ __global__ void __launch_bounds__(kBlock, 3) k_project_backward(
     __shared__ float warp_camera[kBlock / 32][SP_CAMERA_GRAD_STRIDE];
     __shared__ float s_lr[FUSED ? S : 1];
     __shared__ bool last_block;
-    const uint32_t g0 = blockIdx.x * kBlock;
+    // Blocks [first_block, first_block + gridDim.x) of the total_blocks covering the n
+    // Gaussians: all at once, or in chunks launched one after the other on one stream; the
+    // last block of all to finish reduces the camera gradient.
+    const uint32_t block = first_block + blockIdx.x;
+    const uint32_t g0 = block * kBlock;
     const uint32_t here = min((uint32_t)kBlock, n - g0);
     stage_in(params + (size_t)g0 * S, here * S, sp);
     if (FUSED && threadIdx.x < (uint32_t)S) s_lr[threadIdx.x] = adam.step.lr[threadIdx.x];
@@ -518,14 +522,14 @@ __global__ void __launch_bounds__(kBlock, 3) k_project_backward(
         float s = 0.0f;
 #pragma unroll
         for (int w = 0; w < kBlock / 32; ++w) s += warp_camera[w][t];
-        camera_partials[(size_t)blockIdx.x * SP_CAMERA_GRAD_STRIDE + t] = s;
+        camera_partials[(size_t)block * SP_CAMERA_GRAD_STRIDE + t] = s;
     }
     // reduce_camera_gradient.wgsl:10-34 by the last block to finish, in block order.
     __threadfence();
     __syncthreads();
     if (t == 0) {
         cuda::atomic_ref<uint32_t, cuda::thread_scope_device> done(*camera_done);
-        last_block = done.fetch_add(1u, cuda::memory_order_acq_rel) == gridDim.x - 1;
+        last_block = done.fetch_add(1u, cuda::memory_order_acq_rel) == total_blocks - 1;
     }
     __syncthreads();
     if (!last_block) return;
@@ -533,7 +537,7 @@ __global__ void __launch_bounds__(kBlock, 3) k_project_backward(
     float sums[SP_CAMERA_GRAD_STRIDE];
 #pragma unroll
     for (int c = 0; c < SP_CAMERA_GRAD_STRIDE; ++c) sums[c] = 0.0f;
-    for (uint32_t b = t; b < gridDim.x; b += kBlock)
+    for (uint32_t b = t; b < total_blocks; b += kBlock)
 #pragma unroll
         for (int c = 0; c < SP_CAMERA_GRAD_STRIDE; ++c) sums[c] += __ldcg(camera_partials + (size_t)b * SP_CAMERA_GRAD_STRIDE + c);
     // The staging buffer (at least 14 floats per thread) is free again: reuse it.
@@ -630,8 +634,13 @@ cudaError_t launch_project_backward(const float* params, uint64_t n, int sh_degr
                                     const uint32_t* offsets, const float* slot_gradients, uint64_t capacity,
                                     const float4* gaussian_gradients, float* param_gradients, int accumulate,
                                     float* camera_partials, uint32_t* camera_done, float* camera_gradient,
-                                    float4* densify_stats, const AdamLaunch* adam, cudaStream_t stream) {
-    const unsigned grid = grid_for(n, kBlock);
+                                    float4* densify_stats, const AdamLaunch* adam, uint64_t first, uint64_t count,
+                                    cudaStream_t stream) {
+    const unsigned total_blocks = grid_for(n, kBlock);
+    if (first % kBlock != 0 || first > n || count > n - first) return cudaErrorInvalidValue;
+    const unsigned first_block = (unsigned)(first / kBlock);
+    const unsigned grid = grid_for(count, kBlock);
+    if (grid == 0) return cudaSuccess;
     const size_t smem = (size_t)kBlock * SP_PARAM_STRIDE(sh_degree) * sizeof(float);
     cudaError_t err = cudaSuccess;
     FusedAdam fused{};
@@ -650,7 +659,7 @@ cudaError_t launch_project_backward(const float* params, uint64_t n, int sh_degr
     k_project_backward<D, M, F, V><<<grid, kBlock, smem, stream>>>(                                            \
         params, (uint32_t)n, cam, cam_device, records, radii, offsets, slot_gradients, capacity,               \
         gaussian_gradients, param_gradients, accumulate, camera_partials, camera_done, camera_gradient,        \
-        densify_stats, fused);                                                                                 \
+        densify_stats, fused, first_block, total_blocks);                                                      \
     return cudaGetLastError();
 #define SPLAT_PB_CAM(D, M, F)              \
     if (cam_device) {                      \

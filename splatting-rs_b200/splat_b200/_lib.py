@@ -186,6 +186,8 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "sp_forward": (c_int, [_P]),
     "sp_loss": (c_int, [_P, c_uint32]),
     "sp_backward": (c_int, [_P]),
+    "sp_backward_blend": (c_int, [_P]),
+    "sp_backward_project": (c_int, [_P, c_uint64, c_uint64]),
     "sp_write_loss_gradient": (c_int, [_P, _P, c_int]),
     "sp_write_image": (c_int, [_P, _P, c_int]),
     "sp_param_gradients": (_P, [_P]),

@@ -353,6 +353,14 @@ class Rasterizer:
             self._check(status, "read_intersections")
         return out
 
+    def encode_backward_blend(self) -> None:
+        """The blend half of encode_backward (sp_backward_blend)."""
+        self._check(self.lib.sp_backward_blend(self.handle), "backward_blend")
+
+    def encode_backward_project(self, first: int, count: int) -> None:
+        """The projection backward of Gaussians [first, first + count) (sp_backward_project)."""
+        self._check(self.lib.sp_backward_project(self.handle, int(first), int(count)), "backward_project")
+
     def encode_backward_adam(self, adam, rate_factor: float) -> None:
         """encode_backward then adam.encode_step(rate_factor) as one fused pass
         (sp_backward_adam); the parameter gradients are consumed, not written."""

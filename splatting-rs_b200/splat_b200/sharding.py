@@ -7,14 +7,20 @@ Two exchanges, through torch.distributed (NCCL over NVLink on GPUs, gloo on CPU)
 buffers the library and the caller own, viewed as tensors without a copy:
 
 - "sharded" (when the Gaussians split evenly over the ranks): a reduce-scatter of the
-  gradients, so that each rank holds the summed gradients of its own contiguous share of
-  the Gaussians; Adam (and the scale clamp) on that share only (sp_adam_step_range); an
+  gradients, so that each rank holds the summed gradients of its own share of the
+  Gaussians; Adam (and the scale clamp) on that share only (sp_adam_step_range); an
   all-gather of the updated parameters. The same bytes cross NVLink as with an all-reduce,
-  and each rank does 1/world of the Adam work.
+  and each rank does 1/world of the Adam work. The Gaussians are cut into `chunks` ranges:
+  the projection backward runs range by range, each range's reduce-scatter is issued as
+  soon as its gradients are written and runs beside the backward of the next ones, and each
+  range's all-gather beside the Adam steps of the next ones. A rank's share is its 1/world
+  of every range.
 - "allreduce": one all-reduce (sum) of the gradients, then the full Adam step on every rank.
 """
 
 from __future__ import annotations
+
+import math
 
 
 def view_of(step: int, rank: int, world: int, views: int) -> int:
@@ -37,6 +43,20 @@ def even_shards(gaussians: int, world: int) -> bool:
     return world > 1 and gaussians % world == 0
 
 
+def chunk_ranges(gaussians: int, chunks: int, world: int, align: int = 256) -> list[tuple[int, int]]:
+    """`chunks` consecutive ranges covering the Gaussians, each starting on a multiple of
+    `align` (the projection backward's block) with a length divisible by `world`."""
+    step = align * world // math.gcd(align, world)
+    size = -(-gaussians // chunks)
+    size = -(-size // step) * step
+    out, first = [], 0
+    while first < gaussians:
+        count = min(size, gaussians - first)
+        out.append((first, count))
+        first += count
+    return out
+
+
 class GradientExchange:
     """The step's exchange and Adam update for one rank (see the module docstring).
 
@@ -45,7 +65,7 @@ class GradientExchange:
     `gradients`."""
 
     def __init__(self, adam, params, gradients, gaussians: int, stride: int, rank: int, world: int,
-                 mode: str | None = None, group=None):
+                 mode: str | None = None, group=None, chunks: int = 4):
         if mode is None:
             mode = "sharded" if even_shards(gaussians, world) else "allreduce"
         if mode == "sharded" and not even_shards(gaussians, world):
@@ -54,26 +74,62 @@ class GradientExchange:
             raise ValueError(f"unknown exchange {mode!r}")
         self.adam, self.params, self.gradients = adam, params, gradients
         self.rank, self.world, self.mode, self.group = rank, world, mode, group
-        self.share = gaussians // world
-        self.first = rank * self.share
-        lo, hi = self.first * stride, (self.first + self.share) * stride
-        self.gradient_shard = gradients[lo:hi]
-        self.param_shard = params[lo:hi]
+        self.stride = stride
+        self.ranges = chunk_ranges(gaussians, chunks, world) if mode == "sharded" else [(0, gaussians)]
+        if mode == "sharded" and any(count % world for _, count in self.ranges):
+            raise ValueError("every range must split evenly over the ranks")
 
-    def __call__(self, rate_factor: float) -> None:
+    def _share(self, first: int, count: int) -> tuple[int, int]:
+        """This rank's part [first, first + n) of the range."""
+        part = count // self.world
+        return first + self.rank * part, part
+
+    def _views(self, tensor, first: int, count: int):
+        """The range and this rank's part of it, as views of a flat parameter-like tensor."""
+        s = self.stride
+        own, part = self._share(first, count)
+        return tensor[first * s:(first + count) * s], tensor[own * s:(own + part) * s]
+
+    def backward_step(self, project, rate_factor: float) -> None:
+        """The projection backward (`project(first, count)`, e.g. the rasterizer's
+        encode_backward_project), the exchange and the Adam step, the collectives of each
+        range overlapping the work on the next ones."""
         import torch.distributed as dist
 
-        if self.world == 1:
-            self.adam.encode_step(rate_factor)
-        elif self.mode == "sharded":
-            # In place: each rank's share of the gradient buffer receives the sum over ranks.
-            dist.reduce_scatter_tensor(self.gradient_shard, self.gradients, group=self.group)
-            self.adam.advance(rate_factor)
-            self.adam.step_range(self.first, self.share)
-            dist.all_gather_into_tensor(self.params, self.param_shard, group=self.group)
+        if self.world == 1 or self.mode != "sharded":
+            for first, count in self.ranges:
+                project(first, count)
+            self(rate_factor)
+            return
+        scatters = []
+        for first, count in self.ranges:
+            project(first, count)
+            whole, own = self._views(self.gradients, first, count)
+            # In place: this rank's part of the range receives the sum over the ranks.
+            scatters.append(dist.reduce_scatter_tensor(own, whole, group=self.group, async_op=True))
+        self.adam.advance(rate_factor)
+        gathers = []
+        for (first, count), scatter in zip(self.ranges, scatters):
+            scatter.wait()
+            self.adam.step_range(*self._share(first, count))
+            whole, own = self._views(self.params, first, count)
+            gathers.append(dist.all_gather_into_tensor(whole, own, group=self.group, async_op=True))
+        for gather in gathers:
+            gather.wait()
+
+    def __call__(self, rate_factor: float) -> None:
+        """The exchange and the Adam step after a whole backward (gradients all written)."""
+        if self.mode == "sharded" and self.world > 1:
+            self.backward_step(lambda first, count: None, rate_factor)
         else:
+            self._replicated(rate_factor)
+
+    def _replicated(self, rate_factor: float) -> None:
+        import torch.distributed as dist
+
+        if self.world > 1:
             dist.all_reduce(self.gradients, group=self.group)
-            self.adam.encode_step(rate_factor)
+        self.adam.encode_step(rate_factor)
 
 
 class ViewShardedStep:
@@ -100,6 +156,6 @@ class ViewShardedStep:
             # Backward with the Adam step fused into the projection backward.
             r.encode_backward_adam(self.adam, rate_factor)
         else:
-            r.encode_backward()
-            self.exchange(rate_factor)
+            r.encode_backward_blend()
+            self.exchange.backward_step(r.encode_backward_project, rate_factor)
         return view
