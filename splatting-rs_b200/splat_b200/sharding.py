@@ -10,11 +10,13 @@ buffers the library and the caller own, viewed as tensors without a copy:
   gradients, so that each rank holds the summed gradients of its own share of the
   Gaussians; Adam (and the scale clamp) on that share only (sp_adam_step_range); an
   all-gather of the updated parameters. The same bytes cross NVLink as with an all-reduce,
-  and each rank does 1/world of the Adam work. The Gaussians are cut into `chunks` ranges:
-  the projection backward runs range by range, each range's reduce-scatter is issued as
-  soon as its gradients are written and runs beside the backward of the next ones, and each
-  range's all-gather beside the Adam steps of the next ones. A rank's share is its 1/world
-  of every range.
+  and each rank does 1/world of the Adam work. With `chunks` > 1 the Gaussians are cut
+  into ranges: the projection backward runs range by range, each range's reduce-scatter is
+  issued as soon as its gradients are written and runs beside the backward of the next
+  ones, and each range's all-gather beside the Adam steps of the next ones; a rank's share is
+  then its 1/world of every range. Measured on two B200s with 4 ranges this was slower than
+  one (the ranges' backward launches end in partial waves, and the concurrent NCCL kernels
+  slow the Adam steps), so one range is the default.
 - "allreduce": one all-reduce (sum) of the gradients, then the full Adam step on every rank.
 """
 
@@ -65,7 +67,7 @@ class GradientExchange:
     `gradients`."""
 
     def __init__(self, adam, params, gradients, gaussians: int, stride: int, rank: int, world: int,
-                 mode: str | None = None, group=None, chunks: int = 4):
+                 mode: str | None = None, group=None, chunks: int = 1):
         if mode is None:
             mode = "sharded" if even_shards(gaussians, world) else "allreduce"
         if mode == "sharded" and not even_shards(gaussians, world):

@@ -84,7 +84,7 @@ class _OracleAdam:
         self._apply(first, count)
 
 
-def _rank_main(rank: int, world: int, port: int, out_dir: str, mode: str) -> None:
+def _rank_main(rank: int, world: int, port: int, out_dir: str, mode: str, chunks: int) -> None:
     import torch
     import torch.distributed as dist
 
@@ -100,7 +100,7 @@ def _rank_main(rank: int, world: int, port: int, out_dir: str, mode: str) -> Non
     gradients = torch.zeros_like(params)
     lr = sb.LEARNING_RATES_3DGS.by_slot(np.float32(1.0), 14)
     adam = _OracleAdam(oracle, params.numpy(), gradients.numpy(), lr)
-    exchange = GradientExchange(adam, params, gradients, len(cloud), 14, rank, world, mode)
+    exchange = GradientExchange(adam, params, gradients, len(cloud), 14, rank, world, mode, chunks=chunks)
     for step in range(2):
         view = view_of(step, rank, world, len(cams))
         gradients.copy_(torch.from_numpy(_gradient(oracle, cloud, cams[view], gt[view], params.numpy())))
@@ -116,19 +116,20 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
-@pytest.mark.parametrize("mode", ["allreduce", "sharded"])
-def test_two_gloo_ranks_equal_one_process_summing_their_views(tmp_path, mode):
+@pytest.mark.parametrize("mode,chunks", [("allreduce", 1), ("sharded", 1), ("sharded", 4)])
+def test_two_gloo_ranks_equal_one_process_summing_their_views(tmp_path, mode, chunks):
     """Two ranks, each the gradient of its own view, exchanged by an all-reduce or by a
-    reduce-scatter + Adam on each rank's half + all-gather (in place, as on the GPUs): the
-    same parameters on both ranks, equal to one process summing both views' gradients."""
+    reduce-scatter + Adam on each rank's half + all-gather (in place, as on the GPUs; whole,
+    or range by range with asynchronous collectives): the same parameters on both ranks,
+    equal to one process summing both views' gradients."""
     import torch.multiprocessing as mp
 
     import oracle
     import splat_b200 as sb
 
     world = 2
-    mp.start_processes(_rank_main, args=(world, _free_port(), str(tmp_path), mode), nprocs=world, join=True,
-                       start_method="spawn")
+    mp.start_processes(_rank_main, args=(world, _free_port(), str(tmp_path), mode, chunks), nprocs=world,
+                       join=True, start_method="spawn")
     ranks = [np.load(tmp_path / f"rank{r}.npy") for r in range(world)]
     assert np.array_equal(ranks[0], ranks[1]), "ranks diverged"
     # One process: the same two steps, each summing the gradients of views
