@@ -85,6 +85,7 @@ struct sp_rasterizer {
     std::vector<void*> allocations;
 
     float4* records = nullptr;
+    float4* reach = nullptr;  // the blend kernels' culling constants per Gaussian
     uint32_t* radii = nullptr;
     uint32_t* offsets = nullptr;
     uint32_t* block_totals = nullptr;
@@ -421,6 +422,7 @@ sp_status sp_rasterizer_create(sp_context* ctx, const float* d_params, uint64_t 
         return s;                                             \
     }
     SP_ALLOC(r->records, n * kRecord);
+    SP_ALLOC(r->reach, n);
     SP_ALLOC(r->radii, n);
     SP_ALLOC(r->offsets, n);
     SP_ALLOC(r->block_totals, r->blocks);
@@ -512,7 +514,7 @@ sp_status sp_forward(sp_rasterizer* r) {
         KernelSpan span(ctx, SP_K_PROJECT);
         SP_CUDA(ctx, launch_project(r->params, r->n, (int)r->options.sh_degree, r->camera,
                                     r->camera_on_device ? r->camera_dev : nullptr, r->records, r->radii, r->offsets,
-                                    r->block_totals, r->plan.compressed ? r->meta : nullptr, st));
+                                    r->block_totals, r->plan.compressed ? r->meta : nullptr, r->reach, st));
     }
     {
         KernelSpan span(ctx, SP_K_SCAN);
@@ -544,7 +546,7 @@ sp_status sp_forward(sp_rasterizer* r) {
     }
     {
         KernelSpan span(ctx, SP_K_BLEND_FORWARD);
-        SP_CUDA(ctx, launch_blend_forward(r->records, r->values[r->sorted_buffer], r->ranges, r->tile_order,
+        SP_CUDA(ctx, launch_blend_forward(r->records, r->reach, r->values[r->sorted_buffer], r->ranges, r->tile_order,
                                           r->camera, r->image, r->contributions, st));
     }
     r->forward_done = true;
@@ -576,7 +578,7 @@ sp_status blend_backward(sp_rasterizer* r) {
     KernelSpan span(r->ctx, SP_K_BLEND_BACKWARD);
     if (r->options.backward_mode == SP_BWD_ATOMIC)
         SP_CUDA(r->ctx, cudaMemsetAsync(r->gaussian_gradients, 0, r->n * 3 * sizeof(float4), st));
-    SP_CUDA(r->ctx, launch_blend_backward((int)r->options.backward_mode, r->records, r->values[r->sorted_buffer],
+    SP_CUDA(r->ctx, launch_blend_backward((int)r->options.backward_mode, r->records, r->reach, r->values[r->sorted_buffer],
                                           r->ranges, r->tile_order, r->offsets, r->camera, r->image,
                                           r->contributions, r->loss_gradient, r->slot_gradients,
                                           r->gaussian_gradients, st));

@@ -98,23 +98,40 @@ __device__ __forceinline__ uint32_t compact(const uint8_t* masks, uint32_t n, ui
     return length;
 }
 
+// Whether the ellipse a x^2 + 2 b x y + c y^2 <= q meets the rectangle [x0, x1] x [y0, y1]
+// (coordinates relative to its centre), with kx = -b/c and ky = -b/a precomputed: as
+// ellipse_meets_rect, the minima along the edges at the clamped stationary points.
+__device__ __forceinline__ bool ellipse_meets_rect_k(float a, float b, float c, float kx, float ky, float q, float x0,
+                                                     float x1, float y0, float y1) {
+    if (x0 <= 0.0f && x1 >= 0.0f && y0 <= 0.0f && y1 >= 0.0f) return true;
+    float best = INFINITY;
+    const float xs[2] = {x0, x1}, ys[2] = {y0, y1};
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+        const float x = xs[e];
+        const float y = fminf(fmaxf(kx * x, y0), y1);
+        best = fminf(best, a * x * x + 2.0f * b * x * y + c * y * y);
+        const float yy = ys[e];
+        const float xx = fminf(fmaxf(ky * yy, x0), x1);
+        best = fminf(best, a * xx * xx + 2.0f * b * xx * yy + c * yy * yy);
+    }
+    return best <= q;
+}
+
 // Whether a Gaussian can reach the rectangle of pixel centres [x0, x0 + 7] x [y0, y0 + ROWS - 1]:
 // op * exp(power) >= 1/255 somewhere in it, i.e. the ellipse d^T C d <= 2 ln(255 op) of the
-// conic C (padded by 1 % in the level) meets the rectangle (padded by 0.05 px). A
-// bounding-box test first, then the exact one.
+// conic C (padded by 1 % in the level) meets the rectangle (padded by 0.05 px). `r` holds the
+// projection's constants of the Gaussian (its half extents and slopes, reach_of in
+// project.cu); a bounding-box test first, then the exact one.
 template <int ROWS>
-__device__ __forceinline__ bool reaches(float4 a, float4 b, float x0, float y0) {
-    const float level = b.y * 255.0f;
-    if (!(level > 1.0f)) return false;
-    const float det = a.z * b.x - a.w * a.w;
-    if (!(det > 0.0f) || !(a.z > 0.0f) || !(b.x > 0.0f)) return true;
-    const float q = 2.02f * __logf(level) + 0.02f;
+__device__ __forceinline__ bool reaches(float4 a, float4 b, float4 r, float x0, float y0) {
+    if (!(r.x >= 0.0f)) return false;        // the opacity keeps alpha below 1/255
+    if (!(r.x < INFINITY)) return true;      // degenerate conic: never culled
     const float lo_x = x0 - a.x - 0.05f, hi_x = lo_x + 7.1f;
     const float lo_y = y0 - a.y - 0.05f, hi_y = lo_y + (float)(ROWS - 1) + 0.1f;
-    const float ex = sqrtf(q * b.x / det) + 0.05f;
-    const float ey = sqrtf(q * a.z / det) + 0.05f;
-    if (ex < lo_x || -ex > hi_x || ey < lo_y || -ey > hi_y) return false;
-    return ellipse_meets_rect(a.z, a.w, b.x, q, lo_x, hi_x, lo_y, hi_y);
+    if (r.x < lo_x || -r.x > hi_x || r.y < lo_y || -r.y > hi_y) return false;
+    const float q = 2.02f * __logf(b.y * 255.0f) + 0.02f;
+    return ellipse_meets_rect_k(a.z, a.w, b.x, r.z, r.w, q, lo_x, hi_x, lo_y, hi_y);
 }
 
 // One warp's staging area: the records of a 32-entry chunk of the tile list that reach the
@@ -130,9 +147,9 @@ struct WarpStage {
 // Loads entries base .. base + 31 (below `end`) of the tile list, one per lane, keeps those
 // that reach the warp's 8 x ROWS pixels at (x0, y0), compacted into `st`; returns how many.
 template <int ROWS>
-__device__ __forceinline__ uint32_t stage_chunk(const float4* __restrict__ records, const uint32_t* __restrict__ sorted,
-                                                uint32_t first, uint32_t base, uint32_t end, float x0, float y0,
-                                                uint32_t lane, WarpStage& st) {
+__device__ __forceinline__ uint32_t stage_chunk(const float4* __restrict__ records, const float4* __restrict__ reach,
+                                                const uint32_t* __restrict__ sorted, uint32_t first, uint32_t base,
+                                                uint32_t end, float x0, float y0, uint32_t lane, WarpStage& st) {
     const uint32_t j = base + lane;
     bool take = false;
     float4 a, b;
@@ -144,7 +161,7 @@ __device__ __forceinline__ uint32_t stage_chunk(const float4* __restrict__ recor
         a = rec[0];
         b = rec[1];
         c = rec[2].x;
-        take = reaches<ROWS>(a, b, x0, y0);
+        take = reaches<ROWS>(a, b, reach[g], x0, y0);
     }
     const uint32_t ballot = __ballot_sync(kFull, take);
     if (take) {
@@ -220,6 +237,7 @@ __global__ void __launch_bounds__(kPairThreads, 8) k_blend_forward(const float4*
                                                                    const uint32_t* __restrict__ sorted,
                                                                    const uint2* __restrict__ ranges,
                                                                    const uint32_t* __restrict__ order,
+                                                                   const float4* __restrict__ reach,
                                                                    const sp_camera_uniform cam,
                                                                    float4* __restrict__ image,
                                                                    uint32_t* __restrict__ contributions) {
@@ -242,7 +260,8 @@ __global__ void __launch_bounds__(kPairThreads, 8) k_blend_forward(const float4*
     bool done0 = !inside0, done1 = !inside1;
     for (uint32_t base = 0; base < count; base += 32) {
         if (__all_sync(kFull, done0 && done1)) break;
-        const uint32_t n = stage_chunk<8>(records, sorted, range.x, base, count, (float)bx, (float)by, lane, st);
+        const uint32_t n =
+            stage_chunk<8>(records, reach, sorted, range.x, base, count, (float)bx, (float)by, lane, st);
         for (uint32_t i = 0; i < n && !(done0 && done1); ++i) {
             const float4 a = st.a[i], b = st.b[i];
             const Falloff f = falloff(a, b, fpx, fpy);
@@ -481,9 +500,9 @@ __global__ void __launch_bounds__(kTilePixels) k_blend_backward(
 // lanes at once.
 __global__ void __launch_bounds__(kPairThreads, 6) k_blend_backward_atomic(
     const float4* __restrict__ records, const uint32_t* __restrict__ sorted, const uint2* __restrict__ ranges,
-    const uint32_t* __restrict__ order, const sp_camera_uniform cam, const float4* __restrict__ image,
-    const uint32_t* __restrict__ contributions, const float4* __restrict__ loss_gradient,
-    float4* __restrict__ gaussian_gradients) {
+    const uint32_t* __restrict__ order, const float4* __restrict__ reach, const sp_camera_uniform cam,
+    const float4* __restrict__ image, const uint32_t* __restrict__ contributions,
+    const float4* __restrict__ loss_gradient, float4* __restrict__ gaussian_gradients) {
     __shared__ WarpStage s_stage[kPairWarps];
     const uint32_t tile = order[blockIdx.x];
     const uint32_t gx = tile % cam.tiles_x, gy = tile / cam.tiles_x;
@@ -521,7 +540,7 @@ __global__ void __launch_bounds__(kPairThreads, 6) k_blend_backward_atomic(
     const float2 behind_t = mul2(gt, transmittance);
     for (int base = end ? (int)((end - 1) & ~31u) : -32; base >= 0; base -= 32) {
         const uint32_t n =
-            stage_chunk<8>(records, sorted, range.x, (uint32_t)base, end, (float)bx, (float)by, lane, st);
+            stage_chunk<8>(records, reach, sorted, range.x, (uint32_t)base, end, (float)bx, (float)by, lane, st);
         for (int i = (int)n - 1; i >= 0; --i) {
             const uint32_t j = st.j[i];
             const float4 a = st.a[i], b = st.b[i];
@@ -676,16 +695,16 @@ cudaError_t launch_tile_order(const uint2* ranges, uint32_t tiles, uint32_t* ord
     return cudaGetLastError();
 }
 
-cudaError_t launch_blend_forward(const float4* records, const uint32_t* sorted_gaussians, const uint2* ranges,
-                                 const uint32_t* order, const sp_camera_uniform& cam, float4* image,
-                                 uint32_t* contributions, cudaStream_t stream) {
+cudaError_t launch_blend_forward(const float4* records, const float4* reach, const uint32_t* sorted_gaussians,
+                                 const uint2* ranges, const uint32_t* order, const sp_camera_uniform& cam,
+                                 float4* image, uint32_t* contributions, cudaStream_t stream) {
     const unsigned tiles = cam.tiles_x * cam.tiles_y;
-    k_blend_forward<<<tiles, kPairThreads, 0, stream>>>(records, sorted_gaussians, ranges, order, cam, image,
+    k_blend_forward<<<tiles, kPairThreads, 0, stream>>>(records, sorted_gaussians, ranges, order, reach, cam, image,
                                                         contributions);
     return cudaGetLastError();
 }
 
-cudaError_t launch_blend_backward(int mode, const float4* records, const uint32_t* sorted_gaussians,
+cudaError_t launch_blend_backward(int mode, const float4* records, const float4* reach, const uint32_t* sorted_gaussians,
                                   const uint2* ranges, const uint32_t* order, const uint32_t* offsets,
                                   const sp_camera_uniform& cam, const float4* image, const uint32_t* contributions,
                                   const float4* loss_gradient, float* slot_gradients, float4* gaussian_gradients,
@@ -696,8 +715,8 @@ cudaError_t launch_blend_backward(int mode, const float4* records, const uint32_
             records, sorted_gaussians, ranges, order, offsets, cam, image, contributions, loss_gradient,
             slot_gradients, gaussian_gradients);
     else
-        k_blend_backward_atomic<<<tiles, kPairThreads, 0, stream>>>(records, sorted_gaussians, ranges, order, cam,
-                                                                    image, contributions, loss_gradient,
+        k_blend_backward_atomic<<<tiles, kPairThreads, 0, stream>>>(records, sorted_gaussians, ranges, order, reach,
+                                                                    cam, image, contributions, loss_gradient,
                                                                     gaussian_gradients);
     return cudaGetLastError();
 }

@@ -20,7 +20,7 @@ namespace splat {
 cudaError_t launch_project(const float* params, uint64_t n, int sh_degree, const sp_camera_uniform& cam,
                            const sp_camera_uniform* cam_device, float4* records, uint32_t* radii,
                            uint32_t* local_offsets, uint32_t* block_totals, DeviceMeta* depth_range,
-                           cudaStream_t stream);
+                           float4* reach, cudaStream_t stream);
 // scan_tile_counts (scan.wgsl:64-81): scans the block totals into 64-bit block offsets,
 // fills the meta (count, overflow, sort partitions, this frame's key geometry) and zeroes
 // the sort's histograms and partition tickets for this forward pass.
@@ -80,12 +80,13 @@ cudaError_t launch_ranges(const SortPlan& plan, const void* keys, const DeviceMe
 // octave), so that the longest tiles start first and the short ones fill the last wave.
 cudaError_t launch_tile_order(const uint2* ranges, uint32_t tiles, uint32_t* order, cudaStream_t stream);
 // rasterize_forward.wgsl:22-88; block b blends tile order[b].
-cudaError_t launch_blend_forward(const float4* records, const uint32_t* sorted_gaussians, const uint2* ranges,
-                                 const uint32_t* order, const sp_camera_uniform& cam, float4* image,
-                                 uint32_t* contributions, cudaStream_t stream);
+cudaError_t launch_blend_forward(const float4* records, const float4* reach, const uint32_t* sorted_gaussians,
+                                 const uint2* ranges, const uint32_t* order, const sp_camera_uniform& cam,
+                                 float4* image, uint32_t* contributions, cudaStream_t stream);
 // rasterize_backward.wgsl:30-133. mode SP_BWD_*: slot sums (deterministic) or atomics
 // into gaussian_gradients (3 float4 per Gaussian, zeroed by the caller).
-cudaError_t launch_blend_backward(int mode, const float4* records, const uint32_t* sorted_gaussians,
+cudaError_t launch_blend_backward(int mode, const float4* records, const float4* reach,
+                                  const uint32_t* sorted_gaussians,
                                   const uint2* ranges, const uint32_t* order, const uint32_t* offsets,
                                   const sp_camera_uniform& cam, const float4* image, const uint32_t* contributions,
                                   const float4* loss_gradient, float* slot_gradients, float4* gaussian_gradients,

@@ -104,13 +104,28 @@ __device__ __forceinline__ const sp_camera_uniform& pick_camera(const sp_camera_
     else return argument;
 }
 
+// The blend kernels' culling constants of a projected Gaussian (record a, b): the half
+// extents (ex, ey) of the ellipse d^T C d <= q, q = 2.02 ln(255 opacity) + 0.02, outside of
+// which its alpha is below 1/255 (padded by 1 % in the level and 0.05 px), and the slopes
+// -b/c, -b/a of the conic's minimum along a vertical and a horizontal line. ex < 0: the
+// opacity alone keeps alpha below 1/255; ex = inf: a degenerate conic, never culled.
+__device__ __forceinline__ float4 reach_of(float4 a, float4 b) {
+    const float level = b.y * 255.0f;
+    if (!(level > 1.0f)) return make_float4(-1.0f, -1.0f, 0.0f, 0.0f);
+    const float det = a.z * b.x - a.w * a.w;
+    if (!(det > 0.0f) || !(a.z > 0.0f) || !(b.x > 0.0f)) return make_float4(INFINITY, INFINITY, 0.0f, 0.0f);
+    const float q = 2.02f * __logf(level) + 0.02f;
+    return make_float4(sqrtf(q * b.x / det) + 0.05f, sqrtf(q * a.z / det) + 0.05f, -a.w / b.x, -a.w / a.z);
+}
+
 template <int DEG, bool DEV>
 __global__ void __launch_bounds__(kBlock) k_project(const float* __restrict__ params, uint32_t n,
                                                     const sp_camera_uniform camera_argument,
                                                     const sp_camera_uniform* __restrict__ camera_device,
                                                     float4* __restrict__ records, uint32_t* __restrict__ radii,
                                                     uint32_t* __restrict__ local_offsets,
-                                                    uint32_t* __restrict__ block_totals, DeviceMeta* depth_range) {
+                                                    uint32_t* __restrict__ block_totals, DeviceMeta* depth_range,
+                                                    float4* __restrict__ reach) {
     constexpr int S = SP_PARAM_STRIDE(DEG);
     extern __shared__ float4 smem4[];
     __shared__ sp_camera_uniform s_cam;
@@ -132,6 +147,7 @@ __global__ void __launch_bounds__(kBlock) k_project(const float* __restrict__ pa
         out[1] = rec[1];
         out[2] = rec[2];
         radii[g0 + t] = radius;
+        reach[g0 + t] = radius > 0 ? reach_of(rec[0], rec[1]) : make_float4(-1.0f, -1.0f, 0.0f, 0.0f);
     }
     uint32_t total;
     const uint32_t exclusive = block_exclusive_scan(count, &total);
@@ -594,14 +610,14 @@ cudaError_t set_smem(Kernel kernel, size_t bytes) {
 cudaError_t launch_project(const float* params, uint64_t n, int sh_degree, const sp_camera_uniform& cam,
                            const sp_camera_uniform* cam_device, float4* records, uint32_t* radii,
                            uint32_t* local_offsets, uint32_t* block_totals, DeviceMeta* depth_range,
-                           cudaStream_t stream) {
+                           float4* reach, cudaStream_t stream) {
     const unsigned grid = grid_for(n, kBlock);
     const size_t smem = (size_t)kBlock * SP_PARAM_STRIDE(sh_degree) * sizeof(float);
     cudaError_t err = cudaSuccess;
 #define SPLAT_PROJECT_ONE(D, V)                                                                           \
     if ((err = set_smem(k_project<D, V>, smem)) != cudaSuccess) return err;                                \
     k_project<D, V><<<grid, kBlock, smem, stream>>>(params, (uint32_t)n, cam, cam_device, records, radii,  \
-                                                    local_offsets, block_totals, depth_range);            \
+                                                    local_offsets, block_totals, depth_range, reach);     \
     return cudaGetLastError();
 #define SPLAT_PROJECT(D)                \
     if (sh_degree == D) {               \
