@@ -97,6 +97,34 @@ typedef struct sp_densify_stats {
     float _pad;
 } sp_densify_stats;
 
+/* DensifySettings (densify.rs:19-45): when and how strongly the Gaussians are densified and
+ * pruned. opacity_reset_interval 0 is None. */
+typedef struct sp_densify_settings {
+    uint32_t interval;
+    uint32_t start;
+    float stop_fraction;
+    float gradient_threshold;
+    float split_scale_fraction;
+    float prune_opacity;
+    float max_screen_radius;
+    float max_growth;
+    uint32_t opacity_reset_interval;
+    uint32_t _pad;
+} sp_densify_settings;
+
+/* DensifyReport (densify.rs:97-111). */
+typedef struct sp_densify_report {
+    uint64_t before;
+    uint64_t cloned;
+    uint64_t split;
+    uint64_t pruned_transparent;
+    uint64_t pruned_oversized;
+    uint64_t over_budget;
+    uint64_t after;
+    uint32_t opacity_reset;
+    uint32_t _pad;
+} sp_densify_report;
+
 /* Projected, rasterizer.rs:46-61 / common.wgsl:49-61 (the diagnostics mirror). 80 bytes. */
 typedef struct sp_projected {
     float mean[2];
@@ -240,6 +268,9 @@ sp_status sp_backward_project(sp_rasterizer* r, uint64_t first, uint64_t count);
  * host memory (src_is_device = 0) or device memory (1). */
 sp_status sp_write_loss_gradient(sp_rasterizer* r, const float* src, int src_is_device);
 sp_status sp_write_image(sp_rasterizer* r, const float* src, int src_is_device);
+/* Overwrites the accumulated densify statistics with N sp_densify_stats from host memory
+ * (diagnostics and tests; the backward passes accumulate them otherwise). */
+sp_status sp_write_densify_stats(sp_rasterizer* r, const sp_densify_stats* host);
 /* Rasterizer::param_gradients (rasterizer.rs:467-469): device pointer to N * stride floats. */
 float* sp_param_gradients(sp_rasterizer* r);
 /* Zeroes the parameter gradients (for accumulate_gradients batches). */
@@ -336,7 +367,8 @@ enum {
     SP_K_ADAM = 10,
     SP_K_TILE_ORDER = 11, /* the blend kernels' tile schedule (no counterpart in the reference) */
     SP_K_BACKWARD_ADAM = 12, /* projection backward with the Adam step fused (sp_backward_adam) */
-    SP_K_COUNT = 13
+    SP_K_DENSIFY = 13,       /* the densification's kernels (sp_densify_plan, sp_densify_apply) */
+    SP_K_COUNT = 14
 };
 /* Starts (1) or stops (0) recording events around every kernel launch of the context. */
 sp_status sp_profile_enable(sp_context* ctx, int enable);
@@ -371,6 +403,48 @@ sp_status sp_adam_read_moments(sp_adam* adam, float* host_first, float* host_sec
 /* position_rate_factor (optimizer.rs:59-62): 0.01^(step / max(steps - 1, 1)). Returns a
  * negative value where the reference asserts (steps == 0 or step >= steps). */
 float sp_position_rate_factor(uint64_t step, uint64_t steps);
+/* Adam::resumed (optimizer.rs:164-188) from moments already in device memory (for example
+ * those sp_densify_apply wrote): copied into the new optimiser's own buffers. */
+sp_status sp_adam_resume_device(const sp_adam* from, float* d_params, const float* d_gradients,
+                                uint64_t gaussian_count, const float* d_first_moment, const float* d_second_moment,
+                                sp_adam** out);
+
+/* ----------------------------------------------------------------- densification */
+
+/* DensifySettings::densifies_after (densify.rs:77-83): 1 when the Gaussians are densified
+ * after `done` (1-based) of `steps` steps, else 0; -1 where the reference asserts
+ * (interval 0, done outside 1..=steps). */
+int sp_densify_after(const sp_densify_settings* settings, uint64_t done, uint64_t steps);
+/* DensifySettings::resets_opacity_after (densify.rs:84-94): 1 or 0; -1 where the reference
+ * asserts (a reset interval that is not a multiple of the densify interval). */
+int sp_resets_opacity_after(const sp_densify_settings* settings, uint64_t done);
+
+/* densify (densify.rs:147-257) on the device, where the reference reads every buffer back
+ * and rebuilds on the CPU (training.rs:238-266). Two calls around the caller's allocation
+ * of the new buffers:
+ *
+ * sp_densify_plan decides the fate of every Gaussian of `r` from its parameters and the
+ * densify statistics its backward passes accumulated (pruned when nearly transparent or
+ * oversized on screen; cloned or split when its mean screen-space gradient is above the
+ * threshold, the highest first while the count stays within `max_count`), and fills
+ * `report` (one small read-back: the call's only synchronisation). `adam` must be the
+ * optimiser of r's parameters. When every Gaussian would be pruned it returns
+ * SP_ERR_INVALID, with the report filled and no plan (the reference panics).
+ *
+ * sp_densify_apply writes the report->after Gaussians (stride floats each) and their
+ * moments into device buffers of at least `capacity` Gaussians: the kept and cloned ones
+ * with their moments in index order, then each clone's copy and each split's two children
+ * (centres sampled from the Gaussian with SplitMix64 seeded with `seed`, scales / 1.6) with
+ * zero moments; with `reset_opacity`, every opacity lowered to 0.01 at most and its
+ * moments zeroed. The parameters, moments and statistics must not change between the
+ * calls. The outputs must not overlap the inputs. */
+typedef struct sp_densify sp_densify;
+sp_status sp_densify_plan(sp_rasterizer* r, const sp_adam* adam, float extent, uint64_t max_count,
+                          const sp_densify_settings* settings, int reset_opacity, uint64_t seed, sp_densify** out,
+                          sp_densify_report* report);
+sp_status sp_densify_apply(sp_densify* plan, float* d_params, float* d_first_moment, float* d_second_moment,
+                           uint64_t capacity);
+void sp_densify_destroy(sp_densify* plan);
 
 /* ------------------------------------------------------------- pose chain (host f64) */
 

@@ -72,6 +72,9 @@ def lib() -> ctypes.CDLL:
         _lib.or_sp_expf.argtypes = [c_float]
         _lib.or_train_step.restype = c_double
         _lib.or_get_threads.restype = c_int
+        _lib.or_splitmix64.restype = c_uint64
+        _lib.or_total_order_key.restype = c_uint32
+        _lib.or_densify.restype = c_int
     return _lib
 
 
@@ -240,3 +243,49 @@ def train_step(params, sh_degree, cam, gt_view, m, v, lr_by_slot, step, max_log_
                                      _p(np.ascontiguousarray(lr_by_slot, np.float32)), c_uint32(step),
                                      c_float(max_log_scale), c_float(max_log_anisotropy), ctypes.byref(count))
     return float(loss_value), int(count.value)
+
+
+class DensifyReportC(ctypes.Structure):
+    """sp_densify_report (64 bytes)."""
+
+    _fields_ = [(k, c_uint64) for k in ("before", "cloned", "split", "pruned_transparent", "pruned_oversized",
+                                         "over_budget", "after")] + [("opacity_reset", c_uint32), ("_pad", c_uint32)]
+
+
+REPORT_FIELDS = ("before", "cloned", "split", "pruned_transparent", "pruned_oversized", "over_budget", "after",
+                 "opacity_reset")
+
+
+def densify(params, first, second, stats, stride, extent, max_count, settings, reset_opacity, seed):
+    """densify (densify.rs:147-257). `settings` is an sp_densify_settings ctypes structure,
+    `stats` an (n, 4) float32 array of sp_densify_stats. Returns (params, first, second,
+    report dict); raises ValueError when every Gaussian was pruned."""
+    params = np.ascontiguousarray(params, np.float32).reshape(-1)
+    first = np.ascontiguousarray(first, np.float32).reshape(-1)
+    second = np.ascontiguousarray(second, np.float32).reshape(-1)
+    stats = np.ascontiguousarray(stats, np.float32).reshape(-1, 4)
+    n = params.size // stride
+    assert stats.shape[0] == n and first.size == second.size == params.size
+    report = DensifyReportC()
+    # The first call sizes the outputs (status 2 when they do not fit).
+    status = lib().or_densify(_p(params), _p(first), _p(second), _p(stats), c_uint64(n), c_uint32(stride),
+                              c_float(extent), c_uint64(max_count), ctypes.byref(settings), c_int(reset_opacity),
+                              c_uint64(seed), None, None, None, c_uint64(0), ctypes.byref(report))
+    out = {k: int(getattr(report, k)) for k in REPORT_FIELDS}
+    if status == 1:
+        raise ValueError(f"densification pruned every Gaussian: {out}")
+    after = out["after"]
+    p, m, v = (np.empty(after * stride, np.float32) for _ in range(3))
+    status = lib().or_densify(_p(params), _p(first), _p(second), _p(stats), c_uint64(n), c_uint32(stride),
+                              c_float(extent), c_uint64(max_count), ctypes.byref(settings), c_int(reset_opacity),
+                              c_uint64(seed), _p(p), _p(m), _p(v), c_uint64(after), ctypes.byref(report))
+    assert status == 0, status
+    return p, m, v, out
+
+
+def splitmix64(seed: int, index: int) -> int:
+    return int(lib().or_splitmix64(c_uint64(seed), c_uint64(index)))
+
+
+def total_order_key(value: float) -> int:
+    return int(lib().or_total_order_key(c_float(value)))

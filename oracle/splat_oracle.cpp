@@ -871,4 +871,151 @@ double or_train_step(float* params, uint64_t n, uint32_t sh_degree, const sp_cam
     return loss / (double)pixels;
 }
 
+// ---------------------------------------------------------------------------- densify
+
+uint64_t or_splitmix64(uint64_t seed, uint64_t index) {
+    // densify.rs:279-285: state += 0x9e3779b97f4a7c15, then the finaliser; the (index + 1)-th
+    // call's state is seed + (index + 1) * increment.
+    uint64_t z = seed + (index + 1) * 0x9e3779b97f4a7c15ull;
+    z = (z ^ (z >> 30)) * 0xbf58476d1ce4e5b9ull;
+    z = (z ^ (z >> 27)) * 0x94d049bb133111ebull;
+    return z ^ (z >> 31);
+}
+
+uint32_t or_total_order_key(float value) {
+    // f32::total_cmp as an unsigned key: negative values bit-inverted, the others with the
+    // sign bit set.
+    uint32_t bits;
+    std::memcpy(&bits, &value, 4);
+    return (bits & 0x80000000u) ? ~bits : (bits | 0x80000000u);
+}
+
+namespace {
+
+// SplitMix64::uniform (densify.rs:287-290): (0, 1].
+float densify_uniform(uint64_t draw) { return ((float)(draw >> 40) + 1.0f) / (float)(1ull << 24); }
+
+// split_child (densify.rs:259-273) with the draws starting at `index` of the stream.
+void split_child(const float* gaussian, uint32_t stride, uint64_t seed, uint64_t index, float* child) {
+    float local[3];
+    for (int k = 0; k < 3; ++k) {
+        const float scale = std::exp(gaussian[3 + k]);
+        // SplitMix64::standard_normal (densify.rs:292-296), Box-Muller.
+        const float u = densify_uniform(or_splitmix64(seed, index + 2 * k));
+        const float v = densify_uniform(or_splitmix64(seed, index + 2 * k + 1));
+        const float normal = std::sqrt(-2.0f * std::log(u)) * std::cos(6.28318530717958647692f * v);
+        local[k] = scale * normal;
+    }
+    // nalgebra 0.34 (Cargo.lock): UnitQuaternion::from_quaternion(Quaternion::new(w, x, y, z))
+    // divides by the norm of the coordinates stored as (x, y, z, w), whose 4-vector dot product
+    // sums (x^2 + z^2) + (y^2 + w^2); the rotation of a vector v is t w + q x t + v with
+    // t = 2 (q x v).
+    const float w0 = gaussian[6], x0 = gaussian[7], y0 = gaussian[8], z0 = gaussian[9];
+    const float norm = std::sqrt((x0 * x0 + z0 * z0) + (y0 * y0 + w0 * w0));
+    const float w = w0 / norm, qx = x0 / norm, qy = y0 / norm, qz = z0 / norm;
+    const float t[3] = {2.0f * (qy * local[2] - qz * local[1]), 2.0f * (qz * local[0] - qx * local[2]),
+                        2.0f * (qx * local[1] - qy * local[0])};
+    const float c[3] = {qy * t[2] - qz * t[1], qz * t[0] - qx * t[2], qx * t[1] - qy * t[0]};
+    std::memcpy(child, gaussian, stride * sizeof(float));
+    const float log_divisor = std::log(1.6f);
+    for (int k = 0; k < 3; ++k) {
+        child[k] += t[k] * w + c[k] + local[k];
+        child[3 + k] -= log_divisor;
+    }
+}
+
+}  // namespace
+
+int or_densify(const float* params, const float* first_moment, const float* second_moment,
+               const sp_densify_stats* stats, uint64_t n, uint32_t stride, float extent, uint64_t max_count,
+               const sp_densify_settings* settings, int reset_opacity, uint64_t seed, float* out_params,
+               float* out_first, float* out_second, uint64_t out_capacity, sp_densify_report* report) {
+    // densify.rs:147-257.
+    enum Fate : uint8_t { Kept, Cloned, Split, PrunedTransparent, PrunedOversized };
+    const float split_log_scale = std::log(settings->split_scale_fraction * extent);
+    std::vector<uint8_t> fate(n);
+    for (uint64_t g = 0; g < n; ++g) {
+        // gaussians.rs:87-89 with the host libm's exp.
+        const float logit = params[g * stride + SP_SLOT_OPACITY];
+        if (1.0f / (1.0f + std::exp(-logit)) < settings->prune_opacity)
+            fate[g] = PrunedTransparent;
+        else if (stats[g].max_radius >= settings->max_screen_radius)
+            fate[g] = PrunedOversized;
+        else
+            fate[g] = Kept;
+    }
+    auto mean_gradient = [&](uint64_t g) {
+        return stats[g].visible_count > 0.0f ? stats[g].mean_gradient_sum / stats[g].visible_count : 0.0f;
+    };
+    std::vector<uint64_t> candidates;
+    for (uint64_t g = 0; g < n; ++g)
+        if (fate[g] == Kept && mean_gradient(g) > settings->gradient_threshold) candidates.push_back(g);
+    // sort_by(|a, b| mean_gradient(b).total_cmp(&mean_gradient(a))), a stable sort.
+    std::stable_sort(candidates.begin(), candidates.end(), [&](uint64_t a, uint64_t b) {
+        return or_total_order_key(mean_gradient(b)) < or_total_order_key(mean_gradient(a));
+    });
+    uint64_t kept = 0;
+    for (uint64_t g = 0; g < n; ++g) kept += fate[g] == Kept;
+    const uint64_t budget = std::min<uint64_t>(max_count > kept ? max_count - kept : 0, candidates.size());
+    for (uint64_t c = 0; c < budget; ++c) {
+        const uint64_t g = candidates[c];
+        float largest = -INFINITY;
+        for (int k = 0; k < 3; ++k) largest = std::fmax(largest, params[g * stride + 3 + k]);  // f32::max
+        fate[g] = largest > split_log_scale ? Split : Cloned;
+    }
+    sp_densify_report r{};
+    r.before = n;
+    r.over_budget = candidates.size() - budget;
+    for (uint64_t g = 0; g < n; ++g) {
+        r.cloned += fate[g] == Cloned;
+        r.split += fate[g] == Split;
+        r.pruned_transparent += fate[g] == PrunedTransparent;
+        r.pruned_oversized += fate[g] == PrunedOversized;
+    }
+    const uint64_t copies = kept - r.split;  // kept and cloned Gaussians keep their place
+    r.after = copies + r.cloned + 2 * r.split;
+    r.opacity_reset = reset_opacity ? 1u : 0u;
+    *report = r;
+    if (r.after == 0) return 1;
+    if (out_capacity < r.after) return 2;
+    uint64_t o = 0, made = copies, splits = 0;
+    std::vector<float> child(stride);
+    for (uint64_t g = 0; g < n; ++g) {
+        const float* gaussian = params + g * stride;
+        if (fate[g] == Kept || fate[g] == Cloned) {
+            std::memcpy(out_params + o * stride, gaussian, stride * sizeof(float));
+            std::memcpy(out_first + o * stride, first_moment + g * stride, stride * sizeof(float));
+            std::memcpy(out_second + o * stride, second_moment + g * stride, stride * sizeof(float));
+            ++o;
+        }
+    }
+    // The new Gaussians after the kept ones, in index order: a clone's copy or a split's two
+    // children, with zero moments.
+    for (uint64_t g = 0; g < n; ++g) {
+        const float* gaussian = params + g * stride;
+        if (fate[g] == Cloned) {
+            std::memcpy(out_params + made * stride, gaussian, stride * sizeof(float));
+            ++made;
+        } else if (fate[g] == Split) {
+            for (int c = 0; c < 2; ++c) {
+                split_child(gaussian, stride, seed, splits * 12 + c * 6, out_params + made * stride);
+                ++made;
+            }
+            ++splits;
+        }
+    }
+    std::memset(out_first + copies * stride, 0, (r.after - copies) * stride * sizeof(float));
+    std::memset(out_second + copies * stride, 0, (r.after - copies) * stride * sizeof(float));
+    if (reset_opacity) {
+        const float reset_logit = std::log(0.01f / (1.0f - 0.01f));  // logit(RESET_OPACITY)
+        for (uint64_t g = 0; g < r.after; ++g) {
+            float& slot = out_params[g * stride + SP_SLOT_OPACITY];
+            slot = std::fmin(slot, reset_logit);  // f32::min
+            out_first[g * stride + SP_SLOT_OPACITY] = 0.0f;
+            out_second[g * stride + SP_SLOT_OPACITY] = 0.0f;
+        }
+    }
+    return 0;
+}
+
 }  // extern "C"

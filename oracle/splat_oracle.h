@@ -92,6 +92,19 @@ double or_train_step(float* params, uint64_t n, uint32_t sh_degree, const sp_cam
                      const float* lr_by_slot, uint32_t step, float max_log_scale, float max_log_anisotropy,
                      uint64_t* count);
 
+/* densify.rs:147-257 (densify) with split_child (259-273) and SplitMix64 (275-297): the
+ * Gaussians and moments after one densification, `stride` floats per Gaussian. Fills
+ * `report`; writes the outputs when out_capacity >= report->after. Returns 0, 1 when every
+ * Gaussian was pruned (the reference panics), 2 when the outputs did not fit. */
+int or_densify(const float* params, const float* first_moment, const float* second_moment,
+               const sp_densify_stats* stats, uint64_t n, uint32_t stride, float extent, uint64_t max_count,
+               const sp_densify_settings* settings, int reset_opacity, uint64_t seed, float* out_params,
+               float* out_first, float* out_second, uint64_t out_capacity, sp_densify_report* report);
+/* One draw of the SplitMix64 stream seeded with `seed`: the (index + 1)-th next_u64. */
+uint64_t or_splitmix64(uint64_t seed, uint64_t index);
+/* f32::total_cmp order as an unsigned key (the densify candidates' sort order). */
+uint32_t or_total_order_key(float value);
+
 /* Threads the oracle's OpenMP loops use (0 = all). */
 void or_set_threads(int threads);
 int or_get_threads(void);

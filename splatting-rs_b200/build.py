@@ -2,9 +2,9 @@
 
 Each CUDA source is compiled separately (in parallel) and linked into one shared library
 with the CUDA runtime linked statically, so the library loads next to any other CUDA
-runtime in the process (PyTorch's included). project.cu and adam.cu are compiled with
--fmad=false: their results are compared bit for bit with the CPU oracle; so is
-pose_device.cu, so that its f64 pose chain rounds as the host's does.
+runtime in the process (PyTorch's included). project.cu, adam.cu and densify.cu are
+compiled with -fmad=false: their results are compared bit for bit with the CPU oracle; so
+is pose_device.cu, so that its f64 pose chain rounds as the host's does.
 
     python splatting-rs_b200/build.py [--force] [--ptxas-verbose]
 """
@@ -27,9 +27,9 @@ LIBRARY = HERE / "splat_b200" / "libsplat_b200.so"
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", f"-I{INCLUDE}", "--expt-relaxed-constexpr"]
-EXACT = {"project.cu", "adam.cu", "pose_device.cu"}
+EXACT = {"project.cu", "adam.cu", "pose_device.cu", "densify.cu"}
 SOURCES = ["project.cu", "sort.cu", "blend.cu", "loss.cu", "adam.cu", "api.cu", "pose.cpp", "pose_device.cu",
-           "noalloc.cu"]
+           "densify.cu", "noalloc.cu"]
 
 
 def nvcc() -> str:

@@ -9,6 +9,7 @@
 #include <string>
 #include <vector>
 
+#include "densify.h"
 #include "kernels.h"
 #include "pose_math.h"
 #include "pose_state.h"
@@ -671,6 +672,14 @@ sp_status sp_write_image(sp_rasterizer* r, const float* src, int src_is_device) 
     return write_pixels(r, r ? r->image : nullptr, src, src_is_device);
 }
 
+sp_status sp_write_densify_stats(sp_rasterizer* r, const sp_densify_stats* host) {
+    if (!r || !host) return SP_ERR_INVALID;
+    SP_CHECK(select_device(r->ctx));
+    SP_CUDA(r->ctx, cudaMemcpyAsync(r->densify_stats, host, r->n * sizeof(float4), cudaMemcpyHostToDevice,
+                                    r->ctx->stream));
+    return sync_stream(r->ctx);
+}
+
 float* sp_param_gradients(sp_rasterizer* r) { return r ? r->param_gradients : nullptr; }
 
 float* sp_camera_gradient_device(sp_rasterizer* r) { return r ? r->camera_gradient : nullptr; }
@@ -1055,9 +1064,11 @@ sp_status sp_profile_read(sp_context* ctx, double* ms, uint64_t* launches) {
 
 // ------------------------------------------------------------------------------- Adam
 
+// Moments `m` and `v` (host or device memory by `kind`; null: zeroed) are copied on the
+// context's stream, which then finishes them before the call returns.
 static sp_status adam_make(sp_context* ctx, float* d_params, const float* d_gradients, uint64_t n, uint32_t sh_degree,
                            const sp_learning_rates& rates, float position_scale, uint32_t step,
-                           const float* host_m, const float* host_v, sp_adam** out) {
+                           const float* m, const float* v, cudaMemcpyKind kind, sp_adam** out) {
     // optimizer.rs:137-159, 200-243.
     SP_REQUIRE(ctx, n > 0, SP_ERR_INVALID, "no Gaussians");
     SP_REQUIRE(ctx, d_params && d_gradients, SP_ERR_INVALID, "null params or gradients buffer");
@@ -1080,13 +1091,14 @@ static sp_status adam_make(sp_context* ctx, float* d_params, const float* d_grad
     cudaError_t err = cudaMalloc(&a->first_moment, bytes);
     if (err == cudaSuccess) err = cudaMalloc(&a->second_moment, bytes);
     if (err == cudaSuccess) {
-        if (host_m) err = cudaMemcpy(a->first_moment, host_m, bytes, cudaMemcpyHostToDevice);
-        else err = cudaMemset(a->first_moment, 0, bytes);
+        if (m) err = cudaMemcpyAsync(a->first_moment, m, bytes, kind, ctx->stream);
+        else err = cudaMemsetAsync(a->first_moment, 0, bytes, ctx->stream);
     }
     if (err == cudaSuccess) {
-        if (host_v) err = cudaMemcpy(a->second_moment, host_v, bytes, cudaMemcpyHostToDevice);
-        else err = cudaMemset(a->second_moment, 0, bytes);
+        if (v) err = cudaMemcpyAsync(a->second_moment, v, bytes, kind, ctx->stream);
+        else err = cudaMemsetAsync(a->second_moment, 0, bytes, ctx->stream);
     }
+    if (err == cudaSuccess) err = cudaStreamSynchronize(ctx->stream);
     if (err != cudaSuccess) {
         cudaFree(a->first_moment);
         cudaFree(a->second_moment);
@@ -1102,7 +1114,7 @@ sp_status sp_adam_create(sp_context* ctx, float* d_params, const float* d_gradie
     if (!ctx || !rates || !out) return SP_ERR_INVALID;
     *out = nullptr;
     return adam_make(ctx, d_params, d_gradients, gaussian_count, sh_degree, *rates, position_scale, 0, nullptr,
-                     nullptr, out);
+                     nullptr, cudaMemcpyHostToDevice, out);
 }
 
 sp_status sp_adam_resume(const sp_adam* from, float* d_params, const float* d_gradients, uint64_t gaussian_count,
@@ -1111,7 +1123,19 @@ sp_status sp_adam_resume(const sp_adam* from, float* d_params, const float* d_gr
     *out = nullptr;
     SP_REQUIRE(from->ctx, host_first_moment && host_second_moment, SP_ERR_INVALID, "moments");
     return adam_make(from->ctx, d_params, d_gradients, gaussian_count, from->sh_degree, from->rates,
-                     from->position_scale, from->step, host_first_moment, host_second_moment, out);
+                     from->position_scale, from->step, host_first_moment, host_second_moment,
+                     cudaMemcpyHostToDevice, out);
+}
+
+sp_status sp_adam_resume_device(const sp_adam* from, float* d_params, const float* d_gradients,
+                                uint64_t gaussian_count, const float* d_first_moment, const float* d_second_moment,
+                                sp_adam** out) {
+    if (!from || !out) return SP_ERR_INVALID;
+    *out = nullptr;
+    SP_REQUIRE(from->ctx, d_first_moment && d_second_moment, SP_ERR_INVALID, "moments");
+    return adam_make(from->ctx, d_params, d_gradients, gaussian_count, from->sh_degree, from->rates,
+                     from->position_scale, from->step, d_first_moment, d_second_moment,
+                     cudaMemcpyDeviceToDevice, out);
 }
 
 void sp_adam_destroy(sp_adam* a) {
@@ -1167,6 +1191,122 @@ float sp_position_rate_factor(uint64_t step, uint64_t steps) {
     // optimizer.rs:59-62 asserts steps > 0 && step < steps.
     if (steps == 0 || step >= steps) return -1.0f;
     return position_rate_factor(step, steps);
+}
+
+// ----------------------------------------------------------------------- densification
+
+int sp_densify_after(const sp_densify_settings* s, uint64_t done, uint64_t steps) {
+    // densify.rs:77-83.
+    if (!s || s->interval == 0 || done < 1 || done > steps) return -1;
+    return done >= s->start && done % s->interval == 0 && (float)done <= s->stop_fraction * (float)steps;
+}
+
+int sp_resets_opacity_after(const sp_densify_settings* s, uint64_t done) {
+    // densify.rs:84-94; interval 0 is None.
+    if (!s) return -1;
+    if (s->opacity_reset_interval == 0) return 0;
+    if (s->interval == 0 || s->opacity_reset_interval % s->interval != 0) return -1;
+    return done % s->opacity_reset_interval == 0;
+}
+
+}  // extern "C"
+
+struct sp_densify {
+    sp_rasterizer* r = nullptr;
+    const sp_adam* adam = nullptr;
+    DensifyConstants constants{};
+    uint64_t seed = 0;
+    uint32_t reset_opacity = 0;
+    void* block = nullptr;  // fate, keys, tallies and state in one allocation
+    uint8_t* fate = nullptr;
+    uint32_t* keys = nullptr;
+    DensifyTally* tallies = nullptr;
+    DensifyState* state = nullptr;
+    sp_densify_report report{};
+};
+
+extern "C" {
+
+void sp_densify_destroy(sp_densify* plan) {
+    if (!plan) return;
+    cudaSetDevice(plan->r->ctx->device);
+    cudaStreamSynchronize(plan->r->ctx->stream);
+    cudaFree(plan->block);
+    delete plan;
+}
+
+sp_status sp_densify_plan(sp_rasterizer* r, const sp_adam* adam, float extent, uint64_t max_count,
+                          const sp_densify_settings* settings, int reset_opacity, uint64_t seed, sp_densify** out,
+                          sp_densify_report* report) {
+    if (!r || !adam || !settings || !out || !report) return SP_ERR_INVALID;
+    *out = nullptr;
+    sp_context* ctx = r->ctx;
+    // densify.rs:163-166.
+    SP_REQUIRE(ctx, extent > 0.0f, SP_ERR_INVALID, "camera extent must be positive");
+    SP_REQUIRE(ctx, adam->ctx == ctx && adam->params == r->params && adam->n == r->n && adam->stride == r->stride,
+               SP_ERR_INVALID, "the optimiser is not the one of the rasterizer's parameters");
+    SP_CHECK(select_device(ctx));
+    sp_densify* plan = new sp_densify();
+    plan->r = r;
+    plan->adam = adam;
+    plan->seed = seed;
+    plan->reset_opacity = reset_opacity ? 1u : 0u;
+    DensifyConstants& c = plan->constants;
+    c.prune_opacity = settings->prune_opacity;
+    c.max_screen_radius = settings->max_screen_radius;
+    c.gradient_threshold = settings->gradient_threshold;
+    c.split_log_scale = std::log(settings->split_scale_fraction * extent);
+    c.log_split_divisor = std::log(1.6f);                  // SPLIT_SCALE_DIVISOR
+    c.reset_logit = std::log(0.01f / (1.0f - 0.01f));     // logit(RESET_OPACITY)
+    const uint64_t n = r->n;
+    const uint32_t tiles = densify_tiles(n);
+    auto align = [](size_t x) { return (x + 255) & ~(size_t)255; };
+    const size_t fate_bytes = align(n), keys_bytes = align(n * 4), tally_bytes = align(tiles * sizeof(DensifyTally));
+    cudaError_t err = cudaMalloc(&plan->block, fate_bytes + keys_bytes + tally_bytes + sizeof(DensifyState));
+    if (err != cudaSuccess) {
+        delete plan;
+        return cuda_fail(ctx, err, "densify scratch");
+    }
+    char* base = static_cast<char*>(plan->block);
+    plan->fate = reinterpret_cast<uint8_t*>(base);
+    plan->keys = reinterpret_cast<uint32_t*>(base + fate_bytes);
+    plan->tallies = reinterpret_cast<DensifyTally*>(base + fate_bytes + keys_bytes);
+    plan->state = reinterpret_cast<DensifyState*>(base + fate_bytes + keys_bytes + tally_bytes);
+    sp_status status = SP_OK;
+    {
+        KernelSpan span(ctx, SP_K_DENSIFY);
+        err = launch_densify_plan(r->params, r->densify_stats, n, r->stride, c, max_count, plan->fate, plan->keys,
+                                  plan->tallies, plan->state, plan->reset_opacity, ctx->stream);
+    }
+    if (err != cudaSuccess) status = cuda_fail(ctx, err, "densify plan");
+    if (status == SP_OK)
+        status = read_device(ctx, &plan->report, &plan->state->report, sizeof(sp_densify_report));
+    if (status != SP_OK) {
+        sp_densify_destroy(plan);
+        return status;
+    }
+    *report = plan->report;
+    if (plan->report.after == 0) {
+        sp_densify_destroy(plan);
+        return fail(ctx, SP_ERR_INVALID, "densification pruned every Gaussian");  // densify.rs:255
+    }
+    *out = plan;
+    return SP_OK;
+}
+
+sp_status sp_densify_apply(sp_densify* plan, float* d_params, float* d_first_moment, float* d_second_moment,
+                           uint64_t capacity) {
+    if (!plan) return SP_ERR_INVALID;
+    sp_context* ctx = plan->r->ctx;
+    SP_REQUIRE(ctx, d_params && d_first_moment && d_second_moment, SP_ERR_INVALID, "null output buffer");
+    SP_REQUIRE(ctx, capacity >= plan->report.after, SP_ERR_INVALID, "the outputs hold fewer Gaussians than report.after");
+    SP_CHECK(select_device(ctx));
+    KernelSpan span(ctx, SP_K_DENSIFY);
+    const sp_adam* a = plan->adam;
+    SP_CUDA(ctx, launch_densify_write(plan->r->params, a->first_moment, a->second_moment, plan->r->n, a->sh_degree,
+                                      plan->constants, plan->fate, plan->tallies, plan->state, plan->seed,
+                                      plan->reset_opacity, d_params, d_first_moment, d_second_moment, ctx->stream));
+    return SP_OK;
 }
 
 }  // extern "C"

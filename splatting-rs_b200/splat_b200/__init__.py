@@ -6,10 +6,20 @@ over libsplat_b200.so, the B200-native (sm_100a) differentiable Gaussian-splatti
     PinholeCamera instantsplat-rs/src/camera.rs
     PoseRefinement instantsplat-rs/src/pose_refinement.rs, camera_pose.rs
     Trainer       instantsplat-rs/src/training.rs (the caller of the path)
+    densify       instantsplat-rs/src/densify.rs (on the device)
 """
 
 from ._lib import SplatError, load as load_library  # noqa: F401
 from .camera import PinholeCamera, cameras_extent, focal_for_fov, look_at  # noqa: F401
+from .densify import (  # noqa: F401
+    DENSIFY_SHORT_RUN,
+    RESET_OPACITY,
+    Densified,
+    DensifyError,
+    DensifyReport,
+    DensifySettings,
+    densify,
+)
 from .gaussians import GaussianCloud, logit, param_stride, rgb_to_sh_dc, sigmoid  # noqa: F401
 from .optimizer import (  # noqa: F401
     Adam,

@@ -45,6 +45,7 @@ KERNEL_NAMES = (
     "adam",
     "tile_order",
     "backward_adam",
+    "densify",
 )
 
 
@@ -141,6 +142,39 @@ class Options(ctypes.Structure):
     ]
 
 
+class DensifySettingsC(ctypes.Structure):
+    """sp_densify_settings (DensifySettings, densify.rs:19-45), 40 bytes."""
+
+    _fields_ = [
+        ("interval", c_uint32),
+        ("start", c_uint32),
+        ("stop_fraction", c_float),
+        ("gradient_threshold", c_float),
+        ("split_scale_fraction", c_float),
+        ("prune_opacity", c_float),
+        ("max_screen_radius", c_float),
+        ("max_growth", c_float),
+        ("opacity_reset_interval", c_uint32),
+        ("_pad", c_uint32),
+    ]
+
+
+class DensifyReportC(ctypes.Structure):
+    """sp_densify_report (DensifyReport, densify.rs:97-111), 64 bytes."""
+
+    _fields_ = [
+        ("before", c_uint64),
+        ("cloned", c_uint64),
+        ("split", c_uint64),
+        ("pruned_transparent", c_uint64),
+        ("pruned_oversized", c_uint64),
+        ("over_budget", c_uint64),
+        ("after", c_uint64),
+        ("opacity_reset", c_uint32),
+        ("_pad", c_uint32),
+    ]
+
+
 class PinholeCameraC(ctypes.Structure):
     _fields_ = [
         ("rotation", c_double * 9),
@@ -196,6 +230,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "sp_read_loss_gradient": (c_int, [_P, _P]),
     "sp_read_param_gradients": (c_int, [_P, _P]),
     "sp_read_densify_stats": (c_int, [_P, _P]),
+    "sp_write_densify_stats": (c_int, [_P, _P]),
     "sp_read_camera_gradient": (c_int, [_P, POINTER(CameraGradient)]),
     "sp_read_image": (c_int, [_P, _P]),
     "sp_read_pixel_loss": (c_int, [_P, _P]),
@@ -226,6 +261,16 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "sp_adam_steps_taken": (c_uint32, [_P]),
     "sp_adam_read_moments": (c_int, [_P, _P, _P]),
     "sp_position_rate_factor": (c_float, [c_uint64, c_uint64]),
+    "sp_adam_resume_device": (c_int, [_P, _P, _P, c_uint64, _P, _P, POINTER(_P)]),
+    "sp_densify_after": (c_int, [POINTER(DensifySettingsC), c_uint64, c_uint64]),
+    "sp_resets_opacity_after": (c_int, [POINTER(DensifySettingsC), c_uint64]),
+    "sp_densify_plan": (
+        c_int,
+        [_P, _P, c_float, c_uint64, POINTER(DensifySettingsC), c_int, c_uint64, POINTER(_P),
+         POINTER(DensifyReportC)],
+    ),
+    "sp_densify_apply": (c_int, [_P, _P, _P, _P, c_uint64]),
+    "sp_densify_destroy": (None, [_P]),
     "sp_corrected_camera": (
         c_int, [POINTER(PinholeCameraC), POINTER(PoseCorrectionC), c_double, POINTER(PinholeCameraC)]
     ),

@@ -150,6 +150,31 @@ class Adam:
             _handle=handle.value,
         )
 
+    def resumed_device(self, params, gradients, gaussian_count: int, first_moment, second_moment) -> "Adam":
+        """Adam::resumed (optimizer.rs:164-188) from moments in device memory (tensors of
+        gaussian_count * stride floats, e.g. a densification's), copied."""
+        handle = ctypes.c_void_p()
+        status = self.lib.sp_adam_resume_device(
+            self.handle,
+            ctypes.c_void_p(Rasterizer._pointer(params)),
+            ctypes.c_void_p(self._gradient_pointer(gradients)),
+            int(gaussian_count),
+            ctypes.c_void_p(Rasterizer._pointer(first_moment)),
+            ctypes.c_void_p(Rasterizer._pointer(second_moment)),
+            ctypes.byref(handle),
+        )
+        _lib.check(status, self.ctx.handle, "Adam::resumed")
+        return Adam(
+            self.ctx,
+            params,
+            gradients,
+            gaussian_count,
+            self.learning_rates,
+            self.position_scale,
+            self.sh_degree,
+            _handle=handle.value,
+        )
+
     def encode_step(self, position_rate_factor: float = 1.0) -> None:
         """Adam::encode_step (optimizer.rs:248-264), the clamp fused."""
         _lib.check(self.lib.sp_adam_step(self.handle, float(position_rate_factor)), self.ctx.handle, "Adam step")

@@ -323,6 +323,12 @@ class Rasterizer:
             self.lib.sp_read_densify_stats, (self.gaussian_count, 4), np.float32, "read_densify_stats"
         )
 
+    def write_densify_stats(self, stats) -> None:
+        """Overwrites the accumulated densify statistics ((N, 4) float32; diagnostics)."""
+        host = np.ascontiguousarray(stats, np.float32).reshape(self.gaussian_count, 4)
+        self._check(self.lib.sp_write_densify_stats(self.handle, host.ctypes.data_as(ctypes.c_void_p)),
+                    "write_densify_stats")
+
     def read_camera_gradient(self) -> CameraGradient:
         out = CameraGradient()
         self._check(self.lib.sp_read_camera_gradient(self.handle, ctypes.byref(out)), "read_camera_gradient")

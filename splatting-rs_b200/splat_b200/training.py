@@ -1,14 +1,15 @@
 """The training step loop — a mirror of `Trainer` (instantsplat-rs/src/training.rs:86-443),
 the caller that switches its `Rasterizer` / `Adam` for libsplat_b200: one view per step,
 views cycled in order, the position rate decayed over the run, the camera gradient read
-back for the pose refinement when poses are refined. Densification (training.rs:238-266)
-is not part of this path."""
+back for the pose refinement when poses are refined, and with densify settings the
+densification due before a step (training.rs:221-266), run on the device (densify.py)."""
 
 from __future__ import annotations
 
 import numpy as np
 
 from .camera import PinholeCamera, cameras_extent
+from .densify import DensifyReport, DensifySettings, densify
 from .gaussians import GaussianCloud
 from .optimizer import Adam, LearningRates, LEARNING_RATES_3DGS, position_rate_factor
 from .pose import PoseRefinement
@@ -34,6 +35,7 @@ class Trainer:
         refine_poses: bool = False,
         ctx: Context | None = None,
         backward_mode: int | None = None,
+        densify: DensifySettings | None = None,
     ):
         import torch
 
@@ -55,9 +57,14 @@ class Trainer:
         options = default_options(sh_degree=self.sh_degree)
         if backward_mode is not None:
             options.backward_mode = backward_mode
+        self.options = options
+        self.width, self.height = width, height
         self.rasterizer = Rasterizer(
             self.ctx, self.params, len(cloud), width, height, self.ground_truth, len(cameras), options
         )
+        self.gaussian_count = self.initial_gaussian_count = len(cloud)
+        self.densify = densify
+        self.densifications: list[DensifyReport] = []
         self.extent = cameras_extent(self.cameras)
         if not self.extent > 0:
             raise ValueError(f"camera extent {self.extent}: the views' cameras are all at the same position")
@@ -87,9 +94,34 @@ class Trainer:
         if self.poses is not None:
             self.poses.step(view, result[0], rate_factor)
 
-    def train_step(self, step: int, steps: int) -> None:
-        """Trainer::train_step_async (training.rs:221-229), without densification."""
+    def train_step(self, step: int, steps: int) -> DensifyReport | None:
+        """Trainer::train_step_async (training.rs:221-229): the densification due after the
+        previous step if any, then the step. The densification's report when there was one
+        (`params` is then a new buffer)."""
+        settings = self.densify
+        report = None
+        if settings is not None and step > 0 and settings.densifies_after(step, steps):
+            report = self.densify_now(settings)
         self.step(step % self.view_count, position_rate_factor(step, steps))
+        return report
+
+    def densify_now(self, settings: DensifySettings) -> DensifyReport:
+        """Trainer::densify_async (training.rs:238-266) on the device: densifies, then
+        rebuilds the rasterizer and Adam at the new count (the statistics start over)."""
+        max_count = settings.max_count(self.initial_gaussian_count)
+        seed = len(self.densifications)
+        reset_opacity = settings.resets_opacity_after(self.adam.steps_taken())
+        out = densify(self.rasterizer, self.adam, self.extent, max_count, settings, reset_opacity, seed)
+        count = out.report.after
+        rasterizer = Rasterizer(self.ctx, out.params, count, self.width, self.height, self.ground_truth,
+                                self.view_count, self.options)
+        adam = self.adam.resumed_device(out.params, rasterizer, count, out.first_moment, out.second_moment)
+        self.rasterizer.close()
+        self.adam.close()
+        self.params, self.rasterizer, self.adam = out.params, rasterizer, adam
+        self.gaussian_count = count
+        self.densifications.append(out.report)
+        return out.report
 
     def loss(self, view: int) -> LossTerms:
         """Trainer::loss_async (training.rs:366-374)."""

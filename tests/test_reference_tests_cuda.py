@@ -56,3 +56,13 @@ def test_densify_stats_match_the_cpu_mean_gradient():
 
 def test_pose_gradient_matches_finite_differences():
     rt.pose_gradient_matches_finite_differences(make)
+
+
+# ---- densify.rs:299-448 on the device path
+
+import densify_tests as dt  # noqa: E402
+
+
+@pytest.mark.parametrize("case", dt.ALL, ids=[c.__name__ for c in dt.ALL])
+def test_densify(case, ctx):
+    case(lambda *args: dt.cuda_densify(*args, ctx=ctx))
