@@ -277,6 +277,9 @@ float* sp_param_gradients(sp_rasterizer* r);
 sp_status sp_zero_param_gradients(sp_rasterizer* r);
 /* Device pointer to the 14-float camera gradient of the last backward. */
 float* sp_camera_gradient_device(sp_rasterizer* r);
+/* Device pointer to the N accumulated densify statistics (read and written by the
+ * multi-GPU merge of several ranks' statistics before a densification). */
+sp_densify_stats* sp_densify_stats_device(sp_rasterizer* r);
 /* The read_* calls of rasterizer.rs:458-549, into host memory. */
 sp_status sp_read_loss_gradient(sp_rasterizer* r, float* host);      /* P * 4 */
 sp_status sp_read_param_gradients(sp_rasterizer* r, float* host);    /* N * stride */
@@ -400,6 +403,10 @@ sp_status sp_adam_step_range(sp_adam* adam, uint64_t first, uint64_t count);
 uint32_t sp_adam_steps_taken(const sp_adam* adam);
 /* Adam::read_moments_async (optimizer.rs:270-275), into host memory. */
 sp_status sp_adam_read_moments(sp_adam* adam, float* host_first, float* host_second);
+/* Device pointers to the first and second moments (N * stride floats each), for the
+ * multi-GPU gather of the ranks' moment shards. */
+float* sp_adam_first_moment_device(sp_adam* adam);
+float* sp_adam_second_moment_device(sp_adam* adam);
 /* position_rate_factor (optimizer.rs:59-62): 0.01^(step / max(steps - 1, 1)). Returns a
  * negative value where the reference asserts (steps == 0 or step >= steps). */
 float sp_position_rate_factor(uint64_t step, uint64_t steps);

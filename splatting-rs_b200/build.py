@@ -29,7 +29,7 @@ ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", f"-I{INCLUDE}", "--expt-relaxed-constexpr"]
 EXACT = {"project.cu", "adam.cu", "pose_device.cu", "densify.cu"}
 SOURCES = ["project.cu", "sort.cu", "blend.cu", "loss.cu", "adam.cu", "api.cu", "pose.cpp", "pose_device.cu",
-           "densify.cu", "noalloc.cu"]
+           "densify.cu", "noalloc.cu", "ply.cpp"]
 
 
 def nvcc() -> str:

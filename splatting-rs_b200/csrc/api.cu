@@ -684,6 +684,10 @@ float* sp_param_gradients(sp_rasterizer* r) { return r ? r->param_gradients : nu
 
 float* sp_camera_gradient_device(sp_rasterizer* r) { return r ? r->camera_gradient : nullptr; }
 
+sp_densify_stats* sp_densify_stats_device(sp_rasterizer* r) {
+    return r ? reinterpret_cast<sp_densify_stats*>(r->densify_stats) : nullptr;
+}
+
 sp_status sp_zero_param_gradients(sp_rasterizer* r) {
     if (!r) return SP_ERR_INVALID;
     SP_CHECK(select_device(r->ctx));
@@ -1186,6 +1190,10 @@ sp_status sp_adam_read_moments(sp_adam* a, float* host_first, float* host_second
     SP_CHECK(read_device(a->ctx, host_first, a->first_moment, bytes));
     return read_device(a->ctx, host_second, a->second_moment, bytes);
 }
+
+float* sp_adam_first_moment_device(sp_adam* a) { return a ? a->first_moment : nullptr; }
+
+float* sp_adam_second_moment_device(sp_adam* a) { return a ? a->second_moment : nullptr; }
 
 float sp_position_rate_factor(uint64_t step, uint64_t steps) {
     // optimizer.rs:59-62 asserts steps > 0 && step < steps.

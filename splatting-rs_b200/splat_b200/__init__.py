@@ -41,3 +41,4 @@ from .rasterizer import (  # noqa: F401
     SP_KEYS_REF20,
     default_options,
 )
+from .training import Trainer, ground_truth_rgba  # noqa: F401,E402

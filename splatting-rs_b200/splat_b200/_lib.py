@@ -227,6 +227,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "sp_param_gradients": (_P, [_P]),
     "sp_zero_param_gradients": (c_int, [_P]),
     "sp_camera_gradient_device": (_P, [_P]),
+    "sp_densify_stats_device": (_P, [_P]),
     "sp_read_loss_gradient": (c_int, [_P, _P]),
     "sp_read_param_gradients": (c_int, [_P, _P]),
     "sp_read_densify_stats": (c_int, [_P, _P]),
@@ -260,6 +261,8 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "sp_adam_step_range": (c_int, [_P, c_uint64, c_uint64]),
     "sp_adam_steps_taken": (c_uint32, [_P]),
     "sp_adam_read_moments": (c_int, [_P, _P, _P]),
+    "sp_adam_first_moment_device": (_P, [_P]),
+    "sp_adam_second_moment_device": (_P, [_P]),
     "sp_position_rate_factor": (c_float, [c_uint64, c_uint64]),
     "sp_adam_resume_device": (c_int, [_P, _P, _P, c_uint64, _P, _P, POINTER(_P)]),
     "sp_densify_after": (c_int, [POINTER(DensifySettingsC), c_uint64, c_uint64]),
@@ -295,6 +298,10 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "sp_device_poses_step": (c_int, [_P, c_uint32, c_uint32, c_float]),
     "sp_device_poses_download": (c_int, [_P, _P]),
     "sp_train_step_device_poses": (c_int, [_P, _P, _P, c_uint32, c_uint32, c_float, _P]),
+    "sp_ply_write": (c_int, [c_char_p, _P, c_uint64, c_uint32, c_int]),
+    "sp_ply_read_header": (c_int, [c_char_p, POINTER(c_uint64), POINTER(c_uint32)]),
+    "sp_ply_read": (c_int, [c_char_p, _P, c_uint64, c_uint32, c_int]),
+    "sp_ply_error": (c_char_p, []),
 }
 
 

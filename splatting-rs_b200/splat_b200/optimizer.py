@@ -10,7 +10,7 @@ import numpy as np
 
 from . import _lib
 from ._lib import LearningRatesC
-from .rasterizer import Context, Rasterizer
+from .rasterizer import Context, DeviceArray, Rasterizer
 
 ADAM_BETA1 = np.float32(0.9)
 ADAM_BETA2 = np.float32(0.999)
@@ -198,6 +198,16 @@ class Adam:
             "read_moments",
         )
         return m, v
+
+    def moment_tensors(self):
+        """The first and second moments as CUDA tensor views (N * stride floats each)."""
+        import torch
+
+        stride = 11 + 3 * (self.sh_degree + 1) ** 2
+        shape = (self.gaussian_count * stride,)
+        device = f"cuda:{self.ctx.device}"
+        return (torch.as_tensor(DeviceArray(self.lib.sp_adam_first_moment_device(self.handle), shape), device=device),
+                torch.as_tensor(DeviceArray(self.lib.sp_adam_second_moment_device(self.handle), shape), device=device))
 
     def close(self) -> None:
         if getattr(self, "handle", None):

@@ -296,6 +296,12 @@ class Rasterizer:
         ptr = self.lib.sp_camera_gradient_device(self.handle)
         return torch.as_tensor(DeviceArray(ptr, (14,)), device=f"cuda:{self.ctx.device}")
 
+    def densify_stats_tensor(self):
+        """The accumulated densify statistics as an (N, 4) CUDA tensor view."""
+        torch = _torch()
+        ptr = self.lib.sp_densify_stats_device(self.handle)
+        return torch.as_tensor(DeviceArray(ptr, (self.gaussian_count, 4)), device=f"cuda:{self.ctx.device}")
+
     def zero_param_gradients(self) -> None:
         self._check(self.lib.sp_zero_param_gradients(self.handle), "zero_param_gradients")
 

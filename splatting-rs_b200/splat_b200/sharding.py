@@ -18,6 +18,14 @@ buffers the library and the caller own, viewed as tensors without a copy:
   one (the ranges' backward launches end in partial waves, and the concurrent NCCL kernels
   slow the Adam steps), so one range is the default.
 - "allreduce": one all-reduce (sum) of the gradients, then the full Adam step on every rank.
+
+Densification (densify.rs:147-257) with several ranks: each rank's backward passes
+accumulated the densify statistics of its own views, so they are merged first (sums of the
+mean-gradient sums and visible counts, the largest screen radius: what one device would
+have accumulated over all the views, up to the order of the sums), and in the sharded
+exchange each rank's moments are current only on its own share, so the shares are
+all-gathered. Every rank then runs the same densification on the same inputs and gets the
+same Gaussians (the kernels are deterministic).
 """
 
 from __future__ import annotations
@@ -57,6 +65,17 @@ def chunk_ranges(gaussians: int, chunks: int, world: int, align: int = 256) -> l
         out.append((first, count))
         first += count
     return out
+
+
+def merge_densify_stats(stats, group=None) -> None:
+    """In place on `stats` ((N, 4) float32: mean-gradient sum, visible count, max radius, pad),
+    every rank's statistics merged: the first two summed, the radius the largest."""
+    import torch.distributed as dist
+
+    summed = stats.clone()
+    dist.all_reduce(summed, op=dist.ReduceOp.SUM, group=group)
+    dist.all_reduce(stats, op=dist.ReduceOp.MAX, group=group)
+    stats[:, :2] = summed[:, :2]
 
 
 class GradientExchange:
@@ -126,6 +145,18 @@ class GradientExchange:
         else:
             self._replicated(rate_factor)
 
+    def gather_moments(self, first, second) -> None:
+        """Makes Adam's moments (flat tensors like the parameters) whole on every rank: in
+        the sharded exchange each rank updated only its share of every range."""
+        import torch.distributed as dist
+
+        if self.world == 1 or self.mode != "sharded":
+            return
+        for moment in (first, second):
+            for first_gaussian, count in self.ranges:
+                whole, own = self._views(moment, first_gaussian, count)
+                dist.all_gather_into_tensor(whole, own, group=self.group)
+
     def _replicated(self, rate_factor: float) -> None:
         import torch.distributed as dist
 
@@ -142,11 +173,40 @@ class ViewShardedStep:
                  group=None):
         self.rasterizer = rasterizer
         self.adam = adam
+        self.params = params
         self.uniforms = uniforms
         self.rank = rank
         self.world = world
+        self.mode = mode
+        self.group = group
         self.exchange = GradientExchange(adam, params, rasterizer.param_gradients(), rasterizer.gaussian_count,
                                          rasterizer.stride, rank, world, mode, group)
+
+    def densify(self, settings, extent: float, max_count: int, reset_opacity: bool, seed: int):
+        """Trainer::densify_async (training.rs:238-266) on every rank: the statistics merged and
+        the moments gathered (module docstring), densify on the device, then this step's
+        rasterizer, optimiser and exchange rebuilt at the new count (the statistics start
+        over; the exchange is sharded again only when the new count splits evenly). Every rank
+        must call it at the same step. Returns the DensifyReport."""
+        from .densify import densify
+        from .rasterizer import Rasterizer
+
+        r = self.rasterizer
+        if self.world > 1:
+            merge_densify_stats(r.densify_stats_tensor(), self.group)
+            self.exchange.gather_moments(*self.adam.moment_tensors())
+        out = densify(r, self.adam, extent, max_count, settings, reset_opacity, seed)
+        count = out.report.after
+        rasterizer = Rasterizer(r.ctx, out.params, count, r.width, r.height, r._ground_truth, r.view_count,
+                                r.options)
+        adam = self.adam.resumed_device(out.params, rasterizer, count, out.first_moment, out.second_moment)
+        r.close()
+        self.adam.close()
+        self.rasterizer, self.adam, self.params = rasterizer, adam, out.params
+        mode = self.mode if self.mode != "sharded" or even_shards(count, self.world) else None
+        self.exchange = GradientExchange(adam, out.params, rasterizer.param_gradients(), count, rasterizer.stride,
+                                         self.rank, self.world, mode, self.group)
+        return out.report
 
     def __call__(self, step: int, rate_factor: float) -> int:
         view = view_of(step, self.rank, self.world, len(self.uniforms))

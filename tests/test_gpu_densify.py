@@ -174,3 +174,21 @@ def test_training_with_densification_runs_and_lowers_the_loss(ctx):
     assert trainer.gaussian_count <= settings.max_count(trainer.initial_gaussian_count)
     last = trainer.loss(0).total
     assert last < first, (first, last)
+
+
+def test_trainer_writes_and_reads_its_splat_on_the_device(ctx, tmp_path):
+    """The trainer's Gaussians written to a PLY straight from device memory (sp_ply_write) and
+    read back into a device tensor (sp_ply_read): the same floats; the host reader agrees."""
+    from splat_b200 import io
+
+    trainer = _trainer(ctx)
+    for step in range(5):
+        trainer.train_step(step, 10)
+    ctx.sync()
+    path = tmp_path / "splat.ply"
+    io.write_splat_ply_device(path, trainer.params, trainer.gaussian_count, trainer.sh_degree)
+    back, count, degree = io.read_splat_ply_device(path, device=ctx.device)
+    assert (count, degree) == (trainer.gaussian_count, trainer.sh_degree)
+    assert np.array_equal(back.cpu().numpy(), trainer.params.cpu().numpy())
+    host = io.read_splat_ply(path)
+    assert np.array_equal(host.to_packed(), trainer.params.cpu().numpy().reshape(count, -1))

@@ -103,3 +103,56 @@ def test_two_gpus_equal_one_gpu_with_the_same_batch(ctx, tmp_path):
         adam.encode_step(sb.position_rate_factor(s, 10))
     ctx.sync()
     assert np.array_equal(params.cpu().numpy().view(np.uint32), ranks[0].view(np.uint32))
+
+
+def _densify_rank_main(rank: int, world: int, port: int, out_dir: str) -> None:
+    from datetime import timedelta
+
+    import torch
+    import torch.distributed as dist
+
+    sys.path[:0] = [str(ROOT / "splatting-rs_b200")]
+    import splat_b200 as sb
+    from splat_b200.sharding import ViewShardedStep
+
+    torch.cuda.set_device(rank)
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    cloud, cams, gt = _scene()
+    ctx = sb.Context(rank)
+    params = torch.from_numpy(cloud.to_packed()).cuda()
+    gt_dev = torch.from_numpy(gt.reshape(-1)).cuda()
+    opts = sb.default_options(sh_degree=1, backward_mode=sb.SP_BWD_DETERMINISTIC)
+    rast = sb.Rasterizer(ctx, params, len(cloud), 160, 120, gt_dev, len(cams), opts)
+    adam = sb.Adam(ctx, params, rast, len(cloud), sb.LEARNING_RATES_3DGS, 2.0, sh_degree=1)
+    step = ViewShardedStep(rast, adam, params, [c.uniform() for c in cams], rank, world, mode="sharded")
+    settings = sb.DensifySettings(**{**sb.DENSIFY_SHORT_RUN.__dict__, "gradient_threshold": 1e-5})
+    for s in range(STEPS):
+        step(s, sb.position_rate_factor(s, 10))
+    report = step.densify(settings, 2.0, settings.max_count(len(cloud)), False, 0)
+    for s in range(STEPS, STEPS + 2):
+        step(s, sb.position_rate_factor(s, 10))
+    torch.cuda.synchronize()
+    np.save(os.path.join(out_dir, f"densified{rank}.npy"), step.params.cpu().numpy())
+    np.save(os.path.join(out_dir, f"report{rank}.npy"), np.array([report.before, report.after, report.split]))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def test_two_gpus_densify_identically(tmp_path):
+    """Three view-sharded steps on two GPUs, a densification (statistics merged, moment shards
+    gathered, then the same densify on each rank), two more steps: both ranks hold the same
+    Gaussians, at a count the densification changed."""
+    import torch
+    import torch.multiprocessing as mp
+
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    world = 2
+    mp.start_processes(_densify_rank_main, args=(world, _free_port(), str(tmp_path)), nprocs=world, join=True,
+                       start_method="spawn")
+    reports = [np.load(tmp_path / f"report{r}.npy") for r in range(world)]
+    assert np.array_equal(reports[0], reports[1]) and reports[0][1] != reports[0][0]
+    ranks = [np.load(tmp_path / f"densified{r}.npy") for r in range(world)]
+    assert np.array_equal(ranks[0].view(np.uint32), ranks[1].view(np.uint32))

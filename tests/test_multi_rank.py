@@ -145,3 +145,108 @@ def test_two_gloo_ranks_equal_one_process_summing_their_views(tmp_path, mode, ch
         oracle.adam_step(packed, total, m, v, 14, lr, step + 1, float(np.log(np.float32(0.02))),
                          float(np.log(np.float32(10.0))))
     assert np.array_equal(ranks[0], packed)
+
+
+def _stats_and_gradient(oracle, camera, gt_view, packed, stats):
+    cam = oracle.camera_array(camera.uniform())
+    fwd = oracle.render(packed, 0, cam)
+    partials = oracle.ssim(fwd["image"], gt_view, camera.width, camera.height)
+    loss_gradient, _ = oracle.loss(fwd["image"], gt_view, partials, camera.width, camera.height)
+    return oracle.backward(packed, 0, cam, fwd, loss_gradient, stats)["param_gradients"]
+
+
+_DENSIFY_ARGS = dict(extent=0.15, seed=3)
+
+
+def _densify_packed(cloud):
+    """The scene's Gaussians with every other one three e-folds smaller, so that the
+    densification both splits (large) and clones (small) after Adam's scale clamp."""
+    packed = cloud.to_packed().copy()
+    packed.reshape(-1, 14)[::2, 3:6] -= 3.0
+    return packed
+
+
+def _settings():
+    import splat_b200 as sb
+
+    # A low threshold, and splits above ln(0.1 * 0.15) = -4.2 (the clamp caps the log scales
+    # at ln(0.02) = -3.9).
+    return sb.DensifySettings(**{**sb.DENSIFY_SHORT_RUN.__dict__, "gradient_threshold": 1e-6,
+                                 "split_scale_fraction": 0.1})
+
+
+def _densify_rank_main(rank: int, world: int, port: int, out_dir: str) -> None:
+    import torch
+    import torch.distributed as dist
+
+    sys.path[:0] = [str(ROOT / "splatting-rs_b200"), str(ROOT / "oracle")]
+    import oracle
+    import splat_b200 as sb
+    from splat_b200.sharding import GradientExchange, merge_densify_stats
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    cloud, cams, gt = _scene()
+    params = torch.from_numpy(_densify_packed(cloud))
+    gradients = torch.zeros_like(params)
+    lr = sb.LEARNING_RATES_3DGS.by_slot(np.float32(1.0), 14)
+    adam = _OracleAdam(oracle, params.numpy(), gradients.numpy(), lr)
+    exchange = GradientExchange(adam, params, gradients, len(cloud), 14, rank, world, "sharded")
+    stats = torch.zeros((len(cloud), 4), dtype=torch.float32)
+    for step in range(2):
+        view = view_of(step, rank, world, len(cams))
+        gradients.copy_(torch.from_numpy(_stats_and_gradient(oracle, cams[view], gt[view], params.numpy(),
+                                                             stats.numpy())))
+        exchange(1.0)
+    merge_densify_stats(stats)
+    first, second = torch.from_numpy(adam.m), torch.from_numpy(adam.v)
+    exchange.gather_moments(first, second)
+    p, m, v, report = oracle.densify(params.numpy(), first.numpy(), second.numpy(), stats.numpy(), 14,
+                                     _DENSIFY_ARGS["extent"], 10 * len(cloud), _settings().to_c(), 0,
+                                     _DENSIFY_ARGS["seed"])
+    np.savez(os.path.join(out_dir, f"rank{rank}.npz"), p=p, m=m, v=v, stats=stats.numpy(),
+             split=report["split"], cloned=report["cloned"])
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def test_two_gloo_ranks_densify_as_one_process():
+    """Densification after two view-sharded steps on two ranks: the ranks' statistics merged
+    (sums, largest radius) and the sharded moments gathered, then the same densify on each
+    rank: both ranks equal, and equal to one process that summed both views' gradients and
+    merged the two ranks' statistics the same way."""
+    import tempfile
+
+    import torch.multiprocessing as mp
+
+    import oracle
+    import splat_b200 as sb
+
+    world = 2
+    with tempfile.TemporaryDirectory() as out:
+        mp.start_processes(_densify_rank_main, args=(world, _free_port(), out), nprocs=world, join=True,
+                           start_method="spawn")
+        ranks = [dict(np.load(os.path.join(out, f"rank{r}.npz"))) for r in range(world)]
+    for key in ("p", "m", "v", "stats"):
+        assert np.array_equal(ranks[0][key], ranks[1][key]), key
+    assert ranks[0]["split"] > 0 and ranks[0]["cloned"] > 0
+
+    cloud, cams, gt = _scene()
+    packed = _densify_packed(cloud)
+    m, v = np.zeros_like(packed), np.zeros_like(packed)
+    lr = sb.LEARNING_RATES_3DGS.by_slot(np.float32(1.0), 14)
+    per_rank = [np.zeros((len(cloud), 4), np.float32) for _ in range(world)]
+    for step in range(2):
+        grads = []
+        for r in range(world):
+            view = view_of(step, r, world, len(cams))
+            grads.append(_stats_and_gradient(oracle, cams[view], gt[view], packed, per_rank[r]))
+        oracle.adam_step(packed, grads[0] + grads[1], m, v, 14, lr, step + 1, float(np.log(np.float32(0.02))),
+                         float(np.log(np.float32(10.0))))
+    merged = per_rank[0] + per_rank[1]
+    merged[:, 2] = np.maximum(per_rank[0][:, 2], per_rank[1][:, 2])
+    merged[:, 3] = 0.0
+    assert np.array_equal(ranks[0]["stats"], merged)
+    p, mm, vv, _ = oracle.densify(packed, m, v, merged, 14, _DENSIFY_ARGS["extent"], 10 * len(cloud),
+                                  _settings().to_c(), 0, _DENSIFY_ARGS["seed"])
+    assert np.array_equal(ranks[0]["p"], p) and np.array_equal(ranks[0]["m"], mm) and np.array_equal(ranks[0]["v"], vv)
