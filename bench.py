@@ -64,6 +64,7 @@ def parse_args():
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-forward-3m", action="store_true", help="skip the forward-only config-3 measurement")
     p.add_argument("--forward-batches", type=int, default=3, help="timed passes over config 3's 64 cameras")
+    p.add_argument("--no-densify", action="store_true", help="skip the device densification timing")
     return p.parse_args()
 
 
@@ -202,6 +203,45 @@ def cpu_baseline(scene, gt: np.ndarray, seconds: float, threads: int | None = No
                   f"by the C++ oracle (OpenMP), {total:.1f} s",
         "ms_per_step": 1000.0 * total / steps,
     }
+
+
+def cpu_densify(params: np.ndarray, first: np.ndarray, second: np.ndarray, stats: np.ndarray, stride: int,
+                extent: float, max_count: int, settings) -> dict:
+    """The reference's densification flow on the host (training.rs:238-266): the CPU
+    restatement of densify (single-threaded, as the Rust), on buffers already read back."""
+    import oracle
+
+    t0 = time.perf_counter()
+    _, _, _, report = oracle.densify(params, first, second, stats, stride, extent, max_count, settings.to_c(), 0, 0)
+    return {"ms": 1000.0 * (time.perf_counter() - t0), "cores": 1, "kind": "port", "after": report["after"]}
+
+
+def densify_timing(ctx, rast, adam, extent: float, gaussians: int) -> dict:
+    """One densification of the trained state on the device (sp_densify_plan + apply with
+    DENSIFY_SHORT_RUN, the outputs allocated), timed on the host around the call (it
+    synchronises) and per kernel with CUDA events; the state itself is left unchanged."""
+    import torch
+
+    import splat_b200 as sb
+
+    settings = sb.DENSIFY_SHORT_RUN
+    max_count = settings.max_count(gaussians)
+    walls = []
+    for _ in range(4):
+        torch.cuda.synchronize()
+        ctx.profile(True)
+        t0 = time.perf_counter()
+        out = sb.densify(rast, adam, float(extent), max_count, settings, False, 0)
+        walls.append(1000.0 * (time.perf_counter() - t0))
+        ctx.profile(False)
+        kernel_ms, launches = ctx.read_profile()["densify"]
+        del out
+    report = sb.densify(rast, adam, float(extent), max_count, settings, False, 0).report
+    return {"wall_ms": float(np.median(walls[1:])), "kernel_ms": kernel_ms, "launches": launches,
+            "before": report.before, "after": report.after, "cloned": report.cloned, "split": report.split,
+            "pruned": report.pruned_transparent + report.pruned_oversized,
+            "what": "sp_densify_plan + sp_densify_apply (classify, select, scan, write; the report read back) "
+                    "of the benchmark's trained state with DENSIFY_SHORT_RUN; median of 3 after one warm-up"}
 
 
 def run_reference(args) -> None:
@@ -542,6 +582,10 @@ def main() -> None:
                         if d.get("bound") == "fp32" else f"{pk['source']} HBM copy bandwidth"),
     }
 
+    densify = None
+    if world == 1 and not args.no_densify:
+        densify = densify_timing(ctx, train_step.rasterizer, train_step.adam, float(extent), len(cloud))
+
     forward_3m = None
     if not args.no_forward_3m:
         forward_3m = forward_throughput(args, ctx, rank, world, max_over_ranks, barrier)
@@ -551,6 +595,18 @@ def main() -> None:
         baseline = cpu_baseline(scene, gt_host, args.cpu_seconds)
         baseline.pop("ms_per_step", None)
         baseline.pop("steps", None)
+        if densify is not None:
+            # The reference's densification of the same state: read back, then densify on the host.
+            r, a = train_step.rasterizer, train_step.adam
+            torch.cuda.synchronize()
+            t0 = time.perf_counter()
+            host_params = train_step.params.cpu().numpy()
+            first, second = a.read_moments()
+            stats = r.read_densify_stats()
+            readback_ms = 1000.0 * (time.perf_counter() - t0)
+            baseline["densify"] = cpu_densify(host_params, first, second, stats, r.stride, float(extent),
+                                              sb.DENSIFY_SHORT_RUN.max_count(len(cloud)), sb.DENSIFY_SHORT_RUN)
+            baseline["densify"]["readback_ms"] = readback_ms
 
     if rank == 0:
         line = {
@@ -584,6 +640,7 @@ def main() -> None:
             "intersections": int(meta.count),
             "mpix_per_s": value * width * height / 1e6,
             "fwd_mpix_per_s_3M": forward_3m,
+            "densify": densify,
         }
         print(json.dumps(line), flush=True)
     if world > 1:

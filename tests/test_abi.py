@@ -122,3 +122,15 @@ def test_profiler_kernel_names_follow_the_header_enum():
     count = values.pop("count")
     assert count == len(_lib.KERNEL_NAMES)
     assert [name for name, _ in sorted(values.items(), key=lambda kv: kv[1])] == list(_lib.KERNEL_NAMES)
+
+
+def test_a_c_caller_links_and_runs(tmp_path):
+    """tests/c_abi/abi_test.c, compiled with gcc against include/ and linked to the library:
+    the headers compile as C and the host-only entry points behave as declared."""
+    exe = tmp_path / "abi_test"
+    lib_dir = _lib.LIBRARY_PATH.parent
+    subprocess.run(["gcc", "-std=c11", "-Wall", "-Werror", f"-I{ROOT / 'include'}", str(ROOT / "tests" / "c_abi" / "abi_test.c"),
+                    f"-L{lib_dir}", f"-Wl,-rpath,{lib_dir}", "-lsplat_b200", "-lm", "-o", str(exe)], check=True)
+    out = subprocess.run([str(exe), str(tmp_path / "abi.ply")], capture_output=True, text=True)
+    assert out.returncode == 0, out.stderr
+    assert out.stdout.strip() == "ok"

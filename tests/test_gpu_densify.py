@@ -191,4 +191,4 @@ def test_trainer_writes_and_reads_its_splat_on_the_device(ctx, tmp_path):
     assert (count, degree) == (trainer.gaussian_count, trainer.sh_degree)
     assert np.array_equal(back.cpu().numpy(), trainer.params.cpu().numpy())
     host = io.read_splat_ply(path)
-    assert np.array_equal(host.to_packed(), trainer.params.cpu().numpy().reshape(count, -1))
+    assert np.array_equal(host.to_packed().reshape(-1), trainer.params.cpu().numpy())
