@@ -70,7 +70,8 @@ cudaError_t launch_sort_pass(const SortPlan& plan, int pass, uint32_t sequence, 
                              void* keys1, uint32_t* values1, const uint32_t* sort_histograms, uint32_t* sort_tickets,
                              unsigned long long* lookback, uint32_t max_partitions, DeviceMeta* meta,
                              cudaStream_t stream);
-// tile_ranges.wgsl:9-22 over a zeroed range array.
+// tile_ranges.wgsl:9-22: every tile's [start, end) in the sorted keys, (0, 0) for tiles
+// without keys (the reference zeroes the array first; here each tile is written once).
 cudaError_t launch_ranges(const SortPlan& plan, const void* keys, const DeviceMeta* meta, uint64_t capacity,
                           uint2* ranges, uint32_t tiles, cudaStream_t stream);
 

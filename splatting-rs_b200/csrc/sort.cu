@@ -298,17 +298,42 @@ __global__ void __launch_bounds__(kSortThreads, kSortBlocksPerSM)
     }
 }
 
+// tile_ranges.wgsl:9-22 without the zeroed array: each thread takes kRangeItems consecutive
+// sorted keys; where the tile changes between two neighbours it writes the end of the one
+// and the start of the other, and (0, 0) for the tiles in between, which hold no key (so do
+// the tiles before the first key and after the last). Every tile is written exactly once.
+constexpr uint32_t kRangeItems = 4;
+
 template <typename Key>
-__global__ void k_ranges(const Key* __restrict__ keys, const DeviceMeta* __restrict__ meta, uint32_t tiles,
-                         uint2* __restrict__ ranges) {
+__global__ void __launch_bounds__(kBlock) k_ranges(const Key* __restrict__ keys, const DeviceMeta* __restrict__ meta,
+                                                   uint32_t tiles, uint2* __restrict__ ranges) {
     const uint32_t count = meta->count;
     const uint32_t tile_shift = meta->key_shift;
-    for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < count; i += gridDim.x * blockDim.x) {
-        const uint32_t tile = (uint32_t)(keys[i] >> tile_shift);
-        if (tile >= tiles) continue;
-        uint32_t* r = reinterpret_cast<uint32_t*>(ranges + tile);
-        if (i == 0 || (uint32_t)(keys[i - 1] >> tile_shift) != tile) r[0] = i;
-        if (i + 1 == count || (uint32_t)(keys[i + 1] >> tile_shift) != tile) r[1] = i + 1;
+    const uint32_t threads = gridDim.x * blockDim.x;
+    const uint32_t t = blockIdx.x * blockDim.x + threadIdx.x;
+    if (count == 0) {
+        for (uint32_t tile = t; tile < tiles; tile += threads) ranges[tile] = make_uint2(0u, 0u);
+        return;
+    }
+    auto tile_at = [&](uint32_t i) { return min((uint32_t)(keys[i] >> tile_shift), tiles); };
+    for (uint32_t i0 = t * kRangeItems; i0 < count; i0 += threads * kRangeItems) {
+        // The tile before this thread's first key (`tiles` plays "none" past the end, and the
+        // first key's predecessor is tile -1, as an unsigned wrap below).
+        uint32_t previous = i0 == 0 ? 0xFFFFFFFFu : tile_at(i0 - 1);
+        const uint32_t last = min(i0 + kRangeItems, count);
+        for (uint32_t i = i0; i < last; ++i) {
+            const uint32_t tile = tile_at(i);
+            if (tile != previous) {
+                if (previous != 0xFFFFFFFFu && previous < tiles) ranges[previous].y = i;
+                if (tile < tiles) ranges[tile].x = i;
+                for (uint32_t empty = previous + 1; empty < tile; ++empty) ranges[empty] = make_uint2(0u, 0u);
+            }
+            previous = tile;
+        }
+        if (last == count) {
+            if (previous < tiles) ranges[previous].y = count;
+            for (uint32_t empty = previous + 1; empty < tiles; ++empty) ranges[empty] = make_uint2(0u, 0u);
+        }
     }
 }
 
@@ -382,9 +407,8 @@ cudaError_t launch_sort_pass(const SortPlan& plan, int pass, uint32_t sequence, 
 
 cudaError_t launch_ranges(const SortPlan& plan, const void* keys, const DeviceMeta* meta, uint64_t capacity,
                           uint2* ranges, uint32_t tiles, cudaStream_t stream) {
-    cudaError_t err = cudaMemsetAsync(ranges, 0, (size_t)tiles * sizeof(uint2), stream);
-    if (err != cudaSuccess) return err;
-    const unsigned grid = (unsigned)std::min<uint64_t>(std::max<uint64_t>(grid_for(capacity, kBlock), 1), 148 * 16);
+    const unsigned grid = (unsigned)std::min<uint64_t>(
+        std::max<uint64_t>(grid_for((capacity + kRangeItems - 1) / kRangeItems, kBlock), 1), 148 * 8);
     if (plan.key64)
         k_ranges<unsigned long long><<<grid, kBlock, 0, stream>>>(static_cast<const unsigned long long*>(keys), meta,
                                                                    tiles, ranges);
