@@ -65,6 +65,9 @@ def parse_args():
     p.add_argument("--no-forward-3m", action="store_true", help="skip the forward-only config-3 measurement")
     p.add_argument("--forward-batches", type=int, default=3, help="timed passes over config 3's 64 cameras")
     p.add_argument("--no-densify", action="store_true", help="skip the device densification timing")
+    p.add_argument("--tiles", choices=["ellipse", "rectangle"], default="ellipse",
+                   help="tile culling: the ellipse's tiles only (the same images and gradients, shorter lists) "
+                        "or the reference's whole bounding rectangles")
     return p.parse_args()
 
 
@@ -325,7 +328,8 @@ def forward_throughput(args, ctx, rank: int, world: int, max_over_ranks, barrier
     cams = scene.cameras[rank::world]
     w, h = cams[0].width, cams[0].height
     params = torch.from_numpy(scene.cloud.to_packed()).cuda()
-    opts = sb.default_options(sh_degree=scene.cloud.sh_degree)
+    opts = sb.default_options(sh_degree=scene.cloud.sh_degree,
+                              tile_culling=sb.SP_TILES_ELLIPSE if args.tiles == "ellipse" else sb.SP_TILES_RECTANGLE)
     rast = sb.Rasterizer(ctx, params, len(scene.cloud), w, h, None, 0, opts)
     uniforms = [c.uniform() for c in cams]
 
@@ -393,7 +397,9 @@ def main() -> None:
     views = len(cams)
     width, height = cams[0].width, cams[0].height
     ctx = sb.Context(local)
-    options = lambda: sb.default_options(sh_degree=deg, backward_mode=sb.SP_BWD_ATOMIC)  # noqa: E731
+    culling = sb.SP_TILES_ELLIPSE if args.tiles == "ellipse" else sb.SP_TILES_RECTANGLE
+    options = lambda: sb.default_options(sh_degree=deg, backward_mode=sb.SP_BWD_ATOMIC,  # noqa: E731
+                                         tile_culling=culling)
     gt_host = build_ground_truth(ctx, scene, options)
     params = torch.from_numpy(cloud.to_packed()).cuda()
     initial = params.clone()
@@ -623,6 +629,10 @@ def main() -> None:
             "dtype": "f32",
             "data": "synthetic",
             "config": config_dict(scene, world),
+            "tile_culling": (f"{args.tiles}: " + (
+                "keys only for the bounding rectangle's tiles the Gaussian's alpha can reach (the same images, "
+                "losses and gradients as the reference's whole rectangles)"
+                if args.tiles == "ellipse" else "the reference's whole bounding rectangles")),
             "clocks": clock_summary,
             "e2e": {
                 "value": e2e_value,

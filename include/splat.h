@@ -179,6 +179,20 @@ enum {
     SP_KEYS_FULL32 = 1
 };
 
+/* Which tiles of a Gaussian get a key. */
+enum {
+    /* Every tile of its bounding rectangle (project_forward.wgsl:76-83): the reference's
+     * intersection lists. */
+    SP_TILES_RECTANGLE = 0,
+    /* Only the rectangle's tiles where its alpha can reach 1/255 at a pixel centre (its
+     * ellipse at that level, padded, meets the tile): shorter lists, fewer keys to sort. The
+     * dropped pairs are ones the blend skips at every pixel, so images, losses, gradients
+     * and parameters are those of SP_TILES_RECTANGLE; intersection counts, list indices and
+     * contribution counts are of the shorter lists. Needs SP_BWD_ATOMIC (the deterministic
+     * backward addresses its slots by the tile's place in the rectangle). */
+    SP_TILES_ELLIPSE = 1
+};
+
 /* How the blend backward sums each Gaussian's gradient over the pixels of a tile. */
 enum {
     /* One write per (Gaussian, tile) slot, summed per Gaussian afterwards in slot order,
@@ -198,6 +212,8 @@ typedef struct sp_options {
      * sp_zero_param_gradients. */
     uint32_t accumulate_gradients;
     sp_loss_weights loss_weights;        /* default LOSS_WEIGHTS (loss.rs:32-36) */
+    /* SP_TILES_* (default SP_TILES_RECTANGLE). */
+    uint32_t tile_culling;
 } sp_options;
 
 typedef struct sp_context sp_context;

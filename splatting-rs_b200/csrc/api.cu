@@ -348,6 +348,7 @@ void sp_options_default(sp_options* out) {
     out->loss_weights.l1 = SP_LOSS_L1;
     out->loss_weights.dssim = SP_LOSS_DSSIM;
     out->loss_weights.alpha = SP_LOSS_ALPHA;
+    out->tile_culling = SP_TILES_RECTANGLE;
 }
 
 void sp_rasterizer_destroy(sp_rasterizer* r) {
@@ -378,6 +379,12 @@ sp_status sp_rasterizer_create(sp_context* ctx, const float* d_params, uint64_t 
     SP_REQUIRE(ctx, opt.backward_mode == SP_BWD_DETERMINISTIC || opt.backward_mode == SP_BWD_ATOMIC, SP_ERR_INVALID,
                "backward mode");
     SP_REQUIRE(ctx, opt.intersections_per_gaussian > 0, SP_ERR_INVALID, "intersections per Gaussian");
+    SP_REQUIRE(ctx, opt.tile_culling == SP_TILES_RECTANGLE || opt.tile_culling == SP_TILES_ELLIPSE, SP_ERR_INVALID,
+               "tile culling");
+    // The deterministic backward addresses its per-(Gaussian, tile) slots by the tile's index
+    // in the Gaussian's rectangle.
+    SP_REQUIRE(ctx, opt.tile_culling == SP_TILES_RECTANGLE || opt.backward_mode == SP_BWD_ATOMIC, SP_ERR_INVALID,
+               "tile culling needs the atomic backward");
     const uint32_t tiles_x = (width + SP_TILE - 1) / SP_TILE, tiles_y = (height + SP_TILE - 1) / SP_TILE;
     SP_REQUIRE(ctx, tiles_x <= 0xffffu && tiles_y <= 0xffffu, SP_ERR_TOO_MANY_TILES,
                "over 65535 tiles on a side");
@@ -515,7 +522,8 @@ sp_status sp_forward(sp_rasterizer* r) {
         KernelSpan span(ctx, SP_K_PROJECT);
         SP_CUDA(ctx, launch_project(r->params, r->n, (int)r->options.sh_degree, r->camera,
                                     r->camera_on_device ? r->camera_dev : nullptr, r->records, r->radii, r->offsets,
-                                    r->block_totals, r->plan.compressed ? r->meta : nullptr, r->reach, st));
+                                    r->block_totals, r->plan.compressed ? r->meta : nullptr, r->reach,
+                                    (int)r->options.tile_culling, st));
     }
     {
         KernelSpan span(ctx, SP_K_SCAN);
@@ -525,8 +533,8 @@ sp_status sp_forward(sp_rasterizer* r) {
     {
         KernelSpan span(ctx, SP_K_EMIT);
         SP_CUDA(ctx, launch_emit(r->records, r->offsets, r->block_offsets, r->n, r->camera,
-                                 (int)r->options.key_mode, r->plan, r->meta, r->keys[0], r->keys[1], r->values[0],
-                                 r->values[1], r->sort_histograms, st));
+                                 (int)r->options.key_mode, (int)r->options.tile_culling, r->plan, r->meta, r->keys[0],
+                                 r->keys[1], r->values[0], r->values[1], r->sort_histograms, st));
     }
     // Passes past the frame's key width return at once; the result lands in buffer passes & 1.
     for (int pass = 0; pass < r->plan.passes; ++pass) {

@@ -17,10 +17,12 @@ namespace splat {
 // The camera is `cam`, or when `cam_device` is non-null the 80 B there (written on the device).
 // With `depth_range` non-null (compressed keys) the depth keys' range of the Gaussians that
 // emit keys is accumulated into its depth_lo / depth_hi.
+// With `tile_culling` the tile counts are those of tile_cull.cuh (the rectangle's tiles the
+// ellipse reaches) instead of the rectangle's area.
 cudaError_t launch_project(const float* params, uint64_t n, int sh_degree, const sp_camera_uniform& cam,
                            const sp_camera_uniform* cam_device, float4* records, uint32_t* radii,
                            uint32_t* local_offsets, uint32_t* block_totals, DeviceMeta* depth_range,
-                           float4* reach, cudaStream_t stream);
+                           float4* reach, int tile_culling, cudaStream_t stream);
 // scan_tile_counts (scan.wgsl:64-81): scans the block totals into 64-bit block offsets,
 // fills the meta (count, overflow, sort partitions, this frame's key geometry) and zeroes
 // the sort's histograms and partition tickets for this forward pass.
@@ -60,10 +62,12 @@ cudaError_t launch_to_projected(const float4* records, const uint32_t* radii, ui
 // and Gaussian index per covered tile, and accumulates every sort pass's digit histogram.
 // Keys and values go to ping-pong buffer meta->first_buffer, so that the frame's last sort
 // pass lands in buffer plan.passes & 1.
+// With `tile_culling`, only the tiles of tile_cull.cuh get keys (the counts of launch_project
+// with the same flag).
 cudaError_t launch_emit(const float4* records, uint32_t* offsets, const unsigned long long* block_offsets, uint64_t n,
-                        const sp_camera_uniform& cam, int key_mode, const SortPlan& plan, const DeviceMeta* meta,
-                        void* keys0, void* keys1, uint32_t* values0, uint32_t* values1, uint32_t* sort_histograms,
-                        cudaStream_t stream);
+                        const sp_camera_uniform& cam, int key_mode, int tile_culling, const SortPlan& plan,
+                        const DeviceMeta* meta, void* keys0, void* keys1, uint32_t* values0, uint32_t* values1,
+                        uint32_t* sort_histograms, cudaStream_t stream);
 // One onesweep pass (stable, 8-bit digit `pass`) between the two ping-pong buffers; a pass at
 // or past the frame's meta->passes does nothing.
 cudaError_t launch_sort_pass(const SortPlan& plan, int pass, uint32_t sequence, void* keys0, uint32_t* values0,

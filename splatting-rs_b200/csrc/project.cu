@@ -7,6 +7,7 @@
 
 #include "adam_math.cuh"
 #include "kernels.h"
+#include "tile_cull.cuh"
 #include "project_math.cuh"
 
 namespace splat {
@@ -125,7 +126,7 @@ __global__ void __launch_bounds__(kBlock) k_project(const float* __restrict__ pa
                                                     float4* __restrict__ records, uint32_t* __restrict__ radii,
                                                     uint32_t* __restrict__ local_offsets,
                                                     uint32_t* __restrict__ block_totals, DeviceMeta* depth_range,
-                                                    float4* __restrict__ reach) {
+                                                    float4* __restrict__ reach, uint32_t cull) {
     constexpr int S = SP_PARAM_STRIDE(DEG);
     extern __shared__ float4 smem4[];
     __shared__ sp_camera_uniform s_cam;
@@ -148,6 +149,11 @@ __global__ void __launch_bounds__(kBlock) k_project(const float* __restrict__ pa
         out[2] = rec[2];
         radii[g0 + t] = radius;
         reach[g0 + t] = radius > 0 ? reach_of(rec[0], rec[1]) : make_float4(-1.0f, -1.0f, 0.0f, 0.0f);
+        if (cull && count) {
+            // Only the rectangle's tiles the ellipse reaches get keys (tile_cull.cuh).
+            const uint32_t lo = __float_as_uint(rec[2].z), hi = __float_as_uint(rec[2].w);
+            count = culled_tile_count(rec[0], rec[1], lo & 0xffffu, lo >> 16, hi & 0xffffu, hi >> 16);
+        }
     }
     uint32_t total;
     const uint32_t exclusive = block_exclusive_scan(count, &total);
@@ -610,14 +616,15 @@ cudaError_t set_smem(Kernel kernel, size_t bytes) {
 cudaError_t launch_project(const float* params, uint64_t n, int sh_degree, const sp_camera_uniform& cam,
                            const sp_camera_uniform* cam_device, float4* records, uint32_t* radii,
                            uint32_t* local_offsets, uint32_t* block_totals, DeviceMeta* depth_range,
-                           float4* reach, cudaStream_t stream) {
+                           float4* reach, int tile_culling, cudaStream_t stream) {
     const unsigned grid = grid_for(n, kBlock);
     const size_t smem = (size_t)kBlock * SP_PARAM_STRIDE(sh_degree) * sizeof(float);
     cudaError_t err = cudaSuccess;
 #define SPLAT_PROJECT_ONE(D, V)                                                                           \
     if ((err = set_smem(k_project<D, V>, smem)) != cudaSuccess) return err;                                \
     k_project<D, V><<<grid, kBlock, smem, stream>>>(params, (uint32_t)n, cam, cam_device, records, radii,  \
-                                                    local_offsets, block_totals, depth_range, reach);     \
+                                                    local_offsets, block_totals, depth_range, reach,      \
+                                                    (uint32_t)tile_culling);                              \
     return cudaGetLastError();
 #define SPLAT_PROJECT(D)                \
     if (sh_degree == D) {               \

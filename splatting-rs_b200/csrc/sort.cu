@@ -14,6 +14,7 @@
 #include <cuda/atomic>
 
 #include "kernels.h"
+#include "tile_cull.cuh"
 
 namespace splat {
 namespace {
@@ -44,8 +45,11 @@ __device__ __forceinline__ Key compose_key(uint32_t tile, uint32_t shift, uint32
 // offsets are an exclusive scan in Gaussian order), so its lanes write them together, key by
 // key, whatever the rectangles' sizes: balanced work and coalesced stores. The sort's digit
 // histograms are accumulated on the way: per Gaussian (weighted by its tile count) for the
-// passes whose digit holds depth bits only, per key for the others.
-template <typename Key>
+// passes whose digit holds depth bits only, per key for the others. With CULL the warp walks
+// its rectangles' tiles 32 at a time in the same order and keeps those tile_cull.cuh keeps
+// (a ballot compacts them into the slots), so the keys are the rectangle's, minus the culled
+// tiles, in the same order.
+template <typename Key, bool CULL>
 __global__ void __launch_bounds__(kBlock) k_emit(const float4* __restrict__ records, uint32_t* __restrict__ offsets,
                                                  const unsigned long long* __restrict__ block_offsets, uint32_t n,
                                                  uint32_t tiles_x, int key_mode, const DeviceMeta* __restrict__ meta,
@@ -64,8 +68,9 @@ __global__ void __launch_bounds__(kBlock) k_emit(const float4* __restrict__ reco
     __syncthreads();
     const unsigned long long capacity = meta->capacity;
     const uint32_t g = blockIdx.x * kBlock + t;
-    uint32_t x0 = 0, y0 = 0, w = 1, count = 0;
+    uint32_t x0 = 0, y0 = 0, w = 1, count = 0, area = 0;
     float depth = 0.0f;
+    float4 ra = make_float4(0.0f, 0.0f, 0.0f, 0.0f), rb = ra;
     unsigned long long index = 0;
     if (g < n) {
         const float4 r2 = records[(size_t)g * kRecord + 2];
@@ -74,7 +79,13 @@ __global__ void __launch_bounds__(kBlock) k_emit(const float4* __restrict__ reco
         y0 = lo >> 16;
         const uint32_t x1 = hi & 0xffffu, y1 = hi >> 16;
         w = max(x1 - x0, 1u);
-        count = (x1 - x0) * (y1 - y0);
+        area = (x1 - x0) * (y1 - y0);
+        count = area;
+        if (CULL && area) {
+            ra = records[(size_t)g * kRecord];
+            rb = records[(size_t)g * kRecord + 1];
+            count = culled_tile_count(ra, rb, x0, y0, x1, y1);
+        }
         depth = r2.y;
         index = block_offsets[blockIdx.x] + offsets[g];
         offsets[g] = (uint32_t)index;
@@ -86,20 +97,22 @@ __global__ void __launch_bounds__(kBlock) k_emit(const float4* __restrict__ reco
                 atomicAdd(&hist[p][(depth_key >> (8 * p)) & 255u], (uint32_t)kept);
         }
     }
-    // Exclusive scan of the counts over the warp.
-    uint32_t inclusive = count;
+    // Exclusive scan over the warp of what it walks: the keys, or with CULL the rectangles' tiles.
+    const uint32_t walk = CULL ? area : count;
+    uint32_t inclusive = walk;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
         const uint32_t up = __shfl_up_sync(0xffffffffu, inclusive, o);
         if (lane >= (uint32_t)o) inclusive += up;
     }
-    const uint32_t exclusive = inclusive - count;
+    const uint32_t exclusive = inclusive - walk;
     const uint32_t total = __shfl_sync(0xffffffffu, inclusive, 31);
     const unsigned long long start = __shfl_sync(0xffffffffu, index, 0);
     const int first_tile_pass = (int)tile_shift / 8;
+    uint32_t written = 0;  // CULL: keys the warp has written so far
     for (uint32_t round = 0; round * 32 < total; ++round) {
         const uint32_t e = round * 32 + lane;
-        // The lane whose slots hold e: the last with exclusive <= e.
+        // The lane whose walk holds e: the last with exclusive <= e.
         uint32_t owner = 0;
 #pragma unroll
         for (uint32_t step = 16; step > 0; step >>= 1)
@@ -109,11 +122,29 @@ __global__ void __launch_bounds__(kBlock) k_emit(const float4* __restrict__ reco
         const uint32_t ow = __shfl_sync(0xffffffffu, w, owner);
         const float odepth = __shfl_sync(0xffffffffu, depth, owner);
         const uint32_t og = __shfl_sync(0xffffffffu, g, owner);
-        const unsigned long long slot = start + e;
-        if (e < total && slot < capacity) {
-            const uint32_t row = local / ow;
-            const Key key = compose_key<Key>((oy0 + row) * tiles_x + ox0 + (local - row * ow), tile_shift,
-                                             depth_part(key_mode, odepth, base));
+        const uint32_t row = local / ow, column = ox0 + (local - row * ow);
+        unsigned long long slot;
+        bool emit;
+        if constexpr (CULL) {
+            const float4 oa = make_float4(__shfl_sync(0xffffffffu, ra.x, owner), __shfl_sync(0xffffffffu, ra.y, owner),
+                                          __shfl_sync(0xffffffffu, ra.z, owner), __shfl_sync(0xffffffffu, ra.w, owner));
+            const float4 ob = make_float4(__shfl_sync(0xffffffffu, rb.x, owner), __shfl_sync(0xffffffffu, rb.y, owner),
+                                          0.0f, 0.0f);
+            bool keep = false;
+            if (e < total) {
+                const uint2 span = tile_row_span(oa, ob, oy0 + row, ox0, ox0 + ow);
+                keep = column >= span.x && column < span.y;
+            }
+            const uint32_t ballot = __ballot_sync(0xffffffffu, keep);
+            slot = start + written + __popc(ballot & ((1u << lane) - 1u));
+            written += __popc(ballot);
+            emit = keep;
+        } else {
+            slot = start + e;
+            emit = e < total;
+        }
+        if (emit && slot < capacity) {
+            const Key key = compose_key<Key>((oy0 + row) * tiles_x + column, tile_shift, depth_part(key_mode, odepth, base));
             keys[slot] = key;
             values[slot] = og;
             for (int p = first_tile_pass; p < passes; ++p)
@@ -351,21 +382,22 @@ int sort_grid() {
 }  // namespace
 
 cudaError_t launch_emit(const float4* records, uint32_t* offsets, const unsigned long long* block_offsets, uint64_t n,
-                        const sp_camera_uniform& cam, int key_mode, const SortPlan& plan, const DeviceMeta* meta,
-                        void* keys0, void* keys1, uint32_t* values0, uint32_t* values1, uint32_t* sort_histograms,
-                        cudaStream_t stream) {
+                        const sp_camera_uniform& cam, int key_mode, int tile_culling, const SortPlan& plan,
+                        const DeviceMeta* meta, void* keys0, void* keys1, uint32_t* values0, uint32_t* values1,
+                        uint32_t* sort_histograms, cudaStream_t stream) {
     const unsigned grid = grid_for(n, kBlock);
+#define SPLAT_EMIT(K, C)                                                                                          \
+    k_emit<K, C><<<grid, kBlock, 0, stream>>>(records, offsets, block_offsets, (uint32_t)n, cam.tiles_x, key_mode, \
+                                              meta, static_cast<K*>(keys0), static_cast<K*>(keys1), values0,      \
+                                              values1, sort_histograms)
     if (plan.key64) {
-        using K = unsigned long long;
-        k_emit<K><<<grid, kBlock, 0, stream>>>(records, offsets, block_offsets, (uint32_t)n, cam.tiles_x, key_mode,
-                                               meta, static_cast<K*>(keys0), static_cast<K*>(keys1), values0, values1,
-                                               sort_histograms);
+        if (tile_culling) SPLAT_EMIT(unsigned long long, true);
+        else SPLAT_EMIT(unsigned long long, false);
     } else {
-        using K = uint32_t;
-        k_emit<K><<<grid, kBlock, 0, stream>>>(records, offsets, block_offsets, (uint32_t)n, cam.tiles_x, key_mode,
-                                               meta, static_cast<K*>(keys0), static_cast<K*>(keys1), values0, values1,
-                                               sort_histograms);
+        if (tile_culling) SPLAT_EMIT(uint32_t, true);
+        else SPLAT_EMIT(uint32_t, false);
     }
+#undef SPLAT_EMIT
     return cudaGetLastError();
 }
 

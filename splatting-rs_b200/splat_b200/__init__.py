@@ -39,6 +39,8 @@ from .rasterizer import (  # noqa: F401
     SP_BWD_DETERMINISTIC,
     SP_KEYS_FULL32,
     SP_KEYS_REF20,
+    SP_TILES_ELLIPSE,
+    SP_TILES_RECTANGLE,
     default_options,
 )
 from .training import Trainer, ground_truth_rgba  # noqa: F401,E402

@@ -29,6 +29,8 @@ SP_KEYS_REF20 = 0
 SP_KEYS_FULL32 = 1
 SP_BWD_DETERMINISTIC = 0
 SP_BWD_ATOMIC = 1
+SP_TILES_RECTANGLE = 0
+SP_TILES_ELLIPSE = 1
 
 # Kernels of the per-kernel profiler (SP_K_*), in enum order.
 KERNEL_NAMES = (
@@ -139,6 +141,7 @@ class Options(ctypes.Structure):
         ("intersections_per_gaussian", c_uint32),
         ("accumulate_gradients", c_uint32),
         ("loss_weights", LossWeights),
+        ("tile_culling", c_uint32),
     ]
 
 

@@ -25,6 +25,8 @@ from ._lib import (
     SP_BWD_DETERMINISTIC,
     SP_KEYS_FULL32,
     SP_KEYS_REF20,
+    SP_TILES_ELLIPSE,
+    SP_TILES_RECTANGLE,
 )
 from .camera import PinholeCamera
 
@@ -172,6 +174,7 @@ def default_options(
     key_mode: int = SP_KEYS_REF20,
     intersections_per_gaussian: int = 24,
     accumulate_gradients: bool = False,
+    tile_culling: int = 0,
 ) -> Options:
     opt = Options()
     _lib.load().sp_options_default(ctypes.byref(opt))
@@ -180,6 +183,7 @@ def default_options(
     opt.key_mode = key_mode
     opt.intersections_per_gaussian = intersections_per_gaussian
     opt.accumulate_gradients = 1 if accumulate_gradients else 0
+    opt.tile_culling = tile_culling
     return opt
 
 

@@ -23,6 +23,12 @@ int main(int argc, char** argv) {
     const char* path = argc > 1 ? argv[1] : "abi_test.ply";
     CHECK(sp_version() != NULL && strlen(sp_version()) > 0);
     CHECK(sp_status_string(SP_OK) != NULL);
+    /* The struct layouts a Rust #[repr(C)] binding mirrors. */
+    CHECK(sizeof(sp_options) == 36 && sizeof(sp_densify_settings) == 40 && sizeof(sp_densify_report) == 64);
+    CHECK(sizeof(sp_camera_uniform) == 80 && sizeof(sp_densify_stats) == 16);
+    sp_options defaults;
+    sp_options_default(&defaults);
+    CHECK(defaults.tile_culling == SP_TILES_RECTANGLE && defaults.intersections_per_gaussian == 24);
 
     /* DENSIFY_SHORT_RUN (densify.rs:59-69): densified after 50, 100, 150 of 300 steps. */
     sp_densify_settings s = {50, 50, 0.5f, 2e-4f, 0.01f, 0.005f, 100.0f, 2.0f, 0, 0};

@@ -61,6 +61,8 @@ def test_struct_layouts_match_the_reference():
     assert (p.conic.offset, p.depth.offset, p.color.offset, p.opacity.offset, p.radius.offset) == (16, 28, 32, 44, 48)
     assert (p.tile_min.offset, p.tile_max.offset) == (56, 64)
     assert ctypes.sizeof(_lib.IntersectionMeta) == 20 and ctypes.sizeof(_lib.DensifyStats) == 16
+    assert ctypes.sizeof(_lib.Options) == 36 and _lib.Options.tile_culling.offset == 32
+    assert ctypes.sizeof(_lib.DensifySettingsC) == 40 and ctypes.sizeof(_lib.DensifyReportC) == 64
 
 
 def test_default_options_are_the_reference_behaviour():
