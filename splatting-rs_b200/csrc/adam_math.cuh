@@ -10,20 +10,35 @@ namespace splat {
 
 // One Adam step's constants: the learning rate of every parameter slot (optimizer.rs:248-256
 // folds the position-rate factor in), the bias corrections 1 - beta^t and the clamp bounds.
+// inv_bias1 / inv_bias2 are the correctly rounded reciprocals 1 / bias (host IEEE division).
 struct AdamStep {
     float lr[SP_PARAM_STRIDE(3)];
     float bias1, bias2, max_log_scale, max_log_anisotropy;
+    float inv_bias1, inv_bias2;
 };
 
+// a / b, correctly rounded, for a divisor fixed for the whole step: Markstein's correction
+// (IBM J. Res. Dev. 34(1), 1990) of q0 = RN(a * RN(1/b)) by one fused multiply-add,
+// q = RN(q0 + (a - b q0) RN(1/b)), the remainder a - b q0 exact in the FMA. Checked equal to
+// the IEEE division for every significand of a (at three exponents) and every Adam bias
+// correction 1 - beta^t of beta 0.9 and 0.999 (t to 40000); zeros, infinities, NaN and
+// magnitudes outside [2^-100, 2^100] take the IEEE division itself.
+__device__ __forceinline__ float div_by_step_constant(float a, float b, float inv_b) {
+    const float magnitude = fabsf(a);
+    if (!(magnitude >= 0x1p-100f && magnitude <= 0x1p100f)) return __fdiv_rn(a, b);
+    const float q0 = __fmul_rn(a, inv_b);
+    const float remainder = __fmaf_rn(-q0, b, a);
+    return __fmaf_rn(remainder, inv_b, q0);
+}
+
 // adam.wgsl:26-35 for one parameter: updates the moments, returns the parameter.
-__device__ __forceinline__ float adam_update(float p, float g, float& m, float& v, float lr, float bias1,
-                                             float bias2) {
+__device__ __forceinline__ float adam_update(float p, float g, float& m, float& v, float lr, const AdamStep& step) {
     const float mm = SP_ADAM_BETA1 * m + (1.0f - SP_ADAM_BETA1) * g;
     const float vv = SP_ADAM_BETA2 * v + (1.0f - SP_ADAM_BETA2) * g * g;
     m = mm;
     v = vv;
-    const float m_hat = mm / bias1;
-    const float v_hat = vv / bias2;
+    const float m_hat = div_by_step_constant(mm, step.bias1, step.inv_bias1);
+    const float v_hat = div_by_step_constant(vv, step.bias2, step.inv_bias2);
     return p - lr * m_hat / (__fsqrt_rn(v_hat) + SP_ADAM_EPSILON);
 }
 
@@ -71,10 +86,10 @@ __device__ __forceinline__ void adam_block(float* __restrict__ params, float* __
             const uint32_t s1 = (s0 + 1 == (uint32_t)S) ? 0 : s0 + 1;
             const uint32_t s2 = (s1 + 1 == (uint32_t)S) ? 0 : s1 + 1;
             const uint32_t s3 = (s2 + 1 == (uint32_t)S) ? 0 : s2 + 1;
-            p.x = adam_update(p.x, g.x, a.x, b.x, lr[s0], step.bias1, step.bias2);
-            p.y = adam_update(p.y, g.y, a.y, b.y, lr[s1], step.bias1, step.bias2);
-            p.z = adam_update(p.z, g.z, a.z, b.z, lr[s2], step.bias1, step.bias2);
-            p.w = adam_update(p.w, g.w, a.w, b.w, lr[s3], step.bias1, step.bias2);
+            p.x = adam_update(p.x, g.x, a.x, b.x, lr[s0], step);
+            p.y = adam_update(p.y, g.y, a.y, b.y, lr[s1], step);
+            p.z = adam_update(p.z, g.z, a.z, b.z, lr[s2], step);
+            p.w = adam_update(p.w, g.w, a.w, b.w, lr[s3], step);
             m14[i] = a;
             m24[i] = b;
             s4[i] = p;
@@ -83,7 +98,7 @@ __device__ __forceinline__ void adam_block(float* __restrict__ params, float* __
     }
     for (uint32_t i = done + t; i < floats; i += threads) {
         float m = m1[f0 + i], v = m2[f0 + i];
-        staged[i] = adam_update(params[f0 + i], staged[i], m, v, lr[i % S], step.bias1, step.bias2);
+        staged[i] = adam_update(params[f0 + i], staged[i], m, v, lr[i % S], step);
         m1[f0 + i] = m;
         m2[f0 + i] = v;
     }

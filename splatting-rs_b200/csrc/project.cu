@@ -152,7 +152,7 @@ __global__ void __launch_bounds__(kBlock) k_project(const float* __restrict__ pa
         if (cull && count) {
             // Only the rectangle's tiles the ellipse reaches get keys (tile_cull.cuh).
             const uint32_t lo = __float_as_uint(rec[2].z), hi = __float_as_uint(rec[2].w);
-            count = culled_tile_count(rec[0], rec[1], lo & 0xffffu, lo >> 16, hi & 0xffffu, hi >> 16);
+            count = culled_tile_count(cull_ellipse(rec[0], rec[1]), lo & 0xffffu, lo >> 16, hi & 0xffffu, hi >> 16);
         }
     }
     uint32_t total;
@@ -674,6 +674,8 @@ cudaError_t launch_project_backward(const float* params, uint64_t n, int sh_degr
         for (int k = 0; k < SP_PARAM_STRIDE(sh_degree); ++k) fused.step.lr[k] = adam->lr_by_slot[k];
         fused.step.bias1 = adam->bias1;
         fused.step.bias2 = adam->bias2;
+        fused.step.inv_bias1 = 1.0f / adam->bias1;
+        fused.step.inv_bias2 = 1.0f / adam->bias2;
         fused.step.max_log_scale = adam->max_log_scale;
         fused.step.max_log_anisotropy = adam->max_log_anisotropy;
     }

@@ -70,7 +70,7 @@ __global__ void __launch_bounds__(kBlock) k_emit(const float4* __restrict__ reco
     const uint32_t g = blockIdx.x * kBlock + t;
     uint32_t x0 = 0, y0 = 0, w = 1, count = 0, area = 0;
     float depth = 0.0f;
-    float4 ra = make_float4(0.0f, 0.0f, 0.0f, 0.0f), rb = ra;
+    CullEllipse ellipse{};
     unsigned long long index = 0;
     if (g < n) {
         const float4 r2 = records[(size_t)g * kRecord + 2];
@@ -82,9 +82,8 @@ __global__ void __launch_bounds__(kBlock) k_emit(const float4* __restrict__ reco
         area = (x1 - x0) * (y1 - y0);
         count = area;
         if (CULL && area) {
-            ra = records[(size_t)g * kRecord];
-            rb = records[(size_t)g * kRecord + 1];
-            count = culled_tile_count(ra, rb, x0, y0, x1, y1);
+            ellipse = cull_ellipse(records[(size_t)g * kRecord], records[(size_t)g * kRecord + 1]);
+            count = culled_tile_count(ellipse, x0, y0, x1, y1);
         }
         depth = r2.y;
         index = block_offsets[blockIdx.x] + offsets[g];
@@ -126,13 +125,18 @@ __global__ void __launch_bounds__(kBlock) k_emit(const float4* __restrict__ reco
         unsigned long long slot;
         bool emit;
         if constexpr (CULL) {
-            const float4 oa = make_float4(__shfl_sync(0xffffffffu, ra.x, owner), __shfl_sync(0xffffffffu, ra.y, owner),
-                                          __shfl_sync(0xffffffffu, ra.z, owner), __shfl_sync(0xffffffffu, ra.w, owner));
-            const float4 ob = make_float4(__shfl_sync(0xffffffffu, rb.x, owner), __shfl_sync(0xffffffffu, rb.y, owner),
-                                          0.0f, 0.0f);
+            CullEllipse oe;
+            oe.mx = __shfl_sync(0xffffffffu, ellipse.mx, owner);
+            oe.my = __shfl_sync(0xffffffffu, ellipse.my, owner);
+            oe.b = __shfl_sync(0xffffffffu, ellipse.b, owner);
+            oe.inv_a = __shfl_sync(0xffffffffu, ellipse.inv_a, owner);
+            oe.qa = __shfl_sync(0xffffffffu, ellipse.qa, owner);
+            oe.det = __shfl_sync(0xffffffffu, ellipse.det, owner);
+            oe.ey = __shfl_sync(0xffffffffu, ellipse.ey, owner);
+            oe.stationary = __shfl_sync(0xffffffffu, ellipse.stationary, owner);
             bool keep = false;
             if (e < total) {
-                const uint2 span = tile_row_span(oa, ob, oy0 + row, ox0, ox0 + ow);
+                const uint2 span = tile_row_span(oe, oy0 + row, ox0, ox0 + ow);
                 keep = column >= span.x && column < span.y;
             }
             const uint32_t ballot = __ballot_sync(0xffffffffu, keep);

@@ -9,54 +9,112 @@
 // the tile's rectangle of pixel centres. Per tile row the ellipse's x-extent over the row's
 // band is exact: its right end is the concave x_max(y) = (-b y + sqrt(a q - det y^2)) / a at
 // its stationary point y = -b sqrt(q / (det c)) clamped to the band, the left end likewise.
+// The hardware's approximate sqrt, reciprocal and log2 (relative errors near 2^-22) are far
+// inside that padding.
 //
-// The projection counts the tiles (for the tile offsets) and the emission enumerates them
-// with this same function; every operation has an explicit rounding, so both translation units
-// (one built with -fmad=false) get the same spans.
+// The projection counts the tiles (for the tile offsets) and the emission enumerates them with
+// these same functions; every operation is an explicit instruction (rounded multiplies and
+// adds, PTX approximations), so both translation units, one of them built with -fmad=false,
+// get the same spans.
 #pragma once
 
 #include "common.cuh"
 
 namespace splat {
+namespace cull {
 
-// The columns [first, end) of tile row `row` that the Gaussian of record (a, b) reaches,
-// within its rectangle's columns [x0, x1). mean = (a.x, a.y), conic = (a.z, a.w, b.x),
-// opacity = b.y.
-__device__ __forceinline__ uint2 tile_row_span(float4 a, float4 b, uint32_t row, uint32_t x0, uint32_t x1) {
+__device__ __forceinline__ float sqrt_approx(float x) {
+    float r;
+    asm("sqrt.approx.f32 %0, %1;" : "=f"(r) : "f"(x));
+    return r;
+}
+__device__ __forceinline__ float rcp_approx(float x) {
+    float r;
+    asm("rcp.approx.f32 %0, %1;" : "=f"(r) : "f"(x));
+    return r;
+}
+__device__ __forceinline__ float lg2_approx(float x) {
+    float r;
+    asm("lg2.approx.f32 %0, %1;" : "=f"(r) : "f"(x));
+    return r;
+}
+
+}  // namespace cull
+
+// A Gaussian's culling ellipse, relative to its mean: a x^2 + 2 b x y + c y^2 <= q.
+struct CullEllipse {
+    float mx, my;        // mean
+    float b, inv_a;      // conic b, 1 / a
+    float qa, det;       // a q, a c - b^2 (half width at height y: sqrt(a q - det y^2) / a)
+    float ey;            // vertical half extent; < 0: reaches no pixel; inf: keep every tile
+    float stationary;    // b sqrt(q / (det c)): x_max peaks at -stationary, x_min bottoms at +stationary
+};
+
+// The ellipse of record (a, b): mean = (a.x, a.y), conic = (a.z, a.w, b.x), opacity = b.y.
+__device__ __forceinline__ CullEllipse cull_ellipse(float4 a, float4 b) {
+    CullEllipse e;
+    e.mx = a.x;
+    e.my = a.y;
+    e.b = a.w;
+    e.inv_a = 0.0f;
+    e.qa = 0.0f;
+    e.det = 0.0f;
+    e.stationary = 0.0f;
     const float level = __fmul_rn(b.y, 255.0f);
-    if (!(level > 1.0f)) return make_uint2(x0, x0);  // alpha below 1/255 everywhere
+    if (!(level > 1.0f)) {  // alpha below 1/255 everywhere
+        e.ey = -1.0f;
+        return e;
+    }
     const float ca = a.z, cb = a.w, cc = b.x;
     const float det = __fsub_rn(__fmul_rn(ca, cc), __fmul_rn(cb, cb));
-    if (!(det > 0.0f) || !(ca > 0.0f) || !(cc > 0.0f)) return make_uint2(x0, x1);  // degenerate: keep all
-    const float q = __fadd_rn(__fmul_rn(2.02f, __logf(level)), 0.02f);
-    // The ellipse's vertical half extent, and the row's band of pixel centres (padded).
-    const float ey = __fsqrt_rn(__fdiv_rn(__fmul_rn(q, ca), det));
-    const float lo = __fsub_rn(__fsub_rn((float)(row * SP_TILE), a.y), 0.05f);
+    if (!(det > 0.0f) || !(ca > 0.0f) || !(cc > 0.0f)) {  // degenerate conic: never culled
+        e.ey = INFINITY;
+        return e;
+    }
+    // q = 2.02 ln(level) + 0.02 = 2.02 ln(2) log2(level) + 0.02.
+    const float q = __fadd_rn(__fmul_rn(1.40015730f, cull::lg2_approx(level)), 0.02f);
+    const float inv_det = cull::rcp_approx(det);
+    e.inv_a = cull::rcp_approx(ca);
+    e.qa = __fmul_rn(q, ca);
+    e.det = det;
+    e.ey = cull::sqrt_approx(__fmul_rn(e.qa, inv_det));
+    e.stationary = __fmul_rn(cb, cull::sqrt_approx(__fmul_rn(__fmul_rn(q, inv_det), cull::rcp_approx(cc))));
+    return e;
+}
+
+// The columns [first, end) of tile row `row` the ellipse reaches, within the rectangle's
+// columns [x0, x1).
+__device__ __forceinline__ uint2 tile_row_span(const CullEllipse& e, uint32_t row, uint32_t x0, uint32_t x1) {
+    if (!(e.ey >= 0.0f)) return make_uint2(x0, x0);
+    if (!(e.ey < INFINITY)) return make_uint2(x0, x1);
+    // The row's band of pixel centres, padded by 0.05 px, clamped to the ellipse's extent.
+    const float lo = __fsub_rn(__fsub_rn((float)(row * SP_TILE), e.my), 0.05f);
     const float hi = __fadd_rn(lo, (float)(SP_TILE - 1) + 0.1f);
-    const float y0 = fmaxf(lo, -ey), y1 = fminf(hi, ey);
+    const float y0 = fmaxf(lo, -e.ey), y1 = fminf(hi, e.ey);
     if (!(y0 <= y1)) return make_uint2(x0, x0);
-    const float stationary = __fmul_rn(cb, __fsqrt_rn(__fdiv_rn(q, __fmul_rn(det, cc))));
-    auto half_width = [&](float y) {
-        return __fsqrt_rn(fmaxf(0.0f, __fsub_rn(__fmul_rn(ca, q), __fmul_rn(det, __fmul_rn(y, y)))));
-    };
-    const float yr = fminf(fmaxf(-stationary, y0), y1);  // where x_max peaks
-    const float yl = fminf(fmaxf(stationary, y0), y1);   // where x_min bottoms
-    const float right = __fdiv_rn(__fadd_rn(-__fmul_rn(cb, yr), half_width(yr)), ca);
-    const float left = __fdiv_rn(__fsub_rn(-__fmul_rn(cb, yl), half_width(yl)), ca);
-    // Columns whose pixel centres [16 t, 16 t + 15] come within 0.05 px of [left, right].
-    const float first = ceilf(__fdiv_rn(__fsub_rn(__fadd_rn(left, a.x), (float)(SP_TILE - 1) + 0.05f), (float)SP_TILE));
-    const float last = floorf(__fdiv_rn(__fadd_rn(__fadd_rn(right, a.x), 0.05f), (float)SP_TILE));
-    const float c0 = fmaxf(first, (float)x0), c1 = fminf(last + 1.0f, (float)x1);
+    const float yr = fminf(fmaxf(-e.stationary, y0), y1);  // where x_max peaks
+    const float yl = fminf(fmaxf(e.stationary, y0), y1);   // where x_min bottoms
+    const float wr = cull::sqrt_approx(fmaxf(0.0f, __fsub_rn(e.qa, __fmul_rn(e.det, __fmul_rn(yr, yr)))));
+    const float wl = cull::sqrt_approx(fmaxf(0.0f, __fsub_rn(e.qa, __fmul_rn(e.det, __fmul_rn(yl, yl)))));
+    const float right = __fmul_rn(__fsub_rn(wr, __fmul_rn(e.b, yr)), e.inv_a);
+    const float left = __fmul_rn(__fadd_rn(wl, __fmul_rn(e.b, yl)), -e.inv_a);
+    // Columns whose pixel centres [16 t, 16 t + 15] come within 0.05 px of [left, right]
+    // (1 / 16 is exact).
+    constexpr float kInvTile = 1.0f / (float)SP_TILE;
+    const float first = ceilf(__fmul_rn(__fsub_rn(__fadd_rn(left, e.mx), (float)(SP_TILE - 1) + 0.05f), kInvTile));
+    const float last = floorf(__fmul_rn(__fadd_rn(__fadd_rn(right, e.mx), 0.05f), kInvTile));
+    const float c0 = fmaxf(first, (float)x0), c1 = fminf(__fadd_rn(last, 1.0f), (float)x1);
     if (!(c0 < c1)) return make_uint2(x0, x0);
     return make_uint2((uint32_t)c0, (uint32_t)c1);
 }
 
-// The number of tiles of the rectangle [x0, x1) x [y0, y1) the Gaussian reaches.
-__device__ __forceinline__ uint32_t culled_tile_count(float4 a, float4 b, uint32_t x0, uint32_t y0, uint32_t x1,
+// The number of tiles of the rectangle [x0, x1) x [y0, y1) the ellipse reaches.
+__device__ __forceinline__ uint32_t culled_tile_count(const CullEllipse& e, uint32_t x0, uint32_t y0, uint32_t x1,
                                                       uint32_t y1) {
+    if (!(e.ey >= 0.0f)) return 0u;
     uint32_t count = 0;
     for (uint32_t row = y0; row < y1; ++row) {
-        const uint2 span = tile_row_span(a, b, row, x0, x1);
+        const uint2 span = tile_row_span(e, row, x0, x1);
         count += span.y - span.x;
     }
     return count;

@@ -48,7 +48,8 @@ def run(ctx, cloud, camera, culling, weights):
     rast.encode_forward()
     meta = rast.read_intersections()
     _, gauss = rast.read_sorted_intersections()
-    out = dict(count=int(meta.count), gauss=gauss, ranges=rast.read_tile_ranges(), image=rast.read_image().rgbt,
+    out = dict(count=int(meta.count), gauss=gauss, ranges=rast.read_tile_ranges().reshape(-1, 2),
+               image=rast.read_image().rgbt,
                projected=rast.read_projected())
     rast.write_loss_gradient(weights)
     rast.encode_backward()
@@ -109,7 +110,7 @@ def test_culling_changes_no_result(ctx, name):
     # As close as two runs of the atomic backward with rectangles (plus a floor).
     spread = np.abs(again["gradients"].reshape(-1, stride) - g_full).max(axis=0)
     scale = np.abs(g_full).max(axis=0)
-    assert np.all(np.abs(g_culled - g_full).max(axis=0) <= 4.0 * spread + 1e-6 * scale + 1e-9), name
+    assert np.all(np.abs(g_culled - g_full).max(axis=0) <= 4.0 * spread + 1e-5 * scale + 1e-9), name
     assert np.array_equal(culled["stats"][:, 1:3], full["stats"][:, 1:3])
     assert np.allclose(culled["stats"][:, 0], full["stats"][:, 0], rtol=1e-5, atol=1e-9)
 
