@@ -443,13 +443,22 @@ def main() -> None:
         device_step(args.warmup + i)
     ctx.profile(False)
     profile = ctx.read_profile()
+    # The blend kernels' algorithmic work is the reference's per-pixel loops over its lists (the
+    # whole rectangles), counted on a rasterizer with the reference's lists even when the timed
+    # one culls tiles by the ellipse (whose lists hold the same contributing entries).
+    counter = rast if culling == sb.SP_TILES_RECTANGLE else sb.Rasterizer(
+        ctx, params, len(cloud), width, height, gt, views,
+        sb.default_options(sh_degree=deg, backward_mode=sb.SP_BWD_ATOMIC))
     fwd_pairs, bwd_pairs = 0, 0
     for v in range(views):
-        rast.set_camera(uniforms[v])
-        rast.encode_forward()
-        f, b = rast.count_blend_work()
+        counter.set_camera(uniforms[v])
+        counter.encode_forward()
+        f, b = counter.count_blend_work()
         fwd_pairs += f
         bwd_pairs += b
+    if counter is not rast:
+        counter.close()
+        del counter
     first_timed = args.warmup + views
 
     # ---- value: device-resident throughput.

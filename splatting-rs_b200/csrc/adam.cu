@@ -48,8 +48,6 @@ cudaError_t launch_adam(float* params, const float* gradients, float* first_mome
     for (int k = 0; k < stride; ++k) args.lr[k] = lr_by_slot_host[k];
     args.bias1 = bias1;
     args.bias2 = bias2;
-    args.inv_bias1 = 1.0f / bias1;
-    args.inv_bias2 = 1.0f / bias2;
     args.max_log_scale = max_log_scale;
     args.max_log_anisotropy = max_log_anisotropy;
     const unsigned grid = grid_for(count, kGaussiansPerBlock);

@@ -10,26 +10,10 @@ namespace splat {
 
 // One Adam step's constants: the learning rate of every parameter slot (optimizer.rs:248-256
 // folds the position-rate factor in), the bias corrections 1 - beta^t and the clamp bounds.
-// inv_bias1 / inv_bias2 are the correctly rounded reciprocals 1 / bias (host IEEE division).
 struct AdamStep {
     float lr[SP_PARAM_STRIDE(3)];
     float bias1, bias2, max_log_scale, max_log_anisotropy;
-    float inv_bias1, inv_bias2;
 };
-
-// a / b, correctly rounded, for a divisor fixed for the whole step: Markstein's correction
-// (IBM J. Res. Dev. 34(1), 1990) of q0 = RN(a * RN(1/b)) by one fused multiply-add,
-// q = RN(q0 + (a - b q0) RN(1/b)), the remainder a - b q0 exact in the FMA. Checked equal to
-// the IEEE division for every significand of a (at three exponents) and every Adam bias
-// correction 1 - beta^t of beta 0.9 and 0.999 (t to 40000); zeros, infinities, NaN and
-// magnitudes outside [2^-100, 2^100] take the IEEE division itself.
-__device__ __forceinline__ float div_by_step_constant(float a, float b, float inv_b) {
-    const float magnitude = fabsf(a);
-    if (!(magnitude >= 0x1p-100f && magnitude <= 0x1p100f)) return __fdiv_rn(a, b);
-    const float q0 = __fmul_rn(a, inv_b);
-    const float remainder = __fmaf_rn(-q0, b, a);
-    return __fmaf_rn(remainder, inv_b, q0);
-}
 
 // adam.wgsl:26-35 for one parameter: updates the moments, returns the parameter.
 __device__ __forceinline__ float adam_update(float p, float g, float& m, float& v, float lr, const AdamStep& step) {
@@ -37,8 +21,8 @@ __device__ __forceinline__ float adam_update(float p, float g, float& m, float& 
     const float vv = SP_ADAM_BETA2 * v + (1.0f - SP_ADAM_BETA2) * g * g;
     m = mm;
     v = vv;
-    const float m_hat = div_by_step_constant(mm, step.bias1, step.inv_bias1);
-    const float v_hat = div_by_step_constant(vv, step.bias2, step.inv_bias2);
+    const float m_hat = mm / step.bias1;
+    const float v_hat = vv / step.bias2;
     return p - lr * m_hat / (__fsqrt_rn(v_hat) + SP_ADAM_EPSILON);
 }
 

@@ -674,8 +674,6 @@ cudaError_t launch_project_backward(const float* params, uint64_t n, int sh_degr
         for (int k = 0; k < SP_PARAM_STRIDE(sh_degree); ++k) fused.step.lr[k] = adam->lr_by_slot[k];
         fused.step.bias1 = adam->bias1;
         fused.step.bias2 = adam->bias2;
-        fused.step.inv_bias1 = 1.0f / adam->bias1;
-        fused.step.inv_bias2 = 1.0f / adam->bias2;
         fused.step.max_log_scale = adam->max_log_scale;
         fused.step.max_log_anisotropy = adam->max_log_anisotropy;
     }
