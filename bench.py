@@ -568,9 +568,11 @@ def main() -> None:
             entry.update(bound="fp32", achieved=achieved, peak=fp32_peak, unit="T FP32 ops/s",
                          frac=achieved / fp32_peak, pairs_per_launch=bwd_pairs / views)
         elif name == "adam":
-            achieved = n_params * 28 / (kms / n * 1e-3) / 1e9
+            # The sharded exchange steps this rank's share of the Gaussians only.
+            stepped = n_params // world if world > 1 and train_step.exchange.mode == "sharded" else n_params
+            achieved = stepped * 28 / (kms / n * 1e-3) / 1e9
             entry.update(bound="hbm", achieved=achieved, peak=pk["hbm_gbs"], unit="GB/s", frac=achieved / pk["hbm_gbs"],
-                         bytes_per_launch=n_params * 28)
+                         bytes_per_launch=stepped * 28)
         elif name == "backward_adam":
             # Parameters and both moments read and written, the 9 blend sums read.
             b = n_params * 24 + len(cloud) * 36

@@ -45,10 +45,12 @@ __device__ __forceinline__ Key compose_key(uint32_t tile, uint32_t shift, uint32
 // offsets are an exclusive scan in Gaussian order), so its lanes write them together, key by
 // key, whatever the rectangles' sizes: balanced work and coalesced stores. The sort's digit
 // histograms are accumulated on the way: per Gaussian (weighted by its tile count) for the
-// passes whose digit holds depth bits only, per key for the others. With CULL the warp walks
-// its rectangles' tiles 32 at a time in the same order and keeps those tile_cull.cuh keeps
-// (a ballot compacts them into the slots), so the keys are the rectangle's, minus the culled
-// tiles, in the same order.
+// passes whose digit holds depth bits only, per key for the others.
+//
+// With CULL the warp walks its rectangles' tile rows 32 at a time: each lane takes one
+// (Gaussian, row) and the row's span of reached tiles (tile_cull.cuh, as the projection
+// counted them), then the warp writes the 32 rows' keys together; the keys are the
+// rectangle's, minus the culled tiles, in the same order.
 template <typename Key, bool CULL>
 __global__ void __launch_bounds__(kBlock) k_emit(const float4* __restrict__ records, uint32_t* __restrict__ offsets,
                                                  const unsigned long long* __restrict__ block_offsets, uint32_t n,
@@ -68,7 +70,7 @@ __global__ void __launch_bounds__(kBlock) k_emit(const float4* __restrict__ reco
     __syncthreads();
     const unsigned long long capacity = meta->capacity;
     const uint32_t g = blockIdx.x * kBlock + t;
-    uint32_t x0 = 0, y0 = 0, w = 1, count = 0, area = 0;
+    uint32_t x0 = 0, y0 = 0, w = 1, rows = 0, count = 0;
     float depth = 0.0f;
     CullEllipse ellipse{};
     unsigned long long index = 0;
@@ -79,25 +81,22 @@ __global__ void __launch_bounds__(kBlock) k_emit(const float4* __restrict__ reco
         y0 = lo >> 16;
         const uint32_t x1 = hi & 0xffffu, y1 = hi >> 16;
         w = max(x1 - x0, 1u);
-        area = (x1 - x0) * (y1 - y0);
-        count = area;
-        if (CULL && area) {
-            ellipse = cull_ellipse(records[(size_t)g * kRecord], records[(size_t)g * kRecord + 1]);
-            count = culled_tile_count(ellipse, x0, y0, x1, y1);
-        }
+        count = (x1 - x0) * (y1 - y0);
+        rows = count ? y1 - y0 : 0u;
+        if (CULL && count) ellipse = cull_ellipse(records[(size_t)g * kRecord], records[(size_t)g * kRecord + 1]);
         depth = r2.y;
         index = block_offsets[blockIdx.x] + offsets[g];
         offsets[g] = (uint32_t)index;
-        // Depth-only digits: the same for every key of the Gaussian.
+        // Depth-only digits: the same for every key of the Gaussian (with CULL, per row below).
         const unsigned long long kept = index >= capacity ? 0ull : min((unsigned long long)count, capacity - index);
-        if (kept) {
+        if (!CULL && kept) {
             const uint32_t depth_key = depth_part(key_mode, depth, base);
             for (int p = 0; p < passes && 8 * p + 8 <= (int)tile_shift; ++p)
                 atomicAdd(&hist[p][(depth_key >> (8 * p)) & 255u], (uint32_t)kept);
         }
     }
-    // Exclusive scan over the warp of what it walks: the keys, or with CULL the rectangles' tiles.
-    const uint32_t walk = CULL ? area : count;
+    // Exclusive scan over the warp of what it walks: the keys, or with CULL the rows.
+    const uint32_t walk = CULL ? rows : count;
     uint32_t inclusive = walk;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
@@ -108,23 +107,30 @@ __global__ void __launch_bounds__(kBlock) k_emit(const float4* __restrict__ reco
     const uint32_t total = __shfl_sync(0xffffffffu, inclusive, 31);
     const unsigned long long start = __shfl_sync(0xffffffffu, index, 0);
     const int first_tile_pass = (int)tile_shift / 8;
-    uint32_t written = 0;  // CULL: keys the warp has written so far
-    for (uint32_t round = 0; round * 32 < total; ++round) {
-        const uint32_t e = round * 32 + lane;
-        // The lane whose walk holds e: the last with exclusive <= e.
-        uint32_t owner = 0;
+    // The last lane whose (nondecreasing) exclusive prefix `prefix` is at most e.
+    auto holder = [&](uint32_t prefix, uint32_t e) {
+        uint32_t h = 0;
 #pragma unroll
         for (uint32_t step = 16; step > 0; step >>= 1)
-            if (__shfl_sync(0xffffffffu, exclusive, owner + step) <= e) owner += step;
-        const uint32_t local = e - __shfl_sync(0xffffffffu, exclusive, owner);
-        const uint32_t ox0 = __shfl_sync(0xffffffffu, x0, owner), oy0 = __shfl_sync(0xffffffffu, y0, owner);
-        const uint32_t ow = __shfl_sync(0xffffffffu, w, owner);
-        const float odepth = __shfl_sync(0xffffffffu, depth, owner);
-        const uint32_t og = __shfl_sync(0xffffffffu, g, owner);
-        const uint32_t row = local / ow, column = ox0 + (local - row * ow);
-        unsigned long long slot;
-        bool emit;
-        if constexpr (CULL) {
+            if (__shfl_sync(0xffffffffu, prefix, h + step) <= e) h += step;
+        return h;
+    };
+    auto write_key = [&](unsigned long long slot, uint32_t tile, float key_depth, uint32_t gaussian) {
+        const Key key = compose_key<Key>(tile, tile_shift, depth_part(key_mode, key_depth, base));
+        keys[slot] = key;
+        values[slot] = gaussian;
+        for (int p = first_tile_pass; p < passes; ++p) atomicAdd(&hist[p][(uint32_t)(key >> (8 * p)) & 255u], 1u);
+    };
+    if constexpr (CULL) {
+        unsigned long long written = 0;  // keys of the warp's earlier rounds
+        for (uint32_t round = 0; round * 32 < total; ++round) {
+            // This lane's (Gaussian, row) of the round, and the row's span of tiles.
+            const uint32_t p = round * 32 + lane;
+            const uint32_t owner = holder(exclusive, p);
+            const uint32_t row = __shfl_sync(0xffffffffu, y0, owner) + (p - __shfl_sync(0xffffffffu, exclusive, owner));
+            const uint32_t ox0 = __shfl_sync(0xffffffffu, x0, owner), ow = __shfl_sync(0xffffffffu, w, owner);
+            const float odepth = __shfl_sync(0xffffffffu, depth, owner);
+            const uint32_t og = __shfl_sync(0xffffffffu, g, owner);
             CullEllipse oe;
             oe.mx = __shfl_sync(0xffffffffu, ellipse.mx, owner);
             oe.my = __shfl_sync(0xffffffffu, ellipse.my, owner);
@@ -134,25 +140,53 @@ __global__ void __launch_bounds__(kBlock) k_emit(const float4* __restrict__ reco
             oe.det = __shfl_sync(0xffffffffu, ellipse.det, owner);
             oe.ey = __shfl_sync(0xffffffffu, ellipse.ey, owner);
             oe.stationary = __shfl_sync(0xffffffffu, ellipse.stationary, owner);
-            bool keep = false;
-            if (e < total) {
-                const uint2 span = tile_row_span(oe, oy0 + row, ox0, ox0 + ow);
-                keep = column >= span.x && column < span.y;
+            uint2 span = make_uint2(0u, 0u);
+            if (p < total) span = tile_row_span(oe, row, ox0, ox0 + ow);
+            const uint32_t length = span.y - span.x;
+            uint32_t row_inclusive = length;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const uint32_t up = __shfl_up_sync(0xffffffffu, row_inclusive, o);
+                if (lane >= (uint32_t)o) row_inclusive += up;
             }
-            const uint32_t ballot = __ballot_sync(0xffffffffu, keep);
-            slot = start + written + __popc(ballot & ((1u << lane) - 1u));
-            written += __popc(ballot);
-            emit = keep;
-        } else {
-            slot = start + e;
-            emit = e < total;
+            const uint32_t row_exclusive = row_inclusive - length;
+            const uint32_t round_keys = __shfl_sync(0xffffffffu, row_inclusive, 31);
+            // Depth-only digits, weighted by the row's keys that fit.
+            const unsigned long long row_slot = start + written + row_exclusive;
+            const unsigned long long kept =
+                row_slot >= capacity ? 0ull : min((unsigned long long)length, capacity - row_slot);
+            if (kept) {
+                const uint32_t depth_key = depth_part(key_mode, odepth, base);
+                for (int q = 0; q < passes && 8 * q + 8 <= (int)tile_shift; ++q)
+                    atomicAdd(&hist[q][(depth_key >> (8 * q)) & 255u], (uint32_t)kept);
+            }
+            // The round's keys, 32 at a time.
+            for (uint32_t e0 = 0; e0 < round_keys; e0 += 32) {
+                const uint32_t e = e0 + lane;
+                const uint32_t src = holder(row_exclusive, e);
+                const uint32_t column = __shfl_sync(0xffffffffu, span.x, src) +
+                                        (e - __shfl_sync(0xffffffffu, row_exclusive, src));
+                const uint32_t key_row = __shfl_sync(0xffffffffu, row, src);
+                const float key_depth = __shfl_sync(0xffffffffu, odepth, src);
+                const uint32_t key_gaussian = __shfl_sync(0xffffffffu, og, src);
+                const unsigned long long slot = start + written + e;
+                if (e < round_keys && slot < capacity) write_key(slot, key_row * tiles_x + column, key_depth, key_gaussian);
+            }
+            written += round_keys;
         }
-        if (emit && slot < capacity) {
-            const Key key = compose_key<Key>((oy0 + row) * tiles_x + column, tile_shift, depth_part(key_mode, odepth, base));
-            keys[slot] = key;
-            values[slot] = og;
-            for (int p = first_tile_pass; p < passes; ++p)
-                atomicAdd(&hist[p][(uint32_t)(key >> (8 * p)) & 255u], 1u);
+    } else {
+        for (uint32_t round = 0; round * 32 < total; ++round) {
+            const uint32_t e = round * 32 + lane;
+            const uint32_t owner = holder(exclusive, e);
+            const uint32_t local = e - __shfl_sync(0xffffffffu, exclusive, owner);
+            const uint32_t ox0 = __shfl_sync(0xffffffffu, x0, owner), oy0 = __shfl_sync(0xffffffffu, y0, owner);
+            const uint32_t ow = __shfl_sync(0xffffffffu, w, owner);
+            const float odepth = __shfl_sync(0xffffffffu, depth, owner);
+            const uint32_t og = __shfl_sync(0xffffffffu, g, owner);
+            const uint32_t row = local / ow;
+            const unsigned long long slot = start + e;
+            if (e < total && slot < capacity)
+                write_key(slot, (oy0 + row) * tiles_x + ox0 + (local - row * ow), odepth, og);
         }
     }
     __syncthreads();
