@@ -112,7 +112,10 @@ def test_culling_changes_no_result(ctx, name):
     scale = np.abs(g_full).max(axis=0)
     assert np.all(np.abs(g_culled - g_full).max(axis=0) <= 4.0 * spread + 1e-5 * scale + 1e-9), name
     assert np.array_equal(culled["stats"][:, 1:3], full["stats"][:, 1:3])
-    assert np.allclose(culled["stats"][:, 0], full["stats"][:, 0], rtol=1e-5, atol=1e-9)
+    # The mean-gradient sums are norms of atomically summed gradients: the same bar.
+    stat_spread = np.abs(again["stats"][:, 0] - full["stats"][:, 0]).max()
+    stat_error = np.abs(culled["stats"][:, 0] - full["stats"][:, 0]).max()
+    assert stat_error <= 4.0 * stat_spread + 1e-5 * np.abs(full["stats"][:, 0]).max() + 1e-9, name
 
 
 def test_culling_rejects_the_deterministic_backward(ctx):
