@@ -64,9 +64,9 @@ constexpr uint32_t kMinDepthKey = 0x3C23Du;
 constexpr int kMaxDepthRangeBits = 19;
 
 constexpr int kSortThreads = 256;
-constexpr int kSortItems = 16;
+constexpr int kSortItems = 24;  // measured best of 8-40 keys per thread and 1-4 blocks per SM
 constexpr int kSortBlocksPerSM = 2;
-constexpr int kSortPartition = kSortThreads * kSortItems;  // 4096 keys per partition
+constexpr int kSortPartition = kSortThreads * kSortItems;  // 6144 keys per partition
 constexpr int kSortMaxPasses = 8;
 constexpr int kSortRadix = 256;
 
