@@ -9,8 +9,9 @@ SSIM/L1 loss, backward, Adam + scale clamp) on the benchmark's config 2.
 One JSON line on rank 0. `value` is device-timed throughput with every input resident in
 HBM; `e2e` is the same step through the public API as the reference's caller runs it
 (camera from the host, pose refinement on: the 56-byte camera gradient and the loss read
-back every step). At N > 1 each rank trains its own views (weak scaling) and the
-parameter gradients are summed by an NCCL all-reduce before every Adam step.
+back every step). At N > 1 each rank trains its own views (weak scaling); by default one
+kernel per rank sums its share of every rank's gradients over NVLink peer memory, steps Adam
+on it and stores the parameters into every rank's buffer (splat_b200/sharding.py, "peer").
 """
 
 from __future__ import annotations
@@ -293,7 +294,15 @@ def run_reference(args) -> None:
     print(json.dumps(line), flush=True)
 
 
-def config_dict(scene, world: int) -> dict:
+EXCHANGES = {
+    "peer": "gradients of each rank's share summed over NVLink peer memory, Adam on the share and the "
+            "parameters stored into every rank's buffer, in one kernel per rank",
+    "sharded": "gradients reduce-scattered, Adam sharded by Gaussians, parameters all-gathered (NCCL)",
+    "allreduce": "gradients all-reduced (NCCL), the Adam step on every rank",
+}
+
+
+def config_dict(scene, world: int, exchange: str = "peer") -> dict:
     cam = scene.cameras[0]
     return {
         "workload": f"config 2: {len(scene.cloud)} Gaussians SH{scene.cloud.sh_degree}, {cam.width}x{cam.height}, "
@@ -304,8 +313,7 @@ def config_dict(scene, world: int) -> dict:
         "height": cam.height,
         "views": len(scene.cameras),
         "views_per_step": world,
-        "parallelism": (f"view-sharded dp{world}: gradients reduce-scattered, Adam sharded by Gaussians, "
-                        f"parameters all-gathered (NCCL)" if world > 1 else "single GPU"),
+        "parallelism": (f"view-sharded dp{world}: {EXCHANGES[exchange]}" if world > 1 else "single GPU"),
         "l2": "working set (params, gradients, Adam moments: >0.4 GB) larger than the 126 MB L2",
     }
 
@@ -380,7 +388,7 @@ def main() -> None:
 
     import splat_b200 as sb
     from splat_b200 import scenes, sharding
-    from splat_b200.sharding import GradientExchange, ViewShardedStep
+    from splat_b200.sharding import ViewShardedStep
 
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -477,7 +485,7 @@ def main() -> None:
     # ---- e2e: the reference caller's step through the public API, poses refined.
     params.copy_(initial)
     adam_e2e = sb.Adam(ctx, params, rast, len(cloud), sb.LEARNING_RATES_3DGS, extent, sh_degree=deg)
-    exchange_e2e = GradientExchange(adam_e2e, params, rast.param_gradients(), len(cloud), rast.stride, rank, world)
+    exchange_e2e = sharding.make_exchange(adam_e2e, params, rast, rank, world)
     poses = sb.PoseRefinement(cams, sb.LEARNING_RATES_3DGS, float(extent))
     e2e_steps = args.e2e_steps or args.steps
 
@@ -573,6 +581,15 @@ def main() -> None:
             achieved = stepped * 28 / (kms / n * 1e-3) / 1e9
             entry.update(bound="hbm", achieved=achieved, peak=pk["hbm_gbs"], unit="GB/s", frac=achieved / pk["hbm_gbs"],
                          bytes_per_launch=stepped * 28)
+        elif name == "peer_adam":
+            # Per launch, this rank's share: every peer's gradients read and the parameters stored
+            # into every peer over NVLink; against the measured 770 GB/s per direction per GPU.
+            share_bytes = n_params // world * 4
+            nvlink = (world - 1) * share_bytes
+            achieved = nvlink / (kms / n * 1e-3) / 1e9
+            entry.update(bound="nvlink", achieved=achieved, peak=770.0, unit="GB/s per direction",
+                         frac=achieved / 770.0, nvlink_bytes_per_direction=nvlink,
+                         hbm_bytes=share_bytes * (1 + 6))
         elif name == "backward_adam":
             # Parameters and both moments read and written, the 9 blend sums read.
             b = n_params * 24 + len(cloud) * 36
@@ -639,7 +656,7 @@ def main() -> None:
             "vs_baseline": None,
             "dtype": "f32",
             "data": "synthetic",
-            "config": config_dict(scene, world),
+            "config": config_dict(scene, world, train_step.exchange.mode),
             "tile_culling": (f"{args.tiles}: " + (
                 "keys only for the bounding rectangle's tiles the Gaussian's alpha can reach (the same images, "
                 "losses and gradients as the reference's whole rectangles)"
@@ -665,6 +682,11 @@ def main() -> None:
         }
         print(json.dumps(line), flush=True)
     if world > 1:
+        # Every rank's last exchange ended with its closing all-reduce: no peer access remains.
+        torch.cuda.synchronize()
+        dist.barrier()
+        train_step.exchange.close()
+        exchange_e2e.close()
         dist.barrier()
         dist.destroy_process_group()
 

@@ -387,7 +387,8 @@ enum {
     SP_K_TILE_ORDER = 11, /* the blend kernels' tile schedule (no counterpart in the reference) */
     SP_K_BACKWARD_ADAM = 12, /* projection backward with the Adam step fused (sp_backward_adam) */
     SP_K_DENSIFY = 13,       /* the densification's kernels (sp_densify_plan, sp_densify_apply) */
-    SP_K_COUNT = 14
+    SP_K_PEER_ADAM = 14,     /* the peer-memory exchange with the Adam step (sp_peer_exchange_step) */
+    SP_K_COUNT = 15
 };
 /* Starts (1) or stops (0) recording events around every kernel launch of the context. */
 sp_status sp_profile_enable(sp_context* ctx, int enable);
@@ -423,6 +424,39 @@ sp_status sp_adam_read_moments(sp_adam* adam, float* host_first, float* host_sec
  * multi-GPU gather of the ranks' moment shards. */
 float* sp_adam_first_moment_device(sp_adam* adam);
 float* sp_adam_second_moment_device(sp_adam* adam);
+
+/* ------------------------------------------------- multi-GPU exchange over peer memory */
+
+/* The view-sharded step of several GPUs (one process each, one node) without a library
+ * collective: each rank sums the parameter gradients of its share of the Gaussians over
+ * every rank's gradient buffer (peer loads over NVLink, in rank order: the sum one GPU
+ * accumulating the ranks' views in order would form), takes the Adam step and the scale clamp
+ * on that share, and stores the updated parameters into its own and every peer's parameter
+ * buffer (peer stores), in one kernel. Shares are [rank n / world, (rank + 1) n / world), n a
+ * multiple of world; each rank's moments are current on its share only.
+ *
+ * Set-up: every rank calls sp_peer_export and gives all ranks' handles (in rank order) to
+ * sp_peer_exchange_create, which maps the peers' buffers (CUDA IPC). Each step: every rank
+ * must have finished its backward before any rank calls sp_peer_exchange_step, and every
+ * rank's call must have finished before any rank's next forward (the caller orders both,
+ * e.g. with a one-element collective on the context's stream before and after). */
+typedef struct sp_peer_handle {
+    uint8_t params[64];         /* cudaIpcMemHandle_t of the allocation holding the parameters */
+    uint8_t gradients[64];      /* ... and of the one holding the parameter gradients */
+    uint64_t params_offset;     /* byte offsets of the two buffers in those allocations */
+    uint64_t gradients_offset;
+    uint64_t gaussian_count;
+    uint32_t stride;
+    int32_t device;
+} sp_peer_handle;
+sp_status sp_peer_export(const sp_adam* adam, sp_peer_handle* out);
+typedef struct sp_peer_exchange sp_peer_exchange;
+/* At most 8 ranks; every rank's optimiser over the same count and stride. */
+sp_status sp_peer_exchange_create(sp_adam* adam, uint32_t rank, uint32_t world, const sp_peer_handle* handles,
+                                  sp_peer_exchange** out);
+/* Enqueues the exchange and the Adam step (position_rate_factor as sp_adam_step). */
+sp_status sp_peer_exchange_step(sp_peer_exchange* exchange, float position_rate_factor);
+void sp_peer_exchange_destroy(sp_peer_exchange* exchange);
 /* position_rate_factor (optimizer.rs:59-62): 0.01^(step / max(steps - 1, 1)). Returns a
  * negative value where the reference asserts (steps == 0 or step >= steps). */
 float sp_position_rate_factor(uint64_t step, uint64_t steps);

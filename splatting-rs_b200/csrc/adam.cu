@@ -38,7 +38,85 @@ __global__ void __launch_bounds__(kBlock) k_adam(float* __restrict__ params, con
     adam_block<S>(params, m1, m2, g0, here, s_p, s_lr, step);
 }
 
+// The peer-memory exchange step: the gradients of the block's Gaussians summed over the
+// ranks in rank order (peer loads, float4 when aligned), Adam + clamp in shared memory as
+// k_adam (adam_block writes this rank's parameters), then the updated parameters stored into
+// every other rank's buffer (peer stores) and fenced at system scope.
+template <int S>
+__global__ void __launch_bounds__(kBlock) k_adam_peer(const PeerBuffers peers, float* __restrict__ m1,
+                                                      float* __restrict__ m2, uint64_t first, uint64_t end,
+                                                      const AdamStep step) {
+    __shared__ float4 s_p4[kGaussiansPerBlock * S / 4 + 1];
+    __shared__ float s_lr[S];
+    float* s_p = reinterpret_cast<float*>(s_p4);
+    const uint32_t t = threadIdx.x;
+    if (t < (uint32_t)S) s_lr[t] = step.lr[t];
+    const uint64_t g0 = first + (uint64_t)blockIdx.x * kGaussiansPerBlock;
+    const uint32_t here = (uint32_t)min((uint64_t)kGaussiansPerBlock, end - g0);
+    const uint64_t f0 = g0 * S;
+    const uint32_t floats = here * S;
+    bool aligned = (f0 & 3u) == 0;
+    for (uint32_t r = 0; r < peers.world; ++r)
+        aligned = aligned && ((reinterpret_cast<uintptr_t>(peers.gradients[r]) |
+                               reinterpret_cast<uintptr_t>(peers.params[r])) & 15u) == 0;
+    const uint32_t vec = aligned ? floats / 4 : 0;
+    for (uint32_t i = t; i < vec; i += kBlock) {
+        float4 sum = reinterpret_cast<const float4*>(peers.gradients[0] + f0)[i];
+        for (uint32_t r = 1; r < peers.world; ++r) {
+            const float4 g = reinterpret_cast<const float4*>(peers.gradients[r] + f0)[i];
+            sum.x = sum.x + g.x;
+            sum.y = sum.y + g.y;
+            sum.z = sum.z + g.z;
+            sum.w = sum.w + g.w;
+        }
+        s_p4[i] = sum;
+    }
+    for (uint32_t i = vec * 4 + t; i < floats; i += kBlock) {
+        float sum = peers.gradients[0][f0 + i];
+        for (uint32_t r = 1; r < peers.world; ++r) sum = sum + peers.gradients[r][f0 + i];
+        s_p[i] = sum;
+    }
+    __syncthreads();
+    float* own = peers.params[peers.rank];
+    adam_block<S>(own, m1, m2, g0, here, s_p, s_lr, step);
+    // adam_block leaves the updated, clamped parameters in s_p.
+    for (uint32_t r = 0; r < peers.world; ++r) {
+        if (r == peers.rank) continue;
+        float* dst = peers.params[r] + f0;
+        for (uint32_t i = t; i < vec; i += kBlock) reinterpret_cast<float4*>(dst)[i] = s_p4[i];
+        for (uint32_t i = vec * 4 + t; i < floats; i += kBlock) dst[i] = s_p[i];
+    }
+    __threadfence_system();
+}
+
 }  // namespace
+
+cudaError_t launch_adam_peer(const PeerBuffers& peers, float* first_moment, float* second_moment, uint64_t first,
+                             uint64_t count, int stride, const float* lr_by_slot_host, float bias1, float bias2,
+                             float max_log_scale, float max_log_anisotropy, cudaStream_t stream) {
+    if (count == 0) return cudaSuccess;
+    if (peers.world == 0 || peers.world > (uint32_t)kMaxPeers || peers.rank >= peers.world) return cudaErrorInvalidValue;
+    AdamStep args{};
+    for (int k = 0; k < stride; ++k) args.lr[k] = lr_by_slot_host[k];
+    args.bias1 = bias1;
+    args.bias2 = bias2;
+    args.max_log_scale = max_log_scale;
+    args.max_log_anisotropy = max_log_anisotropy;
+    const unsigned grid = grid_for(count, kGaussiansPerBlock);
+    const uint64_t end = first + count;
+#define SP_ADAM_PEER(D)                                                                                         \
+    k_adam_peer<SP_PARAM_STRIDE(D)><<<grid, kBlock, 0, stream>>>(peers, first_moment, second_moment, first, end, \
+                                                                 args)
+    switch (stride) {
+        case SP_PARAM_STRIDE(0): SP_ADAM_PEER(0); break;
+        case SP_PARAM_STRIDE(1): SP_ADAM_PEER(1); break;
+        case SP_PARAM_STRIDE(2): SP_ADAM_PEER(2); break;
+        case SP_PARAM_STRIDE(3): SP_ADAM_PEER(3); break;
+        default: return cudaErrorInvalidValue;
+    }
+#undef SP_ADAM_PEER
+    return cudaGetLastError();
+}
 
 cudaError_t launch_adam(float* params, const float* gradients, float* first_moment, float* second_moment,
                         uint64_t first, uint64_t count, int stride, const float* lr_by_slot_host, float bias1,

@@ -9,6 +9,8 @@
 #include <string>
 #include <vector>
 
+#include <cuda.h>
+
 #include "densify.h"
 #include "kernels.h"
 #include "pose_math.h"
@@ -1197,6 +1199,127 @@ sp_status sp_adam_read_moments(sp_adam* a, float* host_first, float* host_second
     const size_t bytes = a->n * a->stride * sizeof(float);
     SP_CHECK(read_device(a->ctx, host_first, a->first_moment, bytes));
     return read_device(a->ctx, host_second, a->second_moment, bytes);
+}
+
+// ------------------------------------------------- multi-GPU exchange over peer memory
+
+}  // extern "C"
+
+namespace {
+
+// The allocation holding device pointer `p` (its base and p's offset in it): CUDA IPC shares
+// whole allocations. cuMemGetAddressRange through the runtime's driver entry point, so the
+// library needs no link to the driver library.
+sp_status allocation_of(sp_context* ctx, const void* p, void** base, uint64_t* offset) {
+    using AddressRange = CUresult (*)(CUdeviceptr*, size_t*, CUdeviceptr);
+    static AddressRange address_range = nullptr;
+    if (!address_range) {
+        void* fn = nullptr;
+        cudaDriverEntryPointQueryResult found;
+        const cudaError_t err = cudaGetDriverEntryPoint("cuMemGetAddressRange", &fn, cudaEnableDefault, &found);
+        if (err != cudaSuccess || found != cudaDriverEntryPointSuccess || !fn)
+            return fail(ctx, SP_ERR_CUDA, "cuMemGetAddressRange is not available");
+        address_range = reinterpret_cast<AddressRange>(fn);
+    }
+    CUdeviceptr b = 0;
+    size_t size = 0;
+    if (address_range(&b, &size, reinterpret_cast<CUdeviceptr>(p)) != CUDA_SUCCESS)
+        return fail(ctx, SP_ERR_CUDA, "the buffer is not a device allocation");
+    *base = reinterpret_cast<void*>(b);
+    *offset = (uint64_t)(reinterpret_cast<uintptr_t>(p) - (uintptr_t)b);
+    return SP_OK;
+}
+
+}  // namespace
+
+struct sp_peer_exchange {
+    sp_adam* adam = nullptr;
+    PeerBuffers peers{};
+    std::vector<void*> opened;  // mapped peer allocations, closed on destroy
+    uint64_t first = 0, count = 0;
+};
+
+extern "C" {
+
+sp_status sp_peer_export(const sp_adam* a, sp_peer_handle* out) {
+    if (!a || !out) return SP_ERR_INVALID;
+    std::memset(out, 0, sizeof(*out));
+    SP_CHECK(select_device(a->ctx));
+    void* base = nullptr;
+    cudaIpcMemHandle_t h;
+    SP_CHECK(allocation_of(a->ctx, a->params, &base, &out->params_offset));
+    SP_CUDA(a->ctx, cudaIpcGetMemHandle(&h, base));
+    std::memcpy(out->params, &h, sizeof(h));
+    SP_CHECK(allocation_of(a->ctx, a->gradients, &base, &out->gradients_offset));
+    SP_CUDA(a->ctx, cudaIpcGetMemHandle(&h, base));
+    std::memcpy(out->gradients, &h, sizeof(h));
+    out->gaussian_count = a->n;
+    out->stride = a->stride;
+    out->device = a->ctx->device;
+    return SP_OK;
+}
+
+void sp_peer_exchange_destroy(sp_peer_exchange* ex) {
+    if (!ex) return;
+    cudaSetDevice(ex->adam->ctx->device);
+    cudaStreamSynchronize(ex->adam->ctx->stream);
+    for (void* p : ex->opened) cudaIpcCloseMemHandle(p);
+    delete ex;
+}
+
+sp_status sp_peer_exchange_create(sp_adam* a, uint32_t rank, uint32_t world, const sp_peer_handle* handles,
+                                  sp_peer_exchange** out) {
+    if (!a || !handles || !out) return SP_ERR_INVALID;
+    *out = nullptr;
+    sp_context* ctx = a->ctx;
+    SP_REQUIRE(ctx, world >= 1 && world <= (uint32_t)kMaxPeers && rank < world, SP_ERR_INVALID,
+               "rank and world (at most 8 ranks)");
+    SP_REQUIRE(ctx, a->n % world == 0, SP_ERR_INVALID, "the Gaussians do not split evenly over the ranks");
+    for (uint32_t r = 0; r < world; ++r)
+        SP_REQUIRE(ctx, handles[r].gaussian_count == a->n && handles[r].stride == a->stride, SP_ERR_INVALID,
+                   "every rank's optimiser must hold the same Gaussians");
+    SP_CHECK(select_device(ctx));
+    sp_peer_exchange* ex = new sp_peer_exchange();
+    ex->adam = a;
+    ex->peers.world = world;
+    ex->peers.rank = rank;
+    ex->count = a->n / world;
+    ex->first = (uint64_t)rank * ex->count;
+    for (uint32_t r = 0; r < world; ++r) {
+        if (r == rank) {
+            ex->peers.params[r] = a->params;
+            ex->peers.gradients[r] = a->gradients;
+            continue;
+        }
+        for (int which = 0; which < 2; ++which) {
+            cudaIpcMemHandle_t h;
+            std::memcpy(&h, which == 0 ? handles[r].params : handles[r].gradients, sizeof(h));
+            void* base = nullptr;
+            const cudaError_t err = cudaIpcOpenMemHandle(&base, h, cudaIpcMemLazyEnablePeerAccess);
+            if (err != cudaSuccess) {
+                sp_peer_exchange_destroy(ex);
+                return cuda_fail(ctx, err, "cudaIpcOpenMemHandle (a peer's buffer)");
+            }
+            ex->opened.push_back(base);
+            char* p = static_cast<char*>(base) + (which == 0 ? handles[r].params_offset : handles[r].gradients_offset);
+            if (which == 0) ex->peers.params[r] = reinterpret_cast<float*>(p);
+            else ex->peers.gradients[r] = reinterpret_cast<const float*>(p);
+        }
+    }
+    *out = ex;
+    return SP_OK;
+}
+
+sp_status sp_peer_exchange_step(sp_peer_exchange* ex, float position_rate_factor) {
+    if (!ex) return SP_ERR_INVALID;
+    sp_adam* a = ex->adam;
+    SP_CHECK(sp_adam_advance(a, position_rate_factor));
+    SP_CHECK(select_device(a->ctx));
+    KernelSpan span(a->ctx, SP_K_PEER_ADAM);
+    SP_CUDA(a->ctx, launch_adam_peer(ex->peers, a->first_moment, a->second_moment, ex->first, ex->count,
+                                     (int)a->stride, a->lr_by_slot.data(), a->bias1, a->bias2, a->max_log_scale,
+                                     a->max_log_anisotropy, a->ctx->stream));
+    return SP_OK;
 }
 
 float* sp_adam_first_moment_device(sp_adam* a) { return a ? a->first_moment : nullptr; }

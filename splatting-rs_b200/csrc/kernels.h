@@ -120,6 +120,20 @@ cudaError_t launch_adam(float* params, const float* gradients, float* first_mome
                         uint64_t first, uint64_t count, int stride, const float* lr_by_slot_host, float bias1,
                         float bias2, float max_log_scale, float max_log_anisotropy, cudaStream_t stream);
 
+// The peer-memory exchange with Adam (sp_peer_exchange_step): per Gaussian of this rank's
+// share [first, first + count), the gradients summed over the ranks' buffers in rank order
+// (peer loads), the Adam step and scale clamp on this rank's parameters and moments, and the
+// updated parameters stored into every rank's parameter buffer (peer stores).
+constexpr int kMaxPeers = 8;
+struct PeerBuffers {
+    const float* gradients[kMaxPeers];
+    float* params[kMaxPeers];
+    uint32_t world, rank;
+};
+cudaError_t launch_adam_peer(const PeerBuffers& peers, float* first_moment, float* second_moment, uint64_t first,
+                             uint64_t count, int stride, const float* lr_by_slot_host, float bias1, float bias2,
+                             float max_log_scale, float max_log_anisotropy, cudaStream_t stream);
+
 // ---- pose_device.cu
 
 namespace pose {

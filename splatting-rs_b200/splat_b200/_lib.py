@@ -48,6 +48,7 @@ KERNEL_NAMES = (
     "tile_order",
     "backward_adam",
     "densify",
+    "peer_adam",
 )
 
 
@@ -178,6 +179,20 @@ class DensifyReportC(ctypes.Structure):
     ]
 
 
+class PeerHandleC(ctypes.Structure):
+    """sp_peer_handle: a rank's parameter and gradient buffers as CUDA IPC handles."""
+
+    _fields_ = [
+        ("params", ctypes.c_uint8 * 64),
+        ("gradients", ctypes.c_uint8 * 64),
+        ("params_offset", c_uint64),
+        ("gradients_offset", c_uint64),
+        ("gaussian_count", c_uint64),
+        ("stride", c_uint32),
+        ("device", ctypes.c_int32),
+    ]
+
+
 class PinholeCameraC(ctypes.Structure):
     _fields_ = [
         ("rotation", c_double * 9),
@@ -265,6 +280,10 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "sp_adam_steps_taken": (c_uint32, [_P]),
     "sp_adam_read_moments": (c_int, [_P, _P, _P]),
     "sp_adam_first_moment_device": (_P, [_P]),
+    "sp_peer_export": (c_int, [_P, POINTER(PeerHandleC)]),
+    "sp_peer_exchange_create": (c_int, [_P, c_uint32, c_uint32, POINTER(PeerHandleC), POINTER(_P)]),
+    "sp_peer_exchange_step": (c_int, [_P, c_float]),
+    "sp_peer_exchange_destroy": (None, [_P]),
     "sp_adam_second_moment_device": (_P, [_P]),
     "sp_position_rate_factor": (c_float, [c_uint64, c_uint64]),
     "sp_adam_resume_device": (c_int, [_P, _P, _P, c_uint64, _P, _P, POINTER(_P)]),

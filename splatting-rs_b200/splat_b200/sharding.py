@@ -18,6 +18,12 @@ buffers the library and the caller own, viewed as tensors without a copy:
   one (the ranges' backward launches end in partial waves, and the concurrent NCCL kernels
   slow the Adam steps), so one range is the default.
 - "allreduce": one all-reduce (sum) of the gradients, then the full Adam step on every rank.
+- "peer" (the default where it applies): no library collective for the data. One kernel per
+  rank (sp_peer_exchange_step) reads its share of every rank's gradients over peer memory
+  (NVLink loads from buffers mapped with CUDA IPC), sums them in rank order, steps Adam on the
+  share and stores the parameters into every rank's buffer (NVLink stores); two one-element
+  NCCL all-reduces on the stream order it after every rank's backward and before every rank's
+  next forward. The transfer and the Adam step run in the same kernel, tile by tile.
 
 Densification (densify.rs:147-257) with several ranks: each rank's backward passes
 accumulated the densify statistics of its own views, so they are merged first (sums of the
@@ -89,9 +95,9 @@ class GradientExchange:
                  mode: str | None = None, group=None, chunks: int = 1):
         if mode is None:
             mode = "sharded" if even_shards(gaussians, world) else "allreduce"
-        if mode == "sharded" and not even_shards(gaussians, world):
+        if mode in ("sharded", "peer") and not even_shards(gaussians, world):
             raise ValueError(f"{gaussians} Gaussians do not split evenly over {world} ranks")
-        if mode not in ("sharded", "allreduce"):
+        if mode not in ("sharded", "allreduce", "peer"):
             raise ValueError(f"unknown exchange {mode!r}")
         self.adam, self.params, self.gradients = adam, params, gradients
         self.rank, self.world, self.mode, self.group = rank, world, mode, group
@@ -99,6 +105,9 @@ class GradientExchange:
         self.ranges = chunk_ranges(gaussians, chunks, world) if mode == "sharded" else [(0, gaussians)]
         if mode == "sharded" and any(count % world for _, count in self.ranges):
             raise ValueError("every range must split evenly over the ranks")
+        self._peer = None
+        if mode == "peer":
+            self._peer = _PeerExchange(adam, rank, world, group)
 
     def _share(self, first: int, count: int) -> tuple[int, int]:
         """This rank's part [first, first + n) of the range."""
@@ -117,6 +126,10 @@ class GradientExchange:
         range overlapping the work on the next ones."""
         import torch.distributed as dist
 
+        if self._peer is not None:
+            project(0, self.ranges[0][1])
+            self._peer.step(rate_factor)
+            return
         if self.world == 1 or self.mode != "sharded":
             for first, count in self.ranges:
                 project(first, count)
@@ -140,7 +153,9 @@ class GradientExchange:
 
     def __call__(self, rate_factor: float) -> None:
         """The exchange and the Adam step after a whole backward (gradients all written)."""
-        if self.mode == "sharded" and self.world > 1:
+        if self._peer is not None:
+            self._peer.step(rate_factor)
+        elif self.mode == "sharded" and self.world > 1:
             self.backward_step(lambda first, count: None, rate_factor)
         else:
             self._replicated(rate_factor)
@@ -150,12 +165,17 @@ class GradientExchange:
         the sharded exchange each rank updated only its share of every range."""
         import torch.distributed as dist
 
-        if self.world == 1 or self.mode != "sharded":
+        if self.world == 1 or self.mode not in ("sharded", "peer"):
             return
         for moment in (first, second):
             for first_gaussian, count in self.ranges:
                 whole, own = self._views(moment, first_gaussian, count)
                 dist.all_gather_into_tensor(whole, own, group=self.group)
+
+    def close(self) -> None:
+        if self._peer is not None:
+            self._peer.close()
+            self._peer = None
 
     def _replicated(self, rate_factor: float) -> None:
         import torch.distributed as dist
@@ -163,6 +183,87 @@ class GradientExchange:
         if self.world > 1:
             dist.all_reduce(self.gradients, group=self.group)
         self.adam.encode_step(rate_factor)
+
+
+def make_exchange(adam, params, rasterizer, rank: int, world: int, mode: str | None = None,
+                  group=None) -> GradientExchange:
+    """The exchange of `mode` for a library optimiser and rasterizer; by default the peer
+    exchange when the Gaussians split evenly over several ranks (the sharded NCCL one when the
+    ranks cannot map each other's buffers), else the all-reduce."""
+    count = rasterizer.gaussian_count
+    if mode in ("sharded", "peer") and not even_shards(count, world):
+        mode = None
+    if mode is None and world > 1 and even_shards(count, world):
+        from ._lib import SplatError
+
+        try:
+            return GradientExchange(adam, params, rasterizer.param_gradients(), count, rasterizer.stride, rank,
+                                    world, "peer", group)
+        except (RuntimeError, SplatError):
+            mode = "sharded"
+    return GradientExchange(adam, params, rasterizer.param_gradients(), count, rasterizer.stride, rank, world,
+                            mode, group)
+
+
+class _PeerExchange:
+    """The "peer" exchange: sp_peer_exchange_* (one kernel sums the ranks' gradients of this
+    rank's share over peer memory, steps Adam on it and stores the parameters into every rank's
+    buffer), between two one-element NCCL all-reduces on the stream that order it after every
+    rank's backward and before every rank's next forward."""
+
+    def __init__(self, adam, rank: int, world: int, group=None):
+        import ctypes
+
+        import torch
+        import torch.distributed as dist
+
+        from . import _lib
+
+        self.lib = adam.lib
+        self.group = group
+        own = _lib.PeerHandleC()
+        exported = self.lib.sp_peer_export(adam.handle, ctypes.byref(own))
+        # Every rank joins the gather, an empty blob for a rank that could not export.
+        blobs = [None] * world
+        dist.all_gather_object(blobs, bytes(own) if exported == 0 else b"", group=group)
+        if any(not blob for blob in blobs):
+            raise RuntimeError("a rank could not export its buffers for the peer exchange")
+        handles = (_lib.PeerHandleC * world)()
+        for r, blob in enumerate(blobs):
+            ctypes.memmove(ctypes.byref(handles[r]), blob, ctypes.sizeof(_lib.PeerHandleC))
+        out = ctypes.c_void_p()
+        status = self.lib.sp_peer_exchange_create(adam.handle, rank, world, handles, ctypes.byref(out))
+        # Every rank learns whether every rank could map its peers before any uses the exchange.
+        ok = torch.tensor([1 if status == 0 else 0], dtype=torch.int32, device=f"cuda:{adam.ctx.device}")
+        dist.all_reduce(ok, op=dist.ReduceOp.MIN, group=group)
+        if status == 0 and int(ok.item()) == 0:
+            self.lib.sp_peer_exchange_destroy(out.value)
+            raise RuntimeError("a peer rank could not map the exchange buffers")
+        _lib.check(status, adam.ctx.handle, "sp_peer_exchange_create")
+        self.handle = out.value
+        self.ctx = adam.ctx
+        self.token = torch.zeros(1, dtype=torch.float32, device=f"cuda:{adam.ctx.device}")
+
+    def _barrier(self) -> None:
+        import torch.distributed as dist
+
+        dist.all_reduce(self.token, group=self.group)
+
+    def step(self, rate_factor: float) -> None:
+        from . import _lib
+
+        self._barrier()  # every rank's gradients are written
+        _lib.check(self.lib.sp_peer_exchange_step(self.handle, float(rate_factor)), self.ctx.handle,
+                   "sp_peer_exchange_step")
+        self._barrier()  # every rank's parameters are written
+
+    def close(self) -> None:
+        if getattr(self, "handle", None):
+            self.lib.sp_peer_exchange_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        self.close()
 
 
 class ViewShardedStep:
@@ -179,15 +280,17 @@ class ViewShardedStep:
         self.world = world
         self.mode = mode
         self.group = group
-        self.exchange = GradientExchange(adam, params, rasterizer.param_gradients(), rasterizer.gaussian_count,
-                                         rasterizer.stride, rank, world, mode, group)
+        self.exchange = self._exchange(adam, params, rasterizer)
+
+    def _exchange(self, adam, params, rasterizer) -> GradientExchange:
+        return make_exchange(adam, params, rasterizer, self.rank, self.world, self.mode, self.group)
 
     def densify(self, settings, extent: float, max_count: int, reset_opacity: bool, seed: int):
         """Trainer::densify_async (training.rs:238-266) on every rank: the statistics merged and
         the moments gathered (module docstring), densify on the device, then this step's
         rasterizer, optimiser and exchange rebuilt at the new count (the statistics start
-        over; the exchange is sharded again only when the new count splits evenly). Every rank
-        must call it at the same step. Returns the DensifyReport."""
+        over; the exchange is sharded, or peer, again only when the new count splits evenly).
+        Every rank must call it at the same step. Returns the DensifyReport."""
         from .densify import densify
         from .rasterizer import Rasterizer
 
@@ -200,12 +303,11 @@ class ViewShardedStep:
         rasterizer = Rasterizer(r.ctx, out.params, count, r.width, r.height, r._ground_truth, r.view_count,
                                 r.options)
         adam = self.adam.resumed_device(out.params, rasterizer, count, out.first_moment, out.second_moment)
+        self.exchange.close()
         r.close()
         self.adam.close()
         self.rasterizer, self.adam, self.params = rasterizer, adam, out.params
-        mode = self.mode if self.mode != "sharded" or even_shards(count, self.world) else None
-        self.exchange = GradientExchange(adam, out.params, rasterizer.param_gradients(), count, rasterizer.stride,
-                                         self.rank, self.world, mode, self.group)
+        self.exchange = self._exchange(adam, out.params, rasterizer)
         return out.report
 
     def __call__(self, step: int, rate_factor: float) -> int:

@@ -2,8 +2,10 @@
 step): each of two NCCL ranks renders its own view, the gradients are reduce-scattered,
 Adam runs on each rank's half of the Gaussians and the parameters are all-gathered. One GPU
 accumulates the same two views' gradients (in rank order) and takes one full Adam step. In
-the deterministic backward the parameters agree bit for bit. Needs two GPUs; skipped on
-one."""
+the deterministic backward the parameters agree bit for bit, with the NCCL exchange
+("sharded") and with the peer-memory one ("peer": one kernel per rank sums the ranks'
+gradients over NVLink, steps Adam on its share and stores the parameters into both ranks'
+buffers). Needs two GPUs; skipped on one."""
 
 from __future__ import annotations
 
@@ -35,7 +37,7 @@ def _scene():
     return cloud, cams, gt
 
 
-def _rank_main(rank: int, world: int, port: int, out_dir: str) -> None:
+def _rank_main(rank: int, world: int, port: int, out_dir: str, mode: str) -> None:
     from datetime import timedelta
 
     import torch
@@ -56,11 +58,14 @@ def _rank_main(rank: int, world: int, port: int, out_dir: str) -> None:
     opts = sb.default_options(sh_degree=1, backward_mode=sb.SP_BWD_DETERMINISTIC)
     rast = sb.Rasterizer(ctx, params, len(cloud), 160, 120, gt_dev, len(cams), opts)
     adam = sb.Adam(ctx, params, rast, len(cloud), sb.LEARNING_RATES_3DGS, 2.0, sh_degree=1)
-    step = ViewShardedStep(rast, adam, params, [c.uniform() for c in cams], rank, world, mode="sharded")
+    step = ViewShardedStep(rast, adam, params, [c.uniform() for c in cams], rank, world, mode=mode)
+    assert step.exchange.mode == mode
     for s in range(STEPS):
         step(s, sb.position_rate_factor(s, 10))
     torch.cuda.synchronize()
     np.save(os.path.join(out_dir, f"rank{rank}.npy"), params.cpu().numpy())
+    dist.barrier()
+    step.exchange.close()
     dist.barrier()
     dist.destroy_process_group()
 
@@ -71,7 +76,8 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
-def test_two_gpus_equal_one_gpu_with_the_same_batch(ctx, tmp_path):
+@pytest.mark.parametrize("mode", ["sharded", "peer"])
+def test_two_gpus_equal_one_gpu_with_the_same_batch(ctx, tmp_path, mode):
     import torch
     import torch.multiprocessing as mp
 
@@ -81,7 +87,7 @@ def test_two_gpus_equal_one_gpu_with_the_same_batch(ctx, tmp_path):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
     world = 2
-    mp.start_processes(_rank_main, args=(world, _free_port(), str(tmp_path)), nprocs=world, join=True,
+    mp.start_processes(_rank_main, args=(world, _free_port(), str(tmp_path), mode), nprocs=world, join=True,
                        start_method="spawn")
     ranks = [np.load(tmp_path / f"rank{r}.npy") for r in range(world)]
     assert np.array_equal(ranks[0], ranks[1]), "the ranks' parameters diverged"
@@ -126,7 +132,8 @@ def _densify_rank_main(rank: int, world: int, port: int, out_dir: str) -> None:
     opts = sb.default_options(sh_degree=1, backward_mode=sb.SP_BWD_DETERMINISTIC)
     rast = sb.Rasterizer(ctx, params, len(cloud), 160, 120, gt_dev, len(cams), opts)
     adam = sb.Adam(ctx, params, rast, len(cloud), sb.LEARNING_RATES_3DGS, 2.0, sh_degree=1)
-    step = ViewShardedStep(rast, adam, params, [c.uniform() for c in cams], rank, world, mode="sharded")
+    step = ViewShardedStep(rast, adam, params, [c.uniform() for c in cams], rank, world)
+    assert step.exchange.mode == "peer"
     settings = sb.DensifySettings(**{**sb.DENSIFY_SHORT_RUN.__dict__, "gradient_threshold": 1e-5})
     for s in range(STEPS):
         step(s, sb.position_rate_factor(s, 10))
@@ -136,6 +143,8 @@ def _densify_rank_main(rank: int, world: int, port: int, out_dir: str) -> None:
     torch.cuda.synchronize()
     np.save(os.path.join(out_dir, f"densified{rank}.npy"), step.params.cpu().numpy())
     np.save(os.path.join(out_dir, f"report{rank}.npy"), np.array([report.before, report.after, report.split]))
+    dist.barrier()
+    step.exchange.close()
     dist.barrier()
     dist.destroy_process_group()
 
