@@ -582,10 +582,12 @@ def main() -> None:
             entry.update(bound="hbm", achieved=achieved, peak=pk["hbm_gbs"], unit="GB/s", frac=achieved / pk["hbm_gbs"],
                          bytes_per_launch=stepped * 28)
         elif name == "peer_adam":
-            # Per launch, this rank's share: every peer's gradients read and the parameters stored
-            # into every peer over NVLink; against the measured 770 GB/s per direction per GPU.
+            # Per launch and link direction of this GPU: its reads of its share of the peers'
+            # gradients and the peers' stores of their shares into it come in, its stores and
+            # the peers' reads of its gradients go out: 2 (world - 1) shares each way, against
+            # the measured 770 GB/s per direction per GPU.
             share_bytes = n_params // world * 4
-            nvlink = (world - 1) * share_bytes
+            nvlink = 2 * (world - 1) * share_bytes
             achieved = nvlink / (kms / n * 1e-3) / 1e9
             entry.update(bound="nvlink", achieved=achieved, peak=770.0, unit="GB/s per direction",
                          frac=achieved / 770.0, nvlink_bytes_per_direction=nvlink,
