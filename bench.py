@@ -66,6 +66,8 @@ def parse_args():
     p.add_argument("--no-forward-3m", action="store_true", help="skip the forward-only config-3 measurement")
     p.add_argument("--forward-batches", type=int, default=3, help="timed passes over config 3's 64 cameras")
     p.add_argument("--no-densify", action="store_true", help="skip the device densification timing")
+    p.add_argument("--exchange", choices=["auto", "peer", "sharded", "allreduce"], default="auto",
+                   help="multi-GPU exchange (auto: peer where the Gaussians split evenly, else all-reduce)")
     p.add_argument("--tiles", choices=["ellipse", "rectangle"], default="ellipse",
                    help="tile culling: the ellipse's tiles only (the same images and gradients, shorter lists) "
                         "or the reference's whole bounding rectangles")
@@ -419,7 +421,8 @@ def main() -> None:
     iterations = scene.iterations
     # One GPU: backward with the Adam step fused. N GPUs: gradients reduce-scattered, Adam on
     # this rank's share of the Gaussians, parameters all-gathered (splat_b200/sharding.py).
-    train_step = ViewShardedStep(rast, adam, params, uniforms, rank, world)
+    exchange_mode = None if args.exchange == "auto" else args.exchange
+    train_step = ViewShardedStep(rast, adam, params, uniforms, rank, world, mode=exchange_mode)
 
     def view_of(step: int) -> int:
         return sharding.view_of(step, rank, world, views)
@@ -485,7 +488,7 @@ def main() -> None:
     # ---- e2e: the reference caller's step through the public API, poses refined.
     params.copy_(initial)
     adam_e2e = sb.Adam(ctx, params, rast, len(cloud), sb.LEARNING_RATES_3DGS, extent, sh_degree=deg)
-    exchange_e2e = sharding.make_exchange(adam_e2e, params, rast, rank, world)
+    exchange_e2e = sharding.make_exchange(adam_e2e, params, rast, rank, world, exchange_mode)
     poses = sb.PoseRefinement(cams, sb.LEARNING_RATES_3DGS, float(extent))
     e2e_steps = args.e2e_steps or args.steps
 
