@@ -250,3 +250,40 @@ def test_two_gloo_ranks_densify_as_one_process():
     p, mm, vv, _ = oracle.densify(packed, m, v, merged, 14, _DENSIFY_ARGS["extent"], 10 * len(cloud),
                                   _settings().to_c(), 0, _DENSIFY_ARGS["seed"])
     assert np.array_equal(ranks[0]["p"], p) and np.array_equal(ranks[0]["m"], mm) and np.array_equal(ranks[0]["v"], vv)
+
+
+class _FakeRasterizer:
+    gaussian_count = 1000
+    stride = 14
+
+    def param_gradients(self):
+        import torch
+
+        return torch.zeros(self.gaussian_count * self.stride)
+
+
+def test_the_exchange_choice(monkeypatch):
+    """make_exchange: the peer exchange by default where the Gaussians split evenly, the NCCL
+    sharded one when the ranks cannot map each other's buffers (every rank learns it in the
+    set-up's collectives), the all-reduce when they do not split evenly."""
+    import torch
+
+    from splat_b200 import sharding
+
+    calls = []
+
+    class Failing:
+        def __init__(self, *args, **kwargs):
+            calls.append(args)
+            raise RuntimeError("a rank could not export its buffers for the peer exchange")
+
+    monkeypatch.setattr(sharding, "_PeerExchange", Failing)
+    params = torch.zeros(1000 * 14)
+    chosen = sharding.make_exchange(None, params, _FakeRasterizer(), 0, 2)
+    assert chosen.mode == "sharded" and len(calls) == 1
+    uneven = _FakeRasterizer()
+    uneven.gaussian_count = 1001
+    assert sharding.make_exchange(None, torch.zeros(1001 * 14), uneven, 0, 2).mode == "allreduce"
+    assert sharding.make_exchange(None, params, _FakeRasterizer(), 0, 1).mode == "allreduce"
+    with pytest.raises(RuntimeError):
+        sharding.make_exchange(None, params, _FakeRasterizer(), 0, 2, mode="peer")
