@@ -48,7 +48,7 @@ BACKWARD_OPS_PER_PAIR = 48
 # from one ncu --set full capture of this workload each (profiles/blend_kernels_config2.txt,
 # profiles/project_backward_adam_config2.txt; cold caches, so an upper bound on the in-bench
 # traffic).
-NCU_TRAFFIC_BYTES = {"blend_backward": 84.8e6, "blend_forward": 35.5e6, "backward_adam": 836.7e6}
+NCU_TRAFFIC_BYTES = {"blend_backward": 85.0e6, "blend_forward": 35.7e6, "backward_adam": 836.7e6}
 
 
 def parse_args():
