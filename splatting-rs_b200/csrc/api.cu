@@ -110,7 +110,8 @@ struct sp_rasterizer {
     float4* ssim_partials = nullptr;
     float4* loss_gradient = nullptr;
     float4* pixel_loss = nullptr;
-    double* loss_sums = nullptr;
+    double* loss_sums = nullptr;    // the loss-sum kernel's workspace
+    double* loss_result = nullptr;  // its 4 sums (inside readback_dev)
     float* slot_gradients = nullptr;
     float4* gaussian_gradients = nullptr;
     float* param_gradients = nullptr;
@@ -126,6 +127,9 @@ struct sp_rasterizer {
         double loss[4];
     };
     StepReadback* readback = nullptr;
+    // Its device side: the camera gradient and the loss sums live here (camera_gradient and
+    // loss_result point into it), so that a step's read-back is one copy.
+    StepReadback* readback_dev = nullptr;
 
     uint64_t pixels() const { return (uint64_t)width * height; }
 };
@@ -252,7 +256,8 @@ void learning_rates_by_slot(const sp_learning_rates& rates, float position_scale
 namespace splat {
 // loss.cu: deterministic sum of the per-pixel loss terms into workspace[0..4) (the
 // workspace holds 4 + 4 * 256 + 1 doubles).
-cudaError_t launch_loss_sums(const float4* pixel_loss, uint64_t pixels, double* workspace, cudaStream_t stream);
+cudaError_t launch_loss_sums(const float4* pixel_loss, uint64_t pixels, double* workspace, double* result,
+                             const uint32_t* status_src, uint32_t* status_dst, cudaStream_t stream);
 }  // namespace splat
 
 extern "C" {
@@ -469,6 +474,9 @@ sp_status sp_rasterizer_create(sp_context* ctx, const float* d_params, uint64_t 
     SP_ALLOC(r->loss_gradient, p);
     SP_ALLOC(r->pixel_loss, p);
     SP_ALLOC(r->loss_sums, 4 + 4 * 256 + 1);
+    SP_ALLOC(r->readback_dev, 1);
+    r->camera_gradient = r->readback_dev->camera;
+    r->loss_result = r->readback_dev->loss;
     if (opt.backward_mode == SP_BWD_DETERMINISTIC) {
         SP_ALLOC(r->slot_gradients, capacity * SP_GRAD_STRIDE);
     } else {
@@ -477,7 +485,6 @@ sp_status sp_rasterizer_create(sp_context* ctx, const float* d_params, uint64_t 
     SP_ALLOC(r->param_gradients, n * r->stride);
     SP_ALLOC(r->camera_partials, (size_t)r->blocks * SP_CAMERA_GRAD_STRIDE);
     SP_ALLOC(r->camera_done, 1);
-    SP_ALLOC(r->camera_gradient, SP_CAMERA_GRAD_STRIDE);
     SP_ALLOC(r->densify_stats, n);
 #undef SP_ALLOC
     {
@@ -746,9 +753,10 @@ sp_status sp_read_loss(sp_rasterizer* r, sp_loss_terms* out) {
     if (!r || !out) return SP_ERR_INVALID;
     SP_CHECK(select_device(r->ctx));
     // LossTerms::from_pixel_loss (loss.rs:49-63): means in f64, summed on the device.
-    SP_CUDA(r->ctx, launch_loss_sums(r->pixel_loss, r->pixels(), r->loss_sums, r->ctx->stream));
+    SP_CUDA(r->ctx, launch_loss_sums(r->pixel_loss, r->pixels(), r->loss_sums, r->loss_result, nullptr, nullptr,
+                                     r->ctx->stream));
     double sums[4];
-    SP_CHECK(read_device(r->ctx, sums, r->loss_sums, sizeof(sums)));
+    SP_CHECK(read_device(r->ctx, sums, r->loss_result, sizeof(sums)));
     const double pixels = (double)r->pixels();
     out->l1 = (float)(sums[0] / pixels);
     out->alpha = (float)(sums[1] / pixels);
@@ -789,15 +797,18 @@ sp_status sp_train_step(sp_rasterizer* r, sp_adam* adam, const sp_camera_uniform
     }
     if (!camera_gradient_out && !loss_out) return SP_OK;
     cudaStream_t st = r->ctx->stream;
-    SP_CUDA(r->ctx, cudaMemcpyAsync(&r->readback->status, &r->meta->status, sizeof(uint32_t), cudaMemcpyDeviceToHost,
-                                    st));
-    if (loss_out) SP_CUDA(r->ctx, launch_loss_sums(r->pixel_loss, r->pixels(), r->loss_sums, st));
-    if (camera_gradient_out)
+    if (loss_out) {
+        // The loss-sum kernel also copies the step's status next to the camera gradient and the
+        // sums: one copy brings the whole read-back.
+        SP_CUDA(r->ctx, launch_loss_sums(r->pixel_loss, r->pixels(), r->loss_sums, r->loss_result, &r->meta->status,
+                                         &r->readback_dev->status, st));
+        SP_CUDA(r->ctx, cudaMemcpyAsync(r->readback, r->readback_dev, sizeof(*r->readback), cudaMemcpyDeviceToHost, st));
+    } else {
+        SP_CUDA(r->ctx, cudaMemcpyAsync(&r->readback->status, &r->meta->status, sizeof(uint32_t),
+                                        cudaMemcpyDeviceToHost, st));
         SP_CUDA(r->ctx, cudaMemcpyAsync(r->readback->camera, r->camera_gradient, sizeof(r->readback->camera),
                                         cudaMemcpyDeviceToHost, st));
-    if (loss_out)
-        SP_CUDA(r->ctx,
-                cudaMemcpyAsync(r->readback->loss, r->loss_sums, sizeof(r->readback->loss), cudaMemcpyDeviceToHost, st));
+    }
     SP_CHECK(sync_stream(r->ctx));
     if (r->readback->status != 0) return device_status(r, nullptr);
     if (camera_gradient_out) std::memcpy(camera_gradient_out, r->readback->camera, sizeof(sp_camera_gradient));
@@ -924,8 +935,10 @@ sp_status sp_train_step_device_poses(sp_rasterizer* r, sp_adam* adam, sp_device_
     SP_CHECK(sp_device_poses_step(dp, view, next_view, position_rate_factor));
     if (pinned_loss_sums) {
         cudaStream_t st = r->ctx->stream;
-        SP_CUDA(r->ctx, launch_loss_sums(r->pixel_loss, r->pixels(), r->loss_sums, st));
-        SP_CUDA(r->ctx, cudaMemcpyAsync(pinned_loss_sums, r->loss_sums, 4 * sizeof(double), cudaMemcpyDeviceToHost, st));
+        SP_CUDA(r->ctx, launch_loss_sums(r->pixel_loss, r->pixels(), r->loss_sums, r->loss_result, nullptr, nullptr,
+                                         st));
+        SP_CUDA(r->ctx,
+                cudaMemcpyAsync(pinned_loss_sums, r->loss_result, 4 * sizeof(double), cudaMemcpyDeviceToHost, st));
     }
     return SP_OK;
 }

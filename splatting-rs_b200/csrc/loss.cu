@@ -333,11 +333,13 @@ constexpr int kSumBlocks = 256;
 // Sums of the 4 per-pixel loss terms in double, in a fixed order (each block a strided
 // share, a tree per block, then the last block adds the block sums in block order), so
 // that the reported loss does not depend on scheduling.
+// The last block also copies the step's status word (status_src, when given) next to the sums,
+// so that a step's read-back is one copy.
 __global__ void __launch_bounds__(kBlock) k_loss_sums(const float4* __restrict__ pixel_loss, uint64_t pixels,
-                                                      double* __restrict__ workspace) {
+                                                      double* __restrict__ workspace, double* __restrict__ result,
+                                                      const uint32_t* status_src, uint32_t* status_dst) {
     __shared__ double s[4][kBlock];
     __shared__ bool last;
-    double* result = workspace;
     double* partials = workspace + 4;
     unsigned int* done = reinterpret_cast<unsigned int*>(workspace + 4 + 4 * kSumBlocks);
     const uint32_t t = threadIdx.x;
@@ -371,13 +373,17 @@ __global__ void __launch_bounds__(kBlock) k_loss_sums(const float4* __restrict__
         for (uint32_t k = 0; k < gridDim.x; ++k) sum += __ldcg(partials + k * 4 + t);
         result[t] = sum;
     }
-    if (t == 0) *done = 0;
+    if (t == 0) {
+        *done = 0;
+        if (status_src) *status_dst = *status_src;
+    }
 }
 
 }  // namespace
 
-cudaError_t launch_loss_sums(const float4* pixel_loss, uint64_t pixels, double* workspace, cudaStream_t stream) {
-    k_loss_sums<<<kSumBlocks, kBlock, 0, stream>>>(pixel_loss, pixels, workspace);
+cudaError_t launch_loss_sums(const float4* pixel_loss, uint64_t pixels, double* workspace, double* result,
+                             const uint32_t* status_src, uint32_t* status_dst, cudaStream_t stream) {
+    k_loss_sums<<<kSumBlocks, kBlock, 0, stream>>>(pixel_loss, pixels, workspace, result, status_src, status_dst);
     return cudaGetLastError();
 }
 
