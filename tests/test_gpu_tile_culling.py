@@ -6,7 +6,8 @@ Bars:
     every removed (tile, Gaussian) pair has alpha below 1/255 at every pixel centre of the
     tile (checked in f64 from the projected records, with a 0.1 % margin);
   - images and per-pixel losses bit for bit; parameter gradients and densify statistics
-    as two runs of the atomic backward agree (float atomics in a different order);
+    within the gradients' parity bar (1e-4 of each slot's largest; float atomics in a
+    different order);
   - 20 training steps: every step's loss within 1e-5 relative.
 """
 
@@ -107,15 +108,16 @@ def test_culling_changes_no_result(ctx, name):
     stride = sb.param_stride(cloud.sh_degree)
     g_full = full["gradients"].reshape(-1, stride)
     g_culled = culled["gradients"].reshape(-1, stride)
-    # As close as two runs of the atomic backward with rectangles (plus a floor).
+    # Float atomics in another order: within the parity bar of the gradients (1e-4 of the
+    # slot's largest), or of the spread between two runs with rectangles where that is larger.
     spread = np.abs(again["gradients"].reshape(-1, stride) - g_full).max(axis=0)
     scale = np.abs(g_full).max(axis=0)
-    assert np.all(np.abs(g_culled - g_full).max(axis=0) <= 4.0 * spread + 1e-5 * scale + 1e-9), name
+    assert np.all(np.abs(g_culled - g_full).max(axis=0) <= 4.0 * spread + 1e-4 * scale + 1e-9), name
     assert np.array_equal(culled["stats"][:, 1:3], full["stats"][:, 1:3])
     # The mean-gradient sums are norms of atomically summed gradients: the same bar.
     stat_spread = np.abs(again["stats"][:, 0] - full["stats"][:, 0]).max()
     stat_error = np.abs(culled["stats"][:, 0] - full["stats"][:, 0]).max()
-    assert stat_error <= 4.0 * stat_spread + 1e-5 * np.abs(full["stats"][:, 0]).max() + 1e-9, name
+    assert stat_error <= 4.0 * stat_spread + 1e-4 * np.abs(full["stats"][:, 0]).max() + 1e-9, name
 
 
 def test_culling_rejects_the_deterministic_backward(ctx):
