@@ -671,9 +671,10 @@ def main() -> None:
                 "value": e2e_value,
                 "unit": UNIT,
                 "h2d_bytes_per_step": 80,
-                "d2h_bytes_per_step": 56 + 32,
+                "d2h_bytes_per_step": 96 if world == 1 else 56 + 32,
                 "what": "set_camera (80-B camera uniform from the host) + forward + loss + backward + Adam, then the "
-                        "camera gradient (56 B) and the loss sums (32 B) read back and the host pose step",
+                        "camera gradient (56 B), the step status and the loss sums (32 B) read back (one 96-B copy "
+                        "on one GPU) and the host pose step",
             },
             "e2e_device_poses": e2e_device,
             "gpu_launches": int(round(launches_per_step * args.steps)),
