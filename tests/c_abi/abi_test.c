@@ -66,6 +66,8 @@ int main(int argc, char** argv) {
     CHECK(sp_forward(NULL) == SP_ERR_INVALID);
     CHECK(sp_adam_step(NULL, 1.0f) == SP_ERR_INVALID);
     CHECK(sp_densify_apply(NULL, NULL, NULL, NULL, 0) == SP_ERR_INVALID);
+    CHECK(sp_peer_export(NULL, NULL) == SP_ERR_INVALID && sp_peer_exchange_step(NULL, 1.0f) == SP_ERR_INVALID);
+    CHECK(sizeof(sp_peer_handle) == 160);
     printf("ok\n");
     return 0;
 }

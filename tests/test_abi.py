@@ -63,6 +63,7 @@ def test_struct_layouts_match_the_reference():
     assert ctypes.sizeof(_lib.IntersectionMeta) == 20 and ctypes.sizeof(_lib.DensifyStats) == 16
     assert ctypes.sizeof(_lib.Options) == 36 and _lib.Options.tile_culling.offset == 32
     assert ctypes.sizeof(_lib.DensifySettingsC) == 40 and ctypes.sizeof(_lib.DensifyReportC) == 64
+    assert ctypes.sizeof(_lib.PeerHandleC) == 160
 
 
 def test_default_options_are_the_reference_behaviour():
