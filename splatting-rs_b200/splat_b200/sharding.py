@@ -3,8 +3,8 @@ parameters replicated, the parameter gradients are summed across ranks, then the
 take one Adam step identical on every rank. The reference trains one view per step on one
 device (instantsplat-rs/src/training.rs:197-229); with one rank this is exactly that step.
 
-Two exchanges, through torch.distributed (NCCL over NVLink on GPUs, gloo on CPU) on the
-buffers the library and the caller own, viewed as tensors without a copy:
+Three exchanges; the first two through torch.distributed (NCCL over NVLink on GPUs, gloo on
+CPU) on the buffers the library and the caller own, viewed as tensors without a copy:
 
 - "sharded" (when the Gaussians split evenly over the ranks): a reduce-scatter of the
   gradients, so that each rank holds the summed gradients of its own share of the
@@ -28,8 +28,8 @@ buffers the library and the caller own, viewed as tensors without a copy:
 Densification (densify.rs:147-257) with several ranks: each rank's backward passes
 accumulated the densify statistics of its own views, so they are merged first (sums of the
 mean-gradient sums and visible counts, the largest screen radius: what one device would
-have accumulated over all the views, up to the order of the sums), and in the sharded
-exchange each rank's moments are current only on its own share, so the shares are
+have accumulated over all the views, up to the order of the sums), and in the sharded and
+peer exchanges each rank's moments are current only on its own share, so the shares are
 all-gathered. Every rank then runs the same densification on the same inputs and gets the
 same Gaussians (the kernels are deterministic).
 """
