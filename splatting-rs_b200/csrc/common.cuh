@@ -78,6 +78,15 @@ __device__ __forceinline__ float warp_sum(float v) {
 
 __device__ __forceinline__ uint32_t lane_id() { return threadIdx.x & 31u; }
 
+// Asks the bulk-copy engine to bring [ptr, ptr + bytes) into L2 (cp.async.bulk.prefetch.L2,
+// sm_90+): a hint with nothing to wait for. The range must lie inside one allocation; it is
+// skipped unless ptr is 16-B aligned, and bytes is rounded down to a multiple of 16.
+__device__ __forceinline__ void prefetch_l2(const void* ptr, uint32_t bytes) {
+    bytes &= ~15u;
+    if (bytes == 0 || (reinterpret_cast<uintptr_t>(ptr) & 15u) != 0) return;
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(ptr), "r"(bytes) : "memory");
+}
+
 __device__ __forceinline__ void raise_status(DeviceMeta* meta, uint32_t status) {
     atomicCAS(&meta->status, 0u, status);
 }

@@ -134,6 +134,9 @@ __global__ void __launch_bounds__(kBlock) k_project(const float* __restrict__ pa
     float* sp = reinterpret_cast<float*>(smem4);
     const uint32_t g0 = blockIdx.x * kBlock;
     const uint32_t here = min((uint32_t)kBlock, n - g0);
+    // The block's whole parameter slice requested at once: the staging loop's loads then
+    // meet it in L2 (measured at config 2: 62 -> 52 us).
+    if (threadIdx.x == 0) prefetch_l2(params + (size_t)g0 * S, here * S * (uint32_t)sizeof(float));
     if constexpr (DEV) load_camera(camera_device, s_cam);
     stage_in(params + (size_t)g0 * S, here * S, sp);
     __syncthreads();
