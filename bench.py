@@ -97,6 +97,7 @@ class ClockSampler:
         self.device = device
         self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
         self.proc = None
+        self.skip = 0
 
     def __enter__(self):
         try:
@@ -108,6 +109,17 @@ class ClockSampler:
             )
         except OSError:
             self.proc = None
+        # nvidia-smi takes a moment to start: wait for its first sample (taken before the
+        # timed region, and left out of the summary) so that short regions are sampled too.
+        self.skip = 0
+        deadline = time.monotonic() + 5.0
+        while self.proc is not None and self.proc.poll() is None and time.monotonic() < deadline:
+            self.file.flush()
+            with open(self.file.name) as f:
+                self.skip = sum(1 for _ in f)
+            if self.skip:
+                break
+            time.sleep(0.02)
         return self
 
     def __exit__(self, *exc):
@@ -123,7 +135,7 @@ class ClockSampler:
         self.file.seek(0)
         sm, sm_max, reasons = [], 0.0, set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for line in self.file.read().splitlines():
+        for line in self.file.read().splitlines()[self.skip:]:
             parts = [x.strip() for x in line.split(",")]
             if len(parts) < 9:
                 continue
