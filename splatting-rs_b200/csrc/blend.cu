@@ -245,6 +245,7 @@ __global__ void __launch_bounds__(kPairThreads, 8) k_blend_forward(const float4*
                                                                    const sp_camera_uniform cam,
                                                                    float4* __restrict__ image,
                                                                    uint32_t* __restrict__ contributions) {
+    chain_enter();
     __shared__ WarpStage s_stage[kPairWarps];
     const uint32_t tile = order[blockIdx.x];
     const uint32_t gx = tile % cam.tiles_x, gy = tile / cam.tiles_x;
@@ -507,6 +508,7 @@ __global__ void __launch_bounds__(kPairThreads, 6) k_blend_backward_atomic(
     const uint32_t* __restrict__ order, const float4* __restrict__ reach, const sp_camera_uniform cam,
     const float4* __restrict__ image, const uint32_t* __restrict__ contributions,
     const float4* __restrict__ loss_gradient, float4* __restrict__ gaussian_gradients) {
+    chain_enter();
     __shared__ WarpStage s_stage[kPairWarps];
     const uint32_t tile = order[blockIdx.x];
     const uint32_t gx = tile % cam.tiles_x, gy = tile / cam.tiles_x;
@@ -618,6 +620,7 @@ __device__ __forceinline__ uint32_t order_bucket(uint2 range) {
 
 __global__ void __launch_bounds__(kOrderThreads) k_tile_order(const uint2* __restrict__ ranges, uint32_t tiles,
                                                               uint32_t* __restrict__ order) {
+    chain_enter();
     __shared__ uint32_t s_next[kOrderBuckets];
     const uint32_t t = threadIdx.x;
     for (uint32_t b = t; b < kOrderBuckets; b += kOrderThreads) s_next[b] = 0;
@@ -705,7 +708,7 @@ cudaError_t launch_count_blend(const float4* records, const uint32_t* sorted_gau
 }
 
 cudaError_t launch_tile_order(const uint2* ranges, uint32_t tiles, uint32_t* order, cudaStream_t stream) {
-    k_tile_order<<<1, kOrderThreads, 0, stream>>>(ranges, tiles, order);
+    launch_chained(k_tile_order, 1, kOrderThreads, 0, stream, ranges, tiles, order);
     return cudaGetLastError();
 }
 
@@ -713,7 +716,7 @@ cudaError_t launch_blend_forward(const float4* records, const float4* reach, con
                                  const uint2* ranges, const uint32_t* order, const sp_camera_uniform& cam,
                                  float4* image, uint32_t* contributions, cudaStream_t stream) {
     const unsigned tiles = cam.tiles_x * cam.tiles_y;
-    k_blend_forward<<<tiles, kPairThreads, 0, stream>>>(records, sorted_gaussians, ranges, order, reach, cam, image,
+    launch_chained(k_blend_forward, tiles, kPairThreads, 0, stream, records, sorted_gaussians, ranges, order, reach, cam, image,
                                                         contributions);
     return cudaGetLastError();
 }
@@ -729,7 +732,7 @@ cudaError_t launch_blend_backward(int mode, const float4* records, const float4*
             records, sorted_gaussians, ranges, order, offsets, cam, image, contributions, loss_gradient,
             slot_gradients, gaussian_gradients);
     else
-        k_blend_backward_atomic<<<tiles, kPairThreads, 0, stream>>>(records, sorted_gaussians, ranges, order, reach,
+        launch_chained(k_blend_backward_atomic, tiles, kPairThreads, 0, stream, records, sorted_gaussians, ranges, order, reach,
                                                                     cam, image, contributions, loss_gradient,
                                                                     gaussian_gradients);
     return cudaGetLastError();

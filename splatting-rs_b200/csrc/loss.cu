@@ -89,6 +89,7 @@ constexpr size_t kLossSmem = (size_t)3 * kSpan * kSpan * sizeof(float) + (size_t
 __global__ void __launch_bounds__(kThreads, 2) k_ssim(const float4* __restrict__ image, const float4* __restrict__ gt,
                                                       uint32_t width, uint32_t height, const Taps taps,
                                                       float4* __restrict__ partials) {
+    chain_enter();
     extern __shared__ float4 smem4[];
     float2* s_in = reinterpret_cast<float2*>(smem4);         // [3][kSpan][kSpan]: (x, y) per channel
     float* s_rows = reinterpret_cast<float*>(s_in + 3 * kSpan * kSpan);  // [5][kSpan][kPitch]
@@ -179,6 +180,7 @@ __global__ void __launch_bounds__(kThreads, 3) k_loss(const float4* __restrict__
                                                       const sp_loss_weights weights,
                                                       float4* __restrict__ loss_gradient,
                                                       float4* __restrict__ pixel_loss) {
+    chain_enter();
     extern __shared__ float4 smem4[];
     float* s_in = reinterpret_cast<float*>(smem4);           // [3][kSpan][kSpan]: d_mu, d_exx, d_exy
     float* s_rows = s_in + 3 * kSpan * kSpan;                // [3][kSpan][kPitch]
@@ -304,7 +306,7 @@ cudaError_t launch_ssim(const float4* image, const float4* ground_truth, uint32_
         configured = true;
     }
     const dim3 grid(grid_for(width, kTile), grid_for(height, kTile));
-    k_ssim<<<grid, kThreads, kSsimSmem, stream>>>(image, ground_truth, width, height, window(), partials);
+    launch_chained(k_ssim, grid, kThreads, kSsimSmem, stream, image, ground_truth, width, height, window(), partials);
     return cudaGetLastError();
 }
 
@@ -319,7 +321,7 @@ cudaError_t launch_loss(const float4* image, const float4* ground_truth, const f
         configured = true;
     }
     const dim3 grid(grid_for(width, kTile), grid_for(height, kTile));
-    k_loss<<<grid, kThreads, kLossSmem, stream>>>(image, ground_truth, partials, width, height, window(), weights,
+    launch_chained(k_loss, grid, kThreads, kLossSmem, stream, image, ground_truth, partials, width, height, window(), weights,
                                                   loss_gradient, pixel_loss);
     return cudaGetLastError();
 }
@@ -339,6 +341,7 @@ constexpr int kSumBlocks = 256;
 __global__ void __launch_bounds__(kBlock) k_loss_sums(const float4* __restrict__ pixel_loss, uint64_t pixels,
                                                       double* __restrict__ workspace, double* __restrict__ result,
                                                       const uint32_t* status_src, uint32_t* status_dst) {
+    chain_enter();
     __shared__ double s[4][kBlock];
     __shared__ bool last;
     double* partials = workspace + 4;
@@ -384,7 +387,7 @@ __global__ void __launch_bounds__(kBlock) k_loss_sums(const float4* __restrict__
 
 cudaError_t launch_loss_sums(const float4* pixel_loss, uint64_t pixels, double* workspace, double* result,
                              const uint32_t* status_src, uint32_t* status_dst, cudaStream_t stream) {
-    k_loss_sums<<<kSumBlocks, kBlock, 0, stream>>>(pixel_loss, pixels, workspace, result, status_src, status_dst);
+    launch_chained(k_loss_sums, kSumBlocks, kBlock, 0, stream, pixel_loss, pixels, workspace, result, status_src, status_dst);
     return cudaGetLastError();
 }
 

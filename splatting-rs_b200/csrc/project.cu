@@ -127,6 +127,7 @@ __global__ void __launch_bounds__(kBlock) k_project(const float* __restrict__ pa
                                                     uint32_t* __restrict__ local_offsets,
                                                     uint32_t* __restrict__ block_totals, DeviceMeta* depth_range,
                                                     float4* __restrict__ reach, uint32_t cull) {
+    chain_enter();
     constexpr int S = SP_PARAM_STRIDE(DEG);
     extern __shared__ float4 smem4[];
     __shared__ sp_camera_uniform s_cam;
@@ -196,6 +197,7 @@ __global__ void __launch_bounds__(1024) k_scan_blocks(const uint32_t* __restrict
                                                       unsigned long long capacity, DeviceMeta* meta,
                                                       uint32_t* sort_histograms, uint32_t* sort_tickets,
                                                       const SortPlan plan) {
+    chain_enter();
     __shared__ unsigned long long warp_sums[32];
     __shared__ unsigned long long carry;
     const uint32_t t = threadIdx.x, lane = t & 31u, warp = t >> 5;
@@ -501,6 +503,7 @@ __global__ void __launch_bounds__(kBlock, 3) k_project_backward(
     unsigned long long capacity, const float4* __restrict__ gaussian_gradients, float* __restrict__ param_gradients,
     int accumulate, float* __restrict__ camera_partials, uint32_t* camera_done, float* __restrict__ camera_gradient,
     float4* __restrict__ densify_stats, const FusedAdam adam, uint32_t first_block, uint32_t total_blocks) {
+    chain_enter();
     constexpr int S = SP_PARAM_STRIDE(DEG);
     __shared__ sp_camera_uniform s_cam;
     const sp_camera_uniform& cam = pick_camera<DEV>(camera_argument, s_cam);
@@ -625,7 +628,7 @@ cudaError_t launch_project(const float* params, uint64_t n, int sh_degree, const
     cudaError_t err = cudaSuccess;
 #define SPLAT_PROJECT_ONE(D, V)                                                                           \
     if ((err = set_smem(k_project<D, V>, smem)) != cudaSuccess) return err;                                \
-    k_project<D, V><<<grid, kBlock, smem, stream>>>(params, (uint32_t)n, cam, cam_device, records, radii,  \
+    launch_chained(k_project<D, V>, grid, kBlock, smem, stream, params, (uint32_t)n, cam, cam_device, records, radii,  \
                                                     local_offsets, block_totals, depth_range, reach,      \
                                                     (uint32_t)tile_culling);                              \
     return cudaGetLastError();
@@ -649,7 +652,7 @@ cudaError_t launch_project(const float* params, uint64_t n, int sh_degree, const
 cudaError_t launch_scan_blocks(const uint32_t* block_totals, unsigned long long* block_offsets, uint32_t blocks,
                                uint64_t capacity, DeviceMeta* meta, uint32_t* sort_histograms,
                                uint32_t* sort_tickets, const SortPlan& plan, cudaStream_t stream) {
-    k_scan_blocks<<<1, 1024, 0, stream>>>(block_totals, block_offsets, blocks, capacity, meta, sort_histograms,
+    launch_chained(k_scan_blocks, 1, 1024, 0, stream, block_totals, block_offsets, blocks, capacity, meta, sort_histograms,
                                           sort_tickets, plan);
     return cudaGetLastError();
 }
@@ -682,7 +685,7 @@ cudaError_t launch_project_backward(const float* params, uint64_t n, int sh_degr
     }
 #define SPLAT_PB_ONE(D, M, F, V)                                                                               \
     if ((err = set_smem(k_project_backward<D, M, F, V>, smem)) != cudaSuccess) return err;                     \
-    k_project_backward<D, M, F, V><<<grid, kBlock, smem, stream>>>(                                            \
+    launch_chained(k_project_backward<D, M, F, V>, grid, kBlock, smem, stream,                                             \
         params, (uint32_t)n, cam, cam_device, records, radii, offsets, slot_gradients, capacity,               \
         gaussian_gradients, param_gradients, accumulate, camera_partials, camera_done, camera_gradient,        \
         densify_stats, fused, first_block, total_blocks);                                                      \

@@ -58,6 +58,7 @@ __global__ void __launch_bounds__(kBlock) k_emit(const float4* __restrict__ reco
                                                  Key* __restrict__ keys0, Key* __restrict__ keys1,
                                                  uint32_t* __restrict__ values0, uint32_t* __restrict__ values1,
                                                  uint32_t* __restrict__ histograms) {
+    chain_enter();
     __shared__ uint32_t hist[kSortMaxPasses][kSortRadix];
     const uint32_t t = threadIdx.x, lane = lane_id();
     // This frame's key geometry (k_scan_blocks): the passes it sorts, the tile shift, the
@@ -205,6 +206,7 @@ __global__ void __launch_bounds__(kSortThreads, kSortBlocksPerSM)
     k_sort_pass(int pass, uint32_t sequence, Key* keys0, uint32_t* values0, Key* keys1, uint32_t* values1,
                 const uint32_t* __restrict__ histogram, uint32_t* ticket, unsigned long long* lookback,
                 DeviceMeta* meta) {
+    chain_enter();
     // Passes past the ones this frame's keys need do nothing; the others ping-pong from the
     // buffer the emission started in.
     if (pass >= (int)meta->passes) return;
@@ -376,6 +378,7 @@ constexpr uint32_t kRangeItems = 4;
 template <typename Key>
 __global__ void __launch_bounds__(kBlock) k_ranges(const Key* __restrict__ keys, const DeviceMeta* __restrict__ meta,
                                                    uint32_t tiles, uint2* __restrict__ ranges) {
+    chain_enter();
     const uint32_t count = meta->count;
     const uint32_t tile_shift = meta->key_shift;
     const uint32_t threads = gridDim.x * blockDim.x;
@@ -425,7 +428,7 @@ cudaError_t launch_emit(const float4* records, uint32_t* offsets, const unsigned
                         uint32_t* sort_histograms, cudaStream_t stream) {
     const unsigned grid = grid_for(n, kBlock);
 #define SPLAT_EMIT(K, C)                                                                                          \
-    k_emit<K, C><<<grid, kBlock, 0, stream>>>(records, offsets, block_offsets, (uint32_t)n, cam.tiles_x, key_mode, \
+    launch_chained(k_emit<K, C>, grid, kBlock, 0, stream, records, offsets, block_offsets, (uint32_t)n, cam.tiles_x, key_mode, \
                                               meta, static_cast<K*>(keys0), static_cast<K*>(keys1), values0,      \
                                               values1, sort_histograms)
     if (plan.key64) {
@@ -455,7 +458,7 @@ cudaError_t launch_sort_pass(const SortPlan& plan, int pass, uint32_t sequence, 
             if (err != cudaSuccess) return err;
             configured = true;
         }
-        k_sort_pass<K><<<grid, kSortThreads, smem, stream>>>(pass, sequence, static_cast<K*>(keys0), values0,
+        launch_chained(k_sort_pass<K>, grid, kSortThreads, smem, stream, pass, sequence, static_cast<K*>(keys0), values0,
                                                              static_cast<K*>(keys1), values1, hist,
                                                              sort_tickets + pass, lookback, meta);
     } else {
@@ -468,7 +471,7 @@ cudaError_t launch_sort_pass(const SortPlan& plan, int pass, uint32_t sequence, 
             if (err != cudaSuccess) return err;
             configured = true;
         }
-        k_sort_pass<K><<<grid, kSortThreads, smem, stream>>>(pass, sequence, static_cast<K*>(keys0), values0,
+        launch_chained(k_sort_pass<K>, grid, kSortThreads, smem, stream, pass, sequence, static_cast<K*>(keys0), values0,
                                                              static_cast<K*>(keys1), values1, hist,
                                                              sort_tickets + pass, lookback, meta);
     }
@@ -480,10 +483,10 @@ cudaError_t launch_ranges(const SortPlan& plan, const void* keys, const DeviceMe
     const unsigned grid = (unsigned)std::min<uint64_t>(
         std::max<uint64_t>(grid_for((capacity + kRangeItems - 1) / kRangeItems, kBlock), 1), 148 * 8);
     if (plan.key64)
-        k_ranges<unsigned long long><<<grid, kBlock, 0, stream>>>(static_cast<const unsigned long long*>(keys), meta,
+        launch_chained(k_ranges<unsigned long long>, grid, kBlock, 0, stream, static_cast<const unsigned long long*>(keys), meta,
                                                                    tiles, ranges);
     else
-        k_ranges<uint32_t><<<grid, kBlock, 0, stream>>>(static_cast<const uint32_t*>(keys), meta, tiles, ranges);
+        launch_chained(k_ranges<uint32_t>, grid, kBlock, 0, stream, static_cast<const uint32_t*>(keys), meta, tiles, ranges);
     return cudaGetLastError();
 }
 
