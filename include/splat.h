@@ -312,9 +312,11 @@ sp_status sp_read_loss(sp_rasterizer* r, sp_loss_terms* out);        /* read_los
  * of `d_pixel_loss` (pixel_count x 4 floats, device) into `d_sums` (4 doubles, device), on
  * `stream` of device `device`, without allocating anything: for callers whose device memory
  * is owned by their own allocator or who cannot afford the device-wide synchronisation of a
- * cudaMalloc / cudaFree. Its scratch is a fixed 8 KiB array in the library that every GPU
- * loading the library keeps until exit; hence the limit: SP_ERR_INVALID for pixel_count 0
- * or above SP_NOALLOC_MAX_PIXELS. The first call on a device looks the array's device
+ * cudaMalloc / cudaFree. Its scratch is a fixed array in the library of 4 * 1024 + 1 doubles
+ * (32,776 bytes, about 32 KiB) that every GPU loading the library keeps until exit; hence the
+ * limit: SP_ERR_INVALID for pixel_count 0 or above SP_NOALLOC_MAX_PIXELS. `d_pixel_loss` must
+ * be 16-byte aligned and `d_sums` 8-byte aligned (SP_ERR_INVALID otherwise, checked before
+ * anything is enqueued). The first call on a device looks the array's device
  * address up (cudaGetSymbolAddress); make that first call before any stream capture. Every
  * call shares the array, so calls that overlap on the GPU race: order them on one stream.
  * Enqueues only; the sums are ready when the stream reaches them. */
@@ -339,7 +341,11 @@ sp_status sp_backward_adam(sp_rasterizer* r, sp_adam* adam, float position_rate_
  * buffers); then, if either
  * output is non-NULL, the camera gradient (56 B) and the loss terms (32 B) are copied to
  * pinned host memory and the stream is synchronised once — the per-step read-back the
- * reference's pose refinement does (training.rs:205-208). */
+ * reference's pose refinement does (training.rs:205-208). With that read-back the step's
+ * errors are reported: SP_ERR_TIMEOUT when a device wait gave up, SP_ERR_OVERFLOW when the
+ * forward pass had more (Gaussian, tile) pairs than the intersection list holds (the step
+ * ran on the truncated list; the reference's read_step_async panics there, training.rs:271
+ * and rasterizer.rs:536-544). */
 sp_status sp_train_step(sp_rasterizer* r, sp_adam* adam, const sp_camera_uniform* camera, uint32_t view,
                         float position_rate_factor, sp_camera_gradient* camera_gradient_out, sp_loss_terms* loss_out);
 /* Rasterizer::render (rasterizer.rs:552-564): set_camera, forward, overflow check, image. */
@@ -367,6 +373,14 @@ sp_status sp_clear_densify_stats(sp_rasterizer* r);
  * including the one that terminates the pixel; backward_pairs = sum over pixels of the
  * contributor count (the entries the backward replays). */
 sp_status sp_count_blend_work(sp_rasterizer* r, uint64_t* forward_pairs, uint64_t* backward_pairs);
+
+/* Error-path test switch (no counterpart in the reference): from the next forward pass on,
+ * sort partition `partition` of every sort pass never posts its digit counts, and its
+ * successors' look-back waits give up after a short limit (a few thousand polls) instead of
+ * the normal one, raising SP_ERR_TIMEOUT, which the next sp_read_intersections or
+ * sp_train_step returns; the scatter stays inside the key buffers (its order is then
+ * wrong). UINT32_MAX switches it off. For tests of the bounded device wait only. */
+sp_status sp_debug_stall_sort_partition(sp_rasterizer* r, uint32_t partition);
 
 /* ------------------------------------------------------------- per-kernel device timing */
 

@@ -13,7 +13,9 @@
  *   e^r, |r| <= ln2 / 2, by its Taylor series to degree 7 in Horner form (truncation
  *   error below 6e-9 relative), then scaling by 2^n through the exponent field.
  *
- * It is accurate to about 1 ulp (tests/test_oracle_math.py measures it against libm).
+ * It is within 1 ulp of the correctly rounded exp over its whole range (the correctly
+ * rounded result in more than 90 % of arguments), within 1 ulp of glibc's expf and within
+ * 2 ulp of CUDA's expf: tests/test_oracle_math.py measures all three.
  */
 #ifndef SPLAT_MATH_H
 #define SPLAT_MATH_H

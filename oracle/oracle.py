@@ -94,6 +94,33 @@ def camera_array(uniform) -> np.ndarray:
     return cam
 
 
+def camera_from_pinhole(rotation, translation, focal, principal_point, width: int, height: int) -> np.ndarray:
+    """PinholeCamera::uniform (camera.rs:46-70) in numpy: world-to-camera rows (R^T, -R^T c)
+    formed in f64 and rounded once to f32, focal and principal point to f32, tiles of 16
+    pixels rounded up. The 80-byte camera record the oracle's functions take."""
+    r = np.asarray(rotation, np.float64).reshape(3, 3)
+    c = [float(v) for v in np.asarray(translation, np.float64).reshape(3)]
+    w = r.T
+    cam = np.zeros(1, CAMERA_DTYPE)
+    for row in range(3):
+        # -(w[row, 0] c0 + w[row, 1] c1 + w[row, 2] c2), summed left to right as the reference.
+        t = -((float(w[row, 0]) * c[0] + float(w[row, 1]) * c[1]) + float(w[row, 2]) * c[2])
+        cam["rows"][0, row, :3] = w[row].astype(np.float32)
+        cam["rows"][0, row, 3] = np.float32(t)
+    cam["focal"][0] = np.array([focal[0], focal[1]], np.float64).astype(np.float32)
+    cam["principal_point"][0] = np.array([principal_point[0], principal_point[1]], np.float64).astype(np.float32)
+    cam["width"], cam["height"] = width, height
+    cam["tiles_x"], cam["tiles_y"] = (width + 15) // 16, (height + 15) // 16
+    return cam
+
+
+def camera_of(camera) -> np.ndarray:
+    """camera_from_pinhole of an object with the PinholeCamera fields (rotation, translation,
+    focal, principal_point, width, height)."""
+    return camera_from_pinhole(camera.rotation, camera.translation, camera.focal, camera.principal_point,
+                               camera.width, camera.height)
+
+
 def set_threads(threads: int) -> None:
     lib().or_set_threads(int(threads))
 

@@ -122,8 +122,8 @@ struct sp_rasterizer {
     // Pinned host staging of the per-step read-back (sp_train_step).
     struct StepReadback {
         float camera[SP_CAMERA_GRAD_STRIDE];
-        uint32_t status;  // DeviceMeta::status of the step
-        uint32_t pad;
+        uint32_t status;    // DeviceMeta::status of the step
+        uint32_t overflow;  // DeviceMeta::overflow of the step's forward pass
         double loss[4];
     };
     StepReadback* readback = nullptr;
@@ -255,9 +255,10 @@ void learning_rates_by_slot(const sp_learning_rates& rates, float position_scale
 
 namespace splat {
 // loss.cu: deterministic sum of the per-pixel loss terms into workspace[0..4) (the
-// workspace holds 4 + 4 * 256 + 1 doubles).
+// workspace holds 4 + 4 * 256 + 1 doubles); with `meta`, its status word and overflow flag
+// are copied into status_dst[0..2).
 cudaError_t launch_loss_sums(const float4* pixel_loss, uint64_t pixels, double* workspace, double* result,
-                             const uint32_t* status_src, uint32_t* status_dst, cudaStream_t stream);
+                             const DeviceMeta* meta, uint32_t* status_dst, cudaStream_t stream);
 }  // namespace splat
 
 extern "C" {
@@ -765,6 +766,12 @@ sp_status sp_read_loss(sp_rasterizer* r, sp_loss_terms* out) {
     return SP_OK;
 }
 
+static sp_status overflow_error(sp_rasterizer* r) {
+    return fail(r->ctx, SP_ERR_OVERFLOW,
+                "intersection list overflow: more than " + std::to_string(r->capacity) +
+                    " (Gaussian, tile) pairs; Gaussians are too large for the image");
+}
+
 sp_status sp_read_intersections(sp_rasterizer* r, sp_intersection_meta* out) {
     if (!r || !out) return SP_ERR_INVALID;
     SP_CHECK(select_device(r->ctx));
@@ -776,10 +783,7 @@ sp_status sp_read_intersections(sp_rasterizer* r, sp_intersection_meta* out) {
     out->overflow = meta.overflow;
     out->capacity = meta.capacity;
     // rasterizer.rs:536-544.
-    if (meta.overflow)
-        return fail(r->ctx, SP_ERR_OVERFLOW,
-                    "intersection list overflow: more than " + std::to_string(r->capacity) +
-                        " (Gaussian, tile) pairs; Gaussians are too large for the image");
+    if (meta.overflow) return overflow_error(r);
     return SP_OK;
 }
 
@@ -800,17 +804,22 @@ sp_status sp_train_step(sp_rasterizer* r, sp_adam* adam, const sp_camera_uniform
     if (loss_out) {
         // The loss-sum kernel also copies the step's status next to the camera gradient and the
         // sums: one copy brings the whole read-back.
-        SP_CUDA(r->ctx, launch_loss_sums(r->pixel_loss, r->pixels(), r->loss_sums, r->loss_result, &r->meta->status,
+        SP_CUDA(r->ctx, launch_loss_sums(r->pixel_loss, r->pixels(), r->loss_sums, r->loss_result, r->meta,
                                          &r->readback_dev->status, st));
         SP_CUDA(r->ctx, cudaMemcpyAsync(r->readback, r->readback_dev, sizeof(*r->readback), cudaMemcpyDeviceToHost, st));
     } else {
         SP_CUDA(r->ctx, cudaMemcpyAsync(&r->readback->status, &r->meta->status, sizeof(uint32_t),
+                                        cudaMemcpyDeviceToHost, st));
+        SP_CUDA(r->ctx, cudaMemcpyAsync(&r->readback->overflow, &r->meta->overflow, sizeof(uint32_t),
                                         cudaMemcpyDeviceToHost, st));
         SP_CUDA(r->ctx, cudaMemcpyAsync(r->readback->camera, r->camera_gradient, sizeof(r->readback->camera),
                                         cudaMemcpyDeviceToHost, st));
     }
     SP_CHECK(sync_stream(r->ctx));
     if (r->readback->status != 0) return device_status(r, nullptr);
+    // The step trained on a truncated intersection list: the error of the reference's
+    // read_step_async -> read_intersections_async (training.rs:271, rasterizer.rs:536-544).
+    if (r->readback->overflow) return overflow_error(r);
     if (camera_gradient_out) std::memcpy(camera_gradient_out, r->readback->camera, sizeof(sp_camera_gradient));
     if (loss_out) {
         const double pixels = (double)r->pixels();
@@ -1062,6 +1071,15 @@ sp_status sp_count_blend_work(sp_rasterizer* r, uint64_t* forward_pairs, uint64_
     *forward_pairs = host[0];
     *backward_pairs = host[1];
     return s;
+}
+
+sp_status sp_debug_stall_sort_partition(sp_rasterizer* r, uint32_t partition) {
+    if (!r) return SP_ERR_INVALID;
+    SP_CHECK(select_device(r->ctx));
+    const uint32_t value = partition == 0xffffffffu ? 0u : partition + 1u;
+    SP_CUDA(r->ctx, cudaMemcpyAsync(&r->meta->stall_partition, &value, sizeof(value), cudaMemcpyHostToDevice,
+                                    r->ctx->stream));
+    return sync_stream(r->ctx);
 }
 
 sp_status sp_profile_enable(sp_context* ctx, int enable) {

@@ -47,7 +47,10 @@ struct DeviceMeta {
     uint32_t passes;            // sort passes this frame needs (<= SortPlan::passes)
     uint32_t first_buffer;      // the emission's ping-pong buffer, so that the last pass
                                 // lands in buffer SortPlan::passes & 1
-    uint32_t pad[1];
+    // Error-path test switch (sp_debug_stall_sort_partition): partition stall_partition - 1 of
+    // every sort pass never posts its look-back record, and waits give up after a short limit;
+    // 0 (the default) is off. Set by the host only; no kernel writes it.
+    uint32_t stall_partition;
 };
 
 // Sort geometry decided on the host from the tile grid.

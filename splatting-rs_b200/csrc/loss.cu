@@ -336,11 +336,11 @@ constexpr int kSumBlocks = 256;
 // Sums of the 4 per-pixel loss terms in double, in a fixed order (each block a strided
 // share, a tree per block, then the last block adds the block sums in block order), so
 // that the reported loss does not depend on scheduling.
-// The last block also copies the step's status word (status_src, when given) next to the sums,
-// so that a step's read-back is one copy.
+// The last block also copies the step's status word and overflow flag (from `meta`, when
+// given) next to the sums, so that a step's read-back is one copy.
 __global__ void __launch_bounds__(kBlock) k_loss_sums(const float4* __restrict__ pixel_loss, uint64_t pixels,
                                                       double* __restrict__ workspace, double* __restrict__ result,
-                                                      const uint32_t* status_src, uint32_t* status_dst) {
+                                                      const DeviceMeta* meta, uint32_t* status_dst) {
     chain_enter();
     __shared__ double s[4][kBlock];
     __shared__ bool last;
@@ -379,15 +379,18 @@ __global__ void __launch_bounds__(kBlock) k_loss_sums(const float4* __restrict__
     }
     if (t == 0) {
         *done = 0;
-        if (status_src) *status_dst = *status_src;
+        if (meta) {
+            status_dst[0] = meta->status;
+            status_dst[1] = meta->overflow;
+        }
     }
 }
 
 }  // namespace
 
 cudaError_t launch_loss_sums(const float4* pixel_loss, uint64_t pixels, double* workspace, double* result,
-                             const uint32_t* status_src, uint32_t* status_dst, cudaStream_t stream) {
-    launch_chained(k_loss_sums, kSumBlocks, kBlock, 0, stream, pixel_loss, pixels, workspace, result, status_src, status_dst);
+                             const DeviceMeta* meta, uint32_t* status_dst, cudaStream_t stream) {
+    launch_chained(k_loss_sums, kSumBlocks, kBlock, 0, stream, pixel_loss, pixels, workspace, result, meta, status_dst);
     return cudaGetLastError();
 }
 

@@ -4,9 +4,11 @@
 // where a cudaMalloc / cudaFree, which synchronise the whole device, would stall them; such
 // callers pass their input and output buffers and need the library to bring nothing else.
 //
-// The reduction's scratch (one partial per block and a completion counter) therefore lives
-// in a fixed file-scope device array of 8 KiB, which every GPU that loads this library
-// holds until the process exits. That fixes the largest input: SP_NOALLOC_MAX_PIXELS pixels.
+// The reduction's scratch (four double partials per block and a completion counter)
+// therefore lives in a fixed file-scope device array of 4 * 1024 + 1 doubles (32,776 bytes,
+// about 32 KiB), which every GPU that loads this library holds until the process exits.
+// That fixes the largest input: SP_NOALLOC_MAX_PIXELS pixels (1024 blocks of 4096).
+#include <cstdint>
 #include <mutex>
 
 #include "kernels.h"
@@ -23,6 +25,7 @@ constexpr int kMaxDevices = 64;
 // every call on a device: the partials are overwritten by each call, the counter is
 // cleared by each call before its kernel runs, so calls that overlap on the GPU race.
 static __device__ __align__(256) double g_scratch[4 * kMaxBlocks + 1];
+static_assert(sizeof(g_scratch) == 32776, "the documented scratch size (include/splat.h) is 32,776 bytes");
 
 // Device address of g_scratch per device, looked up once per device (host code may not
 // take the symbol's address itself: on the host, `g_scratch` is only a stand-in).
@@ -91,6 +94,11 @@ extern "C" sp_status sp_loss_sums_noalloc(int device, const float* d_pixel_loss,
     using namespace splat;
     if (!d_pixel_loss || !d_sums) return SP_ERR_INVALID;
     if (pixel_count == 0 || pixel_count > SP_NOALLOC_MAX_PIXELS) return SP_ERR_INVALID;
+    // The kernel reads the pixels as float4 and writes the sums as doubles: a sub-view of a
+    // caller's buffer that is not aligned for them is refused here, before anything runs,
+    // instead of faulting on the device.
+    if ((reinterpret_cast<uintptr_t>(d_pixel_loss) & 15u) != 0 || (reinterpret_cast<uintptr_t>(d_sums) & 7u) != 0)
+        return SP_ERR_INVALID;
     if (device < 0 || device >= kMaxDevices) return SP_ERR_INVALID;
     int previous = 0;
     if (cudaGetDevice(&previous) != cudaSuccess) return SP_ERR_CUDA;

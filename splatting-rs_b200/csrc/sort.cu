@@ -10,6 +10,7 @@
 // "onesweep" radix sort of Adinets & Merrill, 2022). Passes only cover the significant
 // bits of the key (ceil(log2 tiles) + 20).
 #include <algorithm>
+#include <atomic>
 
 #include <cuda/atomic>
 
@@ -26,6 +27,8 @@ constexpr uint32_t kFlagInclusive = 2u;
 // limit is far above any legitimate wait (a predecessor partition takes microseconds) and
 // bounds a stuck wait to well under a second.
 constexpr uint32_t kLookbackSpinLimit = 1u << 21;
+// The limit while the error-path test switch (DeviceMeta::stall_partition) is on.
+constexpr uint32_t kLookbackSpinLimitTest = 1u << 12;
 constexpr int kLookbackWindow = 8;
 
 // The depth part of a key: the depth's float bits (FULL32), or its 20-bit depth key
@@ -230,6 +233,9 @@ __global__ void __launch_bounds__(kSortThreads, kSortBlocksPerSM)
     const uint32_t count = meta->count;
     const uint32_t partitions = meta->partitions;
     const uint32_t lanes_below = (1u << lane) - 1u;
+    // Error-path test switch: the partition that never posts (none when 0) and the short limit.
+    const uint32_t stalled = meta->stall_partition;
+    const uint32_t spin_limit = stalled ? kLookbackSpinLimitTest : kLookbackSpinLimit;
 
     // Exclusive scan over the digits of this pass's global histogram (thread t = digit t).
     auto block_exclusive = [&](uint32_t v) -> uint32_t {
@@ -298,10 +304,13 @@ __global__ void __launch_bounds__(kSortThreads, kSortBlocksPerSM)
                 lookback[(size_t)part * kSortRadix + t]);
             const unsigned long long tag = (unsigned long long)sequence << 32;
             uint32_t prefix = 0;
+            const bool posts = stalled == 0 || part != stalled - 1;
             if (part == 0) {
-                mine.store(tag | ((unsigned long long)kFlagInclusive << 30) | total, cuda::memory_order_relaxed);
+                if (posts)
+                    mine.store(tag | ((unsigned long long)kFlagInclusive << 30) | total, cuda::memory_order_relaxed);
             } else {
-                mine.store(tag | ((unsigned long long)kFlagAggregate << 30) | total, cuda::memory_order_relaxed);
+                if (posts)
+                    mine.store(tag | ((unsigned long long)kFlagAggregate << 30) | total, cuda::memory_order_relaxed);
                 // Walk back kLookbackWindow predecessors per round trip: read them all, then
                 // add in order up to the first inclusive prefix or the first not yet posted.
                 uint32_t spins = 0;
@@ -334,15 +343,16 @@ __global__ void __launch_bounds__(kSortThreads, kSortBlocksPerSM)
                     if (inclusive) break;
                     k -= taken;
                     if (waiting) {
-                        if (++spins > kLookbackSpinLimit) {
+                        if (++spins > spin_limit) {
                             raise_status(meta, SP_ERR_TIMEOUT);
                             break;
                         }
                         __nanosleep(32);
                     }
                 }
-                mine.store(tag | ((unsigned long long)kFlagInclusive << 30) | (prefix + total),
-                           cuda::memory_order_relaxed);
+                if (posts)
+                    mine.store(tag | ((unsigned long long)kFlagInclusive << 30) | (prefix + total),
+                               cuda::memory_order_relaxed);
             }
             s_out_base[t] = s_global_base[t] + prefix;
         }
@@ -379,7 +389,9 @@ template <typename Key>
 __global__ void __launch_bounds__(kBlock) k_ranges(const Key* __restrict__ keys, const DeviceMeta* __restrict__ meta,
                                                    uint32_t tiles, uint2* __restrict__ ranges) {
     chain_enter();
-    const uint32_t count = meta->count;
+    // A frame whose sort gave up (a look-back wait ran out) holds keys out of order: its tiles
+    // are all left empty, so that the blend kernels read nothing of it.
+    const uint32_t count = meta->status != 0 ? 0u : meta->count;
     const uint32_t tile_shift = meta->key_shift;
     const uint32_t threads = gridDim.x * blockDim.x;
     const uint32_t t = blockIdx.x * blockDim.x + threadIdx.x;
@@ -409,13 +421,20 @@ __global__ void __launch_bounds__(kBlock) k_ranges(const Key* __restrict__ keys,
     }
 }
 
+// The persistent grid of the current device (SM count x blocks per SM), looked up once per
+// device: a process may drive GPUs of different SM counts.
 int sort_grid() {
-    static int grid = 0;
+    constexpr int kDevices = 64;
+    static std::atomic<int> grids[kDevices];
+    int device = 0;
+    cudaGetDevice(&device);
+    if (device < 0 || device >= kDevices) device = 0;
+    int grid = grids[device].load(std::memory_order_relaxed);
     if (grid == 0) {
-        int device = 0, sms = 0;
-        cudaGetDevice(&device);
+        int sms = 0;
         cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
         grid = (sms > 0 ? sms : 148) * kSortBlocksPerSM;
+        grids[device].store(grid, std::memory_order_relaxed);
     }
     return grid;
 }

@@ -178,3 +178,58 @@ def parse_cameras_json(text: str, label: str) -> list[tuple[str, PinholeCamera]]
         out.append((name, PinholeCamera(np.array(rows, np.float64), np.array(position, np.float64), focal, principal,
                                         width, height)))
     return out
+
+
+# ------------------------------------------------------------------ training views (PNG)
+
+# training_frames.rs:16-20: what transparent pixels are blended onto, and the alpha from
+# which a pixel is foreground.
+BACKGROUND_RGB8 = (128, 128, 128)
+FOREGROUND_MIN_ALPHA = 128
+
+
+def training_view_from_rgba8(rgba: np.ndarray, camera: PinholeCamera) -> tuple[np.ndarray, np.ndarray]:
+    """training_view_from_image (training_frames.rs:71-115) at the camera's own size: the
+    colour composited on BACKGROUND_RGB8 by alpha in integer arithmetic
+    (composite_on_background, training_frames.rs:37-46), rgb = channel / 255 as float32, and
+    foreground = alpha >= 128. `rgba` is height x width x 4 uint8. Returns (rgb of P x 3,
+    foreground of P booleans). Views at another size than the camera's are refused (the
+    reference resizes them; the training path here takes views at the camera's size)."""
+    rgba = np.asarray(rgba)
+    if rgba.dtype != np.uint8 or rgba.ndim != 3 or rgba.shape[2] != 4:
+        raise SplatFileError("a training view is an RGBA image of 8-bit channels")
+    height, width = rgba.shape[:2]
+    if (width, height) != (camera.width, camera.height):
+        raise SplatFileError(f"the image is {width}x{height}, its camera is {camera.width}x{camera.height}")
+    alpha = rgba[:, :, 3:4].astype(np.uint32)
+    background = np.array(BACKGROUND_RGB8, np.uint32)
+    composited = (rgba[:, :, :3].astype(np.uint32) * alpha + background * (255 - alpha)) // 255
+    foreground = (rgba[:, :, 3] >= FOREGROUND_MIN_ALPHA).reshape(-1)
+    if not foreground.any():
+        raise SplatFileError("the view has no foreground pixel")
+    rgb = composited.astype(np.float32).reshape(-1, 3) / np.float32(255.0)
+    return rgb, foreground
+
+
+def read_training_view(path, camera: PinholeCamera) -> tuple[np.ndarray, np.ndarray]:
+    """load_training_view (training_frames.rs:60-66) of a PNG at the camera's size."""
+    from PIL import Image
+
+    with Image.open(path) as image:
+        rgba = np.asarray(image.convert("RGBA"))
+    return training_view_from_rgba8(rgba, camera)
+
+
+def read_fit_run(directory) -> tuple[GaussianCloud, list[PinholeCamera], np.ndarray]:
+    """A fit run's splat.ply, cameras.json and input_view{i}.png, as the reference's step
+    timing loads them (examples/step_timing.rs:31-40): the cloud, the cameras in file order and
+    the ground truth of every view (loss::ground_truth_rgba, loss.rs:95-104), views x P x 4."""
+    directory = Path(directory)
+    cloud = read_splat_ply(directory / "splat.ply")
+    cameras = [camera for _, camera in read_cameras_json(directory / "cameras.json")]
+    views = []
+    for i, camera in enumerate(cameras):
+        rgb, foreground = read_training_view(directory / f"input_view{i}.png", camera)
+        mask = foreground.astype(np.float32)[:, None]
+        views.append(np.concatenate([rgb * mask, mask], axis=1))
+    return cloud, cameras, np.stack(views)

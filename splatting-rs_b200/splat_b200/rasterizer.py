@@ -369,6 +369,13 @@ class Rasterizer:
             self._check(status, "read_intersections")
         return out
 
+    def debug_stall_sort_partition(self, partition: int | None) -> None:
+        """Error-path test switch (sp_debug_stall_sort_partition): sort partition `partition`
+        never posts its look-back record, so the next one's wait runs out (SP_ERR_TIMEOUT);
+        None switches it off."""
+        value = 0xFFFFFFFF if partition is None else int(partition)
+        self._check(self.lib.sp_debug_stall_sort_partition(self.handle, value), "debug_stall_sort_partition")
+
     def encode_backward_blend(self) -> None:
         """The blend half of encode_backward (sp_backward_blend)."""
         self._check(self.lib.sp_backward_blend(self.handle), "backward_blend")

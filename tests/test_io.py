@@ -15,7 +15,9 @@ import pytest
 import splat_b200 as sb
 from splat_b200 import io
 
-REFERENCE_EXAMPLE = Path("/root/reference/instantsplat-rs/web/example")
+# The reference's example scene (instantsplat-rs/web/example), copied out of the reference tree
+# by tests/golden/fetch_web_example.py (which __graft_entry__.build() runs where the tree is).
+REFERENCE_EXAMPLE = Path(__file__).resolve().parent / "golden" / "web_example"
 
 PROPERTIES_SH0 = ["x", "y", "z", "nx", "ny", "nz", "f_dc_0", "f_dc_1", "f_dc_2", "opacity", "scale_0", "scale_1",
                   "scale_2", "rot_0", "rot_1", "rot_2", "rot_3"]
@@ -196,9 +198,9 @@ def test_cameras_json_refusals(text, message):
         io.parse_cameras_json(text, "cameras.json")
 
 
-@pytest.mark.skipif(not REFERENCE_EXAMPLE.exists(), reason="the reference tree is not on this machine")
+@pytest.mark.skipif(not (REFERENCE_EXAMPLE / "splat.ply").exists(), reason="the example scene was not fetched")
 def test_reads_the_reference_example_files():
-    """The example splat and cameras the reference ships (web/example), read in place."""
+    """The example splat and cameras the reference ships (web/example)."""
     count, degree = io.read_splat_ply_header(REFERENCE_EXAMPLE / "splat.ply")
     cloud = io.read_splat_ply(REFERENCE_EXAMPLE / "splat.ply")
     assert len(cloud) == count > 0 and cloud.sh_degree == degree
@@ -210,3 +212,35 @@ def test_reads_the_reference_example_files():
     for _, camera in cameras:
         assert camera.width > 0 and camera.height > 0
         assert np.allclose(camera.rotation @ camera.rotation.T, np.eye(3), atol=1e-5)
+
+
+def test_training_view_composites_and_masks():
+    """training_view_from_image (training_frames.rs:71-115) at the camera's size: colours
+    blended onto the 128-grey background by alpha in integer arithmetic, foreground where
+    alpha >= 128 (the reference's composites_shrinks_and_masks test without its resize)."""
+    rgba = np.zeros((2, 3, 4), np.uint8)
+    rgba[0, 0] = [255, 0, 0, 255]    # opaque red
+    rgba[0, 1] = [0, 0, 255, 0]      # transparent: the hidden blue does not show
+    rgba[0, 2] = [200, 100, 50, 128]  # half: (c 128 + 128 127) / 255, foreground
+    rgba[1, :] = [10, 20, 30, 127]   # just below the foreground alpha
+    camera = sb.PinholeCamera(np.eye(3), np.zeros(3), (10.0, 10.0), (1.0, 0.5), 3, 2)
+    rgb, foreground = io.training_view_from_rgba8(rgba, camera)
+    assert foreground.tolist() == [True, False, True, False, False, False]
+    expect = lambda c, a: ((c * a + 128 * (255 - a)) // 255) / np.float32(255.0)  # noqa: E731
+    assert np.array_equal(rgb[0], np.array([1.0, expect(0, 255), expect(0, 255)], np.float32))
+    assert np.array_equal(rgb[1], np.full(3, np.float32(128) / np.float32(255), np.float32))
+    assert np.array_equal(rgb[2], np.array([expect(200, 128), expect(100, 128), expect(50, 128)], np.float32))
+    with pytest.raises(io.SplatFileError):
+        io.training_view_from_rgba8(rgba, camera.with_image_size(4, 2))
+    with pytest.raises(io.SplatFileError, match="no foreground"):
+        io.training_view_from_rgba8(np.zeros((2, 3, 4), np.uint8), camera)
+
+
+@pytest.mark.skipif(not (REFERENCE_EXAMPLE / "splat.ply").exists(), reason="the example scene was not fetched")
+def test_reads_the_reference_example_run():
+    """The example run as the reference's step timing loads it (examples/step_timing.rs:31-40)."""
+    cloud, cameras, gt = io.read_fit_run(REFERENCE_EXAMPLE)
+    assert len(cloud) == 222909 and cloud.sh_degree == 0 and len(cameras) == 6
+    assert gt.shape == (6, 392 * 518, 4)
+    assert np.all((gt[..., 3] == 0.0) | (gt[..., 3] == 1.0))
+    assert np.all(gt[..., :3] <= gt[..., 3:4])
