@@ -66,6 +66,7 @@ def parse_args():
     p.add_argument("--no-forward-3m", action="store_true", help="skip the forward-only config-3 measurement")
     p.add_argument("--forward-batches", type=int, default=3, help="timed passes over config 3's 64 cameras")
     p.add_argument("--no-densify", action="store_true", help="skip the device densification timing")
+    p.add_argument("--no-web-example", action="store_true", help="skip the timing on the reference's example scene")
     p.add_argument("--exchange", choices=["auto", "peer", "sharded", "allreduce"], default="auto",
                    help="multi-GPU exchange (auto: peer where the Gaussians split evenly, else all-reduce)")
     p.add_argument("--tiles", choices=["ellipse", "rectangle"], default="ellipse",
@@ -450,6 +451,80 @@ def config_dict(scene, world: int, exchange: str = "peer") -> dict:
     }
 
 
+# ------------------------------------------------------------------- the example scene
+
+
+WEB_EXAMPLE = ROOT / "tests" / "golden" / "web_example"
+# The reference's published step time on this scene (instantsplat-rs/src/gpu.rs:22-25):
+# examples/step_timing.rs, native wgpu on Metal, shader bounds checks off, Apple M5.
+WEB_EXAMPLE_PUBLISHED_MS = 36.0
+
+
+def web_example_timing(ctx, steps: int = 300, warmup: int = 10) -> dict | None:
+    """instantsplat-rs/examples/step_timing.rs on its own scene (web/example: the splat.ply of a
+    fit run, 222,909 SH-degree-0 Gaussians, 6 views of 392 x 518 with their PNG targets):
+    LEARNING_RATES_SHORT_RUN, views cycled in order, the position rate decayed over `steps`,
+    after `warmup` steps; "fixed" poses (one sp_train_step per step, nothing read back until
+    the end) and "refined" poses (sp_train_step_host_poses: the camera gradient read back and
+    the host pose step every step). Both with the benchmark's options, timed with CUDA events
+    around the loop and a final read of the loss, as the example times its loop."""
+    import torch
+
+    import splat_b200 as sb
+    from splat_b200 import io as splat_io
+
+    if not all((WEB_EXAMPLE / name).is_file() for name in ("splat.ply", "cameras.json", "input_view5.png")):
+        return None
+    cloud, cameras, gt_host = splat_io.read_fit_run(WEB_EXAMPLE)
+    w, h = cameras[0].width, cameras[0].height
+    gt = torch.from_numpy(gt_host.reshape(-1)).cuda()
+    packed = torch.from_numpy(cloud.to_packed()).cuda()
+    rates = sb.LEARNING_RATES_SHORT_RUN
+    extent = float(sb.cameras_extent(cameras))
+    uniforms = [c.uniform() for c in cameras]
+    out = {}
+    for label in ("fixed", "refined"):
+        params = packed.clone()
+        opts = sb.default_options(sh_degree=0, backward_mode=sb.SP_BWD_ATOMIC, tile_culling=sb.SP_TILES_ELLIPSE)
+        rast = sb.Rasterizer(ctx, params, len(cloud), w, h, gt, len(cameras), opts)
+        adam = sb.Adam(ctx, params, rast, len(cloud), rates, extent)
+        poses = sb.PoseRefinement(cameras, rates, extent) if label == "refined" else None
+
+        def step(i: int, total: int) -> None:
+            view = i % len(cameras)
+            factor = sb.position_rate_factor(i, total)
+            if poses is None:
+                rast.train_step(adam, uniforms[view], view, factor, read_back=False)
+            else:
+                rast.train_step_host_poses(adam, poses, view, factor)
+
+        for i in range(warmup):
+            step(i % len(cameras), steps)
+        rast.read_loss()
+        start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record()
+        for i in range(steps):
+            step(i, steps)
+        loss = rast.read_loss()
+        stop.record()
+        torch.cuda.synchronize()
+        ms = start.elapsed_time(stop) / steps
+        out[label] = {"ms_per_step": ms, "views_per_s": 1000.0 / ms, "loss_after": loss.total}
+        rast.close()
+        del adam, params
+    return {
+        "scene": f"instantsplat-rs/web/example: {len(cloud)} Gaussians SH0, {len(cameras)} views {w}x{h}, "
+                 "LEARNING_RATES_SHORT_RUN",
+        "steps": steps,
+        "warmup": warmup,
+        **out,
+        "published_reference_ms_per_step": WEB_EXAMPLE_PUBLISHED_MS,
+        "published_reference": "36 ms/step, Apple M5, wgpu/Metal, shader bounds checks off "
+                               "(instantsplat-rs/src/gpu.rs:22-25; examples/step_timing.rs)",
+        "speedup_vs_published_fixed": WEB_EXAMPLE_PUBLISHED_MS / out["fixed"]["ms_per_step"],
+    }
+
+
 # ------------------------------------------------------------------------------- main
 
 
@@ -772,6 +847,10 @@ def main() -> None:
     if world == 1 and not args.no_densify:
         densify = densify_timing(ctx, train_step.rasterizer, train_step.adam, float(extent), len(cloud))
 
+    web_example = None
+    if world == 1 and not args.no_web_example:
+        web_example = web_example_timing(ctx)
+
     forward_3m = None
     if not args.no_forward_3m:
         forward_3m = forward_throughput(args, ctx, rank, world, max_over_ranks, barrier)
@@ -833,6 +912,7 @@ def main() -> None:
             "intersections": int(meta.count),
             "mpix_per_s": value * width * height / 1e6,
             "fwd_mpix_per_s_3M": forward_3m,
+            "web_example": web_example,
             "densify": densify,
         }
         print(json.dumps(line), flush=True)

@@ -209,6 +209,57 @@ def blend_backward(proj, gauss, slots, ranges, cam, image, contrib, loss_gradien
     return out
 
 
+def blend_backward_magnitudes(proj, gauss, slots, ranges, cam, image, contrib, loss_gradient, capacity):
+    """blend_backward, and per slot the sums of the absolute values of its per-pixel terms
+    (float64, capacity x 10)."""
+    out = np.zeros(max(capacity, 1) * 10, np.float32)
+    mags = np.zeros(max(capacity, 1) * 10, np.float64)
+    g = np.ascontiguousarray(gauss if len(gauss) else np.zeros(1, np.uint32), np.uint32)
+    s = np.ascontiguousarray(slots if len(slots) else np.zeros(1, np.uint32), np.uint32)
+    lib().or_blend_backward_magnitudes(_p(proj), _p(g), _p(s), _p(ranges), _p(cam), _p(image), _p(contrib),
+                                       _p(np.ascontiguousarray(loss_gradient, np.float32)), _p(out), _p(mags))
+    return out, mags.reshape(-1, 10)
+
+
+def gaussian_sums_of_slots(fwd, slot_values: np.ndarray) -> np.ndarray:
+    """Per Gaussian, the float64 sum of its rectangle's slots (offsets[g] .. + tile count) of
+    `slot_values` (slots x k), as project_backward.wgsl:38-55 gathers them."""
+    proj = fwd["proj"]
+    count = ((proj["tile_max"][:, 0].astype(np.int64) - proj["tile_min"][:, 0]) *
+             (proj["tile_max"][:, 1].astype(np.int64) - proj["tile_min"][:, 1]))
+    count[proj["radius"] == 0] = 0
+    first = fwd["offsets"].astype(np.int64)
+    values = np.asarray(slot_values, np.float64)
+    csum = np.concatenate([np.zeros((1, values.shape[1])), np.cumsum(values, axis=0)])
+    last = np.minimum(first + count, len(values))
+    return csum[last] - csum[np.minimum(first, last)]
+
+
+def gradient_error_scale(params, sh_degree, cam, fwd, slot_magnitudes) -> np.ndarray:
+    """Per parameter gradient (n x stride, float64): sum over the 9 blend sums k of
+    |d gradient / d blend sum k| x (the sum of |terms| that blend sum k gathers). A rounding
+    of the blend's per-pixel terms by a relative e, in any order of summation, moves a
+    parameter gradient by at most about e x this scale: the tests' element-wise floor. The
+    projection backward is linear in the blend sums, so its Jacobian's columns come from
+    nine passes with a unit blend sum per Gaussian."""
+    params = np.ascontiguousarray(params, np.float32)
+    stride = 11 + 3 * (sh_degree + 1) ** 2
+    n = params.size // stride
+    count = int(fwd["meta"]["count"])
+    magnitude = gaussian_sums_of_slots(fwd, np.asarray(slot_magnitudes)[:, :9])
+    scale = np.zeros((n, stride), np.float64)
+    first = fwd["offsets"].astype(np.int64)
+    visible = np.nonzero(fwd["proj"]["radius"])[0]
+    visible = visible[first[visible] < count]
+    for k in range(9):
+        unit = np.zeros((max(count, 1), 10), np.float32)
+        unit[first[visible], k] = 1.0
+        column, _, _ = project_backward(params, sh_degree, cam, fwd["proj"], fwd["offsets"], unit.reshape(-1),
+                                        count)
+        scale += np.abs(column.reshape(n, stride).astype(np.float64)) * magnitude[:, k:k + 1]
+    return scale
+
+
 def project_backward(params, sh_degree, cam, proj, offsets, slot_gradients, capacity, stats=None):
     stride = 11 + 3 * (sh_degree + 1) ** 2
     params = np.ascontiguousarray(params, np.float32)

@@ -543,9 +543,13 @@ void or_loss(const float* image, const float* gt, const float* partials, uint32_
         }
 }
 
-void or_blend_backward(const sp_projected* proj, const uint32_t* sorted_gaussians, const uint32_t* sorted_slots,
-                       const uint32_t* ranges, const sp_camera_uniform* cam, const float* image,
-                       const uint32_t* contributions, const float* loss_gradient, float* intersection_gradients) {
+// The blend backward; with `magnitudes` non-null, each slot also receives the sums of the
+// absolute values of the same terms (in double), from which the tests bound the rounding
+// error that any other summation order of the terms may carry.
+static void blend_backward(const sp_projected* proj, const uint32_t* sorted_gaussians, const uint32_t* sorted_slots,
+                           const uint32_t* ranges, const sp_camera_uniform* cam, const float* image,
+                           const uint32_t* contributions, const float* loss_gradient, float* intersection_gradients,
+                           double* magnitudes) {
     const int64_t tiles = (int64_t)cam->tiles_x * cam->tiles_y;
 #pragma omp parallel for schedule(dynamic, 4) num_threads(threads())
     for (int64_t tile = 0; tile < tiles; ++tile) {
@@ -554,6 +558,7 @@ void or_blend_backward(const sp_projected* proj, const uint32_t* sorted_gaussian
         const uint32_t count = end - start;
         if (count == 0) continue;
         std::vector<float> sums((size_t)count * SP_GRAD_STRIDE, 0.0f);
+        std::vector<double> mags(magnitudes ? (size_t)count * SP_GRAD_STRIDE : 0, 0.0);
         for (uint32_t ly = 0; ly < SP_TILE; ++ly)
             for (uint32_t lx = 0; lx < SP_TILE; ++lx) {
                 const uint32_t px = gx * SP_TILE + lx, py = gy * SP_TILE + ly;
@@ -583,24 +588,52 @@ void or_blend_backward(const sp_projected* proj, const uint32_t* sorted_gaussian
                     for (int c = 0; c < 4; ++c)
                         d_alpha += gradient[c] * (color[c] * transmittance - behind[c] / (1.0f - alpha));
                     float* s = &sums[(size_t)j * SP_GRAD_STRIDE];
-                    for (int c = 0; c < 3; ++c) s[5 + c] += gradient[c] * alpha * transmittance;
+                    float term[SP_GRAD_STRIDE] = {};
+                    for (int c = 0; c < 3; ++c) term[5 + c] = gradient[c] * alpha * transmittance;
                     for (int c = 0; c < 4; ++c) behind[c] += color[c] * alpha * transmittance;
-                    if (alpha_unclamped < SP_MAX_ALPHA) {
-                        s[8] += d_alpha * gaussian;
+                    const bool unclamped = alpha_unclamped < SP_MAX_ALPHA;
+                    if (unclamped) {
+                        term[8] = d_alpha * gaussian;
                         const float d_power = d_alpha * opacity * gaussian;
-                        s[0] += -d_power * (conic[0] * d[0] + conic[1] * d[1]);
-                        s[1] += -d_power * (conic[1] * d[0] + conic[2] * d[1]);
-                        s[2] += -0.5f * d_power * d[0] * d[0];
-                        s[3] += -d_power * d[0] * d[1];
-                        s[4] += -0.5f * d_power * d[1] * d[1];
+                        term[0] = -d_power * (conic[0] * d[0] + conic[1] * d[1]);
+                        term[1] = -d_power * (conic[1] * d[0] + conic[2] * d[1]);
+                        term[2] = -0.5f * d_power * d[0] * d[0];
+                        term[3] = -d_power * d[0] * d[1];
+                        term[4] = -0.5f * d_power * d[1] * d[1];
+                    }
+                    for (int c = 5; c < 8; ++c) s[c] += term[c];
+                    if (unclamped)
+                        for (int c : {8, 0, 1, 2, 3, 4}) s[c] += term[c];
+                    if (magnitudes) {
+                        double* m = &mags[(size_t)j * SP_GRAD_STRIDE];
+                        for (int c = 0; c < 9; ++c) m[c] += std::fabs((double)term[c]);
                     }
                 }
             }
         for (uint32_t j = 0; j < count; ++j) {
             float* out = intersection_gradients + (uint64_t)sorted_slots[start + j] * SP_GRAD_STRIDE;
             for (int c = 0; c < SP_GRAD_STRIDE; ++c) out[c] = sums[(size_t)j * SP_GRAD_STRIDE + c];
+            if (magnitudes) {
+                double* m = magnitudes + (uint64_t)sorted_slots[start + j] * SP_GRAD_STRIDE;
+                for (int c = 0; c < SP_GRAD_STRIDE; ++c) m[c] = mags[(size_t)j * SP_GRAD_STRIDE + c];
+            }
         }
     }
+}
+
+void or_blend_backward(const sp_projected* proj, const uint32_t* sorted_gaussians, const uint32_t* sorted_slots,
+                       const uint32_t* ranges, const sp_camera_uniform* cam, const float* image,
+                       const uint32_t* contributions, const float* loss_gradient, float* intersection_gradients) {
+    blend_backward(proj, sorted_gaussians, sorted_slots, ranges, cam, image, contributions, loss_gradient,
+                   intersection_gradients, nullptr);
+}
+
+void or_blend_backward_magnitudes(const sp_projected* proj, const uint32_t* sorted_gaussians,
+                                  const uint32_t* sorted_slots, const uint32_t* ranges, const sp_camera_uniform* cam,
+                                  const float* image, const uint32_t* contributions, const float* loss_gradient,
+                                  float* intersection_gradients, double* magnitudes) {
+    blend_backward(proj, sorted_gaussians, sorted_slots, ranges, cam, image, contributions, loss_gradient,
+                   intersection_gradients, magnitudes);
 }
 
 void or_project_backward(const float* params, uint64_t n, uint32_t sh_degree, const sp_camera_uniform* cam,

@@ -60,6 +60,14 @@ void or_blend_backward(const sp_projected* proj, const uint32_t* sorted_gaussian
                        const uint32_t* ranges, const sp_camera_uniform* cam, const float* image,
                        const uint32_t* contributions, const float* loss_gradient, float* intersection_gradients);
 
+/* or_blend_backward, and into `magnitudes` (capacity * 10 doubles) per slot the sums of the
+ * absolute values of the same per-pixel terms: the scale of the rounding error any other
+ * order of summing them can carry (for the tests' element-wise bars). */
+void or_blend_backward_magnitudes(const sp_projected* proj, const uint32_t* sorted_gaussians,
+                                  const uint32_t* sorted_slots, const uint32_t* ranges, const sp_camera_uniform* cam,
+                                  const float* image, const uint32_t* contributions, const float* loss_gradient,
+                                  float* intersection_gradients, double* magnitudes);
+
 /* project_backward.wgsl:30-227 + reduce_camera_gradient.wgsl:10-34 (+ SH degree 1-3).
  * param_gradients: n * stride (overwritten); camera_gradient: 14; stats: n (added to). */
 void or_project_backward(const float* params, uint64_t n, uint32_t sh_degree, const sp_camera_uniform* cam,

@@ -16,7 +16,12 @@
 //
 // The arithmetic per (pixel, Gaussian) is the reference's; exp is the hardware 2^x
 // approximation of e^x, and the backward divides by (1 - alpha) through one reciprocal, so
-// images and gradients match the oracle within a tolerance rather than bit for bit.
+// images and gradients match the oracle within a tolerance rather than bit for bit. The
+// decisions that depend on alpha's last bits do not depend on that exp: whether a pixel takes
+// a Gaussian (alpha >= 1/255) and whether its alpha is clamped at 0.99 are tests of the
+// falloff's power (which is the oracle's bit for bit) against the Gaussian's thresholds in
+// record word [3], which the projection derived from the shared, monotone sp_expf; only the
+// termination test (transmittance below 1e-4) reads the blended alpha.
 #include "kernels.h"
 
 namespace splat {
@@ -139,7 +144,7 @@ __device__ __forceinline__ bool reaches(float4 a, float4 b, float4 r, float x0, 
 struct WarpStage {
     float4 a[32];     // mean.x, mean.y, conic.a, conic.b
     float4 b[32];     // conic.c, opacity, colour.r, colour.g
-    float c[32];      // colour.b
+    float4 c[32];     // colour.b, take_from, clamp_from (record word [3]), 0
     uint32_t j[32];   // index in the tile list
     uint32_t g[32];   // Gaussian
 };
@@ -152,15 +157,15 @@ __device__ __forceinline__ uint32_t stage_chunk(const float4* __restrict__ recor
                                                 uint32_t end, float x0, float y0, uint32_t lane, WarpStage& st) {
     const uint32_t j = base + lane;
     bool take = false;
-    float4 a, b;
-    float c = 0.0f;
+    float4 a, b, c;
     uint32_t g = 0;
     if (j < end) {
         g = sorted[first + j];
         const float4* rec = records + (size_t)g * kRecord;
         a = rec[0];
         b = rec[1];
-        c = rec[2].x;
+        const float2 thresholds = *reinterpret_cast<const float2*>(rec + 3);
+        c = make_float4(rec[2].x, thresholds.x, thresholds.y, 0.0f);
         take = reaches<ROWS>(a, b, reach[g], x0, y0);
     }
     const uint32_t ballot = __ballot_sync(kFull, take);
@@ -206,6 +211,7 @@ constexpr int kDirectAtomicLanes = 8;
 struct Falloff {
     float dx;
     float2 dy;
+    float2 power;
     float2 gaussian;
     bool below0, below1;  // power <= 0
 };
@@ -216,6 +222,7 @@ __device__ __forceinline__ Falloff falloff(float4 a, float4 b, float fpx, float2
     f.dy = add2(splat(a.y), neg2(fpy));
     const float2 quad = add2(splat(__fmul_rn(__fmul_rn(a.z, f.dx), f.dx)), mul2(mul2(splat(b.x), f.dy), f.dy));
     const float2 power = add2(mul2(splat(-0.5f), quad), neg2(mul2(splat(__fmul_rn(a.w, f.dx)), f.dy)));
+    f.power = power;
     f.below0 = power.x <= 0.0f;
     f.below1 = power.y <= 0.0f;
     const float2 power2 = mul2(power, splat(kLog2e));
@@ -225,11 +232,11 @@ __device__ __forceinline__ Falloff falloff(float4 a, float4 b, float fpx, float2
 
 // falloff() at one pixel, with the same roundings (for the one-pixel-per-thread kernels).
 __device__ __forceinline__ float falloff1(float4 a, float4 b, float fpx, float fpy, float& dx, float& dy,
-                                          bool& below) {
+                                          bool& below, float& power) {
     dx = a.x - fpx;
     dy = __fadd_rn(a.y, -fpy);
     const float quad = __fadd_rn(__fmul_rn(__fmul_rn(a.z, dx), dx), __fmul_rn(__fmul_rn(b.x, dy), dy));
-    const float power = __fadd_rn(__fmul_rn(-0.5f, quad), -__fmul_rn(__fmul_rn(a.w, dx), dy));
+    power = __fadd_rn(__fmul_rn(-0.5f, quad), -__fmul_rn(__fmul_rn(a.w, dx), dy));
     below = power <= 0.0f;
     return exp2_approx(__fmul_rn(power, kLog2e));
 }
@@ -269,11 +276,12 @@ __global__ void __launch_bounds__(kPairThreads, 8) k_blend_forward(const float4*
             stage_chunk<8>(records, reach, sorted, range.x, base, count, (float)bx, (float)by, lane, st);
         for (uint32_t i = 0; i < n && !(done0 && done1); ++i) {
             const float4 a = st.a[i], b = st.b[i];
+            const float2 c = *reinterpret_cast<const float2*>(&st.c[i]);  // colour.b, take_from
             const Falloff f = falloff(a, b, fpx, fpy);
             const float2 unclamped = mul2(splat(b.y), f.gaussian);
             const float2 alpha = make_float2(fminf(SP_MAX_ALPHA, unclamped.x), fminf(SP_MAX_ALPHA, unclamped.y));
-            bool take0 = !done0 && f.below0 && alpha.x >= SP_MIN_ALPHA;
-            bool take1 = !done1 && f.below1 && alpha.y >= SP_MIN_ALPHA;
+            bool take0 = !done0 && f.below0 && f.power.x >= c.y;
+            bool take1 = !done1 && f.below1 && f.power.y >= c.y;
             const float2 next = mul2(transmittance, add2(splat(1.0f), neg2(alpha)));
             // A pixel whose transmittance would fall below the floor ends before this one.
             const bool end0 = take0 && next.x < SP_MIN_TRANSMITTANCE, end1 = take1 && next.y < SP_MIN_TRANSMITTANCE;
@@ -286,7 +294,7 @@ __global__ void __launch_bounds__(kPairThreads, 8) k_blend_forward(const float4*
             w.y = take1 ? w.y : 0.0f;
             cr = fma2(splat(b.z), w, cr);
             cg = fma2(splat(b.w), w, cg);
-            cb = fma2(splat(st.c[i]), w, cb);
+            cb = fma2(splat(c.x), w, cb);
             const uint32_t j1 = st.j[i] + 1;
             if (take0) {
                 transmittance.x = next.x;
@@ -358,7 +366,7 @@ __global__ void __launch_bounds__(kTilePixels) k_blend_backward(
     constexpr int B = kDet ? kDeterministicBatch : kBatch;
     __shared__ float4 s_a[B];
     __shared__ float4 s_b[B];
-    __shared__ float s_c[B];
+    __shared__ float4 s_c[B];  // colour.b, take_from, clamp_from, 0
     __shared__ uint32_t s_g[B];
     __shared__ uint8_t s_mask[B];
     __shared__ uint16_t s_list[kWarps][B];
@@ -405,7 +413,8 @@ __global__ void __launch_bounds__(kTilePixels) k_blend_backward(
             s_g[t] = g;
             s_a[t] = a;
             s_b[t] = b;
-            s_c[t] = rec[2].x;
+            const float2 thresholds = *reinterpret_cast<const float2*>(rec + 3);
+            s_c[t] = make_float4(rec[2].x, thresholds.x, thresholds.y, 0.0f);
             s_mask[t] = (uint8_t)warp_mask(a, b, gx, gy);
         }
         if (kDet)
@@ -424,18 +433,19 @@ __global__ void __launch_bounds__(kTilePixels) k_blend_backward(
             if (j < contributed) {
                 const float4 a = s_a[k];
                 const float4 b = s_b[k];
-                float dx, dy;
+                const float4 c = s_c[k];
+                float dx, dy, power;
                 bool below;
-                const float gaussian = falloff1(a, b, fpx, fpy, dx, dy, below);
+                const float gaussian = falloff1(a, b, fpx, fpy, dx, dy, below, power);
                 if (below) {
                     const float opacity = b.y;
                     const float alpha_unclamped = opacity * gaussian;
                     const float alpha = fminf(SP_MAX_ALPHA, alpha_unclamped);
-                    if (alpha >= SP_MIN_ALPHA) {
+                    if (power >= c.y) {
                         active = true;
                         const float inv = __fdividef(1.0f, 1.0f - alpha);
                         transmittance = transmittance * inv;
-                        const float cr = b.z, cgr = b.w, cbl = s_c[k];
+                        const float cr = b.z, cgr = b.w, cbl = c.x;
                         const float d_alpha = grad.x * (cr * transmittance - behind_r * inv) +
                                               grad.y * (cgr * transmittance - behind_g * inv) +
                                               grad.z * (cbl * transmittance - behind_b * inv) -
@@ -447,7 +457,7 @@ __global__ void __launch_bounds__(kTilePixels) k_blend_backward(
                         behind_r += cr * w;
                         behind_g += cgr * w;
                         behind_b += cbl * w;
-                        if (alpha_unclamped < SP_MAX_ALPHA) {
+                        if (power < c.z) {
                             v[8] = d_alpha * gaussian;
                             const float d_power = d_alpha * opacity * gaussian;
                             v[0] = -d_power * (a.z * dx + a.w * dy);
@@ -550,11 +560,12 @@ __global__ void __launch_bounds__(kPairThreads, 6) k_blend_backward_atomic(
         for (int i = (int)n - 1; i >= 0; --i) {
             const uint32_t j = st.j[i];
             const float4 a = st.a[i], b = st.b[i];
+            const float4 c = st.c[i];  // colour.b, take_from, clamp_from
             const Falloff f = falloff(a, b, fpx, fpy);
             const float2 unclamped = mul2(splat(b.y), f.gaussian);
             float2 alpha = make_float2(fminf(SP_MAX_ALPHA, unclamped.x), fminf(SP_MAX_ALPHA, unclamped.y));
-            const bool take0 = j < contributed0 && f.below0 && alpha.x >= SP_MIN_ALPHA;
-            const bool take1 = j < contributed1 && f.below1 && alpha.y >= SP_MIN_ALPHA;
+            const bool take0 = j < contributed0 && f.below0 && f.power.x >= c.y;
+            const bool take1 = j < contributed1 && f.below1 && f.power.y >= c.y;
             const uint32_t active = __ballot_sync(kFull, take0 || take1);
             if (!active) continue;
             alpha.x = take0 ? alpha.x : 0.0f;
@@ -564,7 +575,7 @@ __global__ void __launch_bounds__(kPairThreads, 6) k_blend_backward_atomic(
             const float2 divided = mul2(transmittance, inv);
             transmittance.x = take0 ? divided.x : transmittance.x;
             transmittance.y = take1 ? divided.y : transmittance.y;
-            const float cbl = st.c[i];
+            const float cbl = c.x;
             const float2 g_dot_c = fma2(gb, splat(cbl), fma2(gg, splat(b.w), mul2(gr, splat(b.z))));
             const float2 g_dot_behind = fma2(gb, behind_b, fma2(gg, behind_g, fma2(gr, behind_r, behind_t)));
             const float2 d_alpha = fma2(neg2(inv), g_dot_behind, mul2(transmittance, g_dot_c));
@@ -574,8 +585,8 @@ __global__ void __launch_bounds__(kPairThreads, 6) k_blend_backward_atomic(
             behind_g = fma2(splat(b.w), w, behind_g);
             behind_b = fma2(splat(cbl), w, behind_b);
             // The clamp at 0.99 passes no gradient to opacity or the falloff.
-            const float2 gate = make_float2(take0 && unclamped.x < SP_MAX_ALPHA ? f.gaussian.x : 0.0f,
-                                            take1 && unclamped.y < SP_MAX_ALPHA ? f.gaussian.y : 0.0f);
+            const float2 gate = make_float2(take0 && f.power.x < c.z ? f.gaussian.x : 0.0f,
+                                            take1 && f.power.y < c.z ? f.gaussian.y : 0.0f);
             const float2 d_opacity = mul2(d_alpha, gate);
             const float2 nd_power = mul2(d_opacity, splat(-b.y));  // -dL/dpower
             const float2 d_mx = mul2(nd_power, fma2(splat(a.w), f.dy, splat(a.z * f.dx)));
@@ -677,12 +688,11 @@ __global__ void __launch_bounds__(kTilePixels) k_count_blend(const float4* __res
             ++visited;
             const float4* rec = records + (size_t)sorted[j] * kRecord;
             const float4 a = rec[0], b = rec[1];
-            float dx, dy;
+            float dx, dy, power;
             bool below;
-            const float gaussian = falloff1(a, b, fpx, fpy, dx, dy, below);
-            if (!below) continue;
+            const float gaussian = falloff1(a, b, fpx, fpy, dx, dy, below, power);
+            if (!below || power < rec[3].x) continue;
             const float alpha = fminf(SP_MAX_ALPHA, b.y * gaussian);
-            if (alpha < SP_MIN_ALPHA) continue;
             const float next = transmittance * (1.0f - alpha);
             if (next < SP_MIN_TRANSMITTANCE) break;
             transmittance = next;

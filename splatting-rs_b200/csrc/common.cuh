@@ -16,14 +16,20 @@ namespace splat {
 constexpr int kBlock = 256;                 // threads of every 1-D kernel
 constexpr int kTilePixels = SP_TILE * SP_TILE;
 
-// Per-Gaussian blend record written by the projection, 3 float4 (48 B, 16-B aligned):
+// Per-Gaussian blend record written by the projection, 4 float4 (64 B: each record is two
+// whole 32-B L2 sectors):
 //   [0] mean.x, mean.y, conic.a, conic.b
 //   [1] conic.c, opacity, colour.r, colour.g
 //   [2] colour.b, depth, tile_min (x | y << 16), tile_max (x | y << 16)  (bit patterns)
+//   [3] take_from, clamp_from, 0, 0: the blend's alpha decisions as thresholds on the
+//       falloff's power (alpha_thresholds in project.cu): a pixel takes the Gaussian exactly
+//       when power >= take_from (opacity * e^power >= 1/255, rasterize_forward.wgsl:66-68)
+//       and its alpha is clamped to 0.99 exactly when power >= clamp_from (opacity * e^power
+//       >= 0.99); +inf where never.
 // The fields of the reference's 80-B `Projected` (common.wgsl:49-61) that the blend and
 // binning read, without its padding; the radius lives in its own array. A culled Gaussian
 // has an all-zero record and radius 0, as the reference's zeroed `Projected`.
-constexpr int kRecord = 3;
+constexpr int kRecord = 4;
 
 // Device-side bookkeeping of one forward pass (the reference's IntersectionMeta and
 // ScanControl, rasterizer.rs:29-44), plus the status word device code raises errors in.

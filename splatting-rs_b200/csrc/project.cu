@@ -51,10 +51,43 @@ __device__ __forceinline__ uint32_t block_exclusive_scan(uint32_t value, uint32_
     return before + inclusive - value;
 }
 
+// The smallest float power p <= 0 at which opacity * sp_expf(p) >= level in float arithmetic
+// (+inf when not even at p = 0). sp_expf is monotone (include/splat_math.h), so the blend's
+// per-pixel test "opacity * exp(power) >= level", as the oracle evaluates it, holds exactly
+// when power >= this threshold, whatever exp the blend kernels use for the alpha's value.
+// Searched over the float order of -p in [0, 104]: from a double-precision log guess, a
+// bracket of 16 floats either side (widened to the whole range if the guess was off), then
+// bisection.
+__device__ __noinline__ float alpha_threshold(float opacity, float level) {
+    if (!(opacity >= level)) return INFINITY;
+    auto holds = [&](uint32_t u) { return __fmul_rn(opacity, sp_expf(-__uint_as_float(u))) >= level; };
+    const uint32_t last = __float_as_uint(104.0f);  // sp_expf(-104) is 0: never holds there
+    const double guess = -log((double)level / (double)opacity);
+    const uint32_t g = guess > 0.0 ? min(__float_as_uint((float)guess), last) : 0u;
+    // holds(lo) and !holds(hi): the answer is -float(lo) for the largest such lo.
+    uint32_t lo = g > 16u ? g - 16u : 0u, hi = min(g + 16u, last);
+    if (!holds(lo) || holds(hi)) {
+        lo = 0u;
+        hi = last;
+    }
+    while (hi - lo > 1u) {
+        const uint32_t mid = lo + (hi - lo) / 2u;
+        if (holds(mid)) lo = mid;
+        else hi = mid;
+    }
+    return -__uint_as_float(lo);
+}
+
+// The blend's decision thresholds of a Gaussian of opacity `opacity` (record word [3]).
+__device__ __forceinline__ float4 alpha_thresholds(float opacity) {
+    return make_float4(alpha_threshold(opacity, SP_MIN_ALPHA), alpha_threshold(opacity, SP_MAX_ALPHA), 0.0f, 0.0f);
+}
+
 template <int DEG>
-__device__ __forceinline__ void project_one(const float* p, const sp_camera_uniform& cam, float4 rec[3],
+__device__ __forceinline__ void project_one(const float* p, const sp_camera_uniform& cam, float4 rec[kRecord],
                                             uint32_t* radius_out, uint32_t* count_out) {
     rec[0] = rec[1] = rec[2] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    rec[3] = make_float4(INFINITY, INFINITY, 0.0f, 0.0f);
     *radius_out = 0;
     *count_out = 0;
     const float (*rows)[4] = cam.world_to_camera_rows;
@@ -84,6 +117,7 @@ __device__ __forceinline__ void project_one(const float* p, const sp_camera_unif
     rec[0] = make_float4(mean0, mean1, conic0, conic1);
     rec[1] = make_float4(conic2, opacity, max_of(0.0f, col[0]), max_of(0.0f, col[1]));
     rec[2] = make_float4(max_of(0.0f, col[2]), g.pc[2], __uint_as_float(rect_lo), __uint_as_float(rect_hi));
+    rec[3] = alpha_thresholds(opacity);
     *radius_out = (uint32_t)radius;
     *count_out = (uint32_t)cnt;
 }
@@ -144,13 +178,12 @@ __global__ void __launch_bounds__(kBlock) k_project(const float* __restrict__ pa
     const uint32_t t = threadIdx.x;
     uint32_t count = 0;
     if (t < here) {
-        float4 rec[3];
+        float4 rec[kRecord];
         uint32_t radius;
         project_one<DEG>(sp + t * S, cam, rec, &radius, &count);
         float4* out = records + (size_t)(g0 + t) * kRecord;
-        out[0] = rec[0];
-        out[1] = rec[1];
-        out[2] = rec[2];
+#pragma unroll
+        for (int k = 0; k < kRecord; ++k) out[k] = rec[k];
         radii[g0 + t] = radius;
         reach[g0 + t] = radius > 0 ? reach_of(rec[0], rec[1]) : make_float4(-1.0f, -1.0f, 0.0f, 0.0f);
         if (cull && count) {

@@ -5,8 +5,11 @@ It decides the Gaussians' scales (exp of the log-scales), the opacity sigmoid an
 window, so it is measured over the whole float range it accepts and, densely, over the
 arguments those uses meet (log-scales and negated opacity logits within [-16, 16], window
 exponents within [-6, 0]):
-  - against the correctly rounded exp (float64 exp rounded once to float32): at most 1 ulp
-    on normal results, and the same on subnormal ones;
+  - against the correctly rounded exp (float64 exp rounded once to float32): equal on more
+    than 99.99 % of the arguments and never more than 1 ulp apart (an exhaustive run over
+    every float in [-105, 88.72] against the long-double exp found no difference at all);
+  - monotone non-decreasing over the sampled arguments in increasing order (the blend kernels
+    rely on it; the exhaustive run over every float in [-105, 1] found no decrease);
   - against the host libm's expf (glibc, the oracle's and the reference's host exp): at most
     1 ulp apart;
   - against CUDA's expf (torch.exp on a float32 CUDA tensor; CUDA documents a 2-ulp bound for
@@ -58,8 +61,14 @@ def test_sp_expf_within_one_ulp_of_the_correctly_rounded_exp(table):
     subnormal = (want > 0) & ~normal
     if subnormal.any():
         assert _ulp(got[subnormal], want[subnormal]).max() <= 1
-    # Most results are the correctly rounded ones.
-    assert np.mean(got[normal] == want[normal]) > 0.9
+    # The results are the correctly rounded ones.
+    assert np.mean(got[normal] == want[normal]) > 0.9999
+
+
+def test_sp_expf_is_monotone(table):
+    xs, got, _ = table
+    order = np.argsort(xs, kind="stable")
+    assert np.all(np.diff(got[order].astype(np.float64)) >= 0.0)
 
 
 def test_sp_expf_within_one_ulp_of_libm(table):
