@@ -471,6 +471,74 @@ sp_status sp_peer_exchange_create(sp_adam* adam, uint32_t rank, uint32_t world, 
 /* Enqueues the exchange and the Adam step (position_rate_factor as sp_adam_step). */
 sp_status sp_peer_exchange_step(sp_peer_exchange* exchange, float position_rate_factor);
 void sp_peer_exchange_destroy(sp_peer_exchange* exchange);
+/* ------------------------------------------ multi-GPU through the library: communicator */
+
+/* The view-sharded step of several GPUs driven through this ABI alone (no other collective
+ * library in the caller): the communicator the survey of the reference's multi-GPU boundary
+ * names sp_comm_init(ncclUniqueId, nranks, rank), the gradient exchange with the Adam step, and
+ * the collectives of a densification. NCCL is loaded when first needed (libnccl.so.2: the one
+ * already in the process, else the system's); without it these calls return SP_ERR_NCCL and
+ * the rest of the library works. No counterpart in the reference, which trains on one device.
+ *
+ * Use: one rank calls sp_comm_unique_id and passes the 128 bytes to the others over any host
+ * channel; every rank (one process per GPU) calls sp_comm_init with its own context; then, per
+ * step, each rank's backward passes (accumulated over its views with accumulate_gradients, or
+ * one view), then sp_exchange_step on every rank. Collective calls must be made by every rank
+ * in the same order. Every wait on the host for the other ranks is bounded by the
+ * communicator's time limit: past it the communicator is aborted and the call returns
+ * SP_ERR_TIMEOUT (the communicator is then unusable; destroy it). */
+#define SP_COMM_ID_BYTES 128
+typedef struct sp_comm sp_comm;
+/* ncclGetUniqueId: the rendezvous of a new communicator (call on one rank only; that process
+ * must live until every rank's sp_comm_init has returned). */
+sp_status sp_comm_unique_id(uint8_t out[SP_COMM_ID_BYTES]);
+/* The NCCL version loaded (e.g. 22703), 0 when NCCL cannot be loaded. */
+int sp_comm_nccl_version(void);
+/* ncclCommInitRank on ctx's device, non-blocking, waiting up to timeout_ms for every rank. */
+sp_status sp_comm_init(sp_context* ctx, const uint8_t id[SP_COMM_ID_BYTES], uint32_t world, uint32_t rank,
+                       uint32_t timeout_ms, sp_comm** out);
+void sp_comm_destroy(sp_comm* comm);
+uint32_t sp_comm_rank(const sp_comm* comm);
+uint32_t sp_comm_world(const sp_comm* comm);
+/* Enqueues a one-element all-reduce on the context's stream: work any rank enqueues after it
+ * starts only once every rank's work enqueued before it has completed. */
+sp_status sp_comm_barrier(sp_comm* comm);
+/* Waits (host) for the context's stream, up to the time limit; SP_ERR_TIMEOUT past it (a rank
+ * that stopped leaves the others' collectives waiting), with the communicator aborted. */
+sp_status sp_comm_wait(sp_comm* comm);
+/* Sums the parameter gradients of every rank's rasterizer in place (ncclAllReduce). */
+sp_status sp_allreduce_grads(sp_comm* comm, sp_rasterizer* r);
+/* The sharded Adam step: the gradients reduce-scattered in place (rank r receives the sum of
+ * its share [r n / world, (r + 1) n / world) of the Gaussians), Adam and the scale clamp on that
+ * share (moments current on the share only), the parameters all-gathered in place. n must be a
+ * multiple of world. */
+sp_status sp_adam_step_sharded(sp_comm* comm, sp_adam* adam, float position_rate_factor);
+
+/* The exchange of one step, chosen once. */
+enum {
+    SP_EXCHANGE_AUTO = 0,     /* PEER where the Gaussians split evenly, else ALLREDUCE; PEER falls
+                                 back to SHARDED when a rank cannot map its peers' buffers */
+    SP_EXCHANGE_PEER = 1,     /* one kernel per rank over NVLink peer memory (sp_peer_exchange_*),
+                                 between two barriers; handles exchanged through the communicator */
+    SP_EXCHANGE_SHARDED = 2,  /* sp_adam_step_sharded */
+    SP_EXCHANGE_ALLREDUCE = 3 /* sp_allreduce_grads, then the whole Adam step on every rank */
+};
+typedef struct sp_exchange sp_exchange;
+/* Collective: every rank with its optimiser over the same Gaussian count. */
+sp_status sp_exchange_create(sp_comm* comm, sp_adam* adam, uint32_t mode, sp_exchange** out);
+/* The mode in use (SP_EXCHANGE_PEER, _SHARDED or _ALLREDUCE). */
+uint32_t sp_exchange_mode(const sp_exchange* exchange);
+/* Enqueues the exchange and the Adam step; every rank's gradients must be enqueued before. */
+sp_status sp_exchange_step(sp_exchange* exchange, float position_rate_factor);
+/* Makes the Adam moments whole on every rank (the sharded forms keep each rank's share
+ * current only): before a densification. */
+sp_status sp_exchange_gather_moments(sp_exchange* exchange);
+void sp_exchange_destroy(sp_exchange* exchange);
+/* Merges every rank's densify statistics in place before a densification: the mean-gradient
+ * sums and visible counts summed, the largest screen radius kept (what one device
+ * accumulating every view would hold, up to the order of the sums). */
+sp_status sp_comm_merge_densify_stats(sp_comm* comm, sp_rasterizer* r);
+
 /* position_rate_factor (optimizer.rs:59-62): 0.01^(step / max(steps - 1, 1)). Returns a
  * negative value where the reference asserts (steps == 0 or step >= steps). */
 float sp_position_rate_factor(uint64_t step, uint64_t steps);

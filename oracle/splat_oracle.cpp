@@ -543,9 +543,18 @@ void or_loss(const float* image, const float* gt, const float* partials, uint32_
         }
 }
 
-// The blend backward; with `magnitudes` non-null, each slot also receives the sums of the
-// absolute values of the same terms (in double), from which the tests bound the rounding
-// error that any other summation order of the terms may carry.
+// The blend backward; with `magnitudes` non-null, each slot also receives, per component, the
+// sum over its pixels of the term's rounding scale (in double): the magnitude of everything
+// the term is computed from, so that reordered sums, cancellation inside dL/dalpha (the
+// difference of T (g . c) and (g . behind + g_T T_final) / (1 - alpha)) and the rounding the
+// transmittance accumulates over the pixel's contributors are all bounded by a small multiple
+// of 2^-24 times it. Per (pixel, Gaussian):
+//   colour c:   |g_c alpha T| (1 + n)
+//   dL/dalpha:  (T sum_c |g_c colour_c| + (sum_c |g_c behind_c| + |g_T T_final|) / (1 - alpha)) (1 + n)
+//   opacity:    that times e^power;   d_power: that times opacity e^power
+//   mean:       |d_power| scale times (|conic_0 d_0| + |conic_1 d_1|) and (|conic_1 d_0| + |conic_2 d_1|)
+//   conic:      |d_power| scale times d_0^2 / 2, |d_0 d_1|, d_1^2 / 2
+// with n the pixel's contributor count (the length of its transmittance product).
 static void blend_backward(const sp_projected* proj, const uint32_t* sorted_gaussians, const uint32_t* sorted_slots,
                            const uint32_t* ranges, const sp_camera_uniform* cam, const float* image,
                            const uint32_t* contributions, const float* loss_gradient, float* intersection_gradients,
@@ -606,7 +615,24 @@ static void blend_backward(const sp_projected* proj, const uint32_t* sorted_gaus
                         for (int c : {8, 0, 1, 2, 3, 4}) s[c] += term[c];
                     if (magnitudes) {
                         double* m = &mags[(size_t)j * SP_GRAD_STRIDE];
-                        for (int c = 0; c < 9; ++c) m[c] += std::fabs((double)term[c]);
+                        const double depth = 1.0 + (double)contributed, t = transmittance;
+                        for (int c = 0; c < 3; ++c) m[5 + c] += std::fabs((double)term[5 + c]) * depth;
+                        if (unclamped) {
+                            double parts = 0.0, behind_parts = std::fabs((double)gradient[3]) * (double)image[index * 4 + 3];
+                            for (int c = 0; c < 3; ++c) {
+                                parts += std::fabs((double)gradient[c] * (double)color[c]);
+                                behind_parts += std::fabs((double)gradient[c] * ((double)behind[c] - (double)color[c] * alpha * t));
+                            }
+                            const double da = (t * parts + behind_parts / (1.0 - (double)alpha)) * depth;
+                            const double dp = da * (double)opacity * (double)gaussian;
+                            const double d0 = d[0], d1 = d[1];
+                            m[8] += da * (double)gaussian;
+                            m[0] += dp * (std::fabs(conic[0] * d0) + std::fabs(conic[1] * d1));
+                            m[1] += dp * (std::fabs(conic[1] * d0) + std::fabs(conic[2] * d1));
+                            m[2] += dp * 0.5 * d0 * d0;
+                            m[3] += dp * std::fabs(d0 * d1);
+                            m[4] += dp * 0.5 * d1 * d1;
+                        }
                     }
                 }
             }

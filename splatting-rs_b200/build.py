@@ -2,7 +2,8 @@
 
 Each CUDA source is compiled separately (in parallel) and linked into one shared library
 with the CUDA runtime linked statically, so the library loads next to any other CUDA
-runtime in the process (PyTorch's included). project.cu, adam.cu and densify.cu are
+runtime in the process (PyTorch's included). NCCL is not linked: comm.cu loads it at run
+time (dlopen), so the library also loads where NCCL is absent. project.cu, adam.cu and densify.cu are
 compiled with -fmad=false: their results are compared bit for bit with the CPU oracle; so
 is pose_device.cu, so that its f64 pose chain rounds as the host's does.
 
@@ -28,8 +29,8 @@ LIBRARY = HERE / "splat_b200" / "libsplat_b200.so"
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", f"-I{INCLUDE}", "--expt-relaxed-constexpr"]
 EXACT = {"project.cu", "adam.cu", "pose_device.cu", "densify.cu"}
-SOURCES = ["project.cu", "sort.cu", "blend.cu", "loss.cu", "adam.cu", "api.cu", "pose.cpp", "pose_device.cu",
-           "densify.cu", "noalloc.cu", "ply.cpp"]
+SOURCES = ["project.cu", "sort.cu", "blend.cu", "loss.cu", "adam.cu", "api.cu", "comm.cu", "pose.cpp",
+           "pose_device.cu", "densify.cu", "noalloc.cu", "ply.cpp"]
 
 
 def nvcc() -> str:
@@ -77,7 +78,7 @@ def build(force: bool = False, ptxas_verbose: bool = False, quiet: bool = True) 
                     reports.append(f"== {source}\n{err}")
     objects = [BUILD / (s + ".o") for s in SOURCES]
     if todo or _stale(LIBRARY, objects):
-        cmd = [nvcc(), *ARCH, "-shared", "-o", str(LIBRARY), *map(str, objects)]
+        cmd = [nvcc(), *ARCH, "-shared", "-o", str(LIBRARY), *map(str, objects), "-ldl"]
         result = subprocess.run(cmd, capture_output=True, text=True)
         if result.returncode != 0:
             raise RuntimeError(f"link failed:\n{result.stderr}")

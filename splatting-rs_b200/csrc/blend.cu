@@ -207,7 +207,7 @@ constexpr int kDirectAtomicLanes = 8;
 // (rasterize_forward.wgsl:60-66): power = -1/2 (a dx^2 + c dy^2) - b dx dy of the conic
 // (a, b, c), d = mean - pixel, rounded operation by operation in the reference's order
 // (no fused multiply-adds), so that power is the oracle's bit for bit; gaussian = e^power,
-// evaluated as 2^(power log2 e).
+// evaluated as 2^(power log2 e) in packed arithmetic.
 struct Falloff {
     float dx;
     float2 dy;
@@ -218,10 +218,18 @@ struct Falloff {
 
 __device__ __forceinline__ Falloff falloff(float4 a, float4 b, float fpx, float2 fpy) {
     Falloff f;
-    f.dx = a.x - fpx;
-    f.dy = add2(splat(a.y), neg2(fpy));
-    const float2 quad = add2(splat(__fmul_rn(__fmul_rn(a.z, f.dx), f.dx)), mul2(mul2(splat(b.x), f.dy), f.dy));
-    const float2 power = add2(mul2(splat(-0.5f), quad), neg2(mul2(splat(__fmul_rn(a.w, f.dx)), f.dy)));
+    // Scalar operations with explicit rounding: the compiler does not fuse them, whereas the
+    // packed f32x2 products and sums can be fused into FFMA2 whatever their rounding modifier
+    // (measured: a pair's power came out of such a fusion and differed from the oracle's in
+    // its last 14 bits, where the three terms cancel).
+    f.dx = __fadd_rn(a.x, -fpx);
+    f.dy = make_float2(__fadd_rn(a.y, -fpy.x), __fadd_rn(a.y, -fpy.y));
+    const float t0 = __fmul_rn(__fmul_rn(a.z, f.dx), f.dx), cross = __fmul_rn(a.w, f.dx);
+    float2 power;
+    power.x = __fadd_rn(__fmul_rn(-0.5f, __fadd_rn(t0, __fmul_rn(__fmul_rn(b.x, f.dy.x), f.dy.x))),
+                        -__fmul_rn(cross, f.dy.x));
+    power.y = __fadd_rn(__fmul_rn(-0.5f, __fadd_rn(t0, __fmul_rn(__fmul_rn(b.x, f.dy.y), f.dy.y))),
+                        -__fmul_rn(cross, f.dy.y));
     f.power = power;
     f.below0 = power.x <= 0.0f;
     f.below1 = power.y <= 0.0f;
@@ -233,7 +241,7 @@ __device__ __forceinline__ Falloff falloff(float4 a, float4 b, float fpx, float2
 // falloff() at one pixel, with the same roundings (for the one-pixel-per-thread kernels).
 __device__ __forceinline__ float falloff1(float4 a, float4 b, float fpx, float fpy, float& dx, float& dy,
                                           bool& below, float& power) {
-    dx = a.x - fpx;
+    dx = __fadd_rn(a.x, -fpx);
     dy = __fadd_rn(a.y, -fpy);
     const float quad = __fadd_rn(__fmul_rn(__fmul_rn(a.z, dx), dx), __fmul_rn(__fmul_rn(b.x, dy), dy));
     power = __fadd_rn(__fmul_rn(-0.5f, quad), -__fmul_rn(__fmul_rn(a.w, dx), dy));

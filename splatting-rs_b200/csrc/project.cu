@@ -620,7 +620,8 @@ __global__ void k_to_projected(const float4* __restrict__ records, const uint32_
                                sp_projected* __restrict__ out) {
     const uint32_t g = blockIdx.x * blockDim.x + threadIdx.x;
     if (g >= n) return;
-    const float4 a = records[(size_t)g * 3], b = records[(size_t)g * 3 + 1], c = records[(size_t)g * 3 + 2];
+    const float4 a = records[(size_t)g * kRecord], b = records[(size_t)g * kRecord + 1],
+                 c = records[(size_t)g * kRecord + 2];
     sp_projected p;
     p.mean[0] = a.x;
     p.mean[1] = a.y;
