@@ -67,6 +67,8 @@ def parse_args():
     p.add_argument("--forward-batches", type=int, default=3, help="timed passes over config 3's 64 cameras")
     p.add_argument("--no-densify", action="store_true", help="skip the device densification timing")
     p.add_argument("--no-web-example", action="store_true", help="skip the timing on the reference's example scene")
+    p.add_argument("--no-config5", action="store_true", help="skip the 6M-Gaussian multi-GPU configuration")
+    p.add_argument("--config5-iterations", type=int, default=2, help="timed iterations of config 5 (128 views each)")
     p.add_argument("--exchange", choices=["auto", "peer", "sharded", "allreduce"], default="auto",
                    help="multi-GPU exchange (auto: peer where the Gaussians split evenly, else all-reduce)")
     p.add_argument("--tiles", choices=["ellipse", "rectangle"], default="ellipse",
@@ -451,6 +453,96 @@ def config_dict(scene, world: int, exchange: str = "peer") -> dict:
     }
 
 
+# ----------------------------------------------------------------- config 5 (multi-GPU)
+
+
+CONFIG5 = dict(gaussians=6_000_000, width=1600, height=1200, views=128, seed=4)
+
+
+def config5_throughput(args, ctx, comm, rank: int, world: int, max_over_ranks, barrier) -> dict:
+    """BASELINE's multi-GPU configuration: 6M Gaussians SH degree 3, 128 views of 1600 x 1200
+    on a sphere; each iteration every rank accumulates the gradients of its 128 / world views
+    (a contiguous block, in view order), then one exchange and one Adam step (sp_exchange_step
+    through the library's communicator; the whole Adam step on one GPU). Total work per
+    iteration is fixed whatever the GPU count (strong scaling). The scene is drawn on the GPU
+    (scenes.packed_clustered_device, seed 4); the targets are this library's renders of its
+    perturbed copy, masked at coverage 0.5, each rank holding its own views' targets only.
+    Device-timed (CUDA events, max over ranks) over `config5_iterations` iterations after one."""
+    import torch
+
+    import splat_b200 as sb
+    from splat_b200 import scenes
+    from splat_b200.sharding import ViewShardedStep
+
+    c = CONFIG5
+    n, w, h, views = c["gaussians"], c["width"], c["height"], c["views"]
+    if views % world:
+        return {"skipped": f"{views} views do not split over {world} GPUs"}
+    block = views // world
+    device = torch.device("cuda", ctx.device)
+    params, truth = scenes.packed_clustered_device(n, c["seed"], device, perturb=True)
+    cams = scenes.sphere_cameras(views, 4.0, w, h)
+    uniforms = [cam.uniform() for cam in cams]
+    mine = list(range(rank * block, (rank + 1) * block))
+    culling = sb.SP_TILES_ELLIPSE if args.tiles == "ellipse" else sb.SP_TILES_RECTANGLE
+    gt = torch.empty((block, w * h, 4), dtype=torch.float32, device=device)
+    painter = sb.Rasterizer(ctx, truth, n, w, h, None, 0,
+                            sb.default_options(sh_degree=3, backward_mode=sb.SP_BWD_ATOMIC, tile_culling=culling))
+    for k, v in enumerate(mine):
+        rgbt = torch.from_numpy(painter.render(uniforms[v]).rgbt.reshape(-1, 4)).to(device)
+        mask = ((1.0 - rgbt[:, 3]) > 0.5).float()
+        gt[k, :, :3] = rgbt[:, :3] * mask[:, None]
+        gt[k, :, 3] = mask
+    painter.close()
+    del truth
+    opts = sb.default_options(sh_degree=3, backward_mode=sb.SP_BWD_ATOMIC, tile_culling=culling,
+                              accumulate_gradients=True)
+    rast = sb.Rasterizer(ctx, params, n, w, h, gt.reshape(-1), block, opts)
+    extent = float(sb.cameras_extent(cams))
+    adam = sb.Adam(ctx, params, rast, n, sb.LEARNING_RATES_3DGS, extent, sh_degree=3)
+    step = ViewShardedStep(rast, adam, params, uniforms, rank, world, comm=comm, views_per_rank=block,
+                           loss_index=lambda v: v - rank * block)
+    iterations = 200
+    step(0, sb.position_rate_factor(0, iterations))
+    ctx.profile(True)
+    step(1, sb.position_rate_factor(1, iterations))
+    ctx.profile(False)
+    profile = {k: v for k, v in ctx.read_profile().items() if v[1]}
+    meta = rast.read_intersections_unchecked()
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(ctx.device) as clocks:
+        barrier()
+        start.record()
+        for i in range(args.config5_iterations):
+            step(2 + i, sb.position_rate_factor(2 + i, iterations))
+        stop.record()
+        torch.cuda.synchronize()
+    ms = max_over_ranks(start.elapsed_time(stop))
+    exchange_mode = getattr(step.exchange, "mode", "adam")
+    out = {
+        "value": views * args.config5_iterations / (ms / 1000.0),
+        "unit": "views/s",
+        "workload": f"config 5: {n} Gaussians SH3, {views} views {w}x{h} on a sphere; one iteration = every "
+                    f"view's forward, loss and backward accumulated ({block} per GPU), one exchange and one Adam step",
+        "scaling": "strong: 128 views per iteration whatever the GPU count",
+        "n_gpus": world,
+        "iterations": args.config5_iterations,
+        "ms_per_iteration": ms / args.config5_iterations,
+        "exchange": exchange_mode if world > 1 else "none (one GPU: the Adam step)",
+        "intersections_last_view": int(meta.count),
+        "overflow": bool(meta.overflow),
+        "kernels_ms_per_iteration": {k: v[0] for k, v in profile.items()},
+        "clocks": clocks.summary(),
+        "data": "synthetic: drawn on the GPU with torch's generator (seed 4), configs 3-4's distributions",
+    }
+    step.exchange.close() if world > 1 else None
+    rast.close()
+    adam.close()
+    del params, gt
+    torch.cuda.empty_cache()
+    return out
+
+
 # ------------------------------------------------------------------- the example scene
 
 
@@ -627,7 +719,16 @@ def main() -> None:
     # One GPU: backward with the Adam step fused. N GPUs: gradients reduce-scattered, Adam on
     # this rank's share of the Gaussians, parameters all-gathered (splat_b200/sharding.py).
     exchange_mode = None if args.exchange == "auto" else args.exchange
-    train_step = ViewShardedStep(rast, adam, params, uniforms, rank, world, mode=exchange_mode)
+    # N GPUs: the library's own communicator (sp_comm_*) carries the exchange; its id travels
+    # from rank 0 through torch.distributed's object broadcast (plumbing only).
+    comm = None
+    if world > 1:
+        from splat_b200.comm import Communicator
+
+        uid = [Communicator.unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(uid, src=0)
+        comm = Communicator(ctx, uid[0], world, rank, timeout_ms=180_000)
+    train_step = ViewShardedStep(rast, adam, params, uniforms, rank, world, mode=exchange_mode, comm=comm)
 
     def view_of(step: int) -> int:
         return sharding.view_of(step, rank, world, views)
@@ -706,7 +807,7 @@ def main() -> None:
     # ---- e2e: the reference caller's step through the public API, poses refined.
     params.copy_(initial)
     adam_e2e = sb.Adam(ctx, params, rast, len(cloud), sb.LEARNING_RATES_3DGS, extent, sh_degree=deg)
-    exchange_e2e = sharding.make_exchange(adam_e2e, params, rast, rank, world, exchange_mode)
+    exchange_e2e = sharding.make_exchange(adam_e2e, params, rast, rank, world, exchange_mode, comm=comm)
     poses = sb.PoseRefinement(cams, sb.LEARNING_RATES_3DGS, float(extent))
     e2e_steps = args.e2e_steps or args.steps
 
@@ -851,6 +952,10 @@ def main() -> None:
     if world == 1 and not args.no_web_example:
         web_example = web_example_timing(ctx)
 
+    config5 = None
+    if not args.no_config5:
+        config5 = config5_throughput(args, ctx, comm, rank, world, max_over_ranks, barrier)
+
     forward_3m = None
     if not args.no_forward_3m:
         forward_3m = forward_throughput(args, ctx, rank, world, max_over_ranks, barrier)
@@ -913,6 +1018,7 @@ def main() -> None:
             "mpix_per_s": value * width * height / 1e6,
             "fwd_mpix_per_s_3M": forward_3m,
             "web_example": web_example,
+            "config5": config5,
             "densify": densify,
         }
         print(json.dumps(line), flush=True)
@@ -922,6 +1028,7 @@ def main() -> None:
         dist.barrier()
         train_step.exchange.close()
         exchange_e2e.close()
+        comm.close()
         dist.barrier()
         dist.destroy_process_group()
 

@@ -285,6 +285,22 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "sp_peer_exchange_create": (c_int, [_P, c_uint32, c_uint32, POINTER(PeerHandleC), POINTER(_P)]),
     "sp_peer_exchange_step": (c_int, [_P, c_float]),
     "sp_peer_exchange_destroy": (None, [_P]),
+    "sp_comm_unique_id": (c_int, [_P]),
+    "sp_comm_nccl_version": (c_int, []),
+    "sp_comm_init": (c_int, [_P, _P, c_uint32, c_uint32, c_uint32, POINTER(_P)]),
+    "sp_comm_destroy": (None, [_P]),
+    "sp_comm_rank": (c_uint32, [_P]),
+    "sp_comm_world": (c_uint32, [_P]),
+    "sp_comm_barrier": (c_int, [_P]),
+    "sp_comm_wait": (c_int, [_P]),
+    "sp_allreduce_grads": (c_int, [_P, _P]),
+    "sp_adam_step_sharded": (c_int, [_P, _P, c_float]),
+    "sp_exchange_create": (c_int, [_P, _P, c_uint32, POINTER(_P)]),
+    "sp_exchange_mode": (c_uint32, [_P]),
+    "sp_exchange_step": (c_int, [_P, c_float]),
+    "sp_exchange_gather_moments": (c_int, [_P]),
+    "sp_exchange_destroy": (None, [_P]),
+    "sp_comm_merge_densify_stats": (c_int, [_P, _P]),
     "sp_adam_second_moment_device": (_P, [_P]),
     "sp_position_rate_factor": (c_float, [c_uint64, c_uint64]),
     "sp_adam_resume_device": (c_int, [_P, _P, _P, c_uint64, _P, _P, POINTER(_P)]),

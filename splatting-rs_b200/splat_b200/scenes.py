@@ -17,7 +17,7 @@ from dataclasses import dataclass
 import numpy as np
 
 from .camera import PinholeCamera, focal_for_fov, look_at
-from .gaussians import GaussianCloud, rgb_to_sh_dc
+from .gaussians import SH_C0, GaussianCloud, rgb_to_sh_dc
 
 UP = np.array([0.0, 0.0, 1.0])
 
@@ -164,3 +164,34 @@ def config(index: int, scale: float = 1.0) -> Scene:
         cams = sphere_cameras(128, 4.0, 1600, 1200)
         return Scene("6M SH3 1600x1200 x128", cloud, perturbed(cloud, rng), cams, 200, False, seed)
     raise ValueError(f"config {index}")
+
+
+def packed_clustered_device(count: int, seed: int, device, perturb: bool = False):
+    """Configs 3-4's distributions (64 Gaussian clusters of sigma 0.2 with centres uniform in
+    [-1.5, 1.5]^3, log-scales ~N(-5.5, 0.8), random unit quaternions, opacity logits
+    ~N(0.5, 1.5), DC from uniform colours, SH bands 1-3 ~N(0, 0.05)), packed at SH degree 3 (59
+    floats per Gaussian), drawn on the GPU with torch's seeded generator: seconds instead of
+    minutes for the multi-million-Gaussian benchmark scenes. With `perturb`, returns
+    (cloud, truth): the truth a copy with positions + N(0, 0.02) and DC + N(0, 0.1), as
+    `perturbed`. Not the numpy stream of `config` (whose scenes the parity tests use)."""
+    import torch
+
+    g = torch.Generator(device=device)
+    g.manual_seed(seed)
+    f = dict(device=device, dtype=torch.float32, generator=g)
+    packed = torch.empty((count, 59), device=device, dtype=torch.float32)
+    centres = torch.rand((64, 3), **f) * 3.0 - 1.5
+    which = torch.randint(0, 64, (count,), device=device, generator=g)
+    packed[:, 0:3] = centres[which] + torch.randn((count, 3), **f) * 0.2
+    packed[:, 3:6] = torch.randn((count, 3), **f) * 0.8 - 5.5
+    q = torch.randn((count, 4), **f)
+    packed[:, 6:10] = q / q.norm(dim=1, keepdim=True)
+    packed[:, 10] = torch.randn((count,), **f) * 1.5 + 0.5
+    packed[:, 11:14] = (torch.rand((count, 3), **f) - 0.5) / float(SH_C0)
+    packed[:, 14:59] = torch.randn((count, 45), **f) * 0.05
+    if not perturb:
+        return packed.reshape(-1)
+    truth = packed.clone()
+    truth[:, 0:3] += torch.randn((count, 3), **f) * 0.02
+    truth[:, 11:14] += torch.randn((count, 3), **f) * 0.1
+    return packed.reshape(-1), truth.reshape(-1)

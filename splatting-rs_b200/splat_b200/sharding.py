@@ -3,8 +3,11 @@ parameters replicated, the parameter gradients are summed across ranks, then the
 take one Adam step identical on every rank. The reference trains one view per step on one
 device (instantsplat-rs/src/training.rs:197-229); with one rank this is exactly that step.
 
-Three exchanges; the first two through torch.distributed (NCCL over NVLink on GPUs, gloo on
-CPU) on the buffers the library and the caller own, viewed as tensors without a copy:
+With a comm.Communicator (the library's own NCCL communicator, sp_comm_*) every exchange
+below runs inside libsplat_b200 (sp_exchange_*), with no torch.distributed call: the form a
+caller without PyTorch uses, and the benchmark's. Without one, the same three exchanges run
+through torch.distributed (NCCL over NVLink on GPUs, gloo on CPU) on the buffers the library and
+the caller own, viewed as tensors without a copy:
 
 - "sharded" (when the Gaussians split evenly over the ranks): a reduce-scatter of the
   gradients, so that each rank holds the summed gradients of its own share of the
@@ -186,10 +189,16 @@ class GradientExchange:
 
 
 def make_exchange(adam, params, rasterizer, rank: int, world: int, mode: str | None = None,
-                  group=None) -> GradientExchange:
+                  group=None, comm=None):
     """The exchange of `mode` for a library optimiser and rasterizer; by default the peer
     exchange when the Gaussians split evenly over several ranks (the sharded NCCL one when the
-    ranks cannot map each other's buffers), else the all-reduce."""
+    ranks cannot map each other's buffers), else the all-reduce. With `comm` (a
+    comm.Communicator) the library's own exchange (sp_exchange_*) is used, with no
+    torch.distributed call; otherwise the torch.distributed forms of this module."""
+    if comm is not None:
+        from .comm import Exchange
+
+        return Exchange(comm, adam, mode or "auto")
     count = rasterizer.gaussian_count
     if mode in ("sharded", "peer") and not even_shards(count, world):
         mode = None
@@ -266,12 +275,27 @@ class _PeerExchange:
         self.close()
 
 
+def views_of(step: int, rank: int, world: int, views: int, views_per_rank: int = 1) -> list[int]:
+    """The views rank `rank` trains at `step` with `views_per_rank` views per rank and step: the
+    ranks take consecutive blocks, so that one step covers views
+    step * world * b .. (step + 1) * world * b - 1 (mod views), in view order across the ranks."""
+    first = (step * world + rank) * views_per_rank
+    return [(first + k) % views for k in range(views_per_rank)]
+
+
 class ViewShardedStep:
-    """One training step on this rank: set the camera of its view, forward, loss,
-    backward, the gradient exchange and Adam (the scale clamp fused)."""
+    """One training step on this rank: for each of its views (`views_per_rank`, one by
+    default) set the camera, forward, loss and backward, the gradients summed over its views
+    in view order; then the gradient exchange and Adam (the scale clamp fused). With one view
+    per rank and step the rank's backward feeds the exchange directly (one GPU: the backward
+    with the Adam step fused); with several, the rasterizer must accumulate gradients
+    (accumulate_gradients) and they are cleared at the start of each step. The batch of a
+    step is then every rank's views, then one Adam step. `loss_index(view)` gives the view's
+    index in the rasterizer's ground truth (by default the view itself). With `comm` (a
+    comm.Communicator) the exchange is the library's own (sp_exchange_*)."""
 
     def __init__(self, rasterizer, adam, params, uniforms, rank: int, world: int, mode: str | None = None,
-                 group=None):
+                 group=None, comm=None, views_per_rank: int = 1, loss_index=None):
         self.rasterizer = rasterizer
         self.adam = adam
         self.params = params
@@ -280,10 +304,15 @@ class ViewShardedStep:
         self.world = world
         self.mode = mode
         self.group = group
+        self.comm = comm
+        self.views_per_rank = int(views_per_rank)
+        self.loss_index = loss_index or (lambda view: view)
+        if self.views_per_rank > 1 and not rasterizer.options.accumulate_gradients:
+            raise ValueError("several views per step need a rasterizer that accumulates gradients")
         self.exchange = self._exchange(adam, params, rasterizer)
 
-    def _exchange(self, adam, params, rasterizer) -> GradientExchange:
-        return make_exchange(adam, params, rasterizer, self.rank, self.world, self.mode, self.group)
+    def _exchange(self, adam, params, rasterizer):
+        return make_exchange(adam, params, rasterizer, self.rank, self.world, self.mode, self.group, self.comm)
 
     def densify(self, settings, extent: float, max_count: int, reset_opacity: bool, seed: int):
         """Trainer::densify_async (training.rs:238-266) on every rank: the statistics merged and
@@ -295,7 +324,10 @@ class ViewShardedStep:
         from .rasterizer import Rasterizer
 
         r = self.rasterizer
-        if self.world > 1:
+        if self.world > 1 and self.comm is not None:
+            self.comm.merge_densify_stats(r)
+            self.exchange.gather_moments()
+        elif self.world > 1:
             merge_densify_stats(r.densify_stats_tensor(), self.group)
             self.exchange.gather_moments(*self.adam.moment_tensors())
         out = densify(r, self.adam, extent, max_count, settings, reset_opacity, seed)
@@ -311,12 +343,23 @@ class ViewShardedStep:
         return out.report
 
     def __call__(self, step: int, rate_factor: float) -> int:
-        view = view_of(step, self.rank, self.world, len(self.uniforms))
+        """The step; returns this rank's last view."""
+        views = views_of(step, self.rank, self.world, len(self.uniforms), self.views_per_rank)
         r = self.rasterizer
+        if self.views_per_rank > 1:
+            r.zero_param_gradients()
+            for view in views:
+                r.set_camera(self.uniforms[view])
+                r.encode_forward()
+                r.encode_loss(self.loss_index(view))
+                r.encode_backward()
+            self.exchange(rate_factor)
+            return views[-1]
+        view = views[0]
         r.set_camera(self.uniforms[view])
         r.encode_forward()
-        r.encode_loss(view)
-        if self.world == 1:
+        r.encode_loss(self.loss_index(view))
+        if self.world == 1 and not r.options.accumulate_gradients:
             # Backward with the Adam step fused into the projection backward.
             r.encode_backward_adam(self.adam, rate_factor)
         else:

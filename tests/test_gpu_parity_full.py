@@ -43,10 +43,11 @@ Bars:
     near-isotropic Gaussian's rotation gradient is zero up to rounding);
   - camera gradient (14 floats): element-wise 1e-4 relative;
   - densify statistics: visible counts and radii bit-exact;
-  - one training step (example scene): parameters equal to the oracle's step within the
-    rounding of Adam's first update (4 ulp of the parameter + 1e-6 of the rate), except
-    where the two gradients have opposite signs (Adam's first step moves a parameter by its
-    rate times the gradient's sign), which may only happen on at most 1e-3 of them.
+  - one training step (example scene): parameters equal to the oracle's step within what
+    Adam's first update makes of the two end-to-end gradients (it moves a parameter by its
+    rate times g / (|g| + 1e-15): a sign, except for gradients near 1e-15) plus the update's
+    rounding (4 ulp of the parameter + 1e-6 of the rate); opposite gradient signs on at most
+    1e-3 of the parameters.
 """
 
 from __future__ import annotations
@@ -303,7 +304,12 @@ def test_web_example_training_step(ctx):
     got = params.cpu().numpy()
     rate = np.tile(lr, len(cloud)).astype(np.float64)
     spacing = np.abs(np.spacing(want.astype(np.float32))).astype(np.float64)
-    differ = np.abs(got.astype(np.float64) - want) > 4.0 * spacing + 1e-6 * rate
+    # Adam's first update (optimizer.rs:64-66, adam.wgsl:20-37) is rate * g / (|g| + 1e-15): the
+    # two steps can differ by the rate times the difference of that map at the two gradients
+    # (a sign, except where |g| is near 1e-15), plus the roundings of the update.
+    update = lambda g: g / (np.abs(g) + 1e-15)  # noqa: E731
+    allowed = 2.0 * rate * np.abs(update(gpu_gradients) - update(oracle_gradients)) + 4.0 * spacing + 1e-6 * rate
+    differ = np.abs(got.astype(np.float64) - want) > allowed
+    assert not np.any(differ), f"{int(np.sum(differ))} parameters differ after the step beyond Adam's map"
     flipped = np.sign(gpu_gradients) != np.sign(oracle_gradients)
-    assert not np.any(differ & ~flipped), f"{int(np.sum(differ & ~flipped))} parameters differ after the step"
     assert np.mean(flipped) <= 1e-3, f"{np.mean(flipped):.2e} of the gradients have the other sign"
