@@ -798,10 +798,18 @@ def main() -> None:
     if world > 1:
         barrier()
         if rank == 0:
-            gbs = peer_copy_gbs(local, local + 1)
-            nvlink = {"gbs_per_direction": gbs,
-                      "how": f"cudaMemcpyAsync (torch copy_) of 512 MiB from GPU {local} to GPU {local + 1}, "
-                             "10 copies timed with CUDA events after 3 untimed"}
+            copy = peer_copy_gbs(local, local + 1)
+            probe = None
+            if getattr(train_step.exchange, "mode", None) == "peer":
+                # The link as the exchange kernel uses it: SM loads from the next rank's buffer.
+                size = min(256 << 20, len(cloud) * sb.param_stride(deg) * 4) // 16 * 16
+                probe = train_step.exchange.probe_link(1, size)
+            nvlink = {"gbs_per_direction": probe if probe else copy,
+                      "peer_read_gbs": probe,
+                      "copy_engine_gbs": copy,
+                      "how": ("peer-read kernel of the exchange (sp_exchange_probe_link: float4 loads from rank 1's "
+                              "gradient buffer, 4 in flight per thread, CUDA events) " if probe else "")
+                             + f"and cudaMemcpyAsync (torch copy_) of 512 MiB from GPU {local} to GPU {local + 1}"}
         barrier()
 
     # ---- e2e: the reference caller's step through the public API, poses refined.

@@ -530,6 +530,13 @@ sp_status sp_exchange_create(sp_comm* comm, sp_adam* adam, uint32_t mode, sp_exc
 uint32_t sp_exchange_mode(const sp_exchange* exchange);
 /* Enqueues the exchange and the Adam step; every rank's gradients must be enqueued before. */
 sp_status sp_exchange_step(sp_exchange* exchange, float position_rate_factor);
+/* Times one read of `bytes` of rank `peer`'s gradient buffer over NVLink by this rank's GPU
+ * (plain float4 loads from the mapped peer buffer, four in flight per thread as the peer
+ * exchange issues them; CUDA events on the context's stream, after one untimed read), into
+ * *milliseconds: the link bandwidth the exchange is judged against. Peer-memory exchanges only;
+ * the peer must not be writing that buffer meanwhile (call between steps). No counterpart in
+ * the reference. */
+sp_status sp_exchange_probe_link(sp_exchange* exchange, uint32_t peer, uint64_t bytes, float* milliseconds);
 /* Makes the Adam moments whole on every rank (the sharded forms keep each rank's share
  * current only): before a densification. */
 sp_status sp_exchange_gather_moments(sp_exchange* exchange);

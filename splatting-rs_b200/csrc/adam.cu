@@ -137,6 +137,57 @@ cudaError_t launch_adam_peer(const PeerBuffers& peers, float* first_moment, floa
     return cudaGetLastError();
 }
 
+namespace {
+
+// Reads `count` float4 of a (peer's) buffer, four loads in flight per thread as the exchange
+// kernel issues them, and stores one sum per block into `sink` so that no load is dropped:
+// the read bandwidth of the link as the exchange uses it.
+__global__ void __launch_bounds__(kBlock) k_peer_read(const float4* __restrict__ src, uint64_t count,
+                                                      float4* __restrict__ sink) {
+    float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    const uint64_t threads = (uint64_t)gridDim.x * kBlock;
+    uint64_t i = (uint64_t)blockIdx.x * kBlock + threadIdx.x;
+    for (; i + 3 * threads < count; i += 4 * threads) {
+        float4 v[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) v[k] = __ldcg(src + i + k * threads);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            acc.x += v[k].x;
+            acc.y += v[k].y;
+            acc.z += v[k].z;
+            acc.w += v[k].w;
+        }
+    }
+    for (; i < count; i += threads) {
+        const float4 v = __ldcg(src + i);
+        acc.x += v.x;
+        acc.y += v.y;
+        acc.z += v.z;
+        acc.w += v.w;
+    }
+    __shared__ float4 s[kBlock];
+    s[threadIdx.x] = acc;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float4 total = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        for (int k = 0; k < kBlock; ++k) {
+            total.x += s[k].x;
+            total.y += s[k].y;
+            total.z += s[k].z;
+            total.w += s[k].w;
+        }
+        sink[blockIdx.x] = total;
+    }
+}
+
+}  // namespace
+
+cudaError_t launch_peer_read(const float4* src, uint64_t count, float4* sink, unsigned blocks, cudaStream_t stream) {
+    k_peer_read<<<blocks, kBlock, 0, stream>>>(src, count, sink);
+    return cudaGetLastError();
+}
+
 cudaError_t launch_adam(float* params, const float* gradients, float* first_moment, float* second_moment,
                         uint64_t first, uint64_t count, int stride, const float* lr_by_slot_host, float bias1,
                         float bias2, float max_log_scale, float max_log_anisotropy, cudaStream_t stream) {

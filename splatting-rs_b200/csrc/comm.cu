@@ -14,6 +14,7 @@
 #include <dlfcn.h>
 #include <nccl.h>
 
+#include <algorithm>
 #include <chrono>
 #include <cstring>
 #include <mutex>
@@ -344,6 +345,39 @@ sp_status sp_exchange_create(sp_comm* c, sp_adam* a, uint32_t mode, sp_exchange*
 }
 
 uint32_t sp_exchange_mode(const sp_exchange* ex) { return ex ? ex->mode : 0; }
+
+sp_status sp_exchange_probe_link(sp_exchange* ex, uint32_t peer, uint64_t bytes, float* milliseconds) {
+    if (!ex || !milliseconds) return SP_ERR_INVALID;
+    sp_comm* c = ex->comm;
+    SP_REQUIRE(c->ctx, ex->peer != nullptr, SP_ERR_INVALID, "the exchange does not use peer memory");
+    SP_REQUIRE(c->ctx, peer < c->world && peer != c->rank, SP_ERR_INVALID, "the peer must be another rank");
+    const sp_adam* a = ex->adam;
+    SP_REQUIRE(c->ctx, bytes > 0 && bytes % 16 == 0 && bytes <= a->n * a->stride * sizeof(float), SP_ERR_INVALID,
+               "bytes: a multiple of 16 within the peer's gradient buffer");
+    SP_CHECK(select_device(c->ctx));
+    const float4* src = reinterpret_cast<const float4*>(ex->peer->peers.gradients[peer]);
+    SP_REQUIRE(c->ctx, (reinterpret_cast<uintptr_t>(src) & 15u) == 0, SP_ERR_INVALID, "unaligned peer buffer");
+    int sms = 0;
+    SP_CUDA(c->ctx, cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, c->ctx->device));
+    const unsigned blocks = (unsigned)std::max(sms, 1) * 4u;
+    float4* sink = nullptr;
+    SP_CUDA(c->ctx, cudaMalloc(&sink, blocks * sizeof(float4)));
+    cudaEvent_t start = nullptr, stop = nullptr;
+    cudaEventCreate(&start);
+    cudaEventCreate(&stop);
+    cudaStream_t st = c->ctx->stream;
+    // One untimed pass (maps the pages), then the timed one.
+    cudaError_t err = splat::launch_peer_read(src, bytes / 16, sink, blocks, st);
+    if (err == cudaSuccess) err = cudaEventRecord(start, st);
+    if (err == cudaSuccess) err = splat::launch_peer_read(src, bytes / 16, sink, blocks, st);
+    if (err == cudaSuccess) err = cudaEventRecord(stop, st);
+    if (err == cudaSuccess) err = cudaEventSynchronize(stop);
+    if (err == cudaSuccess) err = cudaEventElapsedTime(milliseconds, start, stop);
+    cudaEventDestroy(start);
+    cudaEventDestroy(stop);
+    cudaFree(sink);
+    return err == cudaSuccess ? SP_OK : cuda_fail(c->ctx, err, "peer-read probe");
+}
 
 sp_status sp_exchange_step(sp_exchange* ex, float position_rate_factor) {
     if (!ex) return SP_ERR_INVALID;

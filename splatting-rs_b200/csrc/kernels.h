@@ -134,6 +134,10 @@ cudaError_t launch_adam_peer(const PeerBuffers& peers, float* first_moment, floa
                              uint64_t count, int stride, const float* lr_by_slot_host, float bias1, float bias2,
                              float max_log_scale, float max_log_anisotropy, cudaStream_t stream);
 
+// Reads `count` float4 of `src` (another GPU's memory mapped into this one) with `blocks`
+// blocks and stores one sum per block into sink[blocks]: the peer-read probe of the exchange.
+cudaError_t launch_peer_read(const float4* src, uint64_t count, float4* sink, unsigned blocks, cudaStream_t stream);
+
 // ---- pose_device.cu
 
 namespace pose {

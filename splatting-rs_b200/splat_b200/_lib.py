@@ -297,6 +297,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "sp_adam_step_sharded": (c_int, [_P, _P, c_float]),
     "sp_exchange_create": (c_int, [_P, _P, c_uint32, POINTER(_P)]),
     "sp_exchange_mode": (c_uint32, [_P]),
+    "sp_exchange_probe_link": (c_int, [_P, c_uint32, c_uint64, POINTER(c_float)]),
     "sp_exchange_step": (c_int, [_P, c_float]),
     "sp_exchange_gather_moments": (c_int, [_P]),
     "sp_exchange_destroy": (None, [_P]),

@@ -100,6 +100,14 @@ class Exchange:
         project(0, self.adam.gaussian_count)
         self(rate_factor)
 
+    def probe_link(self, peer: int, bytes_: int) -> float:
+        """GB/s of one read of `bytes_` of rank `peer`'s gradient buffer over NVLink by this
+        GPU (sp_exchange_probe_link; peer-memory exchanges only, between steps)."""
+        ms = ctypes.c_float()
+        _lib.check(self.lib.sp_exchange_probe_link(self.handle, int(peer), int(bytes_), ctypes.byref(ms)),
+                   self.comm.ctx.handle, "sp_exchange_probe_link")
+        return bytes_ / (ms.value / 1000.0) / 1e9
+
     def gather_moments(self, first=None, second=None) -> None:
         _lib.check(self.lib.sp_exchange_gather_moments(self.handle), self.comm.ctx.handle,
                    "sp_exchange_gather_moments")

@@ -309,7 +309,14 @@ def test_web_example_training_step(ctx):
     # (a sign, except where |g| is near 1e-15), plus the roundings of the update.
     update = lambda g: g / (np.abs(g) + 1e-15)  # noqa: E731
     allowed = 2.0 * rate * np.abs(update(gpu_gradients) - update(oracle_gradients)) + 4.0 * spacing + 1e-6 * rate
+    # The scale clamp (clamp_scales.wgsl:15-29) ties a Gaussian's three log-scales to the largest
+    # of them: each may move as far as any of the three.
+    scales = allowed.reshape(len(cloud), stride)[:, 3:6]
+    scales[:] = scales.max(axis=1, keepdims=True)
     differ = np.abs(got.astype(np.float64) - want) > allowed
-    assert not np.any(differ), f"{int(np.sum(differ))} parameters differ after the step beyond Adam's map"
+    detail = [(int(i) // stride, int(i) % stride, float(got[i]), float(want[i]), float(gpu_gradients[i]),
+               float(oracle_gradients[i])) for i in np.nonzero(differ)[0][:8]]
+    assert not np.any(differ), (f"{int(np.sum(differ))} parameters differ after the step beyond Adam's map: "
+                                f"(Gaussian, slot, cuda, oracle, cuda gradient, oracle gradient) {detail}")
     flipped = np.sign(gpu_gradients) != np.sign(oracle_gradients)
     assert np.mean(flipped) <= 1e-3, f"{np.mean(flipped):.2e} of the gradients have the other sign"
