@@ -209,7 +209,7 @@ sp_status sp_rasterizer_create(sp_context* ctx, const float* d_params, uint64_t 
     else sp_options_default(&opt);
     // rasterizer.rs:185-199.
     SP_REQUIRE(ctx, gaussian_count > 0, SP_ERR_INVALID, "no Gaussians");
-    SP_REQUIRE(ctx, gaussian_count < (1ull << 31), SP_ERR_INVALID, "more than 2^31 Gaussians");
+    SP_REQUIRE(ctx, gaussian_count < (1ull << kGaussianBits), SP_ERR_INVALID, "2^28 Gaussians or more");
     SP_REQUIRE(ctx, d_params != nullptr, SP_ERR_INVALID, "null params buffer");
     SP_REQUIRE(ctx, width > 0 && height > 0, SP_ERR_INVALID, "empty image");
     SP_REQUIRE(ctx, view_count == 0 || d_ground_truth != nullptr, SP_ERR_INVALID, "null ground truth buffer");
@@ -373,7 +373,7 @@ sp_status sp_forward(sp_rasterizer* r) {
     }
     {
         KernelSpan span(ctx, SP_K_EMIT);
-        SP_CUDA(ctx, launch_emit(r->records, r->offsets, r->block_offsets, r->n, r->camera,
+        SP_CUDA(ctx, launch_emit(r->records, r->reach, r->offsets, r->block_offsets, r->n, r->camera,
                                  (int)r->options.key_mode, (int)r->options.tile_culling, r->plan, r->meta, r->keys[0],
                                  r->keys[1], r->values[0], r->values[1], r->sort_histograms, st));
     }
@@ -396,7 +396,7 @@ sp_status sp_forward(sp_rasterizer* r) {
     }
     {
         KernelSpan span(ctx, SP_K_BLEND_FORWARD);
-        SP_CUDA(ctx, launch_blend_forward(r->records, r->reach, r->values[r->sorted_buffer], r->ranges, r->tile_order,
+        SP_CUDA(ctx, launch_blend_forward(r->records, r->values[r->sorted_buffer], r->ranges, r->tile_order,
                                           r->camera, r->image, r->contributions, st));
     }
     r->forward_done = true;
@@ -428,7 +428,7 @@ sp_status blend_backward(sp_rasterizer* r) {
     KernelSpan span(r->ctx, SP_K_BLEND_BACKWARD);
     if (r->options.backward_mode == SP_BWD_ATOMIC)
         SP_CUDA(r->ctx, cudaMemsetAsync(r->gaussian_gradients, 0, r->n * 3 * sizeof(float4), st));
-    SP_CUDA(r->ctx, launch_blend_backward((int)r->options.backward_mode, r->records, r->reach, r->values[r->sorted_buffer],
+    SP_CUDA(r->ctx, launch_blend_backward((int)r->options.backward_mode, r->records, r->values[r->sorted_buffer],
                                           r->ranges, r->tile_order, r->offsets, r->camera, r->image,
                                           r->contributions, r->loss_gradient, r->slot_gradients,
                                           r->gaussian_gradients, st));
@@ -826,7 +826,10 @@ sp_status sp_read_sorted_intersections(sp_rasterizer* r, uint64_t* keys_host, ui
             for (uint64_t i = 0; i < count; ++i) keys_host[i] = keys[i];
         }
     }
-    return read_device(r->ctx, gaussians_host, r->values[r->sorted_buffer], count * 4);
+    SP_CHECK(read_device(r->ctx, gaussians_host, r->values[r->sorted_buffer], count * 4));
+    // The Gaussian indices without the blend kernels' block bits.
+    for (uint64_t i = 0; i < count; ++i) gaussians_host[i] &= kGaussianMask;
+    return SP_OK;
 }
 
 sp_status sp_read_tile_ranges(sp_rasterizer* r, uint32_t* host) {

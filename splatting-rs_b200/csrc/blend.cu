@@ -5,8 +5,9 @@
 // 8 x 8 block of it and each lane two pixels of that block, (x, y) and (x, y + 4), whose
 // arithmetic runs as packed f32x2 instructions (FFMA2 / FMUL2 / FADD2 of sm_100). Each warp
 // walks the tile's sorted list on its own, 32 entries at a time: the entries' 48-B records
-// (an L2-resident array) are gathered one per lane, those that can reach the warp's pixels
-// are kept, compacted into the warp's shared-memory stage, and read back as broadcasts.
+// (an L2-resident array) are gathered, one per lane, for the entries whose sorted value
+// marks them as reaching the warp's pixels (block bits set once per key by the emission),
+// compacted into the warp's shared-memory stage, and read back as broadcasts.
 // "Can reach": the Gaussian's alpha is at least 1/255 somewhere in the block's rectangle of
 // pixel centres (the exact ellipse-rectangle test, padded), so only pairs the exact
 // per-pixel test rejects are left out and no result changes.
@@ -103,42 +104,6 @@ __device__ __forceinline__ uint32_t compact(const uint8_t* masks, uint32_t n, ui
     return length;
 }
 
-// Whether the ellipse a x^2 + 2 b x y + c y^2 <= q meets the rectangle [x0, x1] x [y0, y1]
-// (coordinates relative to its centre), with kx = -b/c and ky = -b/a precomputed: as
-// ellipse_meets_rect, the minima along the edges at the clamped stationary points.
-__device__ __forceinline__ bool ellipse_meets_rect_k(float a, float b, float c, float kx, float ky, float q, float x0,
-                                                     float x1, float y0, float y1) {
-    if (x0 <= 0.0f && x1 >= 0.0f && y0 <= 0.0f && y1 >= 0.0f) return true;
-    float best = INFINITY;
-    const float xs[2] = {x0, x1}, ys[2] = {y0, y1};
-#pragma unroll
-    for (int e = 0; e < 2; ++e) {
-        const float x = xs[e];
-        const float y = fminf(fmaxf(kx * x, y0), y1);
-        best = fminf(best, a * x * x + 2.0f * b * x * y + c * y * y);
-        const float yy = ys[e];
-        const float xx = fminf(fmaxf(ky * yy, x0), x1);
-        best = fminf(best, a * xx * xx + 2.0f * b * xx * yy + c * yy * yy);
-    }
-    return best <= q;
-}
-
-// Whether a Gaussian can reach the rectangle of pixel centres [x0, x0 + 7] x [y0, y0 + ROWS - 1]:
-// op * exp(power) >= 1/255 somewhere in it, i.e. the ellipse d^T C d <= 2 ln(255 op) of the
-// conic C (padded by 1 % in the level) meets the rectangle (padded by 0.05 px). `r` holds the
-// projection's constants of the Gaussian (its half extents and slopes, reach_of in
-// project.cu); a bounding-box test first, then the exact one.
-template <int ROWS>
-__device__ __forceinline__ bool reaches(float4 a, float4 b, float4 r, float x0, float y0) {
-    if (!(r.x >= 0.0f)) return false;        // the opacity keeps alpha below 1/255
-    if (!(r.x < INFINITY)) return true;      // degenerate conic: never culled
-    const float lo_x = x0 - a.x - 0.05f, hi_x = lo_x + 7.1f;
-    const float lo_y = y0 - a.y - 0.05f, hi_y = lo_y + (float)(ROWS - 1) + 0.1f;
-    if (r.x < lo_x || -r.x > hi_x || r.y < lo_y || -r.y > hi_y) return false;
-    const float q = 2.02f * __logf(b.y * 255.0f) + 0.02f;
-    return ellipse_meets_rect_k(a.z, a.w, b.x, r.z, r.w, q, lo_x, hi_x, lo_y, hi_y);
-}
-
 // One warp's staging area: the records of a 32-entry chunk of the tile list that reach the
 // warp's 8 x 4 pixels, compacted in list order.
 struct WarpStage {
@@ -149,24 +114,27 @@ struct WarpStage {
     uint32_t g[32];   // Gaussian
 };
 
-// Loads entries base .. base + 31 (below `end`) of the tile list, one per lane, keeps those
-// that reach the warp's 8 x ROWS pixels at (x0, y0), compacted into `st`; returns how many.
-template <int ROWS>
-__device__ __forceinline__ uint32_t stage_chunk(const float4* __restrict__ records, const float4* __restrict__ reach,
-                                                const uint32_t* __restrict__ sorted, uint32_t first, uint32_t base,
-                                                uint32_t end, float x0, float y0, uint32_t lane, WarpStage& st) {
+// Takes entries base .. base + 31 (below `end`) of the tile list, one per lane, keeps those
+// whose value marks them as reaching the warp's 8 x 8 block `warp` (the emission's block
+// bits), gathers only their records, compacted into `st`; returns how many.
+__device__ __forceinline__ uint32_t stage_chunk(const float4* __restrict__ records, const uint32_t* __restrict__ sorted,
+                                                uint32_t first, uint32_t base, uint32_t end, uint32_t warp,
+                                                uint32_t lane, WarpStage& st) {
     const uint32_t j = base + lane;
     bool take = false;
     float4 a, b, c;
     uint32_t g = 0;
     if (j < end) {
-        g = sorted[first + j];
+        const uint32_t value = sorted[first + j];
+        g = value & kGaussianMask;
+        take = (value >> (kGaussianBits + warp)) & 1u;
+    }
+    if (take) {
         const float4* rec = records + (size_t)g * kRecord;
         a = rec[0];
         b = rec[1];
         const float2 thresholds = *reinterpret_cast<const float2*>(rec + 3);
         c = make_float4(rec[2].x, thresholds.x, thresholds.y, 0.0f);
-        take = reaches<ROWS>(a, b, reach[g], x0, y0);
     }
     const uint32_t ballot = __ballot_sync(kFull, take);
     if (take) {
@@ -256,7 +224,6 @@ __global__ void __launch_bounds__(kPairThreads, 8) k_blend_forward(const float4*
                                                                    const uint32_t* __restrict__ sorted,
                                                                    const uint2* __restrict__ ranges,
                                                                    const uint32_t* __restrict__ order,
-                                                                   const float4* __restrict__ reach,
                                                                    const sp_camera_uniform cam,
                                                                    float4* __restrict__ image,
                                                                    uint32_t* __restrict__ contributions) {
@@ -281,7 +248,7 @@ __global__ void __launch_bounds__(kPairThreads, 8) k_blend_forward(const float4*
     for (uint32_t base = 0; base < count; base += 32) {
         if (__all_sync(kFull, done0 && done1)) break;
         const uint32_t n =
-            stage_chunk<8>(records, reach, sorted, range.x, base, count, (float)bx, (float)by, lane, st);
+            stage_chunk(records, sorted, range.x, base, count, warp, lane, st);
         for (uint32_t i = 0; i < n && !(done0 && done1); ++i) {
             const float4 a = st.a[i], b = st.b[i];
             const float2 c = *reinterpret_cast<const float2*>(&st.c[i]);  // colour.b, take_from
@@ -415,7 +382,7 @@ __global__ void __launch_bounds__(kTilePixels) k_blend_backward(
         const uint32_t base = (batches - 1 - bb) * B;
         __syncthreads();
         if (t < (uint32_t)B && base + t < limit) {
-            const uint32_t g = sorted[range.x + base + t];
+            const uint32_t g = sorted[range.x + base + t] & kGaussianMask;
             const float4* rec = records + (size_t)g * kRecord;
             const float4 a = rec[0], b = rec[1];
             s_g[t] = g;
@@ -509,7 +476,7 @@ __global__ void __launch_bounds__(kTilePixels) k_blend_backward(
         // writes every entry of the tile.
         for (uint32_t i = t; i < (count - limit) * SP_GRAD_STRIDE; i += kTilePixels) {
             const uint32_t j = limit + i / SP_GRAD_STRIDE, c = i % SP_GRAD_STRIDE;
-            const uint32_t g = sorted[range.x + j];
+            const uint32_t g = sorted[range.x + j] & kGaussianMask;
             slot_gradients[slot_of(records, offsets, g, gx, gy) * SP_GRAD_STRIDE + c] = 0.0f;
         }
     }
@@ -523,7 +490,7 @@ __global__ void __launch_bounds__(kTilePixels) k_blend_backward(
 // lanes at once.
 __global__ void __launch_bounds__(kPairThreads, 6) k_blend_backward_atomic(
     const float4* __restrict__ records, const uint32_t* __restrict__ sorted, const uint2* __restrict__ ranges,
-    const uint32_t* __restrict__ order, const float4* __restrict__ reach, const sp_camera_uniform cam,
+    const uint32_t* __restrict__ order, const sp_camera_uniform cam,
     const float4* __restrict__ image, const uint32_t* __restrict__ contributions,
     const float4* __restrict__ loss_gradient, float4* __restrict__ gaussian_gradients) {
     chain_enter();
@@ -564,7 +531,7 @@ __global__ void __launch_bounds__(kPairThreads, 6) k_blend_backward_atomic(
     const float2 behind_t = mul2(gt, transmittance);
     for (int base = end ? (int)((end - 1) & ~31u) : -32; base >= 0; base -= 32) {
         const uint32_t n =
-            stage_chunk<8>(records, reach, sorted, range.x, (uint32_t)base, end, (float)bx, (float)by, lane, st);
+            stage_chunk(records, sorted, range.x, (uint32_t)base, end, warp, lane, st);
         for (int i = (int)n - 1; i >= 0; --i) {
             const uint32_t j = st.j[i];
             const float4 a = st.a[i], b = st.b[i];
@@ -694,7 +661,7 @@ __global__ void __launch_bounds__(kTilePixels) k_count_blend(const float4* __res
         float transmittance = 1.0f;
         for (uint32_t j = range.x; j < range.y; ++j) {
             ++visited;
-            const float4* rec = records + (size_t)sorted[j] * kRecord;
+            const float4* rec = records + (size_t)(sorted[j] & kGaussianMask) * kRecord;
             const float4 a = rec[0], b = rec[1];
             float dx, dy, power;
             bool below;
@@ -730,16 +697,16 @@ cudaError_t launch_tile_order(const uint2* ranges, uint32_t tiles, uint32_t* ord
     return cudaGetLastError();
 }
 
-cudaError_t launch_blend_forward(const float4* records, const float4* reach, const uint32_t* sorted_gaussians,
+cudaError_t launch_blend_forward(const float4* records, const uint32_t* sorted_gaussians,
                                  const uint2* ranges, const uint32_t* order, const sp_camera_uniform& cam,
                                  float4* image, uint32_t* contributions, cudaStream_t stream) {
     const unsigned tiles = cam.tiles_x * cam.tiles_y;
-    launch_chained(k_blend_forward, tiles, kPairThreads, 0, stream, records, sorted_gaussians, ranges, order, reach, cam, image,
+    launch_chained(k_blend_forward, tiles, kPairThreads, 0, stream, records, sorted_gaussians, ranges, order, cam, image,
                                                         contributions);
     return cudaGetLastError();
 }
 
-cudaError_t launch_blend_backward(int mode, const float4* records, const float4* reach, const uint32_t* sorted_gaussians,
+cudaError_t launch_blend_backward(int mode, const float4* records, const uint32_t* sorted_gaussians,
                                   const uint2* ranges, const uint32_t* order, const uint32_t* offsets,
                                   const sp_camera_uniform& cam, const float4* image, const uint32_t* contributions,
                                   const float4* loss_gradient, float* slot_gradients, float4* gaussian_gradients,
@@ -750,7 +717,7 @@ cudaError_t launch_blend_backward(int mode, const float4* records, const float4*
             records, sorted_gaussians, ranges, order, offsets, cam, image, contributions, loss_gradient,
             slot_gradients, gaussian_gradients);
     else
-        launch_chained(k_blend_backward_atomic, tiles, kPairThreads, 0, stream, records, sorted_gaussians, ranges, order, reach,
+        launch_chained(k_blend_backward_atomic, tiles, kPairThreads, 0, stream, records, sorted_gaussians, ranges, order,
                                                                     cam, image, contributions, loss_gradient,
                                                                     gaussian_gradients);
     return cudaGetLastError();

@@ -31,6 +31,14 @@ constexpr int kTilePixels = SP_TILE * SP_TILE;
 // has an all-zero record and radius 0, as the reference's zeroed `Projected`.
 constexpr int kRecord = 4;
 
+// A sorted intersection's value: the Gaussian's index in the low 28 bits and, in the high 4,
+// which of the tile's four 8 x 8 pixel blocks (block w at x offset 8 (w & 1), y offset
+// 8 (w >> 1)) the Gaussian can reach (tile_cull.cuh, reaches), decided once per key at emission
+// so that the blend kernels' warps gather only the records that reach their block. Hence at
+// most 2^28 Gaussians.
+constexpr uint32_t kGaussianBits = 28;
+constexpr uint32_t kGaussianMask = (1u << kGaussianBits) - 1u;
+
 // Device-side bookkeeping of one forward pass (the reference's IntersectionMeta and
 // ScanControl, rasterizer.rs:29-44), plus the status word device code raises errors in.
 struct DeviceMeta {

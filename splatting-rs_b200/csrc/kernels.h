@@ -59,12 +59,14 @@ cudaError_t launch_to_projected(const float4* records, const uint32_t* radii, ui
 // ---- sort.cu
 
 // emit_tile_keys.wgsl:13-36: adds the block offsets into the tile offsets, writes one key
-// and Gaussian index per covered tile, and accumulates every sort pass's digit histogram.
+// and value per covered tile (the Gaussian index with its block bits, common.cuh; `reach`:
+// the projection's culling constants), and accumulates every sort pass's digit histogram.
 // Keys and values go to ping-pong buffer meta->first_buffer, so that the frame's last sort
 // pass lands in buffer plan.passes & 1.
 // With `tile_culling`, only the tiles of tile_cull.cuh get keys (the counts of launch_project
 // with the same flag).
-cudaError_t launch_emit(const float4* records, uint32_t* offsets, const unsigned long long* block_offsets, uint64_t n,
+cudaError_t launch_emit(const float4* records, const float4* reach, uint32_t* offsets,
+                        const unsigned long long* block_offsets, uint64_t n,
                         const sp_camera_uniform& cam, int key_mode, int tile_culling, const SortPlan& plan,
                         const DeviceMeta* meta, void* keys0, void* keys1, uint32_t* values0, uint32_t* values1,
                         uint32_t* sort_histograms, cudaStream_t stream);
@@ -85,13 +87,12 @@ cudaError_t launch_ranges(const SortPlan& plan, const void* keys, const DeviceMe
 // octave), so that the longest tiles start first and the short ones fill the last wave.
 cudaError_t launch_tile_order(const uint2* ranges, uint32_t tiles, uint32_t* order, cudaStream_t stream);
 // rasterize_forward.wgsl:22-88; block b blends tile order[b].
-cudaError_t launch_blend_forward(const float4* records, const float4* reach, const uint32_t* sorted_gaussians,
-                                 const uint2* ranges, const uint32_t* order, const sp_camera_uniform& cam,
-                                 float4* image, uint32_t* contributions, cudaStream_t stream);
+cudaError_t launch_blend_forward(const float4* records, const uint32_t* sorted_gaussians, const uint2* ranges,
+                                 const uint32_t* order, const sp_camera_uniform& cam, float4* image,
+                                 uint32_t* contributions, cudaStream_t stream);
 // rasterize_backward.wgsl:30-133. mode SP_BWD_*: slot sums (deterministic) or atomics
 // into gaussian_gradients (3 float4 per Gaussian, zeroed by the caller).
-cudaError_t launch_blend_backward(int mode, const float4* records, const float4* reach,
-                                  const uint32_t* sorted_gaussians,
+cudaError_t launch_blend_backward(int mode, const float4* records, const uint32_t* sorted_gaussians,
                                   const uint2* ranges, const uint32_t* order, const uint32_t* offsets,
                                   const sp_camera_uniform& cam, const float4* image, const uint32_t* contributions,
                                   const float4* loss_gradient, float* slot_gradients, float4* gaussian_gradients,

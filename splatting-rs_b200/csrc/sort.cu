@@ -55,7 +55,8 @@ __device__ __forceinline__ Key compose_key(uint32_t tile, uint32_t shift, uint32
 // counted them), then the warp writes the 32 rows' keys together; the keys are the
 // rectangle's, minus the culled tiles, in the same order.
 template <typename Key, bool CULL>
-__global__ void __launch_bounds__(kBlock) k_emit(const float4* __restrict__ records, uint32_t* __restrict__ offsets,
+__global__ void __launch_bounds__(kBlock) k_emit(const float4* __restrict__ records, const float4* __restrict__ reach,
+                                                 uint32_t* __restrict__ offsets,
                                                  const unsigned long long* __restrict__ block_offsets, uint32_t n,
                                                  uint32_t tiles_x, int key_mode, const DeviceMeta* __restrict__ meta,
                                                  Key* __restrict__ keys0, Key* __restrict__ keys1,
@@ -119,10 +120,13 @@ __global__ void __launch_bounds__(kBlock) k_emit(const float4* __restrict__ reco
             if (__shfl_sync(0xffffffffu, prefix, h + step) <= e) h += step;
         return h;
     };
-    auto write_key = [&](unsigned long long slot, uint32_t tile, float key_depth, uint32_t gaussian) {
+    // The key and the value: the Gaussian with the tile's pixel blocks it can reach (common.cuh).
+    auto write_key = [&](unsigned long long slot, uint32_t tx, uint32_t ty, float key_depth, uint32_t gaussian) {
+        const uint32_t tile = ty * tiles_x + tx;
         const Key key = compose_key<Key>(tile, tile_shift, depth_part(key_mode, key_depth, base));
         keys[slot] = key;
-        values[slot] = gaussian;
+        const float4* rec = records + (size_t)gaussian * kRecord;
+        values[slot] = gaussian | (block_mask(rec[0], rec[1], reach[gaussian], tx, ty) << kGaussianBits);
         for (int p = first_tile_pass; p < passes; ++p) atomicAdd(&hist[p][(uint32_t)(key >> (8 * p)) & 255u], 1u);
     };
     if constexpr (CULL) {
@@ -174,7 +178,7 @@ __global__ void __launch_bounds__(kBlock) k_emit(const float4* __restrict__ reco
                 const float key_depth = __shfl_sync(0xffffffffu, odepth, src);
                 const uint32_t key_gaussian = __shfl_sync(0xffffffffu, og, src);
                 const unsigned long long slot = start + written + e;
-                if (e < round_keys && slot < capacity) write_key(slot, key_row * tiles_x + column, key_depth, key_gaussian);
+                if (e < round_keys && slot < capacity) write_key(slot, column, key_row, key_depth, key_gaussian);
             }
             written += round_keys;
         }
@@ -190,7 +194,7 @@ __global__ void __launch_bounds__(kBlock) k_emit(const float4* __restrict__ reco
             const uint32_t row = local / ow;
             const unsigned long long slot = start + e;
             if (e < total && slot < capacity)
-                write_key(slot, (oy0 + row) * tiles_x + ox0 + (local - row * ow), odepth, og);
+                write_key(slot, ox0 + (local - row * ow), oy0 + row, odepth, og);
         }
     }
     __syncthreads();
@@ -441,13 +445,15 @@ int sort_grid() {
 
 }  // namespace
 
-cudaError_t launch_emit(const float4* records, uint32_t* offsets, const unsigned long long* block_offsets, uint64_t n,
+cudaError_t launch_emit(const float4* records, const float4* reach, uint32_t* offsets,
+                        const unsigned long long* block_offsets, uint64_t n,
                         const sp_camera_uniform& cam, int key_mode, int tile_culling, const SortPlan& plan,
                         const DeviceMeta* meta, void* keys0, void* keys1, uint32_t* values0, uint32_t* values1,
                         uint32_t* sort_histograms, cudaStream_t stream) {
     const unsigned grid = grid_for(n, kBlock);
 #define SPLAT_EMIT(K, C)                                                                                          \
-    launch_chained(k_emit<K, C>, grid, kBlock, 0, stream, records, offsets, block_offsets, (uint32_t)n, cam.tiles_x, key_mode, \
+    launch_chained(k_emit<K, C>, grid, kBlock, 0, stream, records, reach, offsets, block_offsets, (uint32_t)n,         \
+                                              cam.tiles_x, key_mode,                                              \
                                               meta, static_cast<K*>(keys0), static_cast<K*>(keys1), values0,      \
                                               values1, sort_histograms)
     if (plan.key64) {

@@ -120,4 +120,51 @@ __device__ __forceinline__ uint32_t culled_tile_count(const CullEllipse& e, uint
     return count;
 }
 
+// Whether the ellipse a x^2 + 2 b x y + c y^2 <= q meets the rectangle [x0, x1] x [y0, y1]
+// (coordinates relative to its centre), with kx = -b/c and ky = -b/a precomputed: as
+// ellipse_meets_rect, the minima along the edges at the clamped stationary points.
+__device__ __forceinline__ bool ellipse_meets_rect_k(float a, float b, float c, float kx, float ky, float q, float x0,
+                                                     float x1, float y0, float y1) {
+    if (x0 <= 0.0f && x1 >= 0.0f && y0 <= 0.0f && y1 >= 0.0f) return true;
+    float best = INFINITY;
+    const float xs[2] = {x0, x1}, ys[2] = {y0, y1};
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+        const float x = xs[e];
+        const float y = fminf(fmaxf(kx * x, y0), y1);
+        best = fminf(best, a * x * x + 2.0f * b * x * y + c * y * y);
+        const float yy = ys[e];
+        const float xx = fminf(fmaxf(ky * yy, x0), x1);
+        best = fminf(best, a * xx * xx + 2.0f * b * xx * yy + c * yy * yy);
+    }
+    return best <= q;
+}
+
+// Whether a Gaussian can reach the rectangle of pixel centres [x0, x0 + 7] x [y0, y0 + ROWS - 1]:
+// op * exp(power) >= 1/255 somewhere in it, i.e. the ellipse d^T C d <= 2 ln(255 op) of the
+// conic C (padded by 1 % in the level) meets the rectangle (padded by 0.05 px). `r` holds the
+// projection's constants of the Gaussian (its half extents and slopes, reach_of in
+// project.cu); a bounding-box test first, then the exact one.
+template <int ROWS>
+__device__ __forceinline__ bool reaches(float4 a, float4 b, float4 r, float x0, float y0) {
+    if (!(r.x >= 0.0f)) return false;        // the opacity keeps alpha below 1/255
+    if (!(r.x < INFINITY)) return true;      // degenerate conic: never culled
+    const float lo_x = x0 - a.x - 0.05f, hi_x = lo_x + 7.1f;
+    const float lo_y = y0 - a.y - 0.05f, hi_y = lo_y + (float)(ROWS - 1) + 0.1f;
+    if (r.x < lo_x || -r.x > hi_x || r.y < lo_y || -r.y > hi_y) return false;
+    const float q = 2.02f * __logf(b.y * 255.0f) + 0.02f;
+    return ellipse_meets_rect_k(a.z, a.w, b.x, r.z, r.w, q, lo_x, hi_x, lo_y, hi_y);
+}
+
+// Which of tile (tx, ty)'s four 8 x 8 pixel blocks a Gaussian can reach (bit w: the block at
+// x offset 8 (w & 1), y offset 8 (w >> 1)), by `reaches` with the blend kernels' warp layout.
+__device__ __forceinline__ uint32_t block_mask(float4 a, float4 b, float4 r, uint32_t tx, uint32_t ty) {
+    uint32_t mask = 0;
+#pragma unroll
+    for (uint32_t w = 0; w < 4; ++w)
+        if (reaches<8>(a, b, r, (float)(tx * SP_TILE + ((w & 1u) << 3)), (float)(ty * SP_TILE + ((w >> 1) << 3))))
+            mask |= 1u << w;
+    return mask;
+}
+
 }  // namespace splat
