@@ -355,6 +355,7 @@ sp_status sp_set_camera(sp_rasterizer* r, const sp_camera_uniform* camera) {
 }
 
 sp_status sp_forward(sp_rasterizer* r) {
+    NvtxRange range("sp_forward");
     if (!r) return SP_ERR_INVALID;
     sp_context* ctx = r->ctx;
     SP_CHECK(select_device(ctx));
@@ -404,6 +405,7 @@ sp_status sp_forward(sp_rasterizer* r) {
 }
 
 sp_status sp_loss(sp_rasterizer* r, uint32_t view) {
+    NvtxRange range("sp_loss");
     if (!r) return SP_ERR_INVALID;
     SP_REQUIRE(r->ctx, view < r->views, SP_ERR_INVALID, "view index out of range");
     SP_CHECK(select_device(r->ctx));
@@ -438,6 +440,7 @@ sp_status blend_backward(sp_rasterizer* r) {
 }  // namespace
 
 sp_status sp_backward_adam(sp_rasterizer* r, sp_adam* adam, float position_rate_factor) {
+    NvtxRange range("sp_backward_adam");
     if (!r || !adam) return SP_ERR_INVALID;
     SP_REQUIRE(r->ctx, r->forward_done, SP_ERR_INVALID, "backward before any forward pass");
     SP_REQUIRE(r->ctx,
@@ -486,6 +489,7 @@ sp_status sp_backward_project(sp_rasterizer* r, uint64_t first, uint64_t count) 
 }
 
 sp_status sp_backward(sp_rasterizer* r) {
+    NvtxRange range("sp_backward");
     if (!r) return SP_ERR_INVALID;
     SP_REQUIRE(r->ctx, r->forward_done, SP_ERR_INVALID, "backward before any forward pass");
     SP_CHECK(select_device(r->ctx));
@@ -620,6 +624,7 @@ sp_status sp_read_intersections(sp_rasterizer* r, sp_intersection_meta* out) {
 
 sp_status sp_train_step(sp_rasterizer* r, sp_adam* adam, const sp_camera_uniform* camera, uint32_t view,
                         float position_rate_factor, sp_camera_gradient* camera_gradient_out, sp_loss_terms* loss_out) {
+    NvtxRange range("sp_train_step");
     if (!r || !adam || !camera) return SP_ERR_INVALID;
     SP_CHECK(sp_set_camera(r, camera));
     SP_CHECK(sp_forward(r));
@@ -784,6 +789,7 @@ sp_status sp_train_step_device_poses(sp_rasterizer* r, sp_adam* adam, sp_device_
 }
 
 sp_status sp_render(sp_rasterizer* r, const sp_camera_uniform* camera, float* host_rgbt) {
+    NvtxRange range("sp_render");
     if (!r) return SP_ERR_INVALID;
     SP_CHECK(sp_set_camera(r, camera));
     SP_CHECK(sp_forward(r));
@@ -1052,6 +1058,7 @@ sp_status sp_adam_step_range(sp_adam* a, uint64_t first, uint64_t count) {
 }
 
 sp_status sp_adam_step(sp_adam* a, float position_rate_factor) {
+    NvtxRange range("sp_adam_step");
     SP_CHECK(sp_adam_advance(a, position_rate_factor));
     return sp_adam_step_range(a, 0, a->n);
 }
@@ -1169,6 +1176,7 @@ sp_status sp_peer_exchange_create(sp_adam* a, uint32_t rank, uint32_t world, con
 }
 
 sp_status sp_peer_exchange_step(sp_peer_exchange* ex, float position_rate_factor) {
+    NvtxRange range("sp_peer_exchange_step");
     if (!ex) return SP_ERR_INVALID;
     sp_adam* a = ex->adam;
     SP_CHECK(sp_adam_advance(a, position_rate_factor));

@@ -380,6 +380,7 @@ sp_status sp_exchange_probe_link(sp_exchange* ex, uint32_t peer, uint64_t bytes,
 }
 
 sp_status sp_exchange_step(sp_exchange* ex, float position_rate_factor) {
+    NvtxRange range("sp_exchange_step");
     if (!ex) return SP_ERR_INVALID;
     sp_comm* c = ex->comm;
     SP_CHECK(select_device(c->ctx));

@@ -46,8 +46,9 @@ Bars:
   - one training step (example scene): parameters equal to the oracle's step within what
     Adam's first update makes of the two end-to-end gradients (it moves a parameter by its
     rate times g / (|g| + 1e-15): a sign, except for gradients near 1e-15) plus the update's
-    rounding (4 ulp of the parameter + 1e-6 of the rate); opposite gradient signs on at most
-    1e-3 of the parameters.
+    rounding (4 ulp of the parameter + 1e-6 of the rate), and within twice the rate where the
+    oracle's gradient is within its rounding bar of zero (its sign is rounding); opposite signs
+    elsewhere on at most 1e-3 of the parameters.
 """
 
 from __future__ import annotations
@@ -297,10 +298,11 @@ def test_web_example_training_step(ctx):
     want_loss, _ = oracle.train_step(want, 0, ref.cam, ref.gt, m, v, lr, 1, float(np.log(np.float32(0.02) * extent)),
                                      float(np.log(np.float32(10.0))))
     assert abs(loss.total - want_loss) <= 1e-5 * abs(want_loss)
-    # The oracle's own end-to-end gradient (its forward, loss and backward).
+    # The oracle's own end-to-end gradient (its forward, loss and backward) and its rounding scale.
     f = ref.fwd
     lg, _ = ref.loss(f["image"])
-    oracle_gradients = oracle.backward(ref.packed, 0, ref.cam, f, lg)["param_gradients"].astype(np.float64)
+    oracle_gradients, _, _, scale = ref.backward(f["image"], f["contrib"], lg)
+    oracle_gradients = oracle_gradients.astype(np.float64)
     got = params.cpu().numpy()
     rate = np.tile(lr, len(cloud)).astype(np.float64)
     spacing = np.abs(np.spacing(want.astype(np.float32))).astype(np.float64)
@@ -309,6 +311,12 @@ def test_web_example_training_step(ctx):
     # (a sign, except where |g| is near 1e-15), plus the roundings of the update.
     update = lambda g: g / (np.abs(g) + 1e-15)  # noqa: E731
     allowed = 2.0 * rate * np.abs(update(gpu_gradients) - update(oracle_gradients)) + 4.0 * spacing + 1e-6 * rate
+    # A gradient within its rounding bar of zero has no sign to agree on (e.g. a near-isotropic
+    # Gaussian's rotation gradient): its step is the rate either way.
+    bar = (RTOL * np.abs(oracle_gradients).reshape(len(cloud), stride) + ROUNDINGS * EPS * scale)
+    bar[:, CHAIN_SLOTS.start:CHAIN_SLOTS.stop] += CHAIN_FLOOR * scale[:, CHAIN_SLOTS.start:CHAIN_SLOTS.stop]
+    noise = np.abs(oracle_gradients) <= bar.reshape(-1)
+    allowed[noise] += 2.0 * rate[noise]
     # The scale clamp (clamp_scales.wgsl:15-29) ties a Gaussian's three log-scales to the largest
     # of them: each may move as far as any of the three.
     scales = allowed.reshape(len(cloud), stride)[:, 3:6]
@@ -318,5 +326,5 @@ def test_web_example_training_step(ctx):
                float(oracle_gradients[i])) for i in np.nonzero(differ)[0][:8]]
     assert not np.any(differ), (f"{int(np.sum(differ))} parameters differ after the step beyond Adam's map: "
                                 f"(Gaussian, slot, cuda, oracle, cuda gradient, oracle gradient) {detail}")
-    flipped = np.sign(gpu_gradients) != np.sign(oracle_gradients)
+    flipped = (np.sign(gpu_gradients) != np.sign(oracle_gradients)) & ~noise
     assert np.mean(flipped) <= 1e-3, f"{np.mean(flipped):.2e} of the gradients have the other sign"
