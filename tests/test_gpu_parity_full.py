@@ -29,7 +29,7 @@ Bars:
   - loss gradient: 1e-4 relative + 1e-3 of its largest; loss terms: 1e-4 relative (the GPU
     sums the SSIM window separably, the oracle tap by tap: the window variances, E[x^2] - mu^2,
     cancel, and the SSIM gradient divides by them);
-  - parameter gradients, element-wise: |cuda - oracle| <= 1e-4 |oracle| + 128 x 2^-24 x S,
+  - parameter gradients, element-wise: |cuda - oracle| <= 1e-4 |oracle| + 4 x 2^-24 x S,
     where S is the gradient's rounding scale (oracle.gradient_error_scale: the sum over the
     nine blend sums of |d gradient / d blend sum| times that blend sum's magnitude, the sum
     over its pixels of the magnitude of everything its term is computed from, times the
@@ -66,7 +66,7 @@ pytestmark = pytest.mark.gpu
 
 RTOL = 1e-4
 EPS = 2.0 ** -24
-ROUNDINGS = 128.0
+ROUNDINGS = 4.0  # measured at most 0.04 (config 2: 0.01; the example scene: 0.034)
 # Log-scale and rotation slots: their gradients come out of dL/dSigma through the covariance
 # and quaternion chain, whose own terms cancel (for a near-isotropic Gaussian the rotation
 # gradient is zero up to rounding): a floor of 1e-2 of the scale (measured at most 3.3e-3).
