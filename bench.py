@@ -46,9 +46,10 @@ BACKWARD_OPS_PER_PAIR = 48
 
 # DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) per launch of the heaviest kernels,
 # from one ncu --set full capture of this workload each (profiles/blend_kernels_config2.txt,
-# profiles/project_backward_adam_config2.txt; cold caches, so an upper bound on the in-bench
-# traffic).
-NCU_TRAFFIC_BYTES = {"blend_backward": 85.0e6, "blend_forward": 35.7e6, "backward_adam": 836.7e6}
+# profiles/project_config2.txt, profiles/project_backward_adam_config2.txt; cold caches, so an
+# upper bound on the in-bench traffic).
+NCU_TRAFFIC_BYTES = {"blend_backward": 78.9e6, "blend_forward": 28.8e6, "backward_adam": 836.7e6,
+                     "project": 138.1e6, "emit": 42.1e6}
 
 
 def parse_args():
@@ -932,7 +933,8 @@ def main() -> None:
             entry.update(bound="hbm", achieved=achieved, peak=pk["hbm_gbs"], unit="GB/s", frac=achieved / pk["hbm_gbs"],
                          bytes_per_launch=b)
         elif name == "project":
-            b = len(cloud) * (4 * sb.param_stride(deg) + 52)
+            # Parameters in; the 64-B blend record, 16-B culling constants, radius and tile count out.
+            b = len(cloud) * (4 * sb.param_stride(deg) + 88)
             achieved = b / (kms / n * 1e-3) / 1e9
             entry.update(bound="hbm", achieved=achieved, peak=pk["hbm_gbs"], unit="GB/s", frac=achieved / pk["hbm_gbs"],
                          bytes_per_launch=b)
