@@ -70,6 +70,8 @@ def lib() -> ctypes.CDLL:
         _lib.or_libm_expf.argtypes = [c_float]
         _lib.or_sp_expf.restype = c_float
         _lib.or_sp_expf.argtypes = [c_float]
+        _lib.or_sp_expf_exact.restype = c_float
+        _lib.or_sp_expf_exact.argtypes = [c_float]
         _lib.or_train_step.restype = c_double
         _lib.or_get_threads.restype = c_int
         _lib.or_splitmix64.restype = c_uint64
@@ -131,6 +133,10 @@ def threads() -> int:
 
 def sp_expf(x: float) -> float:
     return float(lib().or_sp_expf(float(x)))
+
+
+def sp_expf_exact(x: float) -> float:
+    return float(lib().or_sp_expf_exact(float(x)))
 
 
 def libm_expf(x: float) -> float:

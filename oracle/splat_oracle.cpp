@@ -315,6 +315,7 @@ int or_get_threads(void) { return threads(); }
 
 float or_libm_expf(float x) { return std::exp(x); }
 float or_sp_expf(float x) { return sp_expf(x); }
+float or_sp_expf_exact(float x) { return sp_expf_exact(x); }
 
 void or_project(const float* params, uint64_t n, uint32_t sh_degree, const sp_camera_uniform* cam,
                 sp_projected* out, uint32_t* tile_counts) {
@@ -417,7 +418,7 @@ void or_blend_forward(const sp_projected* proj, const uint32_t* sorted_gaussians
                     const float power = -0.5f * (p.conic[0] * d[0] * d[0] + p.conic[2] * d[1] * d[1]) -
                                         p.conic[1] * d[0] * d[1];
                     if (power <= 0.0f) {
-                        const float alpha = std::min(SP_MAX_ALPHA, p.opacity * sp_expf(power));
+                        const float alpha = std::min(SP_MAX_ALPHA, p.opacity * sp_expf_exact(power));
                         if (alpha >= SP_MIN_ALPHA) {
                             const float next = transmittance * (1.0f - alpha);
                             if (next < SP_MIN_TRANSMITTANCE) break;
@@ -586,7 +587,7 @@ static void blend_backward(const sp_projected* proj, const uint32_t* sorted_gaus
                     const float* conic = p.conic;
                     const float power = -0.5f * (conic[0] * d[0] * d[0] + conic[2] * d[1] * d[1]) - conic[1] * d[0] * d[1];
                     if (power > 0.0f) continue;
-                    const float gaussian = sp_expf(power);
+                    const float gaussian = sp_expf_exact(power);
                     const float opacity = p.opacity;
                     const float alpha_unclamped = opacity * gaussian;
                     const float alpha = std::min(SP_MAX_ALPHA, alpha_unclamped);

@@ -88,9 +88,10 @@ void or_learning_rates_by_slot(const sp_learning_rates* rates, float position_sc
 /* 1 - beta^step as the host computes it for the kernels (adam.wgsl:31-32). */
 float or_bias_correction(float beta, uint32_t step);
 
-/* The libm exp, for checking sp_expf. */
+/* The libm exp, for checking the shared exps (include/splat_math.h). */
 float or_libm_expf(float x);
 float or_sp_expf(float x);
+float or_sp_expf_exact(float x);
 
 /* One full training step of one view (training.rs:197-209 with fixed poses): forward,
  * loss against view `view`, backward, Adam. Scratch buffers are allocated inside. The

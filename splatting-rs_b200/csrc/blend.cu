@@ -21,7 +21,7 @@
 // decisions that depend on alpha's last bits do not depend on that exp: whether a pixel takes
 // a Gaussian (alpha >= 1/255) and whether its alpha is clamped at 0.99 are tests of the
 // falloff's power (which is the oracle's bit for bit) against the Gaussian's thresholds in
-// record word [3], which the projection derived from the shared, monotone sp_expf; only the
+// record word [3], which the projection derived from the shared, monotone sp_expf_exact; only the
 // termination test (transmittance below 1e-4) reads the blended alpha.
 #include "kernels.h"
 

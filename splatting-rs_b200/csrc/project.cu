@@ -51,20 +51,20 @@ __device__ __forceinline__ uint32_t block_exclusive_scan(uint32_t value, uint32_
     return before + inclusive - value;
 }
 
-// The smallest float power p <= 0 at which opacity * sp_expf(p) >= level in float arithmetic
-// (+inf when not even at p = 0). sp_expf is monotone (include/splat_math.h), so the blend's
-// per-pixel test "opacity * exp(power) >= level", as the oracle evaluates it, holds exactly
-// when power >= this threshold, whatever exp the blend kernels use for the alpha's value.
-// Searched over the float order of -p in [0, 104]: from a double-precision log guess (almost
-// always the answer or its neighbour, so that two or three evaluations decide it), a walk of a
-// few floats, then, if the guess was further off, bisection over a bracket of 16 floats either
-// side or, failing that, the whole range.
+// The smallest float power p <= 0 at which opacity * sp_expf_exact(p) >= level in float
+// arithmetic (+inf when not even at p = 0). sp_expf_exact is monotone (include/splat_math.h),
+// so the blend's per-pixel test "opacity * exp(power) >= level", as the oracle evaluates it,
+// holds exactly when power >= this threshold, whatever exp the blend kernels use for alpha.
+// Searched over the float order of -p in [0, 104]: from a guess by the hardware log (a few
+// floats from the answer, so that two to four evaluations decide it), a walk of a few floats,
+// then, if the guess was further off, bisection over a bracket of 16 floats either side or,
+// failing that, the whole range.
 __device__ __noinline__ float alpha_threshold(float opacity, float level) {
     if (!(opacity >= level)) return INFINITY;
-    auto holds = [&](uint32_t u) { return __fmul_rn(opacity, sp_expf(-__uint_as_float(u))) >= level; };
-    const uint32_t last = __float_as_uint(104.0f);  // sp_expf(-104) is 0: never holds there
-    const double guess = -log((double)level / (double)opacity);
-    const uint32_t g = guess > 0.0 ? min(__float_as_uint((float)guess), last) : 0u;
+    auto holds = [&](uint32_t u) { return __fmul_rn(opacity, sp_expf_exact(-__uint_as_float(u))) >= level; };
+    const uint32_t last = __float_as_uint(104.0f);  // sp_expf_exact(-104) is 0: never holds there
+    const float guess = -__logf(__fdividef(level, opacity));
+    const uint32_t g = guess > 0.0f ? min(__float_as_uint(guess), last) : 0u;
     // The answer is -float(u) for the largest u with holds(u) (holds(0) is true, holds(last) false).
     if (holds(g)) {
         for (uint32_t u = g, k = 0; k < 4 && u < last; ++k, ++u)

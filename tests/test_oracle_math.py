@@ -1,19 +1,23 @@
-"""Accuracy of sp_expf (include/splat_math.h), the exp that the projection kernels and the CPU
-oracle share so that radii and tile rectangles come out bit-identical on both sides.
+"""Accuracy of the exps the CUDA kernels and the CPU oracle share (include/splat_math.h), so
+that radii, tile rectangles and the blend's alpha decisions come out bit-identical on both sides.
 
-It decides the Gaussians' scales (exp of the log-scales), the opacity sigmoid and the SSIM
-window, so it is measured over the whole float range it accepts and, densely, over the
-arguments those uses meet (log-scales and negated opacity logits within [-16, 16], window
-exponents within [-6, 0]):
-  - against the correctly rounded exp (float64 exp rounded once to float32): equal on more
-    than 99.99 % of the arguments and never more than 1 ulp apart (an exhaustive run over
-    every float in [-105, 88.72] against the long-double exp found no difference at all);
-  - monotone non-decreasing over the sampled arguments in increasing order (the blend kernels
+sp_expf (single precision) gives the Gaussians' scales (exp of the log-scales), the opacity
+sigmoid and the SSIM window; sp_expf_exact (double precision, rounded once) gives the blend's
+alpha in the oracle and the per-Gaussian power thresholds of the CUDA blend kernels. Both are
+measured over the whole float range they accept and, densely, over the arguments those uses meet
+(log-scales, negated opacity logits and falloff powers within [-16, 16], window exponents within
+[-6, 0]):
+  - sp_expf against the correctly rounded exp (float64 exp rounded once to float32): at most
+    1 ulp apart, equal on more than 90 % of the arguments;
+  - sp_expf_exact against the correctly rounded exp: equal on more than 99.99 % of the
+    arguments and never more than 1 ulp apart (an exhaustive run over every float in
+    [-105, 88.72] against the long-double exp found no difference at all), and monotone
+    non-decreasing over the sampled arguments in increasing order (the blend kernels' thresholds
     rely on it; the exhaustive run over every float in [-105, 1] found no decrease);
-  - against the host libm's expf (glibc, the oracle's and the reference's host exp): at most
-    1 ulp apart;
-  - against CUDA's expf (torch.exp on a float32 CUDA tensor; CUDA documents a 2-ulp bound for
-    expf): at most 2 ulp apart (GPU test).
+  - both against the host libm's expf (glibc, the oracle's and the reference's host exp): at
+    most 1 ulp apart;
+  - both against CUDA's expf (torch.exp on a float32 CUDA tensor; CUDA documents a 2-ulp bound
+    for expf): at most 2 ulp apart (GPU test).
 """
 
 from __future__ import annotations
@@ -44,56 +48,64 @@ def _ulp(a: np.ndarray, b: np.ndarray) -> np.ndarray:
     return np.abs(a.view(np.int32).astype(np.int64) - b.view(np.int32).astype(np.int64))
 
 
-def _sp_expf(xs: np.ndarray) -> np.ndarray:
-    return np.array([oracle.sp_expf(float(x)) for x in xs], np.float32)
+EXPS = {"sp_expf": oracle.sp_expf, "sp_expf_exact": oracle.sp_expf_exact}
+# Least share of the arguments where each is the correctly rounded result.
+CORRECTLY_ROUNDED = {"sp_expf": 0.9, "sp_expf_exact": 0.9999}
 
 
 @pytest.fixture(scope="module")
 def table():
     xs = _arguments()
-    return xs, _sp_expf(xs), np.exp(xs.astype(np.float64)).astype(np.float32)
+    values = {name: np.array([fn(float(x)) for x in xs], np.float32) for name, fn in EXPS.items()}
+    return xs, values, np.exp(xs.astype(np.float64)).astype(np.float32)
 
 
-def test_sp_expf_within_one_ulp_of_the_correctly_rounded_exp(table):
-    xs, got, want = table
+@pytest.mark.parametrize("name", list(EXPS))
+def test_within_one_ulp_of_the_correctly_rounded_exp(table, name):
+    xs, values, want = table
+    got = values[name]
     normal = want >= FLT_MIN
     assert _ulp(got[normal], want[normal]).max() <= 1
     subnormal = (want > 0) & ~normal
     if subnormal.any():
         assert _ulp(got[subnormal], want[subnormal]).max() <= 1
-    # The results are the correctly rounded ones.
-    assert np.mean(got[normal] == want[normal]) > 0.9999
+    assert np.mean(got[normal] == want[normal]) > CORRECTLY_ROUNDED[name]
 
 
-def test_sp_expf_is_monotone(table):
-    xs, got, _ = table
+def test_sp_expf_exact_is_monotone(table):
+    xs, values, _ = table
     order = np.argsort(xs, kind="stable")
-    assert np.all(np.diff(got[order].astype(np.float64)) >= 0.0)
+    assert np.all(np.diff(values["sp_expf_exact"][order].astype(np.float64)) >= 0.0)
 
 
-def test_sp_expf_within_one_ulp_of_libm(table):
-    xs, got, _ = table
+@pytest.mark.parametrize("name", list(EXPS))
+def test_within_one_ulp_of_libm(table, name):
+    xs, values, _ = table
     sample = xs[::7]
     libm = np.array([oracle.libm_expf(float(x)) for x in sample], np.float32)
-    mine = got[::7]
+    mine = values[name][::7]
     positive = libm > 0
     assert _ulp(mine[positive], libm[positive]).max() <= 1
 
 
-def test_sp_expf_special_values():
-    assert np.isnan(oracle.sp_expf(float("nan")))
-    assert oracle.sp_expf(89.0) == float("inf")
-    assert oracle.sp_expf(float("inf")) == float("inf")
-    assert oracle.sp_expf(-105.0) == 0.0
-    assert oracle.sp_expf(float("-inf")) == 0.0
-    assert oracle.sp_expf(0.0) == 1.0
+@pytest.mark.parametrize("name", list(EXPS))
+def test_special_values(name):
+    fn = EXPS[name]
+    assert np.isnan(fn(float("nan")))
+    assert fn(89.0) == float("inf")
+    assert fn(float("inf")) == float("inf")
+    assert fn(-105.0) == 0.0
+    assert fn(float("-inf")) == 0.0
+    assert fn(0.0) == 1.0
 
 
 @pytest.mark.gpu
-def test_sp_expf_within_two_ulp_of_cuda_expf(table):
+@pytest.mark.parametrize("name", list(EXPS))
+def test_within_two_ulp_of_cuda_expf(table, name):
     import torch
 
-    xs, got, _ = table
+    xs, values, _ = table
+    got = values[name]
     cuda = torch.exp(torch.from_numpy(xs).cuda()).cpu().numpy()
     positive = (cuda > 0) & (got > 0) & np.isfinite(cuda)
     assert _ulp(got[positive], cuda[positive]).max() <= 2
