@@ -120,13 +120,18 @@ __global__ void __launch_bounds__(kBlock) k_emit(const float4* __restrict__ reco
             if (__shfl_sync(0xffffffffu, prefix, h + step) <= e) h += step;
         return h;
     };
-    // The key and the value: the Gaussian with the tile's pixel blocks it can reach (common.cuh).
-    auto write_key = [&](unsigned long long slot, uint32_t tx, uint32_t ty, float key_depth, uint32_t gaussian) {
+    // The key and the value: the Gaussian with the tile's pixel blocks it can reach
+    // (common.cuh), given or, without CULL, tested here.
+    auto write_key = [&](unsigned long long slot, uint32_t tx, uint32_t ty, float key_depth, uint32_t gaussian,
+                         uint32_t blocks) {
         const uint32_t tile = ty * tiles_x + tx;
         const Key key = compose_key<Key>(tile, tile_shift, depth_part(key_mode, key_depth, base));
         keys[slot] = key;
-        const float4* rec = records + (size_t)gaussian * kRecord;
-        values[slot] = gaussian | (block_mask(rec[0], rec[1], reach[gaussian], tx, ty) << kGaussianBits);
+        if (!CULL) {
+            const float4* rec = records + (size_t)gaussian * kRecord;
+            blocks = block_mask(rec[0], rec[1], reach[gaussian], tx, ty);
+        }
+        values[slot] = gaussian | (blocks << kGaussianBits);
         for (int p = first_tile_pass; p < passes; ++p) atomicAdd(&hist[p][(uint32_t)(key >> (8 * p)) & 255u], 1u);
     };
     if constexpr (CULL) {
@@ -149,7 +154,29 @@ __global__ void __launch_bounds__(kBlock) k_emit(const float4* __restrict__ reco
             oe.ey = __shfl_sync(0xffffffffu, ellipse.ey, owner);
             oe.stationary = __shfl_sync(0xffffffffu, ellipse.stationary, owner);
             uint2 span = make_uint2(0u, 0u);
-            if (p < total) span = tile_row_span(oe, row, ox0, ox0 + ow);
+            // The ellipse's absolute x-extents over the row's upper and lower 8-pixel bands, from
+            // which each key's pixel blocks follow (the blend's 2 x 2 warp blocks of the tile).
+            float up_l = INFINITY, up_r = -INFINITY, dn_l = INFINITY, dn_r = -INFINITY;
+            if (p < total) {
+                span = tile_row_span(oe, row, ox0, ox0 + ow);
+                if (!(oe.ey < INFINITY)) {
+                    up_l = dn_l = -INFINITY;
+                    up_r = dn_r = INFINITY;
+                } else if (span.y > span.x) {
+                    if (band_extent(oe, row * SP_TILE, SP_TILE / 2, up_l, up_r)) {
+                        up_l = __fadd_rn(up_l, oe.mx);
+                        up_r = __fadd_rn(up_r, oe.mx);
+                    } else {
+                        up_l = INFINITY, up_r = -INFINITY;
+                    }
+                    if (band_extent(oe, row * SP_TILE + SP_TILE / 2, SP_TILE / 2, dn_l, dn_r)) {
+                        dn_l = __fadd_rn(dn_l, oe.mx);
+                        dn_r = __fadd_rn(dn_r, oe.mx);
+                    } else {
+                        dn_l = INFINITY, dn_r = -INFINITY;
+                    }
+                }
+            }
             const uint32_t length = span.y - span.x;
             uint32_t row_inclusive = length;
 #pragma unroll
@@ -177,8 +204,12 @@ __global__ void __launch_bounds__(kBlock) k_emit(const float4* __restrict__ reco
                 const uint32_t key_row = __shfl_sync(0xffffffffu, row, src);
                 const float key_depth = __shfl_sync(0xffffffffu, odepth, src);
                 const uint32_t key_gaussian = __shfl_sync(0xffffffffu, og, src);
+                const float kul = __shfl_sync(0xffffffffu, up_l, src), kur = __shfl_sync(0xffffffffu, up_r, src);
+                const float kdl = __shfl_sync(0xffffffffu, dn_l, src), kdr = __shfl_sync(0xffffffffu, dn_r, src);
+                const uint32_t blocks = half_columns(kul, kur, column) | (half_columns(kdl, kdr, column) << 2);
                 const unsigned long long slot = start + written + e;
-                if (e < round_keys && slot < capacity) write_key(slot, column, key_row, key_depth, key_gaussian);
+                if (e < round_keys && slot < capacity)
+                    write_key(slot, column, key_row, key_depth, key_gaussian, blocks);
             }
             written += round_keys;
         }
@@ -194,7 +225,7 @@ __global__ void __launch_bounds__(kBlock) k_emit(const float4* __restrict__ reco
             const uint32_t row = local / ow;
             const unsigned long long slot = start + e;
             if (e < total && slot < capacity)
-                write_key(slot, ox0 + (local - row * ow), oy0 + row, odepth, og);
+                write_key(slot, ox0 + (local - row * ow), oy0 + row, odepth, og, 0u);
         }
     }
     __syncthreads();

@@ -82,22 +82,42 @@ __device__ __forceinline__ CullEllipse cull_ellipse(float4 a, float4 b) {
     return e;
 }
 
+// The ellipse's x-extent [left, right] (relative to its mean) over the band of pixel-centre
+// rows [first_row, first_row + rows - 1], padded by 0.05 px; false when the band misses it.
+// The ellipse must be neither culled (ey >= 0) nor degenerate (ey finite).
+__device__ __forceinline__ bool band_extent(const CullEllipse& e, uint32_t first_row, uint32_t rows, float& left,
+                                            float& right) {
+    const float lo = __fsub_rn(__fsub_rn((float)first_row, e.my), 0.05f);
+    const float hi = __fadd_rn(lo, (float)(rows - 1) + 0.1f);
+    const float y0 = fmaxf(lo, -e.ey), y1 = fminf(hi, e.ey);
+    if (!(y0 <= y1)) return false;
+    const float yr = fminf(fmaxf(-e.stationary, y0), y1);  // where x_max peaks
+    const float yl = fminf(fmaxf(e.stationary, y0), y1);   // where x_min bottoms
+    const float wr = cull::sqrt_approx(fmaxf(0.0f, __fsub_rn(e.qa, __fmul_rn(e.det, __fmul_rn(yr, yr)))));
+    const float wl = cull::sqrt_approx(fmaxf(0.0f, __fsub_rn(e.qa, __fmul_rn(e.det, __fmul_rn(yl, yl)))));
+    right = __fmul_rn(__fsub_rn(wr, __fmul_rn(e.b, yr)), e.inv_a);
+    left = __fmul_rn(__fadd_rn(wl, __fmul_rn(e.b, yl)), -e.inv_a);
+    return true;
+}
+
+// Which of the two 8-pixel halves of tile column `column` (bit 0: x offset 0, bit 1: offset 8)
+// have a pixel centre within 0.05 px of the absolute x-extent [left, right].
+__device__ __forceinline__ uint32_t half_columns(float left, float right, uint32_t column) {
+    const float x = (float)(column * SP_TILE);
+    uint32_t bits = 0;
+    if (left <= __fadd_rn(x, 7.05f) && right >= __fsub_rn(x, 0.05f)) bits |= 1u;
+    if (left <= __fadd_rn(x, 15.05f) && right >= __fadd_rn(x, 7.95f)) bits |= 2u;
+    return bits;
+}
+
 // The columns [first, end) of tile row `row` the ellipse reaches, within the rectangle's
 // columns [x0, x1).
 __device__ __forceinline__ uint2 tile_row_span(const CullEllipse& e, uint32_t row, uint32_t x0, uint32_t x1) {
     if (!(e.ey >= 0.0f)) return make_uint2(x0, x0);
     if (!(e.ey < INFINITY)) return make_uint2(x0, x1);
     // The row's band of pixel centres, padded by 0.05 px, clamped to the ellipse's extent.
-    const float lo = __fsub_rn(__fsub_rn((float)(row * SP_TILE), e.my), 0.05f);
-    const float hi = __fadd_rn(lo, (float)(SP_TILE - 1) + 0.1f);
-    const float y0 = fmaxf(lo, -e.ey), y1 = fminf(hi, e.ey);
-    if (!(y0 <= y1)) return make_uint2(x0, x0);
-    const float yr = fminf(fmaxf(-e.stationary, y0), y1);  // where x_max peaks
-    const float yl = fminf(fmaxf(e.stationary, y0), y1);   // where x_min bottoms
-    const float wr = cull::sqrt_approx(fmaxf(0.0f, __fsub_rn(e.qa, __fmul_rn(e.det, __fmul_rn(yr, yr)))));
-    const float wl = cull::sqrt_approx(fmaxf(0.0f, __fsub_rn(e.qa, __fmul_rn(e.det, __fmul_rn(yl, yl)))));
-    const float right = __fmul_rn(__fsub_rn(wr, __fmul_rn(e.b, yr)), e.inv_a);
-    const float left = __fmul_rn(__fadd_rn(wl, __fmul_rn(e.b, yl)), -e.inv_a);
+    float left, right;
+    if (!band_extent(e, row * SP_TILE, SP_TILE, left, right)) return make_uint2(x0, x0);
     // Columns whose pixel centres [16 t, 16 t + 15] come within 0.05 px of [left, right]
     // (1 / 16 is exact).
     constexpr float kInvTile = 1.0f / (float)SP_TILE;
