@@ -382,6 +382,15 @@ sp_status sp_count_blend_work(sp_rasterizer* r, uint64_t* forward_pairs, uint64_
  * wrong). UINT32_MAX switches it off. For tests of the bounded device wait only. */
 sp_status sp_debug_stall_sort_partition(sp_rasterizer* r, uint32_t partition);
 
+/* Parity test support (no counterpart in the reference): the falloff power
+ * -1/2 (a dx^2 + c dy^2) - b dx dy (rasterize_forward.wgsl:60-63) exactly as the forward and
+ * atomic backward blend kernels compute it, for `count` items of 12 floats each in device
+ * memory (16-byte aligned): a blend record's words [0] (mean.x, mean.y, conic.a, conic.b) and
+ * [1] (conic.c, ...), then the pixel column x and two pixel rows y0, y1 (and one unused float).
+ * Writes 2 floats per item (the power at (x, y0) and at (x, y1)) to d_powers, on `stream` of
+ * the current device. */
+sp_status sp_debug_falloff_powers(const float* d_items, uint64_t count, float* d_powers, void* stream);
+
 /* ------------------------------------------------------------- per-kernel device timing */
 
 /* Kernels timed by the profiler (CUDA events on the context's stream around each launch;

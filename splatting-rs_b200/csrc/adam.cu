@@ -117,8 +117,7 @@ cudaError_t launch_adam_peer(const PeerBuffers& peers, float* first_moment, floa
     if (peers.world == 0 || peers.world > (uint32_t)kMaxPeers || peers.rank >= peers.world) return cudaErrorInvalidValue;
     AdamStep args{};
     for (int k = 0; k < stride; ++k) args.lr[k] = lr_by_slot_host[k];
-    args.bias1 = bias1;
-    args.bias2 = bias2;
+    args.set_bias(bias1, bias2);
     args.max_log_scale = max_log_scale;
     args.max_log_anisotropy = max_log_anisotropy;
     const unsigned grid = grid_for(count, kGaussiansPerBlock);
@@ -194,8 +193,7 @@ cudaError_t launch_adam(float* params, const float* gradients, float* first_mome
     if (count == 0) return cudaSuccess;
     AdamStep args{};
     for (int k = 0; k < stride; ++k) args.lr[k] = lr_by_slot_host[k];
-    args.bias1 = bias1;
-    args.bias2 = bias2;
+    args.set_bias(bias1, bias2);
     args.max_log_scale = max_log_scale;
     args.max_log_anisotropy = max_log_anisotropy;
     const unsigned grid = grid_for(count, kGaussiansPerBlock);

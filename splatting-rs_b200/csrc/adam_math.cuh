@@ -10,10 +10,40 @@ namespace splat {
 
 // One Adam step's constants: the learning rate of every parameter slot (optimizer.rs:248-256
 // folds the position-rate factor in), the bias corrections 1 - beta^t and the clamp bounds.
+// inv_bias1 / inv_bias2 are the bias corrections' reciprocals in double precision, rounded
+// once (set_bias): the moments are divided by the corrections through them (adam_update).
 struct AdamStep {
     float lr[SP_PARAM_STRIDE(3)];
     float bias1, bias2, max_log_scale, max_log_anisotropy;
+    double inv_bias1, inv_bias2;
+
+    __host__ void set_bias(float b1, float b2) {
+        bias1 = b1;
+        bias2 = b2;
+        inv_bias1 = 1.0 / (double)b1;
+        inv_bias2 = 1.0 / (double)b2;
+    }
 };
+
+// x / b rounded to float, for a float b in [2^-126, 1] given as r = RN64(1 / b): the float
+// rounding of the double product x r. It equals the IEEE single-precision quotient for every
+// float x (zeros, subnormals, infinities and NaN included), at one double multiply and two
+// conversions instead of a single-precision division.
+// Proof. Write x = A 2^a and b = B 2^c with integers A < 2^24 and B in [2^23, 2^24). If B is a
+// power of two, x r is the exact quotient Q = x / b. Otherwise, for Q in the binade
+// [2^e, 2^(e+1)), the float rounding boundaries are M = (2k + 1) 2^(e-24), and
+// (Q - M) B 2^(24-e) = A 2^(a-c-e+24) - B (2k + 1) is a nonzero integer (a zero would make B a
+// power of two), so |Q - M| >= 2^(e-24) / B > 2^-49 Q. Subnormal quotients lie on the grid
+// (2k + 1) 2^-150, at least 2^-150 / B > 2^-174 from it, while Q < 2^-126. The double product
+// carries two roundings (r and x r): |x r - Q| < 2^-51 Q, with neither overflow nor underflow
+// in double for float x and b. So x r lies strictly between the same two rounding boundaries
+// as Q, and rounding it to float gives RN32(Q), the IEEE quotient. tests/test_oracle_math.py
+// checks the identity against numpy's IEEE float32 division: every significand of x for a
+// sample of the bias corrections, and random x over every exponent for the bias corrections
+// of the first 20,000 steps.
+__device__ __forceinline__ float div_by_bias(float x, double reciprocal) {
+    return __double2float_rn((double)x * reciprocal);
+}
 
 // adam.wgsl:26-35 for one parameter: updates the moments, returns the parameter.
 __device__ __forceinline__ float adam_update(float p, float g, float& m, float& v, float lr, const AdamStep& step) {
@@ -21,8 +51,8 @@ __device__ __forceinline__ float adam_update(float p, float g, float& m, float& 
     const float vv = SP_ADAM_BETA2 * v + (1.0f - SP_ADAM_BETA2) * g * g;
     m = mm;
     v = vv;
-    const float m_hat = mm / step.bias1;
-    const float v_hat = vv / step.bias2;
+    const float m_hat = div_by_bias(mm, step.inv_bias1);  // mm / bias1, IEEE
+    const float v_hat = div_by_bias(vv, step.inv_bias2);  // vv / bias2, IEEE
     return p - lr * m_hat / (__fsqrt_rn(v_hat) + SP_ADAM_EPSILON);
 }
 

@@ -186,10 +186,11 @@ struct Falloff {
 
 __device__ __forceinline__ Falloff falloff(float4 a, float4 b, float fpx, float2 fpy) {
     Falloff f;
-    // Scalar operations with explicit rounding: the compiler does not fuse them, whereas the
-    // packed f32x2 products and sums can be fused into FFMA2 whatever their rounding modifier
-    // (measured: a pair's power came out of such a fusion and differed from the oracle's in
-    // its last 14 bits, where the three terms cancel).
+    // Scalar operations with explicit rounding: the compiler does not fuse them, whereas packed
+    // f32x2 products and sums are fused into FFMA2 whatever their rounding modifier, as
+    // intrinsics (__fmul2_rn, __fadd2_rn) and as inline PTX (mul.rn.f32x2, add.rn.f32x2) alike
+    // (measured: such a power differed from the oracle's in up to its last 14 bits where the
+    // three terms cancel; tests/test_gpu_parity.py pins this one bit for bit).
     f.dx = __fadd_rn(a.x, -fpx);
     f.dy = make_float2(__fadd_rn(a.y, -fpy.x), __fadd_rn(a.y, -fpy.y));
     const float t0 = __fmul_rn(__fmul_rn(a.z, f.dx), f.dx), cross = __fmul_rn(a.w, f.dx);
@@ -682,6 +683,16 @@ __global__ void __launch_bounds__(kTilePixels) k_count_blend(const float4* __res
     }
 }
 
+// Test support: the falloff power of item i (record words a = in[3i], b = in[3i + 1], pixel
+// column in[3i + 2].x, rows .y and .z) as falloff() gives it to the forward and the atomic
+// backward.
+__global__ void k_falloff_powers(const float4* __restrict__ in, uint64_t n, float2* __restrict__ out) {
+    const uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    const float4 pixel = in[3 * i + 2];
+    out[i] = falloff(in[3 * i], in[3 * i + 1], pixel.x, make_float2(pixel.y, pixel.z)).power;
+}
+
 }  // namespace
 
 cudaError_t launch_count_blend(const float4* records, const uint32_t* sorted_gaussians, const uint2* ranges,
@@ -724,3 +735,15 @@ cudaError_t launch_blend_backward(int mode, const float4* records, const uint32_
 }
 
 }  // namespace splat
+
+extern "C" sp_status sp_debug_falloff_powers(const float* d_items, uint64_t count, float* d_powers, void* stream) {
+    using namespace splat;
+    if (count == 0) return SP_OK;
+    if (!d_items || !d_powers || (reinterpret_cast<uintptr_t>(d_items) & 15u) != 0 ||
+        (reinterpret_cast<uintptr_t>(d_powers) & 7u) != 0)
+        return SP_ERR_INVALID;
+    const unsigned blocks = (unsigned)((count + 255) / 256);
+    k_falloff_powers<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(reinterpret_cast<const float4*>(d_items),
+                                                                             count, reinterpret_cast<float2*>(d_powers));
+    return cudaGetLastError() == cudaSuccess ? SP_OK : SP_ERR_CUDA;
+}

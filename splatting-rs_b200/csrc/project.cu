@@ -723,8 +723,7 @@ cudaError_t launch_project_backward(const float* params, uint64_t n, int sh_degr
         fused.first_moment = adam->first_moment;
         fused.second_moment = adam->second_moment;
         for (int k = 0; k < SP_PARAM_STRIDE(sh_degree); ++k) fused.step.lr[k] = adam->lr_by_slot[k];
-        fused.step.bias1 = adam->bias1;
-        fused.step.bias2 = adam->bias2;
+        fused.step.set_bias(adam->bias1, adam->bias2);
         fused.step.max_log_scale = adam->max_log_scale;
         fused.step.max_log_anisotropy = adam->max_log_anisotropy;
     }

@@ -116,6 +116,65 @@ def test_image_matches(ctx, name):
     assert mismatched < 5e-3, f"{name}: {mismatched:.4%} of contributor counts differ"
 
 
+def _falloff_items(rng, count):
+    """Blend records (words [0], [1]) and pixels: conics from round to needle-thin (the
+    off-diagonal up to 0.999 of its bound, where the three terms of the power cancel), pixels
+    from the centre out to powers of about -100, integer pixel coordinates as the kernels use."""
+    a = np.exp(rng.uniform(np.log(1e-4), np.log(20.0), count)).astype(np.float32)
+    c = np.exp(rng.uniform(np.log(1e-4), np.log(20.0), count)).astype(np.float32)
+    b = (rng.uniform(-0.999, 0.999, count) * np.sqrt(a * c)).astype(np.float32)
+    mean = rng.uniform(0.0, 2048.0, (count, 2)).astype(np.float32)
+    level = np.where(rng.random(count) < 0.5, 20.0, 200.0)  # |power| up to about level / 2
+    px = np.floor(mean[:, 0] + rng.uniform(-1, 1, count) * np.minimum(np.sqrt(level / a), 3000)).astype(np.float32)
+    py0 = np.floor(mean[:, 1] + rng.uniform(-1, 1, count) * np.minimum(np.sqrt(level / c), 3000)).astype(np.float32)
+    items = np.zeros((count, 12), np.float32)
+    items[:, 0:2] = mean
+    items[:, 2] = a
+    items[:, 3] = b
+    items[:, 4] = c
+    items[:, 5] = 0.5  # opacity (not read)
+    items[:, 8] = px
+    items[:, 9] = py0
+    items[:, 10] = py0 + 4.0  # the lane's second pixel, four rows below
+    return items
+
+
+def _oracle_powers(items):
+    """The power in the oracle's (and rasterize_forward.wgsl:60-63's) operation order, one
+    float32 rounding per operation: -0.5 (a d0 d0 + c d1 d1) - b d0 d1, d = mean - pixel."""
+    f = np.float32
+    out = np.empty((len(items), 2), np.float32)
+    d0 = items[:, 0] - items[:, 8]
+    for k, row in enumerate((9, 10)):
+        d1 = items[:, 1] - items[:, row]
+        quad = (items[:, 2] * d0) * d0 + (items[:, 4] * d1) * d1
+        out[:, k] = f(-0.5) * quad - (items[:, 3] * d0) * d1
+    return out
+
+
+def test_blend_falloff_power_bit_exact(ctx):
+    """The blend kernels' falloff power equals the oracle's bit for bit, cancelling cases
+    included: the take (alpha >= 1/255) and clamp (0.99) decisions rest on it. (Packed f32x2
+    forms of the same operations fail this test: the compiler fuses them into FFMA2.)"""
+    import ctypes
+
+    import torch
+    from splat_b200 import _lib
+
+    items = _falloff_items(np.random.default_rng(61), 1 << 20)
+    want = _oracle_powers(items)
+    d_items = torch.from_numpy(items).cuda()
+    d_powers = torch.empty((len(items), 2), dtype=torch.float32, device="cuda")
+    lib = _lib.load()
+    status = lib.sp_debug_falloff_powers(ctypes.c_void_p(d_items.data_ptr()), len(items),
+                                         ctypes.c_void_p(d_powers.data_ptr()),
+                                         ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+    assert status == _lib.SP_OK
+    got = d_powers.cpu().numpy()
+    assert np.all(np.isfinite(want)) and 0.2 < np.mean((want > -10.0) & (want <= 0.0)) < 0.9
+    assert np.array_equal(got.view(np.uint32), want.view(np.uint32)), int(np.sum(got != want))
+
+
 def test_loss_matches(ctx):
     rng = np.random.default_rng(5)
     width, height = 40, 24

@@ -109,3 +109,46 @@ def test_within_two_ulp_of_cuda_expf(table, name):
     cuda = torch.exp(torch.from_numpy(xs).cuda()).cpu().numpy()
     positive = (cuda > 0) & (got > 0) & np.isfinite(cuda)
     assert _ulp(got[positive], cuda[positive]).max() <= 2
+
+
+# Adam's bias-corrected moments (adam.wgsl:30-31: m / (1 - beta1^t), v / (1 - beta2^t)) are IEEE
+# float divisions in the reference and the oracle; the CUDA kernels form them as the float
+# rounding of x * RN64(1 / b) (div_by_bias in csrc/adam_math.cuh, with a proof that the two are
+# equal for every float x and every float b in [2^-126, 1]). Checked here with numpy's IEEE
+# float32 division and float64 product.
+
+
+def _bias_corrections(beta: float, steps: int) -> np.ndarray:
+    t = np.arange(1, steps + 1, dtype=np.float32)
+    return (np.float32(1.0) - np.power(np.float32(beta), t)).astype(np.float32)
+
+
+def _div_by_bias(x: np.ndarray, b: np.float32) -> np.ndarray:
+    return (x.astype(np.float64) * (1.0 / np.float64(b))).astype(np.float32)
+
+
+def _same_floats(got: np.ndarray, want: np.ndarray) -> bool:
+    nan = np.isnan(want)
+    return bool(np.array_equal(np.isnan(got), nan) and np.array_equal(got[~nan].view(np.uint32), want[~nan].view(np.uint32)))
+
+
+def test_division_by_the_bias_corrections_is_the_ieee_quotient():
+    biases = np.unique(np.concatenate([_bias_corrections(0.9, 20_000), _bias_corrections(0.999, 20_000)]))
+    assert biases.min() > 0 and biases.max() == 1.0 and len(biases) > 10_000
+    # Every significand (x in [1, 2)) for a sample of the corrections, the first steps' included:
+    # for quotients in the normal range the rounding depends on the significands only.
+    significands = (np.arange(1 << 23, dtype=np.uint32) | np.uint32(0x3F800000)).view(np.float32)
+    sample = np.unique(np.concatenate([_bias_corrections(0.9, 4), _bias_corrections(0.999, 4),
+                                       biases[np.linspace(0, len(biases) - 1, 24).astype(int)]]))
+    for b in sample:
+        assert _same_floats(_div_by_bias(significands, b), significands / b), b
+    # Random bit patterns (every exponent: zeros, subnormals, infinities, NaN) for every correction.
+    rng = np.random.default_rng(5)
+    x = rng.integers(0, 1 << 32, size=2048, dtype=np.uint64).astype(np.uint32).view(np.float32)
+    x = np.concatenate([x, np.array([0.0, -0.0, np.inf, -np.inf, 1e-45, -1e-45, 3.4028235e38], np.float32)])
+    for chunk in np.array_split(biases, 16):
+        b = chunk[:, None]
+        with np.errstate(over="ignore", invalid="ignore"):
+            want = x[None, :] / b
+            got = (x[None, :].astype(np.float64) * (1.0 / b.astype(np.float64))).astype(np.float32)
+        assert _same_floats(got.ravel(), want.ravel())
