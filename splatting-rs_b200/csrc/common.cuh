@@ -5,6 +5,7 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <atomic>
 #include <utility>
 
 #include "../../include/splat.h"
@@ -12,6 +13,21 @@
 #include "../../include/splat_math.h"
 
 namespace splat {
+
+// Raises a kernel's dynamic shared-memory limit to `bytes` on the current device, once per
+// device and call site: `done` holds one bit per device, because function attributes are set
+// per device and a process may drive several GPUs (devices past 63 are set at every call).
+template <typename Kernel>
+inline cudaError_t allow_smem_once(Kernel kernel, size_t bytes, std::atomic<unsigned long long>& done) {
+    int device = 0;
+    cudaError_t err = cudaGetDevice(&device);
+    if (err != cudaSuccess) return err;
+    const unsigned long long bit = device < 64 ? 1ull << device : 0ull;
+    if (bit && (done.load(std::memory_order_relaxed) & bit)) return cudaSuccess;
+    err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+    if (err == cudaSuccess) done.fetch_or(bit, std::memory_order_relaxed);
+    return err;
+}
 
 constexpr int kBlock = 256;                 // threads of every 1-D kernel
 constexpr int kTilePixels = SP_TILE * SP_TILE;

@@ -298,13 +298,9 @@ Taps window() {
 
 cudaError_t launch_ssim(const float4* image, const float4* ground_truth, uint32_t width, uint32_t height,
                         float4* partials, cudaStream_t stream) {
-    static bool configured = false;
-    if (!configured) {
-        const cudaError_t err =
-            cudaFuncSetAttribute(k_ssim, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSsimSmem);
-        if (err != cudaSuccess) return err;
-        configured = true;
-    }
+    static std::atomic<unsigned long long> configured{0};
+    const cudaError_t err = allow_smem_once(k_ssim, kSsimSmem, configured);
+    if (err != cudaSuccess) return err;
     const dim3 grid(grid_for(width, kTile), grid_for(height, kTile));
     launch_chained(k_ssim, grid, kThreads, kSsimSmem, stream, image, ground_truth, width, height, window(), partials);
     return cudaGetLastError();
@@ -313,13 +309,9 @@ cudaError_t launch_ssim(const float4* image, const float4* ground_truth, uint32_
 cudaError_t launch_loss(const float4* image, const float4* ground_truth, const float4* partials, uint32_t width,
                         uint32_t height, const sp_loss_weights& weights, float4* loss_gradient, float4* pixel_loss,
                         cudaStream_t stream) {
-    static bool configured = false;
-    if (!configured) {
-        const cudaError_t err =
-            cudaFuncSetAttribute(k_loss, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kLossSmem);
-        if (err != cudaSuccess) return err;
-        configured = true;
-    }
+    static std::atomic<unsigned long long> configured{0};
+    const cudaError_t err = allow_smem_once(k_loss, kLossSmem, configured);
+    if (err != cudaSuccess) return err;
     const dim3 grid(grid_for(width, kTile), grid_for(height, kTile));
     launch_chained(k_loss, grid, kThreads, kLossSmem, stream, image, ground_truth, partials, width, height, window(), weights,
                                                   loss_gradient, pixel_loss);

@@ -507,26 +507,18 @@ cudaError_t launch_sort_pass(const SortPlan& plan, int pass, uint32_t sequence, 
     if (plan.key64) {
         using K = unsigned long long;
         const size_t smem = kSortPartition * (sizeof(K) + sizeof(uint32_t));
-        static bool configured = false;
-        if (!configured) {
-            const cudaError_t err =
-                cudaFuncSetAttribute(k_sort_pass<K>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-            if (err != cudaSuccess) return err;
-            configured = true;
-        }
+        static std::atomic<unsigned long long> configured{0};
+        const cudaError_t err = allow_smem_once(k_sort_pass<K>, smem, configured);
+        if (err != cudaSuccess) return err;
         launch_chained(k_sort_pass<K>, grid, kSortThreads, smem, stream, pass, sequence, static_cast<K*>(keys0), values0,
                                                              static_cast<K*>(keys1), values1, hist,
                                                              sort_tickets + pass, lookback, meta);
     } else {
         using K = uint32_t;
         const size_t smem = kSortPartition * (sizeof(K) + sizeof(uint32_t));
-        static bool configured = false;
-        if (!configured) {
-            const cudaError_t err =
-                cudaFuncSetAttribute(k_sort_pass<K>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-            if (err != cudaSuccess) return err;
-            configured = true;
-        }
+        static std::atomic<unsigned long long> configured{0};
+        const cudaError_t err = allow_smem_once(k_sort_pass<K>, smem, configured);
+        if (err != cudaSuccess) return err;
         launch_chained(k_sort_pass<K>, grid, kSortThreads, smem, stream, pass, sequence, static_cast<K*>(keys0), values0,
                                                              static_cast<K*>(keys1), values1, hist,
                                                              sort_tickets + pass, lookback, meta);
