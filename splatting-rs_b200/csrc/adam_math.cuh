@@ -45,6 +45,28 @@ __device__ __forceinline__ float div_by_bias(float x, double reciprocal) {
     return __double2float_rn((double)x * reciprocal);
 }
 
+// u / d rounded to float for a positive float divisor d whose reciprocal is a normal float
+// (d in [2^-126, 2^126]) or d = +inf (the seed rcp(+inf) = +0 and the residual's d held at the
+// largest float keep y = 0: u y is then the IEEE u / inf, +-0 or NaN): the reciprocal by
+// Newton-Raphson (Markstein's y <- y + y (1 - d y), each step one fused multiply-add for the
+// residual and one for the update) in double precision from the hardware's approximate
+// single-precision reciprocal, then u y in double rounded once to float. It equals the IEEE
+// single-precision quotient for every float u. Proof: the seed's relative error is below
+// 2^-20, so the steps leave at most 2^-40 and then 2^-80 plus the roundings, under
+// 2^-53 (1 + 2^-26) in all; with the product's rounding, u y is within 2^-51 u / d of the
+// exact quotient, which (as for div_by_bias) lies more than 2^-49 of itself from every float
+// rounding boundary, so both round to the same float. tests/test_gpu_parity.py checks it
+// against IEEE float32 division (sp_debug_adam_quotients).
+__device__ __forceinline__ float div_exact(float u, float d) {
+    float seed;
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(seed) : "f"(d));
+    const double dd = (double)fminf(d, 3.40282347e38f);  // the largest float
+    double y = (double)seed;
+    y = fma(y, fma(-dd, y, 1.0), y);
+    y = fma(y, fma(-dd, y, 1.0), y);
+    return __double2float_rn((double)u * y);
+}
+
 // adam.wgsl:26-35 for one parameter: updates the moments, returns the parameter.
 __device__ __forceinline__ float adam_update(float p, float g, float& m, float& v, float lr, const AdamStep& step) {
     const float mm = SP_ADAM_BETA1 * m + (1.0f - SP_ADAM_BETA1) * g;
@@ -53,7 +75,7 @@ __device__ __forceinline__ float adam_update(float p, float g, float& m, float& 
     v = vv;
     const float m_hat = div_by_bias(mm, step.inv_bias1);  // mm / bias1, IEEE
     const float v_hat = div_by_bias(vv, step.inv_bias2);  // vv / bias2, IEEE
-    return p - lr * m_hat / (__fsqrt_rn(v_hat) + SP_ADAM_EPSILON);
+    return p - div_exact(lr * m_hat, __fsqrt_rn(v_hat) + SP_ADAM_EPSILON);  // IEEE quotient
 }
 
 // clamp_scales.wgsl:15-29 on one Gaussian's three log scales, with std::min semantics

@@ -271,6 +271,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "sp_count_blend_work": (c_int, [_P, POINTER(c_uint64), POINTER(c_uint64)]),
     "sp_debug_stall_sort_partition": (c_int, [_P, c_uint32]),
     "sp_debug_falloff_powers": (c_int, [c_void_p, c_uint64, c_void_p, c_void_p]),
+    "sp_debug_adam_quotients": (c_int, [c_void_p, c_void_p, c_uint64, c_void_p, c_void_p]),
     "sp_profile_enable": (c_int, [_P, c_int]),
     "sp_profile_read": (c_int, [_P, POINTER(c_double), POINTER(c_uint64)]),
     "sp_adam_create": (c_int, [_P, _P, _P, c_uint64, c_uint32, POINTER(LearningRatesC), c_float, POINTER(_P)]),

@@ -175,6 +175,50 @@ def test_blend_falloff_power_bit_exact(ctx):
     assert np.array_equal(got.view(np.uint32), want.view(np.uint32)), int(np.sum(got != want))
 
 
+def test_adam_divisions_are_ieee_quotients(ctx):
+    """The Adam step's divisions (csrc/adam_math.cuh: by the bias corrections through a
+    double-precision reciprocal, by sqrt(v_hat) + epsilon through a double-precision
+    Newton-Raphson reciprocal) equal IEEE float32 division bit for bit (NaN for NaN): random
+    dividends over every exponent, the bias corrections of the first 20,000 steps, and
+    update divisors from 1e-15 to 1e19, powers of two and infinity."""
+    import ctypes
+
+    import torch
+    from splat_b200 import _lib
+
+    rng = np.random.default_rng(67)
+    n = 1 << 23
+    x = rng.integers(0, 1 << 32, size=n, dtype=np.uint64).astype(np.uint32).view(np.float32)
+    t = np.arange(1, 20_001, dtype=np.float32)
+    corrections = np.concatenate([np.float32(1) - np.power(np.float32(0.9), t),
+                                  np.float32(1) - np.power(np.float32(0.999), t)]).astype(np.float32)
+    y = np.empty(n, np.float32)
+    half = n // 2
+    y[:half] = rng.choice(corrections, half)
+    y[half:] = np.exp(rng.uniform(np.log(1e-15), np.log(1e19), n - half)).astype(np.float32)
+    y[half:half + 64] = np.float32(2.0) ** np.arange(-48, 16, dtype=np.float32)
+    y[-16:] = np.inf
+    d_x, d_y = torch.from_numpy(x).cuda(), torch.from_numpy(y).cuda()
+    out = torch.empty((n, 2), dtype=torch.float32, device="cuda")
+    lib = _lib.load()
+    status = lib.sp_debug_adam_quotients(ctypes.c_void_p(d_x.data_ptr()), ctypes.c_void_p(d_y.data_ptr()), n,
+                                         ctypes.c_void_p(out.data_ptr()),
+                                         ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+    assert status == _lib.SP_OK
+    got = out.cpu().numpy()
+    with np.errstate(all="ignore"):
+        want = x / y
+    bias = (y > 0) & (y <= 1)
+
+    def same(a, b):
+        nan = np.isnan(b)
+        return np.array_equal(np.isnan(a), nan) and np.array_equal(a[~nan].view(np.uint32), b[~nan].view(np.uint32))
+
+    assert bias.sum() > half
+    assert same(got[bias, 0], want[bias]), int(np.sum(got[bias, 0].view(np.uint32) != want[bias].view(np.uint32)))
+    assert same(got[:, 1], want), int(np.sum(got[:, 1].view(np.uint32) != want.view(np.uint32)))
+
+
 def test_loss_matches(ctx):
     rng = np.random.default_rng(5)
     width, height = 40, 24
