@@ -412,7 +412,10 @@ sp_status sp_loss(sp_rasterizer* r, uint32_t view) {
     const float4* gt = reinterpret_cast<const float4*>(r->ground_truth) + (size_t)view * r->pixels();
     {
         KernelSpan span(r->ctx, SP_K_SSIM);
-        SP_CUDA(r->ctx, launch_ssim(r->image, gt, r->width, r->height, r->ssim_partials, r->ctx->stream));
+        const bool clear = r->options.backward_mode == SP_BWD_ATOMIC;
+        SP_CUDA(r->ctx, launch_ssim(r->image, gt, r->width, r->height, r->ssim_partials,
+                                    clear ? r->gaussian_gradients : nullptr, clear ? r->n * 3 : 0, r->ctx->stream));
+        r->blend_sums_zero = clear;
     }
     {
         KernelSpan span(r->ctx, SP_K_LOSS);
@@ -428,8 +431,10 @@ namespace {
 sp_status blend_backward(sp_rasterizer* r) {
     cudaStream_t st = r->ctx->stream;
     KernelSpan span(r->ctx, SP_K_BLEND_BACKWARD);
-    if (r->options.backward_mode == SP_BWD_ATOMIC)
+    // The sums start at zero: zeroed by this view's sp_loss (k_ssim), else here.
+    if (r->options.backward_mode == SP_BWD_ATOMIC && !r->blend_sums_zero)
         SP_CUDA(r->ctx, cudaMemsetAsync(r->gaussian_gradients, 0, r->n * 3 * sizeof(float4), st));
+    r->blend_sums_zero = false;
     SP_CUDA(r->ctx, launch_blend_backward((int)r->options.backward_mode, r->records, r->values[r->sorted_buffer],
                                           r->ranges, r->tile_order, r->offsets, r->camera, r->image,
                                           r->contributions, r->loss_gradient, r->slot_gradients,

@@ -547,7 +547,6 @@ __global__ void __launch_bounds__(kBlock, 3) k_project_backward(
     unsigned long long capacity, const float4* __restrict__ gaussian_gradients, float* __restrict__ param_gradients,
     int accumulate, float* __restrict__ camera_partials, uint32_t* camera_done, float* __restrict__ camera_gradient,
     float4* __restrict__ densify_stats, const FusedAdam adam, uint32_t first_block, uint32_t total_blocks) {
-    chain_enter();
     constexpr int S = SP_PARAM_STRIDE(DEG);
     __shared__ sp_camera_uniform s_cam;
     const sp_camera_uniform& cam = pick_camera<DEV>(camera_argument, s_cam);
@@ -563,8 +562,13 @@ __global__ void __launch_bounds__(kBlock, 3) k_project_backward(
     const uint32_t block = first_block + blockIdx.x;
     const uint32_t g0 = block * kBlock;
     const uint32_t here = min((uint32_t)kBlock, n - g0);
+    // The parameters, the camera and the rates do not depend on the previous grid of the
+    // chain (the blend backward, which writes only the blend sums): they are staged before
+    // waiting for it, so the first wave's loads overlap that grid's last blocks. Everything
+    // below the wait may read what the blend backward wrote.
     stage_in(params + (size_t)g0 * S, here * S, sp);
     if (FUSED && threadIdx.x < (uint32_t)S) s_lr[threadIdx.x] = adam.step.lr[threadIdx.x];
+    chain_enter();
     __syncthreads();
     const uint32_t t = threadIdx.x;
     float cgrad[SP_CAMERA_GRAD_STRIDE];
