@@ -325,6 +325,18 @@ sp_status sp_loss_sums_noalloc(int device, const float* d_pixel_loss, uint64_t p
 /* read_intersections (rasterizer.rs:536-544): fills `out` and returns SP_ERR_OVERFLOW when
  * the list overflowed (where the reference panics). */
 sp_status sp_read_intersections(sp_rasterizer* r, sp_intersection_meta* out);
+/* The intersection capacity sized from the scan (no counterpart in the reference, whose
+ * capacity is fixed at 24 N, rasterizer.rs:27, and which panics on overflow): the number of
+ * (Gaussian, tile) pairs the last forward pass's scan counted, before truncation at the
+ * capacity. A caller that met SP_ERR_OVERFLOW reserves that many (with a margin) and
+ * renders again. */
+sp_status sp_intersections_needed(sp_rasterizer* r, uint64_t* total);
+/* Grows the intersection buffers (keys, values, the sort's look-back words and, in the
+ * deterministic backward, the per-slot gradients) to `capacity` pairs, below 2^32. Never
+ * shrinks. Synchronises the context's stream; the last forward pass's lists are dropped, so
+ * the next backward needs a forward first. On an allocation failure the rasterizer is left
+ * as it was and SP_ERR_CUDA is returned. */
+sp_status sp_reserve_intersections(sp_rasterizer* r, uint64_t capacity);
 /* sp_backward then sp_adam_step(adam, position_rate_factor) in one pass over the
  * parameters: the projection backward applies the Adam update and the scale clamp to each
  * Gaussian as soon as its gradient is complete, so the parameter gradients are not written

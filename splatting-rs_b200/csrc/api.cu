@@ -607,9 +607,66 @@ sp_status sp_read_loss(sp_rasterizer* r, sp_loss_terms* out) {
 }
 
 static sp_status overflow_error(sp_rasterizer* r) {
+    DeviceMeta meta{};
+    const bool known = read_device(r->ctx, &meta, r->meta, sizeof(meta)) == SP_OK;
+    const uint64_t needed = ((uint64_t)meta.total_hi << 32) | meta.total_lo;
     return fail(r->ctx, SP_ERR_OVERFLOW,
-                "intersection list overflow: more than " + std::to_string(r->capacity) +
-                    " (Gaussian, tile) pairs; Gaussians are too large for the image");
+                "intersection list overflow: " + (known ? std::to_string(needed) : std::string("more than ")) +
+                    (known ? " (Gaussian, tile) pairs, " : "") + "the capacity is " + std::to_string(r->capacity) +
+                    "; Gaussians are too large for the image, or reserve more with sp_reserve_intersections");
+}
+
+sp_status sp_intersections_needed(sp_rasterizer* r, uint64_t* total) {
+    if (!r || !total) return SP_ERR_INVALID;
+    SP_CHECK(select_device(r->ctx));
+    DeviceMeta meta;
+    SP_CHECK(read_device(r->ctx, &meta, r->meta, sizeof(meta)));
+    *total = ((uint64_t)meta.total_hi << 32) | meta.total_lo;
+    return SP_OK;
+}
+
+sp_status sp_reserve_intersections(sp_rasterizer* r, uint64_t capacity) {
+    if (!r) return SP_ERR_INVALID;
+    SP_REQUIRE(r->ctx, capacity < (1ull << 32), SP_ERR_INVALID, "2^32 intersections or more");
+    if (capacity <= r->capacity) return SP_OK;
+    SP_CHECK(select_device(r->ctx));
+    SP_CUDA(r->ctx, cudaStreamSynchronize(r->ctx->stream));
+    const uint32_t partitions = (uint32_t)((capacity + kSortPartition - 1) / kSortPartition);
+    const size_t key_bytes = r->plan.key64 ? 8 : 4;
+    // Every capacity-sized buffer: the key and value ping-pong pairs, the sort's look-back
+    // words and (deterministic backward) the per-slot gradients. The new ones are allocated
+    // first, so that a failure leaves the rasterizer as it was.
+    void** slots[6] = {&r->keys[0], &r->keys[1], reinterpret_cast<void**>(&r->values[0]),
+                       reinterpret_cast<void**>(&r->values[1]), reinterpret_cast<void**>(&r->lookback),
+                       reinterpret_cast<void**>(&r->slot_gradients)};
+    const size_t bytes[6] = {capacity * key_bytes, capacity * key_bytes, capacity * sizeof(uint32_t),
+                             capacity * sizeof(uint32_t),
+                             (size_t)std::max<uint32_t>(partitions, 1) * kSortRadix * sizeof(unsigned long long),
+                             r->slot_gradients ? capacity * SP_GRAD_STRIDE * sizeof(float) : 0};
+    void* fresh[6] = {};
+    for (int k = 0; k < 6; ++k) {
+        if (bytes[k] == 0) continue;
+        cudaError_t err = cudaMalloc(&fresh[k], bytes[k]);
+        if (err == cudaSuccess && k == 4) err = cudaMemset(fresh[k], 0, bytes[k]);
+        if (err != cudaSuccess) {
+            for (int j = 0; j <= k; ++j)
+                if (fresh[j]) cudaFree(fresh[j]);
+            return cuda_fail(r->ctx, err, "cudaMalloc (sp_reserve_intersections)");
+        }
+    }
+    for (int k = 0; k < 6; ++k) {
+        if (!fresh[k]) continue;
+        void* old = *slots[k];
+        auto at = std::find(r->allocations.begin(), r->allocations.end(), old);
+        if (at != r->allocations.end()) r->allocations.erase(at);
+        cudaFree(old);
+        *slots[k] = fresh[k];
+        r->allocations.push_back(fresh[k]);
+    }
+    r->capacity = capacity;
+    r->max_partitions = partitions;
+    r->forward_done = false;  // the lists of the last forward pass are gone
+    return SP_OK;
 }
 
 sp_status sp_read_intersections(sp_rasterizer* r, sp_intersection_meta* out) {

@@ -270,6 +270,8 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "sp_clear_densify_stats": (c_int, [_P]),
     "sp_count_blend_work": (c_int, [_P, POINTER(c_uint64), POINTER(c_uint64)]),
     "sp_debug_stall_sort_partition": (c_int, [_P, c_uint32]),
+    "sp_intersections_needed": (c_int, [_P, POINTER(c_uint64)]),
+    "sp_reserve_intersections": (c_int, [_P, c_uint64]),
     "sp_debug_falloff_powers": (c_int, [c_void_p, c_uint64, c_void_p, c_void_p]),
     "sp_debug_adam_quotients": (c_int, [c_void_p, c_void_p, c_uint64, c_void_p, c_void_p]),
     "sp_profile_enable": (c_int, [_P, c_int]),

@@ -369,6 +369,18 @@ class Rasterizer:
             self._check(status, "read_intersections")
         return out
 
+    def intersections_needed(self) -> int:
+        """The (Gaussian, tile) pairs the last forward pass's scan counted, before truncation at
+        the capacity (sp_intersections_needed)."""
+        out = ctypes.c_uint64()
+        self._check(self.lib.sp_intersections_needed(self.handle, ctypes.byref(out)), "intersections_needed")
+        return int(out.value)
+
+    def reserve_intersections(self, capacity: int) -> None:
+        """Grows the intersection buffers to `capacity` pairs (sp_reserve_intersections); the
+        next backward needs a forward pass first."""
+        self._check(self.lib.sp_reserve_intersections(self.handle, int(capacity)), "reserve_intersections")
+
     def debug_stall_sort_partition(self, partition: int | None) -> None:
         """Error-path test switch (sp_debug_stall_sort_partition): sort partition `partition`
         never posts its look-back record, so the next one's wait runs out (SP_ERR_TIMEOUT);

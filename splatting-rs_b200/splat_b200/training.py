@@ -36,8 +36,17 @@ class Trainer:
         ctx: Context | None = None,
         backward_mode: int | None = None,
         densify: DensifySettings | None = None,
+        capacity: str = "fixed",
     ):
+        """`capacity`: "fixed", the reference's 24 (Gaussian, tile) pairs per Gaussian
+        (rasterizer.rs:27), or "scan": the intersection lists sized from the scan of every
+        view's forward pass, with a quarter of headroom, at construction and after each
+        densification (sp_intersections_needed / sp_reserve_intersections). Either way a step
+        whose lists overflow raises SplatError(SP_ERR_OVERFLOW) naming the pairs it needed."""
         import torch
+
+        if capacity not in ("fixed", "scan"):
+            raise ValueError(f"capacity policy {capacity!r}: 'fixed' or 'scan'")
 
         if not cameras:
             raise ValueError("no views")
@@ -57,7 +66,10 @@ class Trainer:
         options = default_options(sh_degree=self.sh_degree)
         if backward_mode is not None:
             options.backward_mode = backward_mode
+        if capacity == "scan":
+            options.intersections_per_gaussian = 1  # grown from the scan below
         self.options = options
+        self.capacity_policy = capacity
         self.width, self.height = width, height
         self.rasterizer = Rasterizer(
             self.ctx, self.params, len(cloud), width, height, self.ground_truth, len(cameras), options
@@ -78,6 +90,19 @@ class Trainer:
             np.float32(self.extent),
             sh_degree=self.sh_degree,
         )
+        if capacity == "scan":
+            self._size_intersections()
+
+    def _size_intersections(self) -> None:
+        """The "scan" capacity policy: every view's forward pass (its lists may overflow the
+        current capacity; the scan still counts every pair), then the largest count plus a
+        quarter reserved."""
+        needed = 0
+        for view in range(self.view_count):
+            self.rasterizer.set_camera(self.camera(view))
+            self.rasterizer.encode_forward()
+            needed = max(needed, self.rasterizer.intersections_needed())
+        self.rasterizer.reserve_intersections(needed + needed // 4 + 1024)
 
     @property
     def view_count(self) -> int:
@@ -121,6 +146,8 @@ class Trainer:
         self.params, self.rasterizer, self.adam = out.params, rasterizer, adam
         self.gaussian_count = count
         self.densifications.append(out.report)
+        if self.capacity_policy == "scan":
+            self._size_intersections()
         return out.report
 
     def loss(self, view: int) -> LossTerms:
