@@ -71,6 +71,84 @@ def test_loss_curve_matches_the_oracle(ctx, mode):
     assert gpu_losses[-3:].mean() < gpu_losses[:3].mean()
 
 
+def _camera_gradient(values):
+    v = np.asarray(values, np.float32)
+    from splat_b200._lib import CameraGradient
+
+    cg = CameraGradient()
+    for i in range(3):
+        for j in range(3):
+            cg.world_to_camera_rotation_rows[i][j] = float(v[3 * i + j])
+    for i in range(3):
+        cg.world_to_camera_translation[i] = float(v[9 + i])
+    cg.focal[0], cg.focal[1] = float(v[12]), float(v[13])
+    return cg
+
+
+@pytest.mark.parametrize("mode", [sb.SP_BWD_DETERMINISTIC, sb.SP_BWD_ATOMIC])
+def test_loss_curve_with_pose_refinement_matches_the_oracle(ctx, mode):
+    """The same 100 steps with pose refinement on (Trainer::step_async with a PoseRefinement,
+    training.rs:197-209): each step's camera from the refinement, the step, the camera gradient
+    read back and the f64 pose Adam step. The oracle's leg takes the oracle's render, loss,
+    backward and Adam and feeds its own camera gradient to its own refinement (the host pose
+    chain, pinned by the reference's known answers, is the same code on both legs). Bars: every
+    step's loss within 1e-3 relative; the refined poses of views 1 and 2 (view 0 stays fixed)
+    within 1e-3 of how far the refinement moved them (Adam's normalised steps integrate the
+    rounding-level differences of the two legs' camera gradients over the run: measured 1.7e-4)."""
+    import torch
+
+    scene = scenes.config(0)
+    cams = scene.cameras
+    gt = ground_truth(scene)
+    extent = np.float32(sb.cameras_extent(cams))
+    rates = sb.LEARNING_RATES_3DGS
+
+    params = torch.from_numpy(scene.cloud.to_packed()).cuda()
+    gt_dev = torch.from_numpy(gt.reshape(-1)).cuda()
+    rast = sb.Rasterizer(ctx, params, len(scene.cloud), 256, 256, gt_dev, len(cams),
+                         sb.default_options(backward_mode=mode))
+    adam = sb.Adam(ctx, params, rast, len(scene.cloud), rates, extent)
+    poses = sb.PoseRefinement(cams, rates, float(extent))
+    gpu_losses = []
+    for step in range(STEPS):
+        view = step % len(cams)
+        factor = sb.position_rate_factor(step, STEPS)
+        gradient, loss = rast.train_step(adam, poses.camera(view), view, factor)
+        poses.step(view, gradient, factor)
+        gpu_losses.append(loss.total)
+
+    packed = scene.cloud.to_packed().copy()
+    m, v = np.zeros_like(packed), np.zeros_like(packed)
+    max_log = float(np.log(np.float32(0.02) * extent))
+    aniso = float(np.log(np.float32(10.0)))
+    oracle_poses = sb.PoseRefinement(cams, rates, float(extent))
+    oracle_losses = []
+    for step in range(STEPS):
+        view = step % len(cams)
+        factor = sb.position_rate_factor(step, STEPS)
+        cam = oracle.camera_of(oracle_poses.camera(view))
+        fwd = oracle.render(packed, 0, cam)
+        partials = oracle.ssim(fwd["image"], gt[view].reshape(-1), 256, 256)
+        loss_gradient, pixel_loss = oracle.loss(fwd["image"], gt[view].reshape(-1), partials, 256, 256)
+        bwd = oracle.backward(packed, 0, cam, fwd, loss_gradient)
+        lr = oracle.learning_rates_by_slot(rates.to_c(), np.float32(extent * np.float32(factor)), 14)
+        oracle.adam_step(packed, bwd["param_gradients"], m, v, 14, lr, step + 1, max_log, aniso)
+        oracle_poses.step(view, _camera_gradient(bwd["camera_gradient"]), factor)
+        oracle_losses.append(float(np.mean(pixel_loss.reshape(-1, 4)[:, 3].astype(np.float64))))
+
+    gpu_losses, oracle_losses = np.array(gpu_losses), np.array(oracle_losses)
+    rel = np.abs(gpu_losses - oracle_losses) / np.abs(oracle_losses)
+    assert rel.max() < 1e-3, f"step {rel.argmax()}: {gpu_losses[rel.argmax()]} vs {oracle_losses[rel.argmax()]}"
+    assert gpu_losses[-3:].mean() < gpu_losses[:3].mean()
+    for view in range(1, len(cams)):
+        got, want = poses.camera(view), oracle_poses.camera(view)
+        moved = max(np.abs(want.rotation - cams[view].rotation).max(),
+                    np.abs(want.translation - cams[view].translation).max())
+        assert moved > 0.0, "the refinement moved the pose"
+        assert np.abs(got.rotation - want.rotation).max() <= 1e-3 * moved
+        assert np.abs(got.translation - want.translation).max() <= 1e-3 * moved
+
+
 def test_fused_train_step_equals_the_separate_calls(ctx):
     """sp_train_step (one call with its 88-byte read-back) against set_camera, forward, loss,
     backward, Adam and the two reads issued one by one: bit-identical parameters, camera
