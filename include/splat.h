@@ -303,7 +303,9 @@ sp_status sp_read_densify_stats(sp_rasterizer* r, sp_densify_stats* host); /* N 
 sp_status sp_read_camera_gradient(sp_rasterizer* r, sp_camera_gradient* host);
 sp_status sp_read_image(sp_rasterizer* r, float* host_rgbt);         /* P * 4 */
 sp_status sp_read_pixel_loss(sp_rasterizer* r, float* host);         /* P * 4 */
-sp_status sp_read_loss(sp_rasterizer* r, sp_loss_terms* out);        /* read_loss */
+/* read_loss; `out` is filled, and SP_ERR_OVERFLOW (or the device status) returned, when the
+ * frame was rendered from truncated lists. */
+sp_status sp_read_loss(sp_rasterizer* r, sp_loss_terms* out);
 
 /* Largest pixel_count sp_loss_sums_noalloc accepts: 1024 blocks of 4096 pixels. */
 #define SP_NOALLOC_MAX_PIXELS 4194304ull

@@ -590,6 +590,8 @@ sp_status sp_read_pixel_loss(sp_rasterizer* r, float* host) {
     return read_device(r->ctx, host, r->pixel_loss, r->pixels() * sizeof(float4));
 }
 
+static sp_status overflow_error(sp_rasterizer* r);
+
 sp_status sp_read_loss(sp_rasterizer* r, sp_loss_terms* out) {
     if (!r || !out) return SP_ERR_INVALID;
     SP_CHECK(select_device(r->ctx));
@@ -603,6 +605,11 @@ sp_status sp_read_loss(sp_rasterizer* r, sp_loss_terms* out) {
     out->alpha = (float)(sums[1] / pixels);
     out->dssim = (float)(sums[2] / pixels);
     out->total = (float)(sums[3] / pixels);
+    // The loss of a frame rendered from truncated lists, or after a device-side wait gave up,
+    // comes with the error (the terms are filled in all the same).
+    DeviceMeta meta;
+    SP_CHECK(device_status(r, &meta));
+    if (meta.overflow) return overflow_error(r);
     return SP_OK;
 }
 

@@ -35,6 +35,10 @@ def test_reserve_after_overflow_gives_the_full_lists(ctx, mode):
     want = oracle.render(cloud.to_packed(), cloud.sh_degree, oracle.camera_array(camera.uniform()))
     assert needed == len(want["keys"]) > len(cloud)
     assert str(needed) in str(err.value)  # the error names the pairs the frame needs
+    rast.encode_loss(0)  # the loss of a truncated frame comes with the overflow error too
+    with pytest.raises(sb.SplatError) as err:
+        rast.read_loss()
+    assert err.value.status == 3
 
     rast.reserve_intersections(needed)
     rast.reserve_intersections(needed // 2)  # never shrinks

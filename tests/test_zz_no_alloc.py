@@ -82,7 +82,9 @@ def test_noalloc_at_exactly_the_largest_size(ctx):
     camera = sb.PinholeCamera(np.eye(3), np.zeros(3), (1400.0, 1400.0), (1024, 1024), width, height)
     mask = (rng.random(pixels) < 0.5).astype(np.float32)
     gt = np.concatenate([rng.random((pixels, 3)).astype(np.float32) * mask[:, None], mask[:, None]], axis=1)
-    rast, _, _ = make_rasterizer(ctx, cloud, camera, ground_truth=gt.reshape(-1))
+    # Enough list capacity for the frame's 192k (Gaussian, tile) pairs: the loss of a truncated
+    # frame is reported as an overflow.
+    rast, _, _ = make_rasterizer(ctx, cloud, camera, ground_truth=gt.reshape(-1), intersections_per_gaussian=128)
     lib = _lib.load()
     stream = torch.cuda.current_stream().cuda_stream
     rast.encode_forward()
