@@ -852,7 +852,7 @@ def main() -> None:
 
     # ---- e2e with the poses refined on the device (one GPU): the same steps through
     # sp_train_step_device_poses, no host synchronisation per step; each step's loss sums
-    # (32 B) are copied asynchronously into its own slot of a pinned host ring.
+    # (32 B) land in their own slot of a pinned host ring.
     e2e_device = None
     if world == 1:
         params.copy_(initial)
@@ -883,8 +883,8 @@ def main() -> None:
             "h2d_bytes_per_step": 0,
             "d2h_bytes_per_step": 32,
             "what": "sp_train_step_device_poses: forward + loss + backward + Adam + the pose step on the device, "
-                    "the next view's camera written on the device, the loss sums (32 B) copied asynchronously "
-                    "to pinned host memory; no host synchronisation per step",
+                    "the next view's camera written on the device, the loss sums (32 B) written into pinned "
+                    "host memory by the loss-sum kernel; no host synchronisation per step",
         }
         device_poses.close()
         del adam_dp

@@ -700,8 +700,10 @@ sp_status sp_device_poses_download(sp_device_poses* dp, sp_pose_refinement* into
  * with the camera already in place (sp_device_poses_set_camera, or the previous step), loss
  * against `view`, backward + Adam (fused when `adam` steps the rasterizer's own
  * parameters), the pose step of `view` and the camera of next_view; if pinned_loss_sums
- * (page-locked host memory, 4 doubles) is not NULL, the loss sums (L1, alpha, D-SSIM, total;
- * divide by the pixel count for the means) are copied into it asynchronously. */
+ * (4 doubles) is not NULL, the loss sums (L1, alpha, D-SSIM, total; divide by the pixel count
+ * for the means) land in it asynchronously: written by the loss-sum kernel itself when it is
+ * page-locked host memory (cudaHostAlloc, cudaHostRegister, torch's pin_memory), else copied
+ * there from the device. */
 sp_status sp_train_step_device_poses(sp_rasterizer* r, sp_adam* adam, sp_device_poses* dp, uint32_t view,
                                      uint32_t next_view, float position_rate_factor, double* pinned_loss_sums);
 

@@ -849,10 +849,21 @@ sp_status sp_train_step_device_poses(sp_rasterizer* r, sp_adam* adam, sp_device_
     SP_CHECK(sp_device_poses_step(dp, view, next_view, position_rate_factor));
     if (pinned_loss_sums) {
         cudaStream_t st = r->ctx->stream;
-        SP_CUDA(r->ctx, launch_loss_sums(r->pixel_loss, r->pixels(), r->loss_sums, r->loss_result, nullptr, nullptr,
-                                         st));
-        SP_CUDA(r->ctx,
-                cudaMemcpyAsync(pinned_loss_sums, r->loss_result, 4 * sizeof(double), cudaMemcpyDeviceToHost, st));
+        // Page-locked host memory the device can address: the loss-sum kernel writes the sums
+        // there itself, so no copy breaks the launch chain into the next step. Other memory
+        // takes the device buffer and an asynchronous copy.
+        cudaPointerAttributes attributes{};
+        double* direct = nullptr;
+        if (cudaPointerGetAttributes(&attributes, pinned_loss_sums) == cudaSuccess &&
+            attributes.type == cudaMemoryTypeHost && attributes.devicePointer)
+            direct = static_cast<double*>(attributes.devicePointer);
+        else
+            cudaGetLastError();  // an address CUDA does not know: not an error, the copy serves
+        SP_CUDA(r->ctx, launch_loss_sums(r->pixel_loss, r->pixels(), r->loss_sums, direct ? direct : r->loss_result,
+                                         nullptr, nullptr, st));
+        if (!direct)
+            SP_CUDA(r->ctx,
+                    cudaMemcpyAsync(pinned_loss_sums, r->loss_result, 4 * sizeof(double), cudaMemcpyDeviceToHost, st));
     }
     return SP_OK;
 }

@@ -13,6 +13,7 @@ namespace {
 __global__ void k_pose_step(const sp_pinhole_camera* __restrict__ initial, pose::ViewState* states,
                             pose::SharedState* shared, const float* __restrict__ camera_gradient, uint32_t views,
                             uint32_t view, uint32_t next_view, double factor, sp_camera_uniform* camera_out) {
+    chain_enter();  // the camera gradient is the previous grid's (the projection backward's)
     if (threadIdx.x != 0 || blockIdx.x != 0) return;
     if (view < views) {
         sp_camera_gradient g;
@@ -35,8 +36,8 @@ __global__ void k_pose_step(const sp_pinhole_camera* __restrict__ initial, pose:
 cudaError_t launch_pose_step(const sp_pinhole_camera* initial, pose::ViewState* states, pose::SharedState* shared,
                              const float* camera_gradient, uint32_t views, uint32_t view, uint32_t next_view,
                              double factor, sp_camera_uniform* camera_out, cudaStream_t stream) {
-    k_pose_step<<<1, 32, 0, stream>>>(initial, states, shared, camera_gradient, views, view, next_view, factor,
-                                      camera_out);
+    launch_chained(k_pose_step, 1, 32, 0, stream, initial, states, shared, camera_gradient, views, view, next_view,
+                   factor, camera_out);
     return cudaGetLastError();
 }
 
