@@ -87,9 +87,12 @@ void learning_rates_by_slot(const sp_learning_rates& rates, float position_scale
 namespace splat {
 // loss.cu: deterministic sum of the per-pixel loss terms into workspace[0..4) (the
 // workspace holds 4 + 4 * 256 + 1 doubles); with `meta`, its status word and overflow flag
-// are copied into status_dst[0..2).
+// are copied into status_dst[0..2); with mirror_dst (mapped page-locked host memory), the
+// last block then copies mirror_words words from mirror_src there.
 cudaError_t launch_loss_sums(const float4* pixel_loss, uint64_t pixels, double* workspace, double* result,
-                             const DeviceMeta* meta, uint32_t* status_dst, cudaStream_t stream);
+                             const DeviceMeta* meta, uint32_t* status_dst, cudaStream_t stream,
+                             const uint32_t* mirror_src = nullptr, uint32_t* mirror_dst = nullptr,
+                             uint32_t mirror_words = 0);
 }  // namespace splat
 
 extern "C" {
@@ -324,6 +327,11 @@ sp_status sp_rasterizer_create(sp_context* ctx, const float* d_params, uint64_t 
         if (err != cudaSuccess) {
             sp_rasterizer_destroy(r);
             return cuda_fail(ctx, err, "cudaMallocHost");
+        }
+        // Its device view, for the loss-sum kernel to fill it directly (none: a copy does).
+        if (cudaHostGetDevicePointer(&r->readback_mapped, r->readback, 0) != cudaSuccess) {
+            r->readback_mapped = nullptr;
+            cudaGetLastError();
         }
     }
     // The default camera of rasterizer.rs:202-213: identity pose, unit focal.
@@ -708,10 +716,16 @@ sp_status sp_train_step(sp_rasterizer* r, sp_adam* adam, const sp_camera_uniform
     cudaStream_t st = r->ctx->stream;
     if (loss_out) {
         // The loss-sum kernel also copies the step's status next to the camera gradient and the
-        // sums: one copy brings the whole read-back.
+        // sums, then the whole read-back into the page-locked host struct itself (its device
+        // view): no copy follows the step's last kernel (else one copy brings it).
+        const uint32_t words = (uint32_t)(sizeof(sp_rasterizer::StepReadback) / sizeof(uint32_t));
         SP_CUDA(r->ctx, launch_loss_sums(r->pixel_loss, r->pixels(), r->loss_sums, r->loss_result, r->meta,
-                                         &r->readback_dev->status, st));
-        SP_CUDA(r->ctx, cudaMemcpyAsync(r->readback, r->readback_dev, sizeof(*r->readback), cudaMemcpyDeviceToHost, st));
+                                         &r->readback_dev->status, st,
+                                         reinterpret_cast<const uint32_t*>(r->readback_dev),
+                                         reinterpret_cast<uint32_t*>(r->readback_mapped), words));
+        if (!r->readback_mapped)
+            SP_CUDA(r->ctx,
+                    cudaMemcpyAsync(r->readback, r->readback_dev, sizeof(*r->readback), cudaMemcpyDeviceToHost, st));
     } else {
         SP_CUDA(r->ctx, cudaMemcpyAsync(&r->readback->status, &r->meta->status, sizeof(uint32_t),
                                         cudaMemcpyDeviceToHost, st));

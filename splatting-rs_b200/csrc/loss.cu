@@ -340,10 +340,14 @@ constexpr int kSumBlocks = 256;
 // share, a tree per block, then the last block adds the block sums in block order), so
 // that the reported loss does not depend on scheduling.
 // The last block also copies the step's status word and overflow flag (from `meta`, when
-// given) next to the sums, so that a step's read-back is one copy.
+// given) next to the sums, so that a step's read-back is one block of words; with
+// `mirror_dst` (page-locked host memory mapped for the device) it then copies those
+// `mirror_words` words from `mirror_src` there itself, so that no copy follows the kernel.
 __global__ void __launch_bounds__(kBlock) k_loss_sums(const float4* __restrict__ pixel_loss, uint64_t pixels,
                                                       double* __restrict__ workspace, double* __restrict__ result,
-                                                      const DeviceMeta* meta, uint32_t* status_dst) {
+                                                      const DeviceMeta* meta, uint32_t* status_dst,
+                                                      const uint32_t* mirror_src, uint32_t* mirror_dst,
+                                                      uint32_t mirror_words) {
     chain_enter();
     __shared__ double s[4][kBlock];
     __shared__ bool last;
@@ -387,13 +391,19 @@ __global__ void __launch_bounds__(kBlock) k_loss_sums(const float4* __restrict__
             status_dst[1] = meta->overflow;
         }
     }
+    if (mirror_dst) {
+        __syncthreads();  // the sums and the status words above are written
+        for (uint32_t i = t; i < mirror_words; i += kBlock) mirror_dst[i] = __ldcg(mirror_src + i);
+    }
 }
 
 }  // namespace
 
 cudaError_t launch_loss_sums(const float4* pixel_loss, uint64_t pixels, double* workspace, double* result,
-                             const DeviceMeta* meta, uint32_t* status_dst, cudaStream_t stream) {
-    launch_chained(k_loss_sums, kSumBlocks, kBlock, 0, stream, pixel_loss, pixels, workspace, result, meta, status_dst);
+                             const DeviceMeta* meta, uint32_t* status_dst, cudaStream_t stream,
+                             const uint32_t* mirror_src, uint32_t* mirror_dst, uint32_t mirror_words) {
+    launch_chained(k_loss_sums, kSumBlocks, kBlock, 0, stream, pixel_loss, pixels, workspace, result, meta, status_dst,
+                   mirror_src, mirror_dst, mirror_words);
     return cudaGetLastError();
 }
 

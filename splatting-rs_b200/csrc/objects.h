@@ -133,6 +133,7 @@ struct sp_rasterizer {
         double loss[4];
     };
     StepReadback* readback = nullptr;
+    void* readback_mapped = nullptr;  // `readback` as the device addresses it
     // Its device side: the camera gradient and the loss sums live here (camera_gradient and
     // loss_result point into it), so that a step's read-back is one copy.
     StepReadback* readback_dev = nullptr;
