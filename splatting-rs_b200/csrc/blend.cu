@@ -186,19 +186,23 @@ struct Falloff {
 
 __device__ __forceinline__ Falloff falloff(float4 a, float4 b, float fpx, float2 fpy) {
     Falloff f;
-    // Scalar operations with explicit rounding: the compiler does not fuse them, whereas packed
-    // f32x2 products and sums are fused into FFMA2 whatever their rounding modifier, as
-    // intrinsics (__fmul2_rn, __fadd2_rn) and as inline PTX (mul.rn.f32x2, add.rn.f32x2) alike
-    // (measured: such a power differed from the oracle's in up to its last 14 bits where the
-    // three terms cancel; tests/test_gpu_parity.py pins this one bit for bit).
+    // Rounded operation by operation, as the oracle: the sums and differences are scalar
+    // operations with explicit rounding, which the compiler never contracts into a fused
+    // multiply-add; the products are packed (FMUL2, one rounding per lane), which is safe
+    // because every product feeds one of those scalar sums or another product. Packed sums
+    // are not used: the compiler contracts packed products and sums into FFMA2 whatever their
+    // rounding modifier, as intrinsics (__fadd2_rn) and as inline PTX (add.rn.f32x2) alike
+    // (measured: 14 % of such powers differed from the oracle's where the three terms cancel;
+    // tests/test_gpu_parity.py pins this form bit for bit through sp_debug_falloff_powers).
+    // The row offsets dy are sums too, but of no product: packed.
     f.dx = __fadd_rn(a.x, -fpx);
-    f.dy = make_float2(__fadd_rn(a.y, -fpy.x), __fadd_rn(a.y, -fpy.y));
+    f.dy = __fadd2_rn(splat(a.y), make_float2(-fpy.x, -fpy.y));
     const float t0 = __fmul_rn(__fmul_rn(a.z, f.dx), f.dx), cross = __fmul_rn(a.w, f.dx);
-    float2 power;
-    power.x = __fadd_rn(__fmul_rn(-0.5f, __fadd_rn(t0, __fmul_rn(__fmul_rn(b.x, f.dy.x), f.dy.x))),
-                        -__fmul_rn(cross, f.dy.x));
-    power.y = __fadd_rn(__fmul_rn(-0.5f, __fadd_rn(t0, __fmul_rn(__fmul_rn(b.x, f.dy.y), f.dy.y))),
-                        -__fmul_rn(cross, f.dy.y));
+    const float2 q = __fmul2_rn(__fmul2_rn(splat(b.x), f.dy), f.dy);
+    const float2 cd = __fmul2_rn(splat(cross), f.dy);
+    const float2 quad = make_float2(__fadd_rn(t0, q.x), __fadd_rn(t0, q.y));
+    const float2 h = __fmul2_rn(splat(-0.5f), quad);
+    const float2 power = make_float2(__fadd_rn(h.x, -cd.x), __fadd_rn(h.y, -cd.y));
     f.power = power;
     f.below0 = power.x <= 0.0f;
     f.below1 = power.y <= 0.0f;
