@@ -767,13 +767,14 @@ def main() -> None:
     counter = rast if culling == sb.SP_TILES_RECTANGLE else sb.Rasterizer(
         ctx, params, len(cloud), width, height, gt, views,
         sb.default_options(sh_degree=deg, backward_mode=sb.SP_BWD_ATOMIC))
-    fwd_pairs, bwd_pairs = 0, 0
+    fwd_pairs, bwd_pairs, taken_pairs = 0, 0, 0
     for v in range(views):
         counter.set_camera(uniforms[v])
         counter.encode_forward()
-        f, b = counter.count_blend_work()
+        f, b, t = counter.count_blend_work()
         fwd_pairs += f
         bwd_pairs += b
+        taken_pairs += t
     if counter is not rast:
         counter.close()
         del counter
@@ -901,11 +902,17 @@ def main() -> None:
         if name == "blend_forward":
             achieved = fwd_pairs / views * FORWARD_OPS_PER_PAIR / (kms / n * 1e-3) / 1e12
             entry.update(bound="fp32", achieved=achieved, peak=fp32_peak, unit="T FP32 ops/s",
-                         frac=achieved / fp32_peak, pairs_per_launch=fwd_pairs / views)
+                         frac=achieved / fp32_peak, pairs_per_launch=fwd_pairs / views,
+                         # The pairs that blend (alpha >= 1/255 before the termination), of the
+                         # reference's visited pairs the roofline counts.
+                         active_pairs_per_launch=taken_pairs / views,
+                         active_fraction=taken_pairs / max(fwd_pairs, 1))
         elif name == "blend_backward":
             achieved = bwd_pairs / views * BACKWARD_OPS_PER_PAIR / (kms / n * 1e-3) / 1e12
             entry.update(bound="fp32", achieved=achieved, peak=fp32_peak, unit="T FP32 ops/s",
-                         frac=achieved / fp32_peak, pairs_per_launch=bwd_pairs / views)
+                         frac=achieved / fp32_peak, pairs_per_launch=bwd_pairs / views,
+                         active_pairs_per_launch=taken_pairs / views,
+                         active_fraction=taken_pairs / max(bwd_pairs, 1))
         elif name == "adam":
             # The sharded exchange steps this rank's share of the Gaussians only.
             stepped = n_params // world if world > 1 and train_step.exchange.mode == "sharded" else n_params

@@ -385,8 +385,10 @@ sp_status sp_clear_densify_stats(sp_rasterizer* r);
  * pass's per-pixel decisions; no reference counterpart, used for roofline accounting):
  * forward_pairs = sum over pixels of the tile-list entries the forward visits, up to and
  * including the one that terminates the pixel; backward_pairs = sum over pixels of the
- * contributor count (the entries the backward replays). */
-sp_status sp_count_blend_work(sp_rasterizer* r, uint64_t* forward_pairs, uint64_t* backward_pairs);
+ * contributor count (the entries the backward replays); taken_pairs (may be NULL) = sum over
+ * pixels of the entries actually blended (alpha at least 1/255, before the termination). */
+sp_status sp_count_blend_work(sp_rasterizer* r, uint64_t* forward_pairs, uint64_t* backward_pairs,
+                              uint64_t* taken_pairs);
 
 /* Error-path test switch (no counterpart in the reference): from the next forward pass on,
  * sort partition `partition` of every sort pass never posts its digit counts, and its

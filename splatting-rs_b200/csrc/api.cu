@@ -987,23 +987,25 @@ sp_status sp_read_gaussian_blend_gradients(sp_rasterizer* r, float* host) {
     return SP_OK;
 }
 
-sp_status sp_count_blend_work(sp_rasterizer* r, uint64_t* forward_pairs, uint64_t* backward_pairs) {
+sp_status sp_count_blend_work(sp_rasterizer* r, uint64_t* forward_pairs, uint64_t* backward_pairs,
+                              uint64_t* taken_pairs) {
     if (!r || !forward_pairs || !backward_pairs) return SP_ERR_INVALID;
     SP_REQUIRE(r->ctx, r->forward_done, SP_ERR_INVALID, "count before any forward pass");
     SP_CHECK(select_device(r->ctx));
     unsigned long long* counts = nullptr;
-    SP_CUDA(r->ctx, cudaMallocAsync((void**)&counts, 2 * sizeof(unsigned long long), r->ctx->stream));
-    cudaError_t err = cudaMemsetAsync(counts, 0, 2 * sizeof(unsigned long long), r->ctx->stream);
+    SP_CUDA(r->ctx, cudaMallocAsync((void**)&counts, 3 * sizeof(unsigned long long), r->ctx->stream));
+    cudaError_t err = cudaMemsetAsync(counts, 0, 3 * sizeof(unsigned long long), r->ctx->stream);
     if (err == cudaSuccess)
         err = launch_count_blend(r->records, r->values[r->sorted_buffer], r->ranges, r->camera, r->contributions,
                                  counts, r->ctx->stream);
-    unsigned long long host[2] = {0, 0};
+    unsigned long long host[3] = {0, 0, 0};
     sp_status s = err == cudaSuccess ? read_device(r->ctx, host, counts, sizeof(host))
                                      : cuda_fail(r->ctx, err, "launch_count_blend");
     cudaFreeAsync(counts, r->ctx->stream);
     cudaStreamSynchronize(r->ctx->stream);
     *forward_pairs = host[0];
     *backward_pairs = host[1];
+    if (taken_pairs) *taken_pairs = host[2];
     return s;
 }
 

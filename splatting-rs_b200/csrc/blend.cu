@@ -648,7 +648,8 @@ __global__ void __launch_bounds__(kOrderThreads) k_tile_order(const uint2* __res
 }
 
 // The forward's per-pixel walk without the colour, counting the entries visited (up to
-// and including the terminating one), plus the contributor counts the backward replays.
+// and including the terminating one), the entries taken (blended: alpha at least 1/255,
+// before the termination), plus the contributor counts the backward replays.
 __global__ void __launch_bounds__(kTilePixels) k_count_blend(const float4* __restrict__ records,
                                                              const uint32_t* __restrict__ sorted,
                                                              const uint2* __restrict__ ranges,
@@ -659,7 +660,7 @@ __global__ void __launch_bounds__(kTilePixels) k_count_blend(const float4* __res
     const uint32_t gx = tile % cam.tiles_x, gy = tile / cam.tiles_x;
     const uint32_t t = threadIdx.x;
     const uint32_t px = gx * SP_TILE + local_x(t / 32, lane_id()), py = gy * SP_TILE + local_y(t / 32, lane_id());
-    unsigned long long visited = 0, replayed = 0;
+    unsigned long long visited = 0, replayed = 0, taken = 0;
     if (px < cam.width && py < cam.height) {
         const uint2 range = ranges[tile];
         const float fpx = (float)px, fpy = (float)py;
@@ -676,14 +677,17 @@ __global__ void __launch_bounds__(kTilePixels) k_count_blend(const float4* __res
             const float next = transmittance * (1.0f - alpha);
             if (next < SP_MIN_TRANSMITTANCE) break;
             transmittance = next;
+            ++taken;
         }
         replayed = contributions[(size_t)py * cam.width + px];
     }
     visited = __reduce_add_sync(kFull, (unsigned)visited);
     replayed = __reduce_add_sync(kFull, (unsigned)replayed);
+    taken = __reduce_add_sync(kFull, (unsigned)taken);
     if (lane_id() == 0) {
         atomicAdd(counts, visited);
         atomicAdd(counts + 1, replayed);
+        atomicAdd(counts + 2, taken);
     }
 }
 

@@ -268,7 +268,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "sp_read_tile_offsets": (c_int, [_P, _P]),
     "sp_read_gaussian_blend_gradients": (c_int, [_P, _P]),
     "sp_clear_densify_stats": (c_int, [_P]),
-    "sp_count_blend_work": (c_int, [_P, POINTER(c_uint64), POINTER(c_uint64)]),
+    "sp_count_blend_work": (c_int, [_P, POINTER(c_uint64), POINTER(c_uint64), POINTER(c_uint64)]),
     "sp_debug_stall_sort_partition": (c_int, [_P, c_uint32]),
     "sp_intersections_needed": (c_int, [_P, POINTER(c_uint64)]),
     "sp_reserve_intersections": (c_int, [_P, c_uint64]),

@@ -485,11 +485,13 @@ class Rasterizer:
     def read_tile_offsets(self) -> np.ndarray:
         return self._read(self.lib.sp_read_tile_offsets, self.gaussian_count, np.uint32, "read_tile_offsets")
 
-    def count_blend_work(self) -> tuple[int, int]:
-        """(forward pairs visited, backward pairs replayed) of the last forward pass."""
-        fwd, bwd = ctypes.c_uint64(), ctypes.c_uint64()
-        self._check(self.lib.sp_count_blend_work(self.handle, ctypes.byref(fwd), ctypes.byref(bwd)), "count")
-        return int(fwd.value), int(bwd.value)
+    def count_blend_work(self) -> tuple[int, int, int]:
+        """(forward pairs visited, backward pairs replayed, pairs blended) of the last forward
+        pass."""
+        fwd, bwd, taken = ctypes.c_uint64(), ctypes.c_uint64(), ctypes.c_uint64()
+        self._check(self.lib.sp_count_blend_work(self.handle, ctypes.byref(fwd), ctypes.byref(bwd),
+                                                 ctypes.byref(taken)), "count")
+        return int(fwd.value), int(bwd.value), int(taken.value)
 
     def read_gaussian_blend_gradients(self) -> np.ndarray:
         return self._read(

@@ -219,6 +219,17 @@ def test_adam_divisions_are_ieee_quotients(ctx):
     assert same(got[:, 1], want), int(np.sum(got[:, 1].view(np.uint32) != want.view(np.uint32)))
 
 
+def test_blend_work_counts(ctx):
+    """sp_count_blend_work (roofline accounting): the pairs blended, replayed and visited nest,
+    and the pairs replayed are the sum of the contributor counts the forward wrote."""
+    cloud, camera = CASES["config2_5k_sh3_1024x768"]
+    rast, _, _ = make_rasterizer(ctx, cloud, camera)
+    rast.encode_forward()
+    visited, replayed, taken = rast.count_blend_work()
+    assert 0 < taken <= replayed <= visited
+    assert replayed == int(rast.read_contributions().astype(np.int64).sum())
+
+
 def test_loss_matches(ctx):
     rng = np.random.default_rng(5)
     width, height = 40, 24
