@@ -420,15 +420,15 @@ sp_status sp_loss(sp_rasterizer* r, uint32_t view) {
     const float4* gt = reinterpret_cast<const float4*>(r->ground_truth) + (size_t)view * r->pixels();
     {
         KernelSpan span(r->ctx, SP_K_SSIM);
-        const bool clear = r->options.backward_mode == SP_BWD_ATOMIC;
-        SP_CUDA(r->ctx, launch_ssim(r->image, gt, r->width, r->height, r->ssim_partials,
-                                    clear ? r->gaussian_gradients : nullptr, clear ? r->n * 3 : 0, r->ctx->stream));
-        r->blend_sums_zero = clear;
+        SP_CUDA(r->ctx, launch_ssim(r->image, gt, r->width, r->height, r->ssim_partials, r->ctx->stream));
     }
     {
         KernelSpan span(r->ctx, SP_K_LOSS);
+        const bool clear = r->options.backward_mode == SP_BWD_ATOMIC;
         SP_CUDA(r->ctx, launch_loss(r->image, gt, r->ssim_partials, r->width, r->height, r->options.loss_weights,
-                                    r->loss_gradient, r->pixel_loss, r->ctx->stream));
+                                    r->loss_gradient, r->pixel_loss, clear ? r->gaussian_gradients : nullptr,
+                                    clear ? r->n * 3 : 0, r->ctx->stream));
+        r->blend_sums_zero = clear;
     }
     return SP_OK;
 }
@@ -439,7 +439,7 @@ namespace {
 sp_status blend_backward(sp_rasterizer* r) {
     cudaStream_t st = r->ctx->stream;
     KernelSpan span(r->ctx, SP_K_BLEND_BACKWARD);
-    // The sums start at zero: zeroed by this view's sp_loss (k_ssim), else here.
+    // The sums start at zero: zeroed by this view's sp_loss (k_loss), else here.
     if (r->options.backward_mode == SP_BWD_ATOMIC && !r->blend_sums_zero)
         SP_CUDA(r->ctx, cudaMemsetAsync(r->gaussian_gradients, 0, r->n * 3 * sizeof(float4), st));
     r->blend_sums_zero = false;

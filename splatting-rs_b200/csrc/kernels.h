@@ -106,14 +106,14 @@ cudaError_t launch_count_blend(const float4* records, const uint32_t* sorted_gau
 
 // ---- loss.cu
 
-// ssim_forward.wgsl:34-91 (separable window sums in shared memory). When `clear` is given it
-// also zeroes its first `clear_count` float4s (the atomic backward's blend sums for this view).
+// ssim_forward.wgsl:34-91 (separable window sums in shared memory).
 cudaError_t launch_ssim(const float4* image, const float4* ground_truth, uint32_t width, uint32_t height,
-                        float4* partials, float4* clear, uint64_t clear_count, cudaStream_t stream);
-// loss.wgsl:35-97.
+                        float4* partials, cudaStream_t stream);
+// loss.wgsl:35-97. When `clear` is given it also zeroes its first `clear_count` float4s (the
+// atomic backward's blend sums for this view).
 cudaError_t launch_loss(const float4* image, const float4* ground_truth, const float4* partials, uint32_t width,
                         uint32_t height, const sp_loss_weights& weights, float4* loss_gradient, float4* pixel_loss,
-                        cudaStream_t stream);
+                        float4* clear, uint64_t clear_count, cudaStream_t stream);
 
 // ---- adam.cu
 

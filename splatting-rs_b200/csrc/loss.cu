@@ -88,17 +88,7 @@ constexpr size_t kLossSmem = (size_t)3 * kSpan * kSpan * sizeof(float) + (size_t
 // mu_x, E[x^2] and E[xy] (masked), into planar partials[channel][pixel].
 __global__ void __launch_bounds__(kThreads, 2) k_ssim(const float4* __restrict__ image, const float4* __restrict__ gt,
                                                       uint32_t width, uint32_t height, const Taps taps,
-                                                      float4* __restrict__ partials, float4* __restrict__ clear,
-                                                      uint64_t clear_count) {
-    // The atomic backward's per-Gaussian blend sums are zeroed here, a slice per block, for the
-    // backward that follows this loss (instead of a memset that would break the launch chain).
-    // No grid of the chain before this one touches them, so it happens before the wait.
-    if (clear) {
-        const uint64_t blocks = (uint64_t)gridDim.x * gridDim.y, block = (uint64_t)blockIdx.y * gridDim.x + blockIdx.x;
-        const uint64_t per = (clear_count + blocks - 1) / blocks;
-        const uint64_t end = min(clear_count, (block + 1) * per);
-        for (uint64_t i = block * per + threadIdx.x; i < end; i += kThreads) clear[i] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-    }
+                                                      float4* __restrict__ partials) {
     chain_enter();
     extern __shared__ float4 smem4[];
     float2* s_in = reinterpret_cast<float2*>(smem4);         // [3][kSpan][kSpan]: (x, y) per channel
@@ -189,7 +179,18 @@ __global__ void __launch_bounds__(kThreads, 3) k_loss(const float4* __restrict__
                                                       uint32_t height, const Taps taps,
                                                       const sp_loss_weights weights,
                                                       float4* __restrict__ loss_gradient,
-                                                      float4* __restrict__ pixel_loss) {
+                                                      float4* __restrict__ pixel_loss, float4* __restrict__ clear,
+                                                      uint64_t clear_count) {
+    // The atomic backward's per-Gaussian blend sums are zeroed here, a slice per block, for the
+    // backward that follows this loss (instead of a memset that would break the launch chain;
+    // here rather than in k_ssim, which is issue-bound, while these blocks mostly wait on their
+    // loads). No grid of the chain before this one touches them: before the wait.
+    if (clear) {
+        const uint64_t blocks = (uint64_t)gridDim.x * gridDim.y, block = (uint64_t)blockIdx.y * gridDim.x + blockIdx.x;
+        const uint64_t per = (clear_count + blocks - 1) / blocks;
+        const uint64_t end = min(clear_count, (block + 1) * per);
+        for (uint64_t i = block * per + threadIdx.x; i < end; i += kThreads) clear[i] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    }
     chain_enter();
     extern __shared__ float4 smem4[];
     float* s_in = reinterpret_cast<float*>(smem4);           // [3][kSpan][kSpan]: d_mu, d_exx, d_exy
@@ -307,25 +308,24 @@ Taps window() {
 }  // namespace
 
 cudaError_t launch_ssim(const float4* image, const float4* ground_truth, uint32_t width, uint32_t height,
-                        float4* partials, float4* clear, uint64_t clear_count, cudaStream_t stream) {
+                        float4* partials, cudaStream_t stream) {
     static std::atomic<unsigned long long> configured{0};
     const cudaError_t err = allow_smem_once(k_ssim, kSsimSmem, configured);
     if (err != cudaSuccess) return err;
     const dim3 grid(grid_for(width, kTile), grid_for(height, kTile));
-    launch_chained(k_ssim, grid, kThreads, kSsimSmem, stream, image, ground_truth, width, height, window(), partials,
-                   clear, clear_count);
+    launch_chained(k_ssim, grid, kThreads, kSsimSmem, stream, image, ground_truth, width, height, window(), partials);
     return cudaGetLastError();
 }
 
 cudaError_t launch_loss(const float4* image, const float4* ground_truth, const float4* partials, uint32_t width,
                         uint32_t height, const sp_loss_weights& weights, float4* loss_gradient, float4* pixel_loss,
-                        cudaStream_t stream) {
+                        float4* clear, uint64_t clear_count, cudaStream_t stream) {
     static std::atomic<unsigned long long> configured{0};
     const cudaError_t err = allow_smem_once(k_loss, kLossSmem, configured);
     if (err != cudaSuccess) return err;
     const dim3 grid(grid_for(width, kTile), grid_for(height, kTile));
     launch_chained(k_loss, grid, kThreads, kLossSmem, stream, image, ground_truth, partials, width, height, window(), weights,
-                                                  loss_gradient, pixel_loss);
+                                                  loss_gradient, pixel_loss, clear, clear_count);
     return cudaGetLastError();
 }
 

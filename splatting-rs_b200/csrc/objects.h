@@ -86,7 +86,7 @@ struct sp_rasterizer {
     sp_camera_uniform camera{};
     bool has_camera = false;
     bool forward_done = false;
-    // The atomic backward's blend sums were zeroed by the last sp_loss (k_ssim) and no backward
+    // The atomic backward's blend sums were zeroed by the last sp_loss (k_loss) and no backward
     // has added to them since: blend_backward can skip its memset.
     bool blend_sums_zero = false;
     uint32_t sequence = 0;
