@@ -167,9 +167,12 @@ constexpr float kLog2e = 1.4426950408889634f;
 constexpr int kPairWarps = 4;                     // forward / atomic backward: 8 x 8 pixels per warp
 constexpr int kPairThreads = kPairWarps * 32;
 // Atomic backward: a Gaussian's terms from at most this many active lanes are added by those
-// lanes directly (9 atomics each) instead of through the warp reduction (~50 instructions);
-// measured best among 1-16 at config 2 (backward 381 -> 360 us).
-constexpr int kDirectAtomicLanes = 8;
+// lanes directly instead of through the warp reduction (~50 instructions): two float4 vector
+// atomics (sm_90+) and one scalar each, so each lane costs the L2 three atomic operations, not
+// nine. Measured at config 2: 8 -> 20 lanes took the backward from 342 to 319 us (12-24 within
+// 3 us of it; 28 gave 329 us, 32 -- no reduction at all -- 477 us: the L2's atomic units
+// saturate). With scalar atomics the best threshold had been 8.
+constexpr int kDirectAtomicLanes = 20;
 
 // The falloff of one Gaussian at a lane's two pixels (fpx, fpy.x) and (fpx, fpy.y)
 // (rasterize_forward.wgsl:60-66): power = -1/2 (a dx^2 + c dy^2) - b dx dy of the conic
@@ -580,8 +583,10 @@ __global__ void __launch_bounds__(kPairThreads, 6) k_blend_backward_atomic(
             if (__popc(active) <= kDirectAtomicLanes) {
                 // Few lanes hold terms: they add their own, without the warp reduction.
                 if (take0 || take1) {
-#pragma unroll
-                    for (int q = 0; q < 8; ++q) atomicAdd(out + q, v[q]);
+                    // Sums 0-3 (mean, conic a, b) and 4-7 (conic c, colour): float4 words 0 and 1.
+                    float4* out4 = gaussian_gradients + (size_t)st.g[i] * 3;
+                    atomicAdd(out4, make_float4(v[0], v[1], v[2], v[3]));
+                    atomicAdd(out4 + 1, make_float4(v[4], v[5], v[6], v[7]));
                     atomicAdd(out + 8, d_opacity.x + d_opacity.y);
                 }
             } else {
