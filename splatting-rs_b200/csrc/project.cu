@@ -389,8 +389,11 @@ __device__ __forceinline__ void project_backward_one(float* p, uint32_t g, const
     // Opacity and colour (project_backward.wgsl:103-110).
     const float opacity = r1.y;
     p[SP_SLOT_OPACITY] = d_opacity * opacity * (1.0f - opacity);
-    float color_raw[3];
-    raw_color<DEG>(prm, sh, cam, color_raw);
+    // The colour's clamp at zero passes the gradient where the raw colour is positive. The
+    // forward stored max(0, raw) in the record (words 6-8), positive exactly where raw is
+    // (a NaN raw colour is stored as 0 and fails both tests), so the record decides it
+    // without evaluating the SH colour again.
+    const float color_raw[3] = {r1.z, r1.w, r2.x};
     float d_position_sh[3] = {0.0f, 0.0f, 0.0f};
     if (DEG == 0) {
 #pragma unroll
