@@ -407,12 +407,13 @@ sp_status sp_debug_stall_sort_partition(sp_rasterizer* r, uint32_t partition);
  * the current device. */
 sp_status sp_debug_falloff_powers(const float* d_items, uint64_t count, float* d_powers, void* stream);
 
-/* Parity test support (no counterpart in the reference): the Adam step's divisions as its
- * kernels compute them, for `count` operand pairs x, y in device memory. Writes 2 floats per
- * pair to d_quotients (8-byte aligned): x / y as the division by a bias correction
- * 1 - beta^t (y in (0, 1], else 0 is written) and x / y as the update's division by
- * sqrt(v_hat) + epsilon (y in [2^-126, 2^126] or +inf). Both must equal the IEEE
- * single-precision quotient. On `stream` of the current device. */
+/* Parity test support (no counterpart in the reference): the divisions of the Adam step and
+ * the projection as their kernels compute them, for `count` operand pairs x, y in device
+ * memory. Writes 3 floats per pair to d_quotients: x / y as the division by a bias correction
+ * 1 - beta^t (y in (0, 1], else 0 is written), x / y as Adam's division by
+ * sqrt(v_hat) + epsilon (y in [2^-126, 2^126] or +inf, else 0 is written), and x / y as the
+ * projection divides (any y). Each must equal the IEEE single-precision quotient. On
+ * `stream` of the current device. */
 sp_status sp_debug_adam_quotients(const float* d_x, const float* d_y, uint64_t count, float* d_quotients,
                                   void* stream);
 

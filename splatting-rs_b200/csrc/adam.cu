@@ -111,11 +111,14 @@ __global__ void __launch_bounds__(kBlock) k_adam_peer(const PeerBuffers peers, f
 // Test support: the Adam step's two exact divisions on given operands, out[2i] = x / y by
 // div_by_bias (y a bias correction in (0, 1]) and out[2i + 1] = x / y by div_exact.
 __global__ void k_adam_quotients(const float* __restrict__ x, const float* __restrict__ y, uint64_t n,
-                                 float2* __restrict__ out) {
+                                 float* __restrict__ out) {
     const uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= n) return;
     const float a = x[i], b = y[i];
-    out[i] = make_float2(b > 0.0f && b <= 1.0f ? div_by_bias(a, 1.0 / (double)b) : 0.0f, div_exact(a, b));
+    const bool exact_domain = (b >= 1.17549435e-38f && b <= 8.50705917e37f) || b == INFINITY;
+    out[3 * i + 0] = b > 0.0f && b <= 1.0f ? div_by_bias(a, 1.0 / (double)b) : 0.0f;
+    out[3 * i + 1] = exact_domain ? div_exact(a, b) : 0.0f;
+    out[3 * i + 2] = div_rn(a, b);
 }
 
 }  // namespace
@@ -239,7 +242,6 @@ extern "C" sp_status sp_debug_adam_quotients(const float* d_x, const float* d_y,
     if (count == 0) return SP_OK;
     if (!d_x || !d_y || !d_quotients || (reinterpret_cast<uintptr_t>(d_quotients) & 7u) != 0) return SP_ERR_INVALID;
     const unsigned blocks = (unsigned)((count + 255) / 256);
-    k_adam_quotients<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(d_x, d_y, count,
-                                                                              reinterpret_cast<float2*>(d_quotients));
+    k_adam_quotients<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(d_x, d_y, count, d_quotients);
     return cudaGetLastError() == cudaSuccess ? SP_OK : SP_ERR_CUDA;
 }

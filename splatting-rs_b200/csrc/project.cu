@@ -107,12 +107,12 @@ __device__ __forceinline__ void project_one(const float* p, const sp_camera_unif
     Geometry g;
     geometry(p, cam, g);
     if (g.det <= 0.0f) return;
-    const float conic0 = g.c / g.det, conic1 = -g.b / g.det, conic2 = g.a / g.det;
+    const float conic0 = div_rn(g.c, g.det), conic1 = div_rn(-g.b, g.det), conic2 = div_rn(g.a, g.det);
     const float mid = 0.5f * (g.a + g.c);
     const float largest = mid + __fsqrt_rn(max_of(0.1f, mid * mid - g.det));
     const float radius = ceilf(3.0f * __fsqrt_rn(largest));
-    const float mean0 = cam.focal[0] * g.pc[0] / g.pc[2] + cam.principal_point[0];
-    const float mean1 = cam.focal[1] * g.pc[1] / g.pc[2] + cam.principal_point[1];
+    const float mean0 = div_rn(cam.focal[0] * g.pc[0], g.pc[2]) + cam.principal_point[0];
+    const float mean1 = div_rn(cam.focal[1] * g.pc[1], g.pc[2]) + cam.principal_point[1];
     const float tiles0 = (float)cam.tiles_x, tiles1 = (float)cam.tiles_y;
     const float tmin0 = min_of(max_of(floorf((mean0 - radius) / (float)SP_TILE), 0.0f), tiles0);
     const float tmin1 = min_of(max_of(floorf((mean1 - radius) / (float)SP_TILE), 0.0f), tiles1);
@@ -422,7 +422,7 @@ __device__ __forceinline__ void project_backward_one(float* p, uint32_t g, const
         }
         const float dd = dir[0] * d_dir[0] + dir[1] * d_dir[1] + dir[2] * d_dir[2];
 #pragma unroll
-        for (int a = 0; a < 3; ++a) d_position_sh[a] = (d_dir[a] - dir[a] * dd) / len;
+        for (int a = 0; a < 3; ++a) d_position_sh[a] = div_rn(d_dir[a] - dir[a] * dd, len);
     }
     // dL/dcov2d from dL/dconic (project_backward.wgsl:112-121).
     const float C[2][2] = {{r0.z, r0.w}, {r0.w, r1.x}};
@@ -464,13 +464,15 @@ __device__ __forceinline__ void project_backward_one(float* p, uint32_t g, const
             dJ[r][k] = dT[r][0] * geo.W[k][0] + dT[r][1] * geo.W[k][1] + dT[r][2] * geo.W[k][2];
     // project_backward.wgsl:129-141.
     float d_pc[3] = {0.0f, 0.0f, 0.0f};
-    d_pc[0] += geo.clamped[0] ? 0.0f : -fx / geo.z2 * dJ[0][2];
-    d_pc[1] += geo.clamped[1] ? 0.0f : -fy / geo.z2 * dJ[1][2];
-    d_pc[2] += -fx / geo.z2 * dJ[0][0] - fy / geo.z2 * dJ[1][1] + 2.0f * fx * geo.tx / z3 * dJ[0][2] +
-               2.0f * fy * geo.ty / z3 * dJ[1][2];
-    d_pc[0] += d_mean[0] * fx / pc[2];
-    d_pc[1] += d_mean[1] * fy / pc[2];
-    d_pc[2] += -d_mean[0] * fx * pc[0] / geo.z2 - d_mean[1] * fy * pc[1] / geo.z2;
+    // The shader's divisions, each the IEEE quotient (div_rn; -(a / b) is (-a) / b exactly).
+    const float fx_z2 = div_rn(fx, geo.z2), fy_z2 = div_rn(fy, geo.z2);
+    d_pc[0] += geo.clamped[0] ? 0.0f : -fx_z2 * dJ[0][2];
+    d_pc[1] += geo.clamped[1] ? 0.0f : -fy_z2 * dJ[1][2];
+    d_pc[2] += -fx_z2 * dJ[0][0] - fy_z2 * dJ[1][1] + div_rn(2.0f * fx * geo.tx, z3) * dJ[0][2] +
+               div_rn(2.0f * fy * geo.ty, z3) * dJ[1][2];
+    d_pc[0] += div_rn(d_mean[0] * fx, pc[2]);
+    d_pc[1] += div_rn(d_mean[1] * fy, pc[2]);
+    d_pc[2] += div_rn(-d_mean[0] * fx * pc[0], geo.z2) - div_rn(d_mean[1] * fy * pc[1], geo.z2);
 #pragma unroll
     for (int j = 0; j < 3; ++j)
         p[SP_SLOT_POSITION + j] = geo.W[0][j] * d_pc[0] + geo.W[1][j] * d_pc[1] + geo.W[2][j] * d_pc[2];
@@ -485,8 +487,10 @@ __device__ __forceinline__ void project_backward_one(float* p, uint32_t g, const
     cgrad[9] = d_pc[0];
     cgrad[10] = d_pc[1];
     cgrad[11] = d_pc[2];
-    cgrad[12] = d_mean[0] * pc[0] / pc[2] + dJ[0][0] / pc[2] + (geo.clamped[0] ? 0.0f : -geo.tx / geo.z2 * dJ[0][2]);
-    cgrad[13] = d_mean[1] * pc[1] / pc[2] + dJ[1][1] / pc[2] + (geo.clamped[1] ? 0.0f : -geo.ty / geo.z2 * dJ[1][2]);
+    cgrad[12] = div_rn(d_mean[0] * pc[0], pc[2]) + div_rn(dJ[0][0], pc[2]) +
+                (geo.clamped[0] ? 0.0f : div_rn(-geo.tx, geo.z2) * dJ[0][2]);
+    cgrad[13] = div_rn(d_mean[1] * pc[1], pc[2]) + div_rn(dJ[1][1], pc[2]) +
+                (geo.clamped[1] ? 0.0f : div_rn(-geo.ty, geo.z2) * dJ[1][2]);
     if (DEG > 0) {
         // The view direction moves with the position and the camera centre -W^T t.
 #pragma unroll
@@ -528,7 +532,7 @@ __device__ __forceinline__ void project_backward_one(float* p, uint32_t g, const
     };
     const float qdu = geo.q[0] * du[0] + geo.q[1] * du[1] + geo.q[2] * du[2] + geo.q[3] * du[3];
 #pragma unroll
-    for (int k = 0; k < 4; ++k) p[SP_SLOT_ROTATION + k] = (du[k] - geo.q[k] * qdu) / geo.q_length;
+    for (int k = 0; k < 4; ++k) p[SP_SLOT_ROTATION + k] = div_rn(du[k] - geo.q[k] * qdu, geo.q_length);
 }
 
 // FUSED: Adam and the scale clamp are applied to the block's Gaussians as soon as their

@@ -8,6 +8,7 @@
 #pragma once
 
 #include "common.cuh"
+#include "exact_div.cuh"
 
 namespace splat {
 
@@ -59,7 +60,7 @@ __device__ __forceinline__ void geometry(const float* p, const sp_camera_uniform
     const float* qr = p + SP_SLOT_ROTATION;
     g.q_length = __fsqrt_rn(qr[0] * qr[0] + qr[1] * qr[1] + qr[2] * qr[2] + qr[3] * qr[3]);
 #pragma unroll
-    for (int k = 0; k < 4; ++k) g.q[k] = qr[k] / g.q_length;
+    for (int k = 0; k < 4; ++k) g.q[k] = div_rn(qr[k], g.q_length);
     rotation_of(g.q[0], g.q[1], g.q[2], g.q[3], g.R);
 #pragma unroll
     for (int i = 0; i < 3; ++i)
@@ -71,21 +72,21 @@ __device__ __forceinline__ void geometry(const float* p, const sp_camera_uniform
         for (int j = 0; j < 3; ++j)
             g.Sigma[i][j] = g.M[i][0] * g.M[j][0] + g.M[i][1] * g.M[j][1] + g.M[i][2] * g.M[j][2];
     const float fx = cam.focal[0], fy = cam.focal[1];
-    g.limit[0] = SP_VIEW_LIMIT_FACTOR * (float)cam.width / (2.0f * fx);
-    g.limit[1] = SP_VIEW_LIMIT_FACTOR * (float)cam.height / (2.0f * fy);
-    const float xz = g.pc[0] / g.pc[2];
-    const float yz = g.pc[1] / g.pc[2];
+    g.limit[0] = div_rn(SP_VIEW_LIMIT_FACTOR * (float)cam.width, 2.0f * fx);
+    g.limit[1] = div_rn(SP_VIEW_LIMIT_FACTOR * (float)cam.height, 2.0f * fy);
+    const float xz = div_rn(g.pc[0], g.pc[2]);
+    const float yz = div_rn(g.pc[1], g.pc[2]);
     g.clamped[0] = fabsf(xz) > g.limit[0];
     g.clamped[1] = fabsf(yz) > g.limit[1];
     g.tx = min_of(max_of(xz, -g.limit[0]), g.limit[0]) * g.pc[2];
     g.ty = min_of(max_of(yz, -g.limit[1]), g.limit[1]) * g.pc[2];
     g.z2 = g.pc[2] * g.pc[2];
-    g.J[0][0] = fx / g.pc[2];
+    g.J[0][0] = div_rn(fx, g.pc[2]);
     g.J[0][1] = 0.0f;
-    g.J[0][2] = -fx * g.tx / g.z2;
+    g.J[0][2] = div_rn(-fx * g.tx, g.z2);
     g.J[1][0] = 0.0f;
-    g.J[1][1] = fy / g.pc[2];
-    g.J[1][2] = -fy * g.ty / g.z2;
+    g.J[1][1] = div_rn(fy, g.pc[2]);
+    g.J[1][2] = div_rn(-fy * g.ty, g.z2);
 #pragma unroll
     for (int k = 0; k < 3; ++k)
 #pragma unroll
@@ -121,9 +122,9 @@ __device__ __forceinline__ void view_direction(const sp_camera_uniform& cam, con
     for (int j = 0; j < 3; ++j) c[j] = -(r[0][j] * r[0][3] + r[1][j] * r[1][3] + r[2][j] * r[2][3]);
     const float v[3] = {pos[0] - c[0], pos[1] - c[1], pos[2] - c[2]};
     const float len = __fsqrt_rn(v[0] * v[0] + v[1] * v[1] + v[2] * v[2]);
-    dir[0] = v[0] / len;
-    dir[1] = v[1] / len;
-    dir[2] = v[2] / len;
+    dir[0] = div_rn(v[0], len);
+    dir[1] = div_rn(v[1], len);
+    dir[2] = div_rn(v[2], len);
     *length = len;
 }
 

@@ -175,12 +175,15 @@ def test_blend_falloff_power_bit_exact(ctx):
     assert np.array_equal(got.view(np.uint32), want.view(np.uint32)), int(np.sum(got != want))
 
 
-def test_adam_divisions_are_ieee_quotients(ctx):
-    """The Adam step's divisions (csrc/adam_math.cuh: by the bias corrections through a
-    double-precision reciprocal, by sqrt(v_hat) + epsilon through a double-precision
-    Newton-Raphson reciprocal) equal IEEE float32 division bit for bit (NaN for NaN): random
-    dividends over every exponent, the bias corrections of the first 20,000 steps, and
-    update divisors from 1e-15 to 1e19, powers of two and infinity."""
+def test_divisions_are_ieee_quotients(ctx):
+    """The kernels' divisions without the IEEE division instruction sequence
+    (csrc/exact_div.cuh) equal IEEE float32 division bit for bit (NaN for NaN): Adam's by
+    the bias corrections through a double-precision reciprocal and by sqrt(v_hat) + epsilon
+    through a double-precision Newton-Raphson reciprocal, and the projection's div_rn for
+    any divisor. Random dividends over every exponent; the bias corrections of the first
+    20,000 steps; divisors from 1e-15 to 1e19, powers of two, infinity; and for div_rn
+    random divisors over every bit pattern (both signs, zeros, subnormals, above 2^126,
+    infinities, NaN)."""
     import ctypes
 
     import torch
@@ -193,13 +196,20 @@ def test_adam_divisions_are_ieee_quotients(ctx):
     corrections = np.concatenate([np.float32(1) - np.power(np.float32(0.9), t),
                                   np.float32(1) - np.power(np.float32(0.999), t)]).astype(np.float32)
     y = np.empty(n, np.float32)
-    half = n // 2
+    half, quarter = n // 2, n // 4
     y[:half] = rng.choice(corrections, half)
     y[half:] = np.exp(rng.uniform(np.log(1e-15), np.log(1e19), n - half)).astype(np.float32)
     y[half:half + 64] = np.float32(2.0) ** np.arange(-48, 16, dtype=np.float32)
+    # A quarter of the divisors over every bit pattern, then the edges by name.
+    y[half + quarter:] = rng.integers(0, 1 << 32, size=n - half - quarter, dtype=np.uint64).astype(np.uint32).view(
+        np.float32)
+    edges = np.array([0.0, -0.0, np.inf, -np.inf, np.nan, 1e-45, -1e-45, 1.1754942e-38, 1.1754944e-38,
+                      -1.1754944e-38, 8.507059e37, 8.5070597e37, -8.5070597e37, 3.4028235e38, -3.4028235e38,
+                      -1.0, -0.5, -3.0], np.float32)
+    y[-64:-64 + len(edges)] = edges
     y[-16:] = np.inf
     d_x, d_y = torch.from_numpy(x).cuda(), torch.from_numpy(y).cuda()
-    out = torch.empty((n, 2), dtype=torch.float32, device="cuda")
+    out = torch.empty((n, 3), dtype=torch.float32, device="cuda")
     lib = _lib.load()
     status = lib.sp_debug_adam_quotients(ctypes.c_void_p(d_x.data_ptr()), ctypes.c_void_p(d_y.data_ptr()), n,
                                          ctypes.c_void_p(out.data_ptr()),
@@ -209,14 +219,20 @@ def test_adam_divisions_are_ieee_quotients(ctx):
     with np.errstate(all="ignore"):
         want = x / y
     bias = (y > 0) & (y <= 1)
+    update = ((y >= np.float32(2.0) ** -126) & (y <= np.float32(2.0) ** 126)) | (y == np.inf)
 
     def same(a, b):
         nan = np.isnan(b)
         return np.array_equal(np.isnan(a), nan) and np.array_equal(a[~nan].view(np.uint32), b[~nan].view(np.uint32))
 
-    assert bias.sum() > half
-    assert same(got[bias, 0], want[bias]), int(np.sum(got[bias, 0].view(np.uint32) != want[bias].view(np.uint32)))
-    assert same(got[:, 1], want), int(np.sum(got[:, 1].view(np.uint32) != want.view(np.uint32)))
+    def differ(a, b):
+        return int(np.sum(a.view(np.uint32) != b.view(np.uint32)))
+
+    assert bias.sum() > half and update.sum() > half
+    assert same(got[bias, 0], want[bias]), differ(got[bias, 0], want[bias])
+    assert same(got[update, 1], want[update]), differ(got[update, 1], want[update])
+    assert (~update).sum() > n // 16  # div_rn's fallback is exercised
+    assert same(got[:, 2], want), differ(got[:, 2], want)
 
 
 def test_blend_work_counts(ctx):
