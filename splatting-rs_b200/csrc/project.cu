@@ -2,7 +2,9 @@
 // the block totals, and the projection backward (K9) with the camera-gradient reduction
 // (K10) fused in. This file is compiled with -fmad=false: the projection's depth, radius
 // and tile rectangle must match the CPU oracle bit for bit (tile lists are compared
-// exactly), and the backward shares the same forward recomputation.
+// exactly), and the backward shares the same forward recomputation. The backward's
+// divisions go through div_rn (csrc/exact_div.cuh), the same IEEE quotients in fewer
+// instructions, so its gradients are the oracle's bit for bit too.
 #include <cuda/atomic>
 
 #include "adam_math.cuh"
@@ -107,12 +109,12 @@ __device__ __forceinline__ void project_one(const float* p, const sp_camera_unif
     Geometry g;
     geometry(p, cam, g);
     if (g.det <= 0.0f) return;
-    const float conic0 = div_rn(g.c, g.det), conic1 = div_rn(-g.b, g.det), conic2 = div_rn(g.a, g.det);
+    const float conic0 = g.c / g.det, conic1 = -g.b / g.det, conic2 = g.a / g.det;
     const float mid = 0.5f * (g.a + g.c);
     const float largest = mid + __fsqrt_rn(max_of(0.1f, mid * mid - g.det));
     const float radius = ceilf(3.0f * __fsqrt_rn(largest));
-    const float mean0 = div_rn(cam.focal[0] * g.pc[0], g.pc[2]) + cam.principal_point[0];
-    const float mean1 = div_rn(cam.focal[1] * g.pc[1], g.pc[2]) + cam.principal_point[1];
+    const float mean0 = cam.focal[0] * g.pc[0] / g.pc[2] + cam.principal_point[0];
+    const float mean1 = cam.focal[1] * g.pc[1] / g.pc[2] + cam.principal_point[1];
     const float tiles0 = (float)cam.tiles_x, tiles1 = (float)cam.tiles_y;
     const float tmin0 = min_of(max_of(floorf((mean0 - radius) / (float)SP_TILE), 0.0f), tiles0);
     const float tmin1 = min_of(max_of(floorf((mean1 - radius) / (float)SP_TILE), 0.0f), tiles1);
@@ -378,7 +380,7 @@ __device__ __forceinline__ void project_backward_one(float* p, uint32_t g, const
         densify_stats[g] = st;
     }
     Geometry geo;
-    geometry(prm, cam, geo);
+    geometry<true>(prm, cam, geo);
     if (geo.det <= 0.0f) {
         zero_sh();
         return;
@@ -403,7 +405,7 @@ __device__ __forceinline__ void project_backward_one(float* p, uint32_t g, const
 #pragma unroll
         for (int c = 0; c < 3; ++c) d_col[c] = color_raw[c] > 0.0f ? d_color[c] : 0.0f;
         float dir[3], len;
-        view_direction(cam, prm, dir, &len);
+        view_direction<true>(cam, prm, dir, &len);
         float b[16];
         sh_basis<DEG>(dir[0], dir[1], dir[2], b);
         constexpr int kCount = (DEG + 1) * (DEG + 1);

@@ -20,6 +20,15 @@ __device__ __forceinline__ float row_dot(const float r[4], float x, float y, flo
     return r[0] * x + r[1] * y + r[2] * z + r[3] * 1.0f;
 }
 
+// u / d, the IEEE quotient either way: NEWTON takes div_rn (a double-precision reciprocal,
+// fewer instructions where the divisor is in its domain: the backward), otherwise the
+// compiler's division (the forward, where div_rn measured slower).
+template <bool NEWTON>
+__device__ __forceinline__ float quotient(float u, float d) {
+    if constexpr (NEWTON) return div_rn(u, d);
+    else return u / d;
+}
+
 struct Geometry {
     float pc[3];
     float scale[3];
@@ -50,6 +59,7 @@ __device__ __forceinline__ void rotation_of(float r, float x, float y, float z, 
     R[2][2] = 1.0f - 2.0f * (x * x + y * y);
 }
 
+template <bool NEWTON = false>
 __device__ __forceinline__ void geometry(const float* p, const sp_camera_uniform& cam, Geometry& g) {
     const float (*rows)[4] = cam.world_to_camera_rows;
     g.pc[0] = row_dot(rows[0], p[0], p[1], p[2]);
@@ -60,7 +70,7 @@ __device__ __forceinline__ void geometry(const float* p, const sp_camera_uniform
     const float* qr = p + SP_SLOT_ROTATION;
     g.q_length = __fsqrt_rn(qr[0] * qr[0] + qr[1] * qr[1] + qr[2] * qr[2] + qr[3] * qr[3]);
 #pragma unroll
-    for (int k = 0; k < 4; ++k) g.q[k] = div_rn(qr[k], g.q_length);
+    for (int k = 0; k < 4; ++k) g.q[k] = quotient<NEWTON>(qr[k], g.q_length);
     rotation_of(g.q[0], g.q[1], g.q[2], g.q[3], g.R);
 #pragma unroll
     for (int i = 0; i < 3; ++i)
@@ -72,21 +82,21 @@ __device__ __forceinline__ void geometry(const float* p, const sp_camera_uniform
         for (int j = 0; j < 3; ++j)
             g.Sigma[i][j] = g.M[i][0] * g.M[j][0] + g.M[i][1] * g.M[j][1] + g.M[i][2] * g.M[j][2];
     const float fx = cam.focal[0], fy = cam.focal[1];
-    g.limit[0] = div_rn(SP_VIEW_LIMIT_FACTOR * (float)cam.width, 2.0f * fx);
-    g.limit[1] = div_rn(SP_VIEW_LIMIT_FACTOR * (float)cam.height, 2.0f * fy);
-    const float xz = div_rn(g.pc[0], g.pc[2]);
-    const float yz = div_rn(g.pc[1], g.pc[2]);
+    g.limit[0] = quotient<NEWTON>(SP_VIEW_LIMIT_FACTOR * (float)cam.width, 2.0f * fx);
+    g.limit[1] = quotient<NEWTON>(SP_VIEW_LIMIT_FACTOR * (float)cam.height, 2.0f * fy);
+    const float xz = quotient<NEWTON>(g.pc[0], g.pc[2]);
+    const float yz = quotient<NEWTON>(g.pc[1], g.pc[2]);
     g.clamped[0] = fabsf(xz) > g.limit[0];
     g.clamped[1] = fabsf(yz) > g.limit[1];
     g.tx = min_of(max_of(xz, -g.limit[0]), g.limit[0]) * g.pc[2];
     g.ty = min_of(max_of(yz, -g.limit[1]), g.limit[1]) * g.pc[2];
     g.z2 = g.pc[2] * g.pc[2];
-    g.J[0][0] = div_rn(fx, g.pc[2]);
+    g.J[0][0] = quotient<NEWTON>(fx, g.pc[2]);
     g.J[0][1] = 0.0f;
-    g.J[0][2] = div_rn(-fx * g.tx, g.z2);
+    g.J[0][2] = quotient<NEWTON>(-fx * g.tx, g.z2);
     g.J[1][0] = 0.0f;
-    g.J[1][1] = div_rn(fy, g.pc[2]);
-    g.J[1][2] = div_rn(-fy * g.ty, g.z2);
+    g.J[1][1] = quotient<NEWTON>(fy, g.pc[2]);
+    g.J[1][2] = quotient<NEWTON>(-fy * g.ty, g.z2);
 #pragma unroll
     for (int k = 0; k < 3; ++k)
 #pragma unroll
@@ -114,6 +124,7 @@ __device__ __forceinline__ void geometry(const float* p, const sp_camera_uniform
 }
 
 // Camera centre -W^T t and the unit direction from it to `pos` (SH degree >= 1).
+template <bool NEWTON = false>
 __device__ __forceinline__ void view_direction(const sp_camera_uniform& cam, const float* pos, float dir[3],
                                                float* length) {
     const float (*r)[4] = cam.world_to_camera_rows;
@@ -122,9 +133,9 @@ __device__ __forceinline__ void view_direction(const sp_camera_uniform& cam, con
     for (int j = 0; j < 3; ++j) c[j] = -(r[0][j] * r[0][3] + r[1][j] * r[1][3] + r[2][j] * r[2][3]);
     const float v[3] = {pos[0] - c[0], pos[1] - c[1], pos[2] - c[2]};
     const float len = __fsqrt_rn(v[0] * v[0] + v[1] * v[1] + v[2] * v[2]);
-    dir[0] = div_rn(v[0], len);
-    dir[1] = div_rn(v[1], len);
-    dir[2] = div_rn(v[2], len);
+    dir[0] = quotient<NEWTON>(v[0], len);
+    dir[1] = quotient<NEWTON>(v[1], len);
+    dir[2] = quotient<NEWTON>(v[2], len);
     *length = len;
 }
 
