@@ -113,7 +113,7 @@ def test_within_two_ulp_of_cuda_expf(table, name):
 
 # Adam's bias-corrected moments (adam.wgsl:30-31: m / (1 - beta1^t), v / (1 - beta2^t)) are IEEE
 # float divisions in the reference and the oracle; the CUDA kernels form them as the float
-# rounding of x * RN64(1 / b) (div_by_bias in csrc/adam_math.cuh, with a proof that the two are
+# rounding of x * RN64(1 / b) (div_by_bias in csrc/exact_div.cuh, with a proof that the two are
 # equal for every float x and every float b in [2^-126, 1]). Checked here with numpy's IEEE
 # float32 division and float64 product.
 
